@@ -1,0 +1,143 @@
+"""Seeded parameter/gradient sets shared by the golden generator and the tests.
+
+Inputs are rebuilt from seeds everywhere (``torch.manual_seed(0)`` before the
+params in group order; ``torch.manual_seed(1000 + s)`` before step ``s``'s
+grads in param order), so fixtures only need to hold outputs.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+TORCH_DTYPES = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
+
+
+def _conv_flat(shape):
+    o, i, k = shape
+    return (o, i * k)
+
+
+def _vad_groups(flatten=True, grad_dtype="f32"):
+    convs = []
+    for i in range(24):
+        convs.append([(64, 32, 3), (64, 64, 3), (128, 64, 5), (128, 128, 3)][i % 4])
+    mats = [(_conv_flat(c) if flatten else c) for c in convs] + [(128, 128)] * 4 + [(2, 128)] * 2
+    vecs = []
+    for c in convs:
+        vecs += [(c[0],)] * 3          # conv bias, BN weight, BN bias
+    vecs += [(128,)] * 4 + [(2,)] * 2  # Linear biases
+    return [
+        dict(orthogonalize=True, shapes=mats, init=("normal", 0.05), dtype="f32",
+             opts=dict(lr=1e-3, betas=(0.9, 0.95), weight_decay=0.1)),
+        dict(orthogonalize=False, shapes=vecs, init=("normal", 0.05), dtype="f32",
+             opts=dict(lr=1e-3, betas=(0.9, 0.95), weight_decay=0.0)),
+    ]
+
+
+CASES = {
+    # BASELINE config 1 ("CPU-runnable tiny step"), exact shapes.
+    "tiny": dict(steps=10, grad_std=1e-3, groups=[
+        dict(orthogonalize=True, shapes=[(512, 512)] * 4 + [(1024, 512)] * 2 + [(512, 1024)] * 2,
+             init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=1e-3, betas=(0.9, 0.95), weight_decay=0.1, scaling_mode="moonlight")),
+        dict(orthogonalize=False, shapes=[(512,)] * 8, init=("const", 1.0), dtype="f32",
+             opts=dict(lr=1e-3, betas=(0.9, 0.95), weight_decay=0.0, scaling_mode="moonlight")),
+    ]),
+    # Same structure at reduced shapes, stored in full.
+    "tiny_small": dict(steps=10, grad_std=1e-3, groups=[
+        dict(orthogonalize=True, shapes=[(64, 64)] * 4 + [(128, 64)] * 2 + [(64, 128)] * 2,
+             init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=1e-3, betas=(0.9, 0.95), weight_decay=0.1, scaling_mode="moonlight")),
+        dict(orthogonalize=False, shapes=[(64,)] * 8, init=("const", 1.0), dtype="f32",
+             opts=dict(lr=1e-3, betas=(0.9, 0.95), weight_decay=0.0, scaling_mode="moonlight")),
+    ]),
+    # Magnitude-direction decoupling on both groups (split row/col gains, scalar gains).
+    "md_small": dict(steps=4, grad_std=1e-3, groups=[
+        dict(orthogonalize=True, shapes=[(64, 64), (96, 64), (64, 160), (128, 128)],
+             init=("normal", 0.02), dtype="f32", opts=dict(lr=8e-3, decouple_md=True)),
+        dict(orthogonalize=False, shapes=[(64,), (32,), (48, 16)], init=("normal", 0.5), dtype="f32",
+             opts=dict(lr=1e-3, decouple_md=True, weight_decay=0.05)),
+    ]),
+    # bf16 params with state in the param dtype (the reference's own layout).
+    "bf16_small": dict(steps=4, grad_std=1e-4, groups=[
+        dict(orthogonalize=True, shapes=[(64, 64), (192, 64), (64, 192), (128, 64)],
+             init=("normal", 0.02), dtype="bf16", opts=dict(lr=1e-3, betas=(0.9, 0.95), weight_decay=0.1)),
+        dict(orthogonalize=False, shapes=[(64,), (128, 32)], init=("normal", 0.02), dtype="bf16",
+             opts=dict(lr=1e-3, weight_decay=0.1)),
+    ]),
+    # 3-D conv kernels are batches of (in, k) matrices (thorn.py:628-633).
+    "conv_small": dict(steps=3, grad_std=1e-3, groups=[
+        dict(orthogonalize=True, shapes=[(8, 4, 3), (16, 8, 5), (4, 6, 6)], init=("normal", 0.05),
+             dtype="f32", opts=dict(lr=1e-3, weight_decay=0.1, scaling_mode="jordan")),
+        dict(orthogonalize=False, shapes=[(16,)], init=("const", 1.0), dtype="f32", opts=dict(lr=1e-3)),
+    ]),
+    # Option variants: jordan scaling + forced per-neuron norm; RAdam rectification with eps>0.
+    "variants_small": dict(steps=8, grad_std=1e-3, groups=[
+        dict(orthogonalize=True, shapes=[(64, 64), (64, 96), (96, 32)], init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=2e-3, betas=(0.95, 0.9), weight_decay=0.2, scaling_mode="jordan",
+                       force_per_neuron_norm=True)),
+        dict(orthogonalize=True, shapes=[(80, 48)], init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=2e-3, betas=(0.9, 0.0), weight_decay=0.0, scaling_mode="md")),
+        dict(orthogonalize=False, shapes=[(64,), (40, 24)], init=("normal", 0.1), dtype="f32",
+             opts=dict(lr=1e-3, rectify=True, eps=1e-8, weight_decay=0.1, betas=(0.9, 0.95))),
+    ]),
+    # BASELINE config 2 shapes (flattened conv kernels) -- the many-tiny-matrices case.
+    "vad": dict(steps=3, grad_std=1e-3, groups=_vad_groups(flatten=True)),
+}
+
+
+def build_params(case: dict):
+    """Per group, a list of CPU tensors in the group's dtype."""
+    torch.manual_seed(0)
+    out = []
+    for grp in case["groups"]:
+        dt = TORCH_DTYPES[grp["dtype"]]
+        ps = []
+        for shp in grp["shapes"]:
+            kind, val = grp["init"]
+            if kind == "normal":
+                t = torch.randn(shp) * val
+            else:
+                t = torch.full(shp, float(val))
+            ps.append(t.to(dt))
+        out.append(ps)
+    return out
+
+
+def build_grads(case: dict, s: int):
+    """Grads for step ``s`` (0-based), per group, in the group's dtype."""
+    torch.manual_seed(1000 + s)
+    out = []
+    for grp in case["groups"]:
+        dt = TORCH_DTYPES[grp["dtype"]]
+        out.append([(torch.randn(shp) * case["grad_std"]).to(dt) for shp in grp["shapes"]])
+    return out
+
+
+def group_dicts(case: dict, params):
+    """Reference-style param-group dicts (without the dtype bookkeeping)."""
+    gs = []
+    for grp, ps in zip(case["groups"], params):
+        gs.append({"orthogonalize": grp["orthogonalize"], "params": ps, **grp["opts"]})
+    return gs
+
+
+def probe_vector(n: int) -> np.ndarray:
+    """Deterministic projection vector for checksums (no RNG involved)."""
+    i = np.arange(n, dtype=np.float64)
+    return np.cos(0.37 * i + 0.11)
+
+
+def checksum(a: np.ndarray) -> np.ndarray:
+    x = np.asarray(a, dtype=np.float64).reshape(-1)
+    return np.array([x.sum(), (x * x).sum(), (x * probe_vector(x.size)).sum()], dtype=np.float64)
+
+
+def rel_fro(a, b) -> float:
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    den = math.sqrt(float((b * b).sum()))
+    num = math.sqrt(float(((a - b) ** 2).sum()))
+    return num / den if den > 0 else num

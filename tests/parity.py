@@ -1,0 +1,91 @@
+"""Comparison helpers shared by the oracle pin tests and the GPU parity tests."""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+import cases as C
+
+
+def load_golden(path: str) -> dict:
+    with np.load(path) as z:
+        return {k: z[k] for k in z.files}
+
+
+def run_oracle(name: str, steps: int | None = None, state_dtype: str | None = None, cpu_quirks: bool = False):
+    """Step the CPU oracle on a case; returns (oracle, snapshots{tag: (params, states)}).
+
+    ``cpu_quirks`` reproduces torch-CPU scalar rounding (used to pin the oracle
+    against the golden vectors, which were produced on CPU).
+    """
+    from oracle import thorn_oracle as O
+    from oracle.thorn_oracle import OracleTHORN
+
+    O.CPU_ALPHA_ROUNDING = cpu_quirks
+
+    case = C.CASES[name]
+    params = C.build_params(case)
+    groups = []
+    for grp, ps in zip(case["groups"], params):
+        d = {"orthogonalize": grp["orthogonalize"], "dtype": grp["dtype"], **grp["opts"]}
+        if state_dtype:
+            d["state_dtype"] = state_dtype
+        d["params"] = [t.float().numpy() for t in ps]
+        groups.append(d)
+    orc = OracleTHORN(groups)
+    n = case["steps"] if steps is None else steps
+    snaps = {}
+    for s in range(n):
+        grads = C.build_grads(case, s)
+        orc.step([[t.float().numpy() for t in gs] for gs in grads])
+        if s == 0 or s == n - 1:
+            tag = "step1" if s == 0 else "final"
+            snaps[tag] = (
+                [[p.copy() for p in g.params] for g in orc.groups],
+                [[{k: (np.array(v, copy=True) if isinstance(v, np.ndarray) else v) for k, v in st.items()}
+                  for st in g.state] for g in orc.groups],
+            )
+    return orc, snaps
+
+
+def compare_tensor(mine: np.ndarray, gold: dict, key: str, base: np.ndarray | None = None):
+    """Relative error of ``mine`` (minus ``base``) against a golden entry.
+
+    Returns the worst of: relative Frobenius error over the stored values
+    (full array or head), and the checksum bound |d proj| / (||d|| ||r||).
+    """
+    mine = np.asarray(mine, dtype=np.float64)
+    b = np.zeros_like(mine) if base is None else np.asarray(base, dtype=np.float64)
+    if key + "/full" in gold:
+        ref = gold[key + "/full"].astype(np.float64).reshape(mine.shape)
+        return C.rel_fro(mine - b, ref - b)
+    head = gold[key + "/head"].astype(np.float64)
+    n = head.size
+    e1 = C.rel_fro((mine - b).reshape(-1)[:n], head - b.reshape(-1)[:n])
+    cs_ref = gold[key + "/sum"]
+    cs_mine = C.checksum(mine)
+    cs_base = C.checksum(b)
+    d = (mine - b).reshape(-1)
+    scale = math.sqrt(float((d * d).sum())) * math.sqrt(float((C.probe_vector(d.size) ** 2).sum()))
+    e2 = abs((cs_mine[2] - cs_base[2]) - (cs_ref[2] - cs_base[2])) / max(scale, 1e-30)
+    sq_scale = max(float((mine * mine).sum()), 1e-30)
+    e3 = abs(cs_mine[1] - cs_ref[1]) / sq_scale if base is None else 0.0
+    return max(e1, e2, e3)
+
+
+def compare_run(name: str, gold: dict, snaps: dict, init_params):
+    """Per (tag, group, param, key) relative errors; params compared as cumulative updates."""
+    errs = {}
+    for tag, (params, states) in snaps.items():
+        for gi, (ps, sts) in enumerate(zip(params, states)):
+            for pi, (p, st) in enumerate(zip(ps, sts)):
+                base = f"{tag}/g{gi}/p{pi}"
+                errs[(tag, gi, pi, "param")] = compare_tensor(p, gold, base + "/param", init_params[gi][pi])
+                for k, v in st.items():
+                    if k == "step":
+                        assert int(v) == int(gold[f"{base}/{k}"]), (base, k)
+                        continue
+                    if isinstance(v, np.ndarray) or np.isscalar(v):
+                        errs[(tag, gi, pi, k)] = compare_tensor(np.asarray(v, dtype=np.float32), gold, f"{base}/{k}")
+    return errs
