@@ -1,0 +1,240 @@
+/*
+ * thorn_b200: C ABI of the B200 (sm_100a) kernels behind the THORN optimizer step.
+ *
+ * Every entry point takes device pointers, sizes and scalars plus a CUDA
+ * stream (as `void*`, NULL = legacy default stream), enqueues its kernels on
+ * that stream and returns a status code (THORN_OK == 0).  None of them
+ * allocates device memory or synchronises the host; scratch space is passed in
+ * by the caller.  Tensors are dense row-major.  A matrix tensor of any rank >= 2
+ * is viewed as `batch x rows x cols` (batch = product of the leading dims),
+ * which is how the reference treats conv kernels (thorn.py:628-633).
+ *
+ * File references are to thorn/thorn.py of pykeio/THORN v3.1.1.
+ */
+#ifndef THORN_B200_H
+#define THORN_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define THORN_API __attribute__((visibility("default")))
+#else
+#define THORN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+#define THORN_F32 0
+#define THORN_BF16 1
+#define THORN_F16 2
+
+/* status codes */
+#define THORN_OK 0
+#define THORN_ERR_ARG 1          /* bad size / dtype / null pointer */
+#define THORN_ERR_ALIGN 2        /* pointer or leading dimension not aligned as required */
+#define THORN_ERR_CUDA 3         /* a CUDA runtime call or kernel launch failed */
+#define THORN_ERR_UNSUPPORTED 4  /* no device / wrong architecture / missing driver entry point */
+
+/* --------------------------------------------------------------------------
+ * Library information
+ * ------------------------------------------------------------------------ */
+THORN_API int thorn_abi_version(void);
+THORN_API const char* thorn_status_string(int status);
+/* Number of kernels this library has launched in this process. */
+THORN_API uint64_t thorn_launch_count(void);
+/* cudaError_t of the last failing CUDA call inside the library (0 if none). */
+THORN_API int thorn_last_cuda_error(void);
+/* Tensor-core work issued by thorn_ns_batched / thorn_sym_addmm so far:
+ * dense-equivalent FLOPs (2 M N K per product) and FLOPs of the tiles
+ * actually executed (lower-triangle tiles only for symmetric products). */
+THORN_API void thorn_gemm_flops(double* dense, double* executed);
+
+/* --------------------------------------------------------------------------
+ * (R)Adam(-atan2)W over many tensors in one launch per dtype pair.
+ * Replaces _adam_update (thorn.py:838-888) and its Triton kernel
+ * _adam_update_kernel (thorn.py:147-185), which the reference launches once
+ * per parameter (thorn.py:859-874).
+ *   m <- m + (g - m)(1 - beta1);  v <- beta2 v + (1 - beta2) g^2
+ *   u  = atan2(m bc1, sqrt(v bc2))          (eps == 0)
+ *      = m bc1 / (sqrt(v bc2) + eps)        (eps > 0)
+ *      = m                                   (degenerate: RAdam rect == 0)
+ *   u <- u + wd p  where u p >= 0 (cautious weight decay);  p <- p - lr u
+ * ------------------------------------------------------------------------ */
+typedef struct {
+  void* p;            /* param (p_dtype); NULL: update the moments only */
+  const void* g;      /* grad (p_dtype) */
+  void* m;            /* first moment (s_dtype) */
+  void* v;            /* second moment (s_dtype) */
+  int64_t numel;
+  float lr;           /* group lr * rect * magma scale */
+  float bc1;          /* 1 / (1 - beta1^step) */
+  float bc2;          /* 1 / (1 - beta2^step) */
+  int32_t degenerate; /* nonzero: u = m (rect == 0) */
+} thorn_adam_tensor;
+
+THORN_API int thorn_adamw_multi(const thorn_adam_tensor* tensors, int n, int p_dtype, int s_dtype,
+                      float beta1, float beta2, float weight_decay, float eps, void* stream);
+
+/* --------------------------------------------------------------------------
+ * Orthogonalized group, before Newton-Schulz: momentum + Nesterov, and the
+ * per-matrix sum of squares needed to normalise the NS input.  With m == NULL
+ * only the md part runs (no momentum, normsq unused): the direction recovery
+ * of the (R)AdamW group with decouple_md (thorn.py:1704-1705).
+ * Replaces _update_momentum (thorn.py:1376-1381):  m <- beta1 m + g;
+ * u = g + beta1 m (rounded to u_dtype; u itself is not stored -- the NS
+ * input pass recomputes it from g and the new m).  With md != 0 it also does
+ * _recover_direction (thorn.py:890-908): gain = row_sp col_sp (or the scalar
+ * gain); p <- p / gain; g <- g gain (stored back when write_grad != 0) and
+ * accumulates the gain-gradient sums of _update_magnitude (thorn.py:910-932):
+ *   row_gsum[i] += sum_j round(round(p_dir g_raw) col_sp[j])
+ *   col_gsum[j] += sum_i round(round(p_dir g_raw) row_sp[i])
+ * (or row_gsum[0] += sum of round(p_dir g_raw) for a scalar gain).
+ * Accumulators (normsq, *_gsum) must be zeroed by the caller.
+ * ------------------------------------------------------------------------ */
+typedef struct {
+  void* p;
+  void* g;
+  void* m;
+  float* normsq;      /* out (+=): per sub-matrix sum of u^2, [batch] */
+  int64_t batch, rows, cols;
+  const float* row_sp;  /* md: softplus(row_gain) rounded to p dtype, [batch*rows] (scalar gain: [1]) */
+  const float* col_sp;  /* md: softplus(col_gain) rounded to p dtype, [batch*cols] (scalar gain: unused) */
+  int32_t scalar_gain;  /* md: nonzero when the gain is one scalar, row_sp[0] */
+  float* row_gsum;      /* md out (+=): [batch*rows] (scalar gain: [1]) */
+  float* col_gsum;      /* md out (+=): [batch*cols] (unused for a scalar gain) */
+} thorn_ortho_pre_tensor;
+
+THORN_API int thorn_ortho_pre_multi(const thorn_ortho_pre_tensor* tensors, int n, int p_dtype, int s_dtype,
+                          int u_dtype, float beta1, int md, int write_grad, void* stream);
+
+/* --------------------------------------------------------------------------
+ * Newton-Schulz input: X = ns(u / (||u||_F + 1e-8)), transposed to the wide
+ * orientation (rows <= cols) when the sub-matrix is tall.  Replaces
+ * thorn.py:629-635.  u = round_u(fma(beta1, m, g_eff)) is recomputed from the
+ * gradient and the moment written by thorn_ortho_pre_multi, with
+ * g_eff = round_p(g * gain) when md != 0 (g still holds the raw gradient,
+ * i.e. the pre pass ran with write_grad == 0) and g_eff = g otherwise.
+ * x is [batch, min(r,c), ld] with ld = thorn_ns_ld(max(r,c)).
+ * ------------------------------------------------------------------------ */
+typedef struct {
+  const void* g;
+  const void* m;
+  const float* normsq;  /* [batch] sums of squares from thorn_ortho_pre_multi */
+  void* x;              /* out, ns_dtype */
+  int64_t batch, rows, cols;
+  const float* row_sp;  /* md gains as in thorn_ortho_pre_tensor */
+  const float* col_sp;
+  int32_t scalar_gain;
+  int32_t md;
+} thorn_ns_cast_tensor;
+
+THORN_API int64_t thorn_ns_ld(int64_t n);
+THORN_API int thorn_ns_cast_multi(const thorn_ns_cast_tensor* tensors, int n, int p_dtype, int s_dtype, int u_dtype,
+                        int ns_dtype, float beta1, void* stream);
+
+/* --------------------------------------------------------------------------
+ * Newton-Schulz polar factor of a batch of same-shape matrices.
+ * Replaces _polar_decomp_impl (thorn.py:626-662) with its custom op
+ * thorn::sym_addmm (thorn.py:298-377) and torch.bmm/baddbmm (thorn.py:614-624,
+ * 653).  x: normalised input from thorn_ns_cast_multi, [batch, m, ld(n)] with
+ * m = min(rows, cols), n = max(rows, cols).  out: [batch, rows, cols] in the
+ * original orientation, ns_dtype.  Runs the standard quintic for square
+ * matrices and Gram Newton-Schulz (restarts at the listed iterations) for
+ * rectangular ones, with the reference's recurrences and coefficients.
+ * err_flag: device int set nonzero if a bounded wait in a kernel gave up
+ * (may be NULL).
+ * ------------------------------------------------------------------------ */
+THORN_API int64_t thorn_ns_workspace_bytes(int64_t batch, int64_t rows, int64_t cols);
+THORN_API int thorn_ns_batched(const void* x, void* out, void* workspace, int64_t workspace_bytes,
+                     int64_t batch, int64_t rows, int64_t cols, int ns_dtype,
+                     const double* coeffs, int iters, const int32_t* restarts, int n_restarts,
+                     int* err_flag, void* stream);
+
+/* O = alpha A@B + beta C for symmetric A@B and C: the thorn::sym_addmm
+ * contract (thorn.py:298-363).  A [batch, M, K], B [batch, K, M],
+ * C [batch, M, M] (c_batched) or [M, M] or NULL, O [batch, M, M]; all with
+ * leading dimensions a multiple of 8 elements.  Only tiles on or below the
+ * diagonal are computed; the upper triangle is the mirror of the lower. */
+THORN_API int thorn_sym_addmm(const void* A, const void* B, const void* C, void* O, int64_t batch, int64_t M,
+                    int64_t K, int c_batched, float alpha, float beta, int dtype, int* err_flag,
+                    void* stream);
+
+/* --------------------------------------------------------------------------
+ * Per-neuron (row) normalisation statistics for tall matrices.
+ * Replaces _pnn_row_stats_kernel (thorn.py:205-228) and _pnn_reduce_kernel
+ * (thorn.py:230-253) of _per_neuron_norm_update (thorn.py:709-757):
+ *   sumsq_r = sum_j u_rj^2;  s_r = rsqrt(max(sumsq_r / N, eps))
+ *   stats[b] += {sumsq_r, s_r^2 sumsq_r}  (gscale = sqrt(.0) / max(sqrt(.1), eps))
+ * u is the NS output rounded to p_dtype; eps = finfo(p_dtype).eps.
+ * mat_stats must be zeroed by the caller.
+ * ------------------------------------------------------------------------ */
+typedef struct {
+  const void* U;        /* ns_dtype [batch, rows, cols] */
+  float* row_scale;     /* out: s_r, [batch*rows] */
+  float* mat_stats;     /* out (+=): [batch][2] */
+  int64_t batch, rows, cols;
+} thorn_pnn_tensor;
+
+THORN_API int thorn_pnn_stats_multi(const thorn_pnn_tensor* tensors, int n, int u_dtype, int p_dtype, void* stream);
+
+/* --------------------------------------------------------------------------
+ * Orthogonalized group, after Newton-Schulz: scale and apply.
+ * Replaces _ortho_post (thorn.py:1399-1413), _weight_decay_update
+ * (thorn.py:683-702, Triton _wd_update_kernel thorn.py:187-203) and
+ * _pnn_apply_kernel (thorn.py:255-280):
+ *   u = round_p(U) * s_r * gscale_b   (pnn; or * row_scale[r] when mat_stats is NULL)
+ *   u <- u + wd p where u p >= 0;  p <- p - lr u
+ * With p_normsq != NULL also accumulates ||p_new||^2 per sub-matrix (for
+ * the decouple_md renorm).  U may be ns_dtype (bf16/f16) or f32.
+ * ------------------------------------------------------------------------ */
+typedef struct {
+  const void* U;
+  void* p;
+  const float* row_scale;  /* NULL: no row scaling */
+  const float* mat_stats;  /* NULL: row_scale is the final factor */
+  float* p_normsq;         /* NULL or out (+=) [batch] */
+  int64_t batch, rows, cols;
+  float lr;                /* lr * lr_scale (thorn.py:768-780) * magma scale */
+} thorn_ortho_post_tensor;
+
+THORN_API int thorn_ortho_post_multi(const thorn_ortho_post_tensor* tensors, int n, int u_dtype, int p_dtype,
+                           float weight_decay, void* stream);
+
+/* --------------------------------------------------------------------------
+ * Magnitude-direction decoupling helpers (thorn.py:910-977, 1414-1421).
+ * thorn_md_prep:   sp = round_p(softplus(gain)), sig = round_p(sigmoid(gain)) as fp32
+ * thorn_md_gain_grad: grad = round_p(round_p(gsum) * sig)  (p_dtype output)
+ * thorn_md_finalize_multi: renorm to the target norm, then multiply by the
+ *   new gains:  p <- round(round(round(p * round(target / round(round(||p||) + 1e-8)))
+ *                 * row_sp) * col_sp)   (scalar gain: one multiply)
+ * ------------------------------------------------------------------------ */
+THORN_API int thorn_md_prep(const void* gain, int64_t n, float* sp, float* sig, int p_dtype, void* stream);
+THORN_API int thorn_md_gain_grad(const float* gsum, const float* sig, void* grad, int64_t n, int p_dtype,
+                       void* stream);
+
+typedef struct {
+  void* p;
+  const float* normsq;   /* [batch] ||p||^2 (NULL: no renorm) */
+  const float* target;   /* target norm per sub-matrix (stride target_stride) */
+  int64_t target_stride; /* 0: one target for all sub-matrices */
+  const float* row_sp;   /* [batch*rows] (scalar gain: [1]) */
+  const float* col_sp;   /* [batch*cols] (scalar gain: unused) */
+  int32_t scalar_gain;
+  int64_t batch, rows, cols;
+} thorn_md_final_tensor;
+
+THORN_API int thorn_md_finalize_multi(const thorn_md_final_tensor* tensors, int n, int p_dtype, void* stream);
+
+/* Sum of squares per sub-matrix (for renorm on paths that do not run
+ * thorn_ortho_post_multi): out[b] += sum x^2 over batch b.  out zeroed by caller. */
+THORN_API int thorn_sumsq_multi(const void* const* x, float* const* out, const int64_t* batch,
+                      const int64_t* per_batch, int n, int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* THORN_B200_H */

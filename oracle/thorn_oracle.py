@@ -151,12 +151,13 @@ def gram_ns_restarts(coeffs):
             for j, (a, b, c) in enumerate(coeffs):
                 if j == 0 or j in combo:
                     if j != 0:
-                        e = e * q
+                        e *= q
                     r = e ** 2 + K
                     q = np.ones(len(e), dtype=np.float64)
                 z = a + r * (b + r * c)
-                q = q * z
-                r = r * z ** 2
+                # in place, as the reference does: entries appended earlier alias q
+                q *= z
+                r *= z ** 2
                 qv.append(q)
             qm = max(cond(t) for t in qv)
             if qm < q_max:
@@ -171,14 +172,19 @@ def gram_ns_restarts(coeffs):
 # Newton-Schulz polar factor (thorn.py:614-667)
 # ---------------------------------------------------------------------------
 
+# Operand type of the NS GEMMs: "f16" as in the reference (thorn.py:634-635);
+# "bf16" models the optional bf16 mode of the B200 kernels.
+NS_DTYPE = "f16"
+
+
 def _mm16(a, b, c=None, alpha=1.0, beta=1.0):
-    """fp16 GEMM with fp32 accumulation, one rounding: out = alpha*a@b + beta*c."""
+    """16-bit GEMM with fp32 accumulation, one rounding: out = alpha*a@b + beta*c."""
     acc = np.matmul(a, b, dtype=F32)
     if alpha != 1.0:
         acc = acc * F32(alpha)
     if c is not None:
         acc = acc + F32(beta) * c
-    return h16(acc)
+    return rnd(acc, NS_DTYPE)
 
 
 def polar_decomp_2d(X: np.ndarray, coeffs, restarts, src_dtype: str) -> np.ndarray:
@@ -190,7 +196,7 @@ def polar_decomp_2d(X: np.ndarray, coeffs, restarts, src_dtype: str) -> np.ndarr
         X = X.T
     X = np.ascontiguousarray(X, dtype=F32)
     nrm = F32(np.sqrt(np.sum(X.astype(np.float64) ** 2)))
-    X = h16(X / (nrm + F32(1e-8)))
+    X = rnd(X / (nrm + F32(1e-8)), NS_DTYPE)
     if gram:
         R = _mm16(X, X.T)
         Q = None
@@ -203,10 +209,11 @@ def polar_decomp_2d(X: np.ndarray, coeffs, restarts, src_dtype: str) -> np.ndarr
             if i != 0 and i not in restarts:
                 Q = _mm16(Q, Z, Q, beta=a)
             else:
-                # Z + a*I on fp16 tensors: a*I rounds a to fp16 first (thorn.py:648)
+                # Z + a*I (thorn.py:648); on CPU a*I first rounds a to fp16
                 Q = Z.copy()
                 d = np.arange(Q.shape[0])
-                Q[d, d] = h16(Q[d, d] + h16(F32(a)))
+                a16 = rnd(F32(a), NS_DTYPE) if CPU_ALPHA_ROUNDING else F32(a)
+                Q[d, d] = rnd(Q[d, d] + a16, NS_DTYPE)
             if i < last and (i + 1) not in restarts:
                 RZ = _mm16(R, Z, R, beta=a)
                 R = _mm16(Z, RZ, RZ, beta=a)

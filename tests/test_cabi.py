@@ -1,0 +1,115 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol that
+``include/thorn_b200.h`` declares, the ctypes mirrors match the C layouts, and
+the host-only entry points (sizes, status strings, argument validation) work."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from thorn_b200 import _native as N
+from thorn_b200 import build as B
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "thorn_b200.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    B.build()
+    return N.load()
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"THORN_API\s+[\w\s\*]+?\b(thorn_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    for must in ["thorn_adamw_multi", "thorn_ortho_pre_multi", "thorn_ns_cast_multi", "thorn_ns_batched",
+                 "thorn_sym_addmm", "thorn_pnn_stats_multi", "thorn_ortho_post_multi", "thorn_md_prep",
+                 "thorn_md_gain_grad", "thorn_md_finalize_multi", "thorn_sumsq_multi"]:
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    out = subprocess.run(["nm", "-D", "--defined-only", N.library_path()], capture_output=True, text=True,
+                         check=True).stdout
+    exported = set(re.findall(r"\b(thorn_\w+)$", out, flags=re.M))
+    missing = [n for n in declared_functions() if n not in exported]
+    assert not missing, missing
+    for n in declared_functions():
+        assert hasattr(lib, n)
+    # everything the ctypes layer binds is declared
+    assert set(N._PROTOS) <= set(declared_functions())
+
+
+STRUCTS = {
+    "thorn_adam_tensor": (N.AdamTensor, ["p", "g", "m", "v", "numel", "lr", "bc1", "bc2", "degenerate"]),
+    "thorn_ortho_pre_tensor": (N.OrthoPreTensor, ["p", "g", "m", "normsq", "batch", "rows", "cols", "row_sp",
+                                                  "col_sp", "scalar_gain", "row_gsum", "col_gsum"]),
+    "thorn_ns_cast_tensor": (N.NsCastTensor, ["g", "m", "normsq", "x", "batch", "rows", "cols", "row_sp", "col_sp",
+                                              "scalar_gain", "md"]),
+    "thorn_pnn_tensor": (N.PnnTensor, ["U", "row_scale", "mat_stats", "batch", "rows", "cols"]),
+    "thorn_ortho_post_tensor": (N.OrthoPostTensor, ["U", "p", "row_scale", "mat_stats", "p_normsq", "batch",
+                                                    "rows", "cols", "lr"]),
+    "thorn_md_final_tensor": (N.MdFinalTensor, ["p", "normsq", "target", "target_stride", "row_sp", "col_sp",
+                                                "scalar_gain", "batch", "rows", "cols"]),
+}
+
+
+def test_struct_layouts_match_header(tmp_path):
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "thorn_b200.h"', "int main(void) {"]
+    for cname, (_, flds) in STRUCTS.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for f in flds:
+            lines.append(f'  printf("{cname} {f} %zu\\n", offsetof({cname}, {f}));')
+    lines.append("  return 0; }")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split("\n")
+    c = {}
+    for line in out:
+        if line:
+            name, f, v = line.split()
+            c[(name, f)] = int(v)
+    for cname, (st, flds) in STRUCTS.items():
+        assert ctypes.sizeof(st) == c[(cname, "size")], cname
+        for f in flds:
+            assert getattr(st, f).offset == c[(cname, f)], (cname, f)
+
+
+def test_host_only_entry_points(lib):
+    assert lib.thorn_abi_version() == 1
+    assert lib.thorn_status_string(0) == b"ok"
+    assert lib.thorn_status_string(2).startswith(b"misaligned")
+    assert lib.thorn_ns_ld(1) == 8 and lib.thorn_ns_ld(8) == 8 and lib.thorn_ns_ld(4097) == 4104
+    # gram: 2 x-buffers + 5 m x m buffers; square: 4 m x m buffers (bytes, 256-aligned)
+    assert lib.thorn_ns_workspace_bytes(1, 1024, 4096) == 2 * 1024 * 4096 * 2 + 5 * 1024 * 1024 * 2
+    assert lib.thorn_ns_workspace_bytes(3, 512, 512) == 4 * 3 * 512 * 512 * 2
+    assert lib.thorn_ns_workspace_bytes(2, 96, 32) == lib.thorn_ns_workspace_bytes(2, 32, 96)
+    assert lib.thorn_ns_workspace_bytes(0, 8, 8) == 0
+
+
+def test_argument_validation_without_gpu(lib):
+    """Bad arguments are rejected before anything touches the device."""
+    arr = N.array(N.AdamTensor, [])
+    assert lib.thorn_adamw_multi(arr, -1, 0, 0, 0.9, 0.95, 0.0, 0.0, None) == 1
+    assert lib.thorn_adamw_multi(arr, 0, 7, 0, 0.9, 0.95, 0.0, 0.0, None) == 1  # bad dtype
+    bad = N.array(N.AdamTensor, [N.AdamTensor(None, None, None, None, 16, 1e-3, 1.0, 1.0, 0)])
+    assert lib.thorn_adamw_multi(bad, 1, 0, 0, 0.9, 0.95, 0.0, 0.0, None) == 1  # null grad
+    assert lib.thorn_adamw_multi(arr, 0, 0, 0, 0.9, 0.95, 0.0, 0.0, None) == 0  # nothing to do
+    co = (ctypes.c_double * 3)(1.0, 0.0, 0.0)
+    rs = (ctypes.c_int32 * 1)(0)
+    assert lib.thorn_ns_batched(None, None, None, 0, 1, 8, 8, 2, co, 1, rs, 0, None, None) == 1
+    assert lib.thorn_ns_batched(None, None, None, 0, 0, 8, 8, 2, co, 1, rs, 0, None, None) == 0
+    assert lib.thorn_ns_batched(1024, 2048, 4096, 1 << 30, 1, 8, 8, 0, co, 1, rs, 0, None, None) == 1  # f32 NS
+    # symmetric GEMM needs 8-element leading dimensions
+    assert lib.thorn_sym_addmm(16, 16, None, 16, 1, 12, 16, 0, 1.0, 0.0, 2, None, None) == 2
+    pre = N.array(N.OrthoPreTensor, [N.OrthoPreTensor(None, None, None, None, 1, 4, 4, None, None, 0, None, None)])
+    assert lib.thorn_ortho_pre_multi(pre, 1, 0, 0, 0, 0.9, 0, 0, None) == 1
+    assert lib.thorn_md_prep(None, 4, None, None, 0, None) == 1

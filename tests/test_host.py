@@ -1,0 +1,121 @@
+"""Host-side behaviour of the drop-in THORN class (no GPU needed)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.nn as nn
+
+import parity as P
+from thorn_b200 import THORN
+from thorn_b200.coeffs import gram_ns_restarts, optimal_composition
+from thorn_b200.optimizer import GroupConfig, _mat_view
+
+# defaults of the reference's _THORNParameterGroup (thorn.py:541-561)
+REF_DEFAULTS = dict(none_grad=True, weight_decay=0.1, betas=(0.9, 0.95), scaling_mode=None, target_rms=0.2,
+                    target_norm=None, iters=5, rectify=False, eps=0, lower_bound=1e-3, safety_factor=0.03,
+                    cushion=0.02, momentum_align=False, decouple_md=False, gain_lr=1e-3, gain_betas=(0.9, 0.95),
+                    norm_axis=None, split_gain=True, force_per_neuron_norm=False)
+
+
+def test_group_defaults_match_reference():
+    opt = THORN([{"orthogonalize": True, "params": [nn.Parameter(torch.zeros(4, 4))], "lr": 1.0}])
+    assert opt.defaults == REF_DEFAULTS
+    g = opt.param_groups[0]
+    assert set(g) == set(REF_DEFAULTS) | {"orthogonalize", "params", "lr"}
+
+
+def test_coefficients_bit_identical_to_reference(golden_dir):
+    gold = P.load_golden(os.path.join(golden_dir, "coeffs.npz"))
+    i = 0
+    while f"coeffs/{i}/setting" in gold:
+        l, it, sf, cu = gold[f"coeffs/{i}/setting"]
+        co = optimal_composition(float(l), int(it), float(sf), float(cu))
+        assert np.array_equal(np.array(co), gold[f"coeffs/{i}/values"])
+        assert gram_ns_restarts(*co) == list(gold[f"coeffs/{i}/restarts"])
+        i += 1
+
+
+def test_validation_errors():
+    with pytest.raises(ValueError, match="Invalid learning rate"):
+        GroupConfig.from_kwargs(orthogonalize=True, params=[], lr=-1.0)
+    with pytest.raises(ValueError, match="Invalid beta1"):
+        GroupConfig.from_kwargs(orthogonalize=True, params=[], lr=1.0, betas=(1.0, 0.9))
+    with pytest.raises(ValueError, match="Invalid beta2"):
+        GroupConfig.from_kwargs(orthogonalize=True, params=[], lr=1.0, betas=(0.9, -0.1))
+    with pytest.raises(AssertionError, match="ndim >= 2"):
+        THORN([{"orthogonalize": True, "params": [nn.Parameter(torch.zeros(4))], "lr": 1.0}])
+    # the reference accepts bad hyper-parameters at construction and raises on step
+    p = nn.Parameter(torch.zeros(4, 4))
+    opt = THORN([{"orthogonalize": True, "params": [p], "lr": -1.0}])
+    p.grad = torch.zeros(4, 4)
+    with pytest.raises(ValueError):
+        opt.step()
+
+
+def test_scaling_modes_and_rect():
+    g = GroupConfig.from_kwargs(orthogonalize=True, params=[], lr=1.0)
+    assert g.scaling_mode_ == "moonlight"
+    assert abs(g.lr_scale(512, 512) - 0.2 * 512 ** 0.5) < 1e-12
+    g = GroupConfig.from_kwargs(orthogonalize=True, params=[], lr=1.0, decouple_md=True)
+    assert g.scaling_mode_ == "md" and g.lr_scale(1024, 512) == 2 ** 0.5
+    g = GroupConfig.from_kwargs(orthogonalize=True, params=[], lr=1.0, scaling_mode="jordan")
+    assert g.lr_scale(512, 1024) == 1.0 and g.lr_scale(1024, 256) == 2.0
+    g = GroupConfig.from_kwargs(orthogonalize=False, params=[], lr=1.0, rectify=True)
+    assert g.rect(1) == 0.0 and 0 < g.rect(20) < 1
+    assert GroupConfig.from_kwargs(orthogonalize=True, params=[], lr=1.0).needs_pnn(1024, 512)
+    assert not GroupConfig.from_kwargs(orthogonalize=True, params=[], lr=1.0).needs_pnn(512, 1024)
+    assert not GroupConfig.from_kwargs(orthogonalize=True, params=[], lr=1.0, betas=(0.9, 0.0)).needs_pnn(1024, 512)
+
+
+def test_auto_assign_mirrors_reference():
+    class M(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.embed = nn.Embedding(10, 8)
+            self.proj = nn.Linear(8, 8)
+            self.conv = nn.Conv1d(8, 8, 3)
+            self.norm = nn.LayerNorm(8)
+            self.lm_head = nn.Linear(8, 10, bias=False)
+
+    m = M()
+    opt = THORN(m, lr=1e-3)
+    ortho = {id(p) for p in opt.param_groups[0]["params"]}
+    assert ortho == {id(m.proj.weight), id(m.conv.weight)}
+    assert opt.param_groups[0]["orthogonalize"] and not opt.param_groups[1]["orthogonalize"]
+
+
+def test_state_layout_and_no_cpu_path():
+    p = nn.Parameter(torch.randn(6, 4))
+    q = nn.Parameter(torch.randn(5))
+    opt = THORN([{"orthogonalize": True, "params": [p], "lr": 1e-3, "decouple_md": True},
+                 {"orthogonalize": False, "params": [q], "lr": 1e-3, "decouple_md": True}])
+    g0 = GroupConfig.from_kwargs(**opt.param_groups[0])
+    g1 = GroupConfig.from_kwargs(**opt.param_groups[1])
+    opt._init_state(p, opt.state[p], g0, opt.param_groups[0])
+    opt._init_state(q, opt.state[q], g1, opt.param_groups[1])
+    sp, sq = opt.state[p], opt.state[q]
+    assert sp["step"] == 1 and sp["moment"].shape == p.shape
+    assert sp["row_gain"].shape == (6, 1) and sp["col_gain"].shape == (1, 4)
+    assert abs(float(torch.nn.functional.softplus(sp["row_gain"][0, 0])) - 1.0) < 1e-6
+    assert float(sp["target_norm"]) == pytest.approx(6 ** 0.5)
+    assert set(sq) == {"step", "moment", "variance", "gain", "gain_moment", "gain_variance", "target_norm"}
+    assert float(sq["target_norm"]) == pytest.approx(float(q.norm()))
+    # the step runs only on CUDA devices: no CPU fallback
+    p.grad = torch.zeros_like(p)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        opt.step()
+
+
+def test_state_dtype_extension():
+    p = nn.Parameter(torch.randn(8, 8, dtype=torch.bfloat16))
+    opt = THORN([{"orthogonalize": True, "params": [p], "lr": 1e-3, "state_dtype": torch.float32}])
+    g = GroupConfig.from_kwargs(**opt.param_groups[0])
+    opt._init_state(p, opt.state[p], g, opt.param_groups[0])
+    assert opt.state[p]["moment"].dtype == torch.float32
+
+
+def test_mat_view():
+    assert _mat_view((8, 4, 3)) == (8, 4, 3)
+    assert _mat_view((2, 3, 4, 5)) == (6, 4, 5)
+    assert _mat_view((7,)) == (1, 1, 7)

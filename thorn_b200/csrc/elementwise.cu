@@ -1,0 +1,845 @@
+// HBM-bound kernels of the THORN step: multi-tensor (R)Adam(-atan2)W, the
+// orthogonalized group's momentum / NS-input / per-neuron-norm / apply passes
+// and the magnitude-direction decoupling helpers.
+//
+// Every kernel here reads each operand once with 16-byte vector accesses and
+// writes each result once.  Tensors of one call are packed into a by-value
+// kernel parameter (pointer table + block prefix) so one launch covers many
+// parameters; blocks find their tensor with a short scan of the prefix.
+#include <atomic>
+#include <math.h>
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace thorn {
+
+static std::atomic<uint64_t> g_launches{0};
+static std::atomic<int> g_last_cuda_error{0};
+
+void count_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+
+int check_launch() {
+  cudaError_t e = cudaPeekAtLastError();
+  if (e != cudaSuccess) {
+    g_last_cuda_error.store((int)e);
+    cudaGetLastError();
+    return THORN_ERR_CUDA;
+  }
+  return THORN_OK;
+}
+
+// ---------------------------------------------------------------------------
+// multi-tensor packing
+// ---------------------------------------------------------------------------
+constexpr int kThreads = 256;
+constexpr int kMaxT = 24;
+constexpr int64_t kMaxGrid = 1ll << 30;
+
+template <class E>
+struct Pack {
+  E t[kMaxT];
+  int64_t start[kMaxT + 1];
+  int vec[kMaxT];
+  int n;
+};
+
+template <class E>
+__device__ __forceinline__ int find_tensor(const Pack<E>& pk, int64_t bid) {
+  int i = 0;
+  while (i + 1 < pk.n && bid >= pk.start[i + 1]) ++i;
+  return i;
+}
+
+// Build packs of up to kMaxT tensors and launch `launch(pack, nblocks)` for each.
+template <class E, class Blocks, class Vec, class Launch>
+static int launch_packed(const E* ts, int n, Blocks blocks_of, Vec vec_of, Launch launch) {
+  Pack<E> pk;
+  pk.n = 0;
+  int64_t total = 0;
+  auto flush = [&]() -> int {
+    if (pk.n == 0) return THORN_OK;
+    launch(pk, total);
+    count_launch();
+    int st = check_launch();
+    pk.n = 0;
+    total = 0;
+    return st;
+  };
+  for (int i = 0; i < n; ++i) {
+    int64_t nb = blocks_of(ts[i]);
+    if (nb <= 0) continue;
+    if (pk.n == kMaxT || total + nb > kMaxGrid) {
+      int st = flush();
+      if (st) return st;
+    }
+    pk.t[pk.n] = ts[i];
+    pk.vec[pk.n] = vec_of(ts[i]) ? 1 : 0;
+    pk.start[pk.n] = total;
+    total += nb;
+    pk.n++;
+    pk.start[pk.n] = total;
+  }
+  return flush();
+}
+
+static inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// 2-D tiling used by the matrix kernels: a tile is kTR rows x 256 columns of
+// one sub-matrix; each warp owns kTR/8 rows and each lane 8 consecutive columns.
+constexpr int kTR = 64;
+constexpr int kTC = 256;
+
+struct Tile {
+  int64_t b, r0, c0;
+};
+__device__ __forceinline__ Tile tile_of(int64_t local, int64_t rows, int64_t cols) {
+  const int64_t tr = (rows + kTR - 1) / kTR, tc = (cols + kTC - 1) / kTC;
+  Tile t;
+  t.b = local / (tr * tc);
+  int64_t rem = local - t.b * tr * tc;
+  t.r0 = (rem / tc) * kTR;
+  t.c0 = (rem % tc) * kTC;
+  return t;
+}
+static inline int64_t tiles_of(int64_t batch, int64_t rows, int64_t cols) {
+  if (batch <= 0 || rows <= 0 || cols <= 0) return 0;
+  return batch * cdiv(rows, kTR) * cdiv(cols, kTC);
+}
+
+// ===========================================================================
+// (R)Adam(-atan2)W  (thorn.py:147-185, 838-888)
+// ===========================================================================
+constexpr int kAdamChunk = kThreads * 8 * 4;  // elements per block
+
+struct AdamScalars {
+  float beta1, beta2, wd, eps;
+};
+struct AdamArgs {
+  Pack<thorn_adam_tensor> pk;
+  AdamScalars s;
+};
+
+template <class P, class S>
+__global__ void __launch_bounds__(kThreads) adam_kernel(const __grid_constant__ AdamArgs a) {
+  const int ti = find_tensor(a.pk, blockIdx.x);
+  const thorn_adam_tensor& e = a.pk.t[ti];
+  const bool vec = a.pk.vec[ti];
+  const int64_t base = (int64_t(blockIdx.x) - a.pk.start[ti]) * kAdamChunk;
+  const float w1 = 1.f - a.s.beta1, w2 = 1.f - a.s.beta2;
+  const P* g = (const P*)e.g;
+  S* M = (S*)e.m;
+  S* V = (S*)e.v;
+  P* p = (P*)e.p;
+#pragma unroll 1
+  for (int it = 0; it < 4; ++it) {
+    const int64_t i0 = base + int64_t(it) * (kThreads * 8) + threadIdx.x * 8;
+    if (i0 >= e.numel) break;
+    const int n = (int)min64(8, e.numel - i0);
+    float gv[8], mv[8], vv[8];
+    load_n(g + i0, gv, n, vec);
+    load_n(M + i0, mv, n, vec);
+    load_n(V + i0, vv, n, vec);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      mv[k] = mv[k] + (gv[k] - mv[k]) * w1;
+      vv[k] = vv[k] * a.s.beta2 + (gv[k] * gv[k]) * w2;
+    }
+    store_n(M + i0, mv, n, vec);
+    store_n(V + i0, vv, n, vec);
+    if (p != nullptr) {
+      float pv[8];
+      load_n(p + i0, pv, n, vec);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        float u;
+        if (e.degenerate) u = mv[k];
+        else if (a.s.eps == 0.f) u = atan2f(mv[k] * e.bc1, sqrtf(vv[k] * e.bc2));
+        else u = (mv[k] * e.bc1) / (sqrtf(vv[k] * e.bc2) + a.s.eps);
+        if (a.s.wd > 0.f && u * pv[k] >= 0.f) u = u + a.s.wd * pv[k];
+        pv[k] = pv[k] - e.lr * u;
+      }
+      store_n(p + i0, pv, n, vec);
+    }
+  }
+}
+
+// ===========================================================================
+// momentum + Nesterov (+ MD direction recovery)  (thorn.py:1376-1381, 890-908)
+// ===========================================================================
+// u = g + beta1 * m, evaluated identically by the momentum pass (for the norm)
+// and by the NS-input pass (for X), so both see the same u.
+template <class U>
+__device__ __forceinline__ float nesterov_u(float g, float m, float b1) {
+  return rnd<U>(__fmaf_rn(b1, m, g));
+}
+struct PreArgs {
+  Pack<thorn_ortho_pre_tensor> pk;
+  float beta1;
+  int write_grad;
+};
+
+template <class P, class S, class U, bool MD>
+__global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_constant__ PreArgs a) {
+  __shared__ float red[32];
+  __shared__ float colacc[MD ? 8 : 1][MD ? kTC : 1];
+  const int ti = find_tensor(a.pk, blockIdx.x);
+  const thorn_ortho_pre_tensor& e = a.pk.t[ti];
+  const bool vec = a.pk.vec[ti];
+  const Tile t = tile_of(int64_t(blockIdx.x) - a.pk.start[ti], e.rows, e.cols);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t c = t.c0 + lane * 8;
+  const int nc = (int)max64(0, min64(8, e.cols - c));
+  const float b1 = a.beta1;
+  float sq = 0.f;
+  float csum[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) csum[k] = 0.f;
+  const bool scalar_gain = MD && e.scalar_gain;
+  const bool momentum = e.m != nullptr;
+  float csp[8];
+  if (MD && !scalar_gain) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) csp[k] = k < nc ? e.col_sp[t.b * e.cols + c + k] : 0.f;
+  }
+  float rsum_scalar = 0.f;
+  for (int rr = warp; rr < kTR; rr += 8) {
+    const int64_t r = t.r0 + rr;
+    if (r >= e.rows) break;
+    float rs = 0.f;
+    if (nc > 0) {
+      const int64_t off = (t.b * e.rows + r) * e.cols + c;
+      float gv[8], mv[8];
+      load_n((const P*)e.g + off, gv, nc, vec);
+      if (momentum) load_n((const S*)e.m + off, mv, nc, vec);
+      if (MD) {
+        float pv[8];
+        load_n((const P*)e.p + off, pv, nc, vec);
+        const float rsp = scalar_gain ? e.row_sp[0] : e.row_sp[t.b * e.rows + r];
+        float part = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (k >= nc) continue;
+          float gain = scalar_gain ? rsp : rnd<P>(rsp * csp[k]);
+          float pd = rnd<P>(pv[k] / gain);
+          float pg = rnd<P>(pd * gv[k]);
+          if (scalar_gain) {
+            part += pg;
+          } else {
+            part += rnd<P>(pg * csp[k]);
+            csum[k] += rnd<P>(pg * rsp);
+          }
+          pv[k] = pd;
+          gv[k] = rnd<P>(gv[k] * gain);
+        }
+        rs = part;
+        store_n((P*)e.p + off, pv, nc, vec);
+        if (a.write_grad) store_n((P*)e.g + off, gv, nc, vec);
+      }
+      if (momentum) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float m1 = rnd<S>(mv[k] * b1);
+          mv[k] = rnd<S>(m1 + gv[k]);
+          const float u = nesterov_u<U>(gv[k], mv[k], b1);
+          if (k < nc) sq += u * u;
+        }
+        store_n((S*)e.m + off, mv, nc, vec);
+      }
+    }
+    if (MD) {
+      rs = warp_sum(rs);
+      if (scalar_gain) rsum_scalar += rs;
+      else if (lane == 0) atomicAdd(e.row_gsum + t.b * e.rows + r, rs);
+    }
+  }
+  if (momentum) {
+    float tot = block_sum(sq, red);
+    if (threadIdx.x == 0 && tot != 0.f) atomicAdd(e.normsq + t.b, tot);
+  }
+  if (MD) {
+    if (scalar_gain) {
+      __syncthreads();
+      float s2 = block_sum(lane == 0 ? rsum_scalar : 0.f, red);
+      if (threadIdx.x == 0) atomicAdd(e.row_gsum, s2);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) colacc[warp][lane * 8 + k] = csum[k];
+      __syncthreads();
+      const int cc = threadIdx.x;  // one column per thread (kTC == kThreads)
+      if (t.c0 + cc < e.cols) {
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) s += colacc[w][cc];
+        atomicAdd(e.col_gsum + t.b * e.cols + t.c0 + cc, s);
+      }
+    }
+  }
+}
+
+// ===========================================================================
+// NS input: normalise + cast (+ transpose tall sub-matrices)  (thorn.py:629-635)
+// ===========================================================================
+struct CastArgs {
+  Pack<thorn_ns_cast_tensor> pk;
+  float beta1;
+};
+
+
+// u for element (b, r, c) exactly as the momentum pass computed it
+template <class P, class U>
+__device__ __forceinline__ float cast_u(const thorn_ns_cast_tensor& e, float g, float m, float b1, int64_t b,
+                                        int64_t r, int64_t c) {
+  if (e.md) {
+    const float gain = e.scalar_gain ? e.row_sp[0] : rnd<P>(e.row_sp[b * e.rows + r] * e.col_sp[b * e.cols + c]);
+    g = rnd<P>(g * gain);
+  }
+  return nesterov_u<U>(g, m, b1);
+}
+
+template <class P, class S, class U, class X>
+__global__ void __launch_bounds__(kThreads) ns_cast_kernel(const __grid_constant__ CastArgs a) {
+  __shared__ float tile[32][33];
+  const int ti = find_tensor(a.pk, blockIdx.x);
+  const thorn_ns_cast_tensor& e = a.pk.t[ti];
+  const int64_t local = int64_t(blockIdx.x) - a.pk.start[ti];
+  const bool tall = e.rows > e.cols;
+  const P* G = (const P*)e.g;
+  const S* M = (const S*)e.m;
+  if (!tall) {
+    const bool vec = a.pk.vec[ti];
+    const Tile t = tile_of(local, e.rows, e.cols);
+    const float d = sqrtf(e.normsq[t.b]) + 1e-8f;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t c = t.c0 + lane * 8;
+    const int nc = (int)max64(0, min64(8, e.cols - c));
+    if (nc == 0) return;
+    const int64_t ld = ns_ld(e.cols);
+    for (int rr = warp; rr < kTR; rr += 8) {
+      const int64_t r = t.r0 + rr;
+      if (r >= e.rows) break;
+      const int64_t off = (t.b * e.rows + r) * e.cols + c;
+      float gv[8], mv[8], v[8];
+      load_n(G + off, gv, nc, vec);
+      load_n(M + off, mv, nc, vec);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = (k < nc ? cast_u<P, U>(e, gv[k], mv[k], a.beta1, t.b, r, c + k) : 0.f) / d;
+      store_n((X*)e.x + (t.b * e.rows + r) * ld + c, v, nc, vec);
+    }
+  } else {
+    // 32x32 tiles through shared memory: read rows of u, write rows of u^T
+    const int64_t tr = (e.rows + 31) / 32, tc = (e.cols + 31) / 32;
+    const int64_t b = local / (tr * tc);
+    const int64_t rem = local - b * tr * tc;
+    const int64_t r0 = (rem / tc) * 32, c0 = (rem % tc) * 32;
+    const float d = sqrtf(e.normsq[b]) + 1e-8f;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const int64_t base = b * e.rows * e.cols;
+    for (int k = ty; k < 32; k += 8) {
+      const int64_t r = r0 + k, cc = c0 + tx;
+      float v = 0.f;
+      if (r < e.rows && cc < e.cols) {
+        const int64_t off = base + r * e.cols + cc;
+        v = cast_u<P, U>(e, to_f(G[off]), to_f(M[off]), a.beta1, b, r, cc) / d;
+      }
+      tile[k][tx] = v;
+    }
+    __syncthreads();
+    const int64_t ld = ns_ld(e.rows);
+    X* x = (X*)e.x + b * e.cols * ld;
+    for (int k = ty; k < 32; k += 8) {
+      const int64_t cc = c0 + k, r = r0 + tx;
+      if (cc < e.cols && r < e.rows) x[cc * ld + r] = from_f<X>(tile[tx][k]);
+    }
+  }
+}
+
+// ===========================================================================
+// per-neuron norm statistics (thorn.py:205-253)
+// ===========================================================================
+struct PnnArgs {
+  Pack<thorn_pnn_tensor> pk;
+  float eps;
+};
+constexpr int kPnnRowsPerBlock = 8;
+
+template <class U, class P>
+__global__ void __launch_bounds__(kThreads) pnn_stats_kernel(const __grid_constant__ PnnArgs a) {
+  const int ti = find_tensor(a.pk, blockIdx.x);
+  const thorn_pnn_tensor& e = a.pk.t[ti];
+  const bool vec = a.pk.vec[ti];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t grow = (int64_t(blockIdx.x) - a.pk.start[ti]) * kPnnRowsPerBlock + warp;  // b*rows + r
+  if (grow >= e.batch * e.rows) return;
+  const U* row = (const U*)e.U + grow * e.cols;
+  float s = 0.f;
+  for (int64_t c = lane * 8; c < e.cols; c += 256) {
+    const int n = (int)min64(8, e.cols - c);
+    float v[8];
+    load_n(row + c, v, n, vec);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float x = rnd<P>(v[k]);
+      if (k < n) s += x * x;
+    }
+  }
+  s = warp_sum(s);
+  if (lane == 0) {
+    const float inv_n = 1.f / (float)e.cols;
+    const float sc = rsqrtf(fmaxf(s * inv_n, a.eps));
+    e.row_scale[grow] = sc;
+    const int64_t b = grow / e.rows;
+    atomicAdd(e.mat_stats + 2 * b, s);
+    atomicAdd(e.mat_stats + 2 * b + 1, sc * sc * s);
+  }
+}
+
+// ===========================================================================
+// apply: pnn scaling + cautious weight decay + update  (thorn.py:187-203, 255-280)
+// ===========================================================================
+struct PostArgs {
+  Pack<thorn_ortho_post_tensor> pk;
+  float wd, eps;
+};
+
+template <class U, class P>
+__global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_constant__ PostArgs a) {
+  __shared__ float red[32];
+  const int ti = find_tensor(a.pk, blockIdx.x);
+  const thorn_ortho_post_tensor& e = a.pk.t[ti];
+  const bool vec = a.pk.vec[ti];
+  const Tile t = tile_of(int64_t(blockIdx.x) - a.pk.start[ti], e.rows, e.cols);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t c = t.c0 + lane * 8;
+  const int nc = (int)max64(0, min64(8, e.cols - c));
+  float gscale = 1.f;
+  if (e.mat_stats != nullptr) {
+    gscale = sqrtf(e.mat_stats[2 * t.b]) / fmaxf(sqrtf(e.mat_stats[2 * t.b + 1]), a.eps);
+  }
+  float sq = 0.f;
+  for (int rr = warp; rr < kTR; rr += 8) {
+    const int64_t r = t.r0 + rr;
+    if (r >= e.rows || nc == 0) break;
+    const int64_t off = (t.b * e.rows + r) * e.cols + c;
+    float scale = 1.f;
+    if (e.row_scale != nullptr) scale = e.row_scale[t.b * e.rows + r] * gscale;
+    float uv[8], pv[8];
+    load_n((const U*)e.U + off, uv, nc, vec);
+    load_n((const P*)e.p + off, pv, nc, vec);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float u = rnd<P>(uv[k]);
+      if (e.row_scale != nullptr) u = u * scale;
+      if (a.wd > 0.f && u * pv[k] >= 0.f) u = u + a.wd * pv[k];
+      pv[k] = rnd<P>(pv[k] - e.lr * u);
+      if (k < nc) sq += pv[k] * pv[k];
+    }
+    store_n((P*)e.p + off, pv, nc, vec);
+  }
+  if (e.p_normsq != nullptr) {
+    float tot = block_sum(sq, red);
+    if (threadIdx.x == 0) atomicAdd(e.p_normsq + t.b, tot);
+  }
+}
+
+// ===========================================================================
+// MD helpers (thorn.py:910-977, 1414-1421)
+// ===========================================================================
+template <class P>
+__global__ void md_prep_kernel(const P* gain, int64_t n, float* sp, float* sig) {
+  int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float x = to_f(gain[i]);
+  float s = x > 20.f ? x : log1pf(expf(x));
+  sp[i] = rnd<P>(s);
+  if (sig) sig[i] = rnd<P>(1.f / (1.f + expf(-x)));
+}
+
+template <class P>
+__global__ void md_gain_grad_kernel(const float* gsum, const float* sig, P* grad, int64_t n) {
+  int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  grad[i] = from_f<P>(rnd<P>(gsum[i]) * sig[i]);
+}
+
+struct FinalArgs {
+  Pack<thorn_md_final_tensor> pk;
+};
+
+template <class P>
+__global__ void __launch_bounds__(kThreads) md_finalize_kernel(const __grid_constant__ FinalArgs a) {
+  const int ti = find_tensor(a.pk, blockIdx.x);
+  const thorn_md_final_tensor& e = a.pk.t[ti];
+  const bool vec = a.pk.vec[ti];
+  const Tile t = tile_of(int64_t(blockIdx.x) - a.pk.start[ti], e.rows, e.cols);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t c = t.c0 + lane * 8;
+  const int nc = (int)max64(0, min64(8, e.cols - c));
+  if (nc == 0) return;
+  float f = 1.f;
+  const bool renorm = e.normsq != nullptr;
+  if (renorm) {
+    float nrm = rnd<P>(sqrtf(e.normsq[t.b]));
+    float tgt = e.target[t.b * e.target_stride];
+    f = rnd<P>(tgt / rnd<P>(nrm + 1e-8f));
+  }
+  const bool split = !e.scalar_gain;
+  float csp[8];
+  if (split) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) csp[k] = k < nc ? e.col_sp[t.b * e.cols + c + k] : 0.f;
+  }
+  for (int rr = warp; rr < kTR; rr += 8) {
+    const int64_t r = t.r0 + rr;
+    if (r >= e.rows) break;
+    const int64_t off = (t.b * e.rows + r) * e.cols + c;
+    float pv[8];
+    load_n((const P*)e.p + off, pv, nc, vec);
+    const float rsp = split ? e.row_sp[t.b * e.rows + r] : e.row_sp[0];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float x = pv[k];
+      if (renorm) x = rnd<P>(x * f);
+      x = rnd<P>(x * rsp);
+      if (split) x = rnd<P>(x * csp[k]);
+      pv[k] = x;
+    }
+    store_n((P*)e.p + off, pv, nc, vec);
+  }
+}
+
+constexpr int kSqChunk = kThreads * 8 * 4;
+struct SumsqEntry {
+  const void* x;
+  float* out;
+  int64_t batch, per;
+};
+struct SumsqArgs {
+  Pack<SumsqEntry> pk;
+};
+
+template <class T>
+__global__ void __launch_bounds__(kThreads) sumsq_kernel(const __grid_constant__ SumsqArgs a) {
+  const int ti = find_tensor(a.pk, blockIdx.x);
+  const SumsqEntry& e = a.pk.t[ti];
+  const int64_t numel = e.batch * e.per;
+  const int64_t base = (int64_t(blockIdx.x) - a.pk.start[ti]) * kSqChunk;
+  const int lane = threadIdx.x & 31;
+  for (int it = 0; it < 4; ++it) {
+    const int64_t i0 = base + int64_t(it) * (kThreads * 8) + threadIdx.x * 8;
+    float s = 0.f;
+    int64_t b = -1;
+    if (i0 < numel) {
+      const T* x = (const T*)e.x;
+      for (int k = 0; k < 8 && i0 + k < numel; ++k) {
+        int64_t bk = (i0 + k) / e.per;
+        float v = to_f(x[i0 + k]);
+        if (b != bk && b >= 0) {
+          atomicAdd(e.out + b, s);
+          s = 0.f;
+        }
+        b = bk;
+        s += v * v;
+      }
+    }
+    // warp-aggregate when the whole warp is in one sub-matrix
+    const int64_t b0 = __shfl_sync(0xffffffffu, b, 0);
+    const bool uni = __all_sync(0xffffffffu, b == b0) && b0 >= 0;
+    if (uni) {
+      s = warp_sum(s);
+      if (lane == 0) atomicAdd(e.out + b0, s);
+    } else if (b >= 0) {
+      atomicAdd(e.out + b, s);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dispatch helpers
+// ---------------------------------------------------------------------------
+template <class F>
+static int dispatch1(int dt, F f) {
+  switch (dt) {
+    case THORN_F32: f((float*)nullptr); return THORN_OK;
+    case THORN_BF16: f((__nv_bfloat16*)nullptr); return THORN_OK;
+    case THORN_F16: f((__half*)nullptr); return THORN_OK;
+  }
+  return THORN_ERR_ARG;
+}
+template <class F>
+static int dispatch2(int a, int b, F f) {
+  int st = THORN_OK;
+  int r = dispatch1(a, [&](auto* pa) {
+    int r2 = dispatch1(b, [&](auto* pb) { f(pa, pb); });
+    if (r2) st = r2;
+  });
+  return r ? r : st;
+}
+static bool valid_dt(int d) { return d == THORN_F32 || d == THORN_BF16 || d == THORN_F16; }
+static size_t dt_size(int d) { return d == THORN_F32 ? 4 : 2; }
+static float dt_eps(int d) {
+  return d == THORN_F32 ? 1.1920928955078125e-07f : (d == THORN_BF16 ? 0.0078125f : 0.0009765625f);
+}
+
+}  // namespace thorn
+
+using namespace thorn;
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" int thorn_abi_version(void) { return 1; }
+
+extern "C" int64_t thorn_ns_ld(int64_t n) { return ns_ld(n); }
+
+extern "C" const char* thorn_status_string(int s) {
+  switch (s) {
+    case THORN_OK: return "ok";
+    case THORN_ERR_ARG: return "invalid argument";
+    case THORN_ERR_ALIGN: return "misaligned pointer or leading dimension";
+    case THORN_ERR_CUDA: return "CUDA error";
+    case THORN_ERR_UNSUPPORTED: return "unsupported device or configuration";
+  }
+  return "unknown status";
+}
+
+extern "C" uint64_t thorn_launch_count(void) { return g_launches.load(); }
+extern "C" int thorn_last_cuda_error(void) { return g_last_cuda_error.load(); }
+
+extern "C" int thorn_adamw_multi(const thorn_adam_tensor* ts, int n, int p_dtype, int s_dtype, float beta1,
+                                 float beta2, float weight_decay, float eps, void* stream) {
+  if (n < 0 || (n > 0 && ts == nullptr) || !valid_dt(p_dtype) || !valid_dt(s_dtype)) return THORN_ERR_ARG;
+  for (int i = 0; i < n; ++i)
+    if (ts[i].numel < 0 || (ts[i].numel > 0 && (!ts[i].g || !ts[i].m || !ts[i].v))) return THORN_ERR_ARG;
+  AdamScalars sc{beta1, beta2, weight_decay, eps};
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = THORN_OK;
+  int d = dispatch2(p_dtype, s_dtype, [&](auto* pp, auto* ps) {
+    using P = std::remove_pointer_t<decltype(pp)>;
+    using S = std::remove_pointer_t<decltype(ps)>;
+    rc = launch_packed(
+        ts, n, [](const thorn_adam_tensor& e) { return cdiv(e.numel, kAdamChunk); },
+        [](const thorn_adam_tensor& e) {
+          return aligned16(e.g) && aligned16(e.m) && aligned16(e.v) && (e.p == nullptr || aligned16(e.p));
+        },
+        [&](const Pack<thorn_adam_tensor>& pk, int64_t nb) {
+          AdamArgs a;
+          a.pk = pk;
+          a.s = sc;
+          adam_kernel<P, S><<<(unsigned)nb, kThreads, 0, st>>>(a);
+        });
+  });
+  return d ? d : rc;
+}
+
+extern "C" int thorn_ortho_pre_multi(const thorn_ortho_pre_tensor* ts, int n, int p_dtype, int s_dtype,
+                                     int u_dtype, float beta1, int md, int write_grad, void* stream) {
+  if (n < 0 || (n > 0 && ts == nullptr) || !valid_dt(p_dtype) || !valid_dt(s_dtype) || !valid_dt(u_dtype))
+    return THORN_ERR_ARG;
+  for (int i = 0; i < n; ++i) {
+    const auto& e = ts[i];
+    if (e.batch < 0 || e.rows < 0 || e.cols < 0) return THORN_ERR_ARG;
+    if (e.batch * e.rows * e.cols > 0 && (!e.g || (e.m && !e.normsq) || (!e.m && !md) || (md && !e.p)))
+      return THORN_ERR_ARG;
+    if (md && (!e.row_gsum || !e.row_sp || (!e.scalar_gain && (!e.col_sp || !e.col_gsum)))) return THORN_ERR_ARG;
+  }
+  PreArgs base;
+  base.beta1 = beta1;
+  base.write_grad = write_grad;
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = THORN_OK;
+  auto blocks = [](const thorn_ortho_pre_tensor& e) { return tiles_of(e.batch, e.rows, e.cols); };
+  auto vec = [](const thorn_ortho_pre_tensor& e) {
+    return (e.cols % 8) == 0 && (e.p == nullptr || aligned16(e.p)) && aligned16(e.g) &&
+           (e.m == nullptr || aligned16(e.m));
+  };
+  int d = dispatch2(p_dtype, s_dtype, [&](auto* pp, auto* ps) {
+    using P = std::remove_pointer_t<decltype(pp)>;
+    using S = std::remove_pointer_t<decltype(ps)>;
+    int d2 = dispatch1(u_dtype, [&](auto* pu) {
+      using U = std::remove_pointer_t<decltype(pu)>;
+      rc = launch_packed(ts, n, blocks, vec, [&](const Pack<thorn_ortho_pre_tensor>& pk, int64_t nb) {
+        PreArgs a = base;
+        a.pk = pk;
+        if (md) ortho_pre_kernel<P, S, U, true><<<(unsigned)nb, kThreads, 0, st>>>(a);
+        else ortho_pre_kernel<P, S, U, false><<<(unsigned)nb, kThreads, 0, st>>>(a);
+      });
+    });
+    if (d2) rc = d2;
+  });
+  return d ? d : rc;
+}
+
+extern "C" int thorn_ns_cast_multi(const thorn_ns_cast_tensor* ts, int n, int p_dtype, int s_dtype, int u_dtype,
+                                   int ns_dtype, float beta1, void* stream) {
+  if (n < 0 || (n > 0 && ts == nullptr) || !valid_dt(p_dtype) || !valid_dt(s_dtype) || !valid_dt(u_dtype) ||
+      (ns_dtype != THORN_F16 && ns_dtype != THORN_BF16))
+    return THORN_ERR_ARG;
+  for (int i = 0; i < n; ++i) {
+    const auto& e = ts[i];
+    if (e.batch < 0 || e.rows < 0 || e.cols < 0) return THORN_ERR_ARG;
+    if (e.batch * e.rows * e.cols > 0 && (!e.g || !e.m || !e.x || !e.normsq)) return THORN_ERR_ARG;
+    if (e.md && (!e.row_sp || (!e.scalar_gain && !e.col_sp))) return THORN_ERR_ARG;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = THORN_OK;
+  auto blocks = [](const thorn_ns_cast_tensor& e) -> int64_t {
+    if (e.batch <= 0 || e.rows <= 0 || e.cols <= 0) return 0;
+    if (e.rows > e.cols) return e.batch * cdiv(e.rows, 32) * cdiv(e.cols, 32);
+    return tiles_of(e.batch, e.rows, e.cols);
+  };
+  auto vec = [](const thorn_ns_cast_tensor& e) {
+    return (e.cols % 8) == 0 && aligned16(e.g) && aligned16(e.m) && aligned16(e.x);
+  };
+  int d = dispatch2(p_dtype, s_dtype, [&](auto* pp, auto* ps) {
+    using P = std::remove_pointer_t<decltype(pp)>;
+    using S = std::remove_pointer_t<decltype(ps)>;
+    int d2 = dispatch2(u_dtype, ns_dtype, [&](auto* pu, auto* px) {
+      using U = std::remove_pointer_t<decltype(pu)>;
+      using X = std::remove_pointer_t<decltype(px)>;
+      if constexpr (std::is_same<X, float>::value) {
+        rc = THORN_ERR_ARG;
+      } else {
+        rc = launch_packed(ts, n, blocks, vec, [&](const Pack<thorn_ns_cast_tensor>& pk, int64_t nb) {
+          CastArgs a;
+          a.pk = pk;
+          a.beta1 = beta1;
+          ns_cast_kernel<P, S, U, X><<<(unsigned)nb, kThreads, 0, st>>>(a);
+        });
+      }
+    });
+    if (d2) rc = d2;
+  });
+  return d ? d : rc;
+}
+
+extern "C" int thorn_pnn_stats_multi(const thorn_pnn_tensor* ts, int n, int u_dtype, int p_dtype, void* stream) {
+  if (n < 0 || (n > 0 && ts == nullptr) || !valid_dt(u_dtype) || !valid_dt(p_dtype)) return THORN_ERR_ARG;
+  for (int i = 0; i < n; ++i)
+    if (ts[i].batch * ts[i].rows * ts[i].cols > 0 && (!ts[i].U || !ts[i].row_scale || !ts[i].mat_stats))
+      return THORN_ERR_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = THORN_OK;
+  const float eps = dt_eps(p_dtype);
+  auto blocks = [](const thorn_pnn_tensor& e) -> int64_t {
+    if (e.batch <= 0 || e.rows <= 0 || e.cols <= 0) return 0;
+    return cdiv(e.batch * e.rows, kPnnRowsPerBlock);
+  };
+  auto vec = [](const thorn_pnn_tensor& e) { return (e.cols % 8) == 0 && aligned16(e.U); };
+  int d = dispatch2(u_dtype, p_dtype, [&](auto* pu, auto* pp) {
+    using U = std::remove_pointer_t<decltype(pu)>;
+    using P = std::remove_pointer_t<decltype(pp)>;
+    rc = launch_packed(ts, n, blocks, vec, [&](const Pack<thorn_pnn_tensor>& pk, int64_t nb) {
+      PnnArgs a;
+      a.pk = pk;
+      a.eps = eps;
+      pnn_stats_kernel<U, P><<<(unsigned)nb, kThreads, 0, st>>>(a);
+    });
+  });
+  return d ? d : rc;
+}
+
+extern "C" int thorn_ortho_post_multi(const thorn_ortho_post_tensor* ts, int n, int u_dtype, int p_dtype,
+                                      float weight_decay, void* stream) {
+  if (n < 0 || (n > 0 && ts == nullptr) || !valid_dt(u_dtype) || !valid_dt(p_dtype)) return THORN_ERR_ARG;
+  for (int i = 0; i < n; ++i)
+    if (ts[i].batch * ts[i].rows * ts[i].cols > 0 && (!ts[i].U || !ts[i].p)) return THORN_ERR_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = THORN_OK;
+  const float eps = dt_eps(p_dtype);
+  auto blocks = [](const thorn_ortho_post_tensor& e) { return tiles_of(e.batch, e.rows, e.cols); };
+  auto vec = [](const thorn_ortho_post_tensor& e) { return (e.cols % 8) == 0 && aligned16(e.U) && aligned16(e.p); };
+  int d = dispatch2(u_dtype, p_dtype, [&](auto* pu, auto* pp) {
+    using U = std::remove_pointer_t<decltype(pu)>;
+    using P = std::remove_pointer_t<decltype(pp)>;
+    rc = launch_packed(ts, n, blocks, vec, [&](const Pack<thorn_ortho_post_tensor>& pk, int64_t nb) {
+      PostArgs a;
+      a.pk = pk;
+      a.wd = weight_decay;
+      a.eps = eps;
+      ortho_post_kernel<U, P><<<(unsigned)nb, kThreads, 0, st>>>(a);
+    });
+  });
+  return d ? d : rc;
+}
+
+extern "C" int thorn_md_prep(const void* gain, int64_t n, float* sp, float* sig, int p_dtype, void* stream) {
+  if (n < 0 || (n > 0 && (!gain || !sp)) || !valid_dt(p_dtype)) return THORN_ERR_ARG;
+  if (n == 0) return THORN_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  int d = dispatch1(p_dtype, [&](auto* pp) {
+    using P = std::remove_pointer_t<decltype(pp)>;
+    md_prep_kernel<P><<<(unsigned)cdiv(n, 256), 256, 0, st>>>((const P*)gain, n, sp, sig);
+  });
+  if (d) return d;
+  count_launch();
+  return check_launch();
+}
+
+extern "C" int thorn_md_gain_grad(const float* gsum, const float* sig, void* grad, int64_t n, int p_dtype,
+                                  void* stream) {
+  if (n < 0 || (n > 0 && (!gsum || !sig || !grad)) || !valid_dt(p_dtype)) return THORN_ERR_ARG;
+  if (n == 0) return THORN_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  int d = dispatch1(p_dtype, [&](auto* pp) {
+    using P = std::remove_pointer_t<decltype(pp)>;
+    md_gain_grad_kernel<P><<<(unsigned)cdiv(n, 256), 256, 0, st>>>(gsum, sig, (P*)grad, n);
+  });
+  if (d) return d;
+  count_launch();
+  return check_launch();
+}
+
+extern "C" int thorn_md_finalize_multi(const thorn_md_final_tensor* ts, int n, int p_dtype, void* stream) {
+  if (n < 0 || (n > 0 && ts == nullptr) || !valid_dt(p_dtype)) return THORN_ERR_ARG;
+  for (int i = 0; i < n; ++i) {
+    const auto& e = ts[i];
+    if (e.batch * e.rows * e.cols > 0 && !e.p) return THORN_ERR_ARG;
+    if (e.normsq && !e.target) return THORN_ERR_ARG;
+    if (!e.row_sp || (!e.scalar_gain && !e.col_sp)) return THORN_ERR_ARG;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = THORN_OK;
+  auto blocks = [](const thorn_md_final_tensor& e) { return tiles_of(e.batch, e.rows, e.cols); };
+  auto vec = [](const thorn_md_final_tensor& e) { return (e.cols % 8) == 0 && aligned16(e.p); };
+  int d = dispatch1(p_dtype, [&](auto* pp) {
+    using P = std::remove_pointer_t<decltype(pp)>;
+    rc = launch_packed(ts, n, blocks, vec, [&](const Pack<thorn_md_final_tensor>& pk, int64_t nb) {
+      FinalArgs a;
+      a.pk = pk;
+      md_finalize_kernel<P><<<(unsigned)nb, kThreads, 0, st>>>(a);
+    });
+  });
+  return d ? d : rc;
+}
+
+extern "C" int thorn_sumsq_multi(const void* const* x, float* const* out, const int64_t* batch,
+                                 const int64_t* per_batch, int n, int dtype, void* stream) {
+  if (n < 0 || (n > 0 && (!x || !out || !batch || !per_batch)) || !valid_dt(dtype)) return THORN_ERR_ARG;
+  SumsqEntry es[kMaxT];
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = THORN_OK;
+  for (int i0 = 0; i0 < n; i0 += kMaxT) {
+    int m = n - i0 < kMaxT ? n - i0 : kMaxT;
+    for (int i = 0; i < m; ++i) {
+      es[i] = SumsqEntry{x[i0 + i], out[i0 + i], batch[i0 + i], per_batch[i0 + i]};
+      if (es[i].batch < 0 || es[i].per < 0 || (es[i].batch * es[i].per > 0 && (!es[i].x || !es[i].out)))
+        return THORN_ERR_ARG;
+    }
+    int d = dispatch1(dtype, [&](auto* px) {
+      using T = std::remove_pointer_t<decltype(px)>;
+      rc = launch_packed(
+          es, m, [](const SumsqEntry& e) { return cdiv(e.batch * e.per, kSqChunk); },
+          [](const SumsqEntry&) { return false; },
+          [&](const Pack<SumsqEntry>& pk, int64_t nb) {
+            SumsqArgs a;
+            a.pk = pk;
+            sumsq_kernel<T><<<(unsigned)nb, kThreads, 0, st>>>(a);
+          });
+    });
+    if (d) return d;
+    if (rc) return rc;
+  }
+  (void)dt_size;
+  return rc;
+}

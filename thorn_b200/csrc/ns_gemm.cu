@@ -1,0 +1,734 @@
+// Newton-Schulz GEMMs on the 5th-generation tensor cores (sm_100a).
+//
+// One persistent kernel serves every product of the NS iteration:
+//   D = alpha * A @ op(B) + beta * C          (fp32 accumulate in TMEM)
+//   D2 = D + diag2 * I                         (optional second output)
+// A is K-major ([rows, K] row-major).  B is either K-major ([N, K], used for
+// X X^T and for products with a symmetric right operand) or MN-major
+// ([K, N], used for Q @ X and B @ X).  With `sym`, only 128x BN tiles that
+// touch the lower triangle are computed; each lower element is stored at
+// (r, c) and mirrored to (c, r), so the output is exactly symmetric.  With
+// `trans_out`, D is stored transposed (the tall-matrix final product).
+//
+// Roles per CTA (192 threads, one CTA per SM):
+//   warp 0      TMA producer: fills a ring of shared-memory stages
+//   warp 1      allocates TMEM; lane 0 issues tcgen05.mma (128 x BN x 16)
+//   warps 2..5  epilogue: tcgen05.ld -> alpha/beta/diag -> global stores
+// Two TMEM accumulators (2 x BN columns) let the epilogue of one tile overlap
+// the MMAs of the next.  Every mbarrier wait is bounded by a wall-clock limit;
+// a timeout sets *err, raises a CTA-wide abort flag and lets all roles exit
+// through the normal teardown (TMEM is always freed).
+#include <cuda.h>
+#include <math.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+#include <vector>
+
+#include "common.cuh"
+
+namespace thorn {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 x 16-bit = one 128-byte swizzle row
+constexpr int kThreadsG = 192;
+constexpr uint64_t kTimeoutNs = 10ull * 1000 * 1000 * 1000;
+
+template <int BN>
+struct Cfg {
+  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kBarBytes = 256;
+  static constexpr int kSmem = kStages * kStageBytes + kBarBytes + 1024;
+};
+
+struct Params {
+  CUtensorMap tmA;
+  CUtensorMap tmB;
+  const void* C;
+  void* D;
+  void* D2;
+  int64_t c_bs, c_ld, d_bs, d_ld, d2_bs, d2_ld;
+  int M, N, K, batch;
+  float alpha, beta, diag2;
+  int sym, trans_out, c_vec, d_vec;
+  int tiles_m, tiles_n, tiles_per_mat, total_tiles, num_kb;
+  int* err;
+};
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait on the phase with parity `parity`.  Returns false on timeout or
+// when another role of this CTA has already aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int* err) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try(bar, parity)) return true;
+    if ((it & 255u) == 0) {
+      if (*abort) return false;
+      if (global_ns() - t0 > kTimeoutNs) {
+        if (err) atomicExch(err, 1);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* tm, uint32_t bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (sm100 layout: version 1).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor: kind::f16, fp32 accumulate, A K-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int bn, bool bf16, bool b_mn) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((b_mn ? 1u : 0u) << 16) |
+         ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+template <int BN>
+__device__ __forceinline__ void decode_tile(const Params& p, int t, int& b, int& tm, int& tn) {
+  b = t / p.tiles_per_mat;
+  int l = t - b * p.tiles_per_mat;
+  if (!p.sym) {
+    tm = l / p.tiles_n;
+    tn = l - tm * p.tiles_n;
+    return;
+  }
+  tm = 0;
+  for (;;) {
+    int cnt = min(p.tiles_n, (tm * BM + BM - 1) / BN + 1);
+    if (l < cnt || tm + 1 >= p.tiles_m) {
+      tn = l;
+      return;
+    }
+    l -= cnt;
+    ++tm;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+template <int BN, bool B_MN, class T>
+__global__ void __launch_bounds__(kThreadsG, 1) ns_gemm_kernel(const __grid_constant__ Params p) {
+  using C_ = Cfg<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C_::kStages * C_::kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + C_::kStages * C_::kBBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + C_::kStages;
+  uint64_t* tfull = bars + 2 * C_::kStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C_::kStages; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), 4 * 32);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tmA)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tmB)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"((uint32_t)C_::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < p.total_tiles && !*abort_flag; t += gridDim.x) {
+        int b, tm, tn;
+        decode_tile<BN>(p, t, b, tm, tn);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.err)) break;
+          const uint32_t fb = smem_u32(&full[stage]);
+          mbar_expect_tx(fb, C_::kStageBytes);
+          tma_load_3d(smem_u32(sA + stage * C_::kABytes), &p.tmA, fb, kb * BK, tm * BM, b);
+          if (!B_MN) {
+            tma_load_3d(smem_u32(sB + stage * C_::kBBytes), &p.tmB, fb, kb * BK, tn * BN, b);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c)
+              tma_load_3d(smem_u32(sB + stage * C_::kBBytes + c * (64 * BK * 2)), &p.tmB, fb, tn * BN + c * 64,
+                          kb * BK, b);
+          }
+          if (++stage == C_::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer -----------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(BN, sizeof(T) == 2 && !std::is_same<T, __half>::value, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int t = blockIdx.x; t < p.total_tiles && !*abort_flag; t += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
+        if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag, p.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * C_::kABytes);
+          const uint32_t b0 = smem_u32(sB + stage * C_::kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = sdesc(a0 + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc(b0 + kk * 2048, 64 * BK * 2, 1024) : sdesc(b0 + kk * 32, 16, 1024);
+            umma(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(smem_u32(&empty[stage]));
+          if (++stage == C_::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(&tfull[acc]));
+      }
+    }
+  } else {
+    // ------------------------------ epilogue -------------------------------
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int rloc = q * 32 + lane;
+    const T* Cp = reinterpret_cast<const T*>(p.C);
+    T* Dp = reinterpret_cast<T*>(p.D);
+    T* D2p = reinterpret_cast<T*>(p.D2);
+    int it = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
+      if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag, p.err)) break;
+      tc_fence_after();
+      int b, tm, tn;
+      decode_tile<BN>(p, t, b, tm, tn);
+      const int row = tm * BM + rloc;
+      const bool row_ok = row < p.M;
+      const int warp_row_max = tm * BM + q * 32 + 31;
+      T* D = Dp + (int64_t)b * p.d_bs;
+      T* D2 = D2p ? D2p + (int64_t)b * p.d2_bs : nullptr;
+      const T* Cb = Cp ? Cp + (int64_t)b * p.c_bs : nullptr;
+#pragma unroll 1
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        const int col0 = tn * BN + ch * 32;
+        if (col0 >= p.N) break;
+        if (p.sym && warp_row_max < col0) continue;  // whole warp above the diagonal
+        float v[32];
+        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + ch * 32), v);
+        const bool full = row_ok && col0 + 32 <= p.N;
+        if (Cb != nullptr) {
+          float cv[32];
+          if (full && p.c_vec) {
+            load_n(Cb + (int64_t)row * p.c_ld + col0, cv, 8, true);
+            load_n(Cb + (int64_t)row * p.c_ld + col0 + 8, cv + 8, 8, true);
+            load_n(Cb + (int64_t)row * p.c_ld + col0 + 16, cv + 16, 8, true);
+            load_n(Cb + (int64_t)row * p.c_ld + col0 + 24, cv + 24, 8, true);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              cv[j] = (row_ok && col0 + j < p.N) ? to_f(Cb[(int64_t)row * p.c_ld + col0 + j]) : 0.f;
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = p.alpha * v[j] + p.beta * cv[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = p.alpha * v[j];
+        }
+        // round once to the output type
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = rnd<T>(v[j]);
+
+        for (int out = 0; out < (D2 ? 2 : 1); ++out) {
+          T* O = out == 0 ? D : D2;
+          const int64_t ld = out == 0 ? p.d_ld : p.d2_ld;
+          float w[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) w[j] = (out == 1 && row == col0 + j) ? rnd<T>(v[j] + p.diag2) : v[j];
+          if (p.trans_out) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (row_ok && col0 + j < p.N) O[(int64_t)(col0 + j) * ld + row] = from_f<T>(w[j]);
+            continue;
+          }
+          const bool lower_full = !p.sym || row >= col0 + 31;
+          if (full && p.d_vec && lower_full) {
+            T* dst = O + (int64_t)row * ld + col0;
+            store_n(dst, w, 8, true);
+            store_n(dst + 8, w + 8, 8, true);
+            store_n(dst + 16, w + 16, 8, true);
+            store_n(dst + 24, w + 24, 8, true);
+          } else if (row_ok) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < p.N && (!p.sym || row >= col0 + j)) O[(int64_t)row * ld + col0 + j] = from_f<T>(w[j]);
+          }
+          if (p.sym && warp_row_max > col0) {
+            // mirror strictly-lower elements: lanes hold consecutive rows -> coalesced
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (row_ok && col0 + j < p.N && row > col0 + j) O[(int64_t)(col0 + j) * ld + row] = from_f<T>(w[j]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&tempty[acc]));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"((uint32_t)C_::kTmemCols)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+struct DevInfo {
+  int sms = 0;
+  int major = 0;
+};
+static DevInfo dev_info() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::mutex mu;
+  static std::vector<DevInfo> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  if ((int)cache.size() <= dev) cache.resize(dev + 1);
+  if (cache[dev].sms == 0) {
+    cudaDeviceGetAttribute(&cache[dev].sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&cache[dev].major, cudaDevAttrComputeCapabilityMajor, dev);
+  }
+  return cache[dev];
+}
+
+// 3-D tiled tensor map over [batch][rows][inner] with 128-byte swizzle.
+static int make_map(CUtensorMap* m, const void* base, int dtype, int64_t inner, int64_t rows, int64_t batch,
+                    int64_t ld, int64_t bs, int box_inner, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return THORN_ERR_UNSUPPORTED;
+  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)batch};
+  int64_t bstride = bs > 0 ? bs : ld * rows;
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(bstride * 2)};
+  cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, dtype == THORN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? THORN_OK : THORN_ERR_ARG;
+}
+
+}  // namespace gemm
+
+// One GEMM of the NS iteration (all pointers device, 16-bit elements).
+struct GemmOp {
+  const void* A = nullptr;
+  int64_t a_ld = 0, a_bs = 0;
+  const void* B = nullptr;
+  int64_t b_ld = 0, b_bs = 0;
+  bool b_mn = false;
+  const void* C = nullptr;
+  int64_t c_ld = 0, c_bs = 0;
+  void* D = nullptr;
+  int64_t d_ld = 0, d_bs = 0;
+  void* D2 = nullptr;
+  int64_t d2_ld = 0, d2_bs = 0;
+  int M = 0, N = 0, K = 0, batch = 1;
+  float alpha = 1.f, beta = 0.f, diag2 = 0.f;
+  bool sym = false, trans_out = false;
+};
+
+// Algorithmic work of the GEMMs issued so far (for roofline reporting).
+static std::atomic<uint64_t> g_flops_dense{0}, g_flops_exec{0};
+
+template <int BN, bool BMN, class T>
+static int launch_gemm(gemm::Params& prm, int grid, cudaStream_t st) {
+  using C_ = gemm::Cfg<BN>;
+  static std::once_flag attr_once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(attr_once[dev & 63], []() {
+    cudaFuncSetAttribute(gemm::ns_gemm_kernel<BN, BMN, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::kSmem);
+  });
+  gemm::ns_gemm_kernel<BN, BMN, T><<<grid, gemm::kThreadsG, C_::kSmem, st>>>(prm);
+  count_launch();
+  return check_launch();
+}
+
+int run_gemm(const GemmOp& op, int dtype, int* err, cudaStream_t st) {
+  using namespace gemm;
+  if (op.M <= 0 || op.N <= 0 || op.K <= 0 || op.batch <= 0) return THORN_OK;
+  if (!op.A || !op.B || !op.D) return THORN_ERR_ARG;
+  if (dtype != THORN_F16 && dtype != THORN_BF16) return THORN_ERR_ARG;
+  if (op.sym && op.M != op.N) return THORN_ERR_ARG;
+  // TMA: 16-byte aligned bases and strides
+  if (!aligned16(op.A) || !aligned16(op.B) || (op.a_ld % 8) || (op.b_ld % 8) || (op.a_bs % 8) || (op.b_bs % 8))
+    return THORN_ERR_ALIGN;
+  DevInfo di = dev_info();
+  if (di.major != 10) return THORN_ERR_UNSUPPORTED;
+  Params prm;
+  memset(&prm, 0, sizeof(prm));
+  const int BN = (op.N > 128) ? 256 : 128;
+  int rc = make_map(&prm.tmA, op.A, dtype, op.K, op.M, op.batch, op.a_ld, op.a_bs, BK, BM);
+  if (rc) return rc;
+  if (op.b_mn) rc = make_map(&prm.tmB, op.B, dtype, op.N, op.K, op.batch, op.b_ld, op.b_bs, 64, BK);
+  else rc = make_map(&prm.tmB, op.B, dtype, op.K, op.N, op.batch, op.b_ld, op.b_bs, BK, BN);
+  if (rc) return rc;
+  prm.C = op.C;
+  prm.D = op.D;
+  prm.D2 = op.D2;
+  prm.c_bs = op.c_bs;
+  prm.c_ld = op.c_ld;
+  prm.d_bs = op.d_bs;
+  prm.d_ld = op.d_ld;
+  prm.d2_bs = op.d2_bs;
+  prm.d2_ld = op.d2_ld;
+  prm.M = op.M;
+  prm.N = op.N;
+  prm.K = op.K;
+  prm.batch = op.batch;
+  prm.alpha = op.alpha;
+  prm.beta = op.beta;
+  prm.diag2 = op.diag2;
+  prm.sym = op.sym;
+  prm.trans_out = op.trans_out;
+  prm.c_vec = op.C && aligned16(op.C) && (op.c_ld % 8) == 0 && (op.c_bs % 8) == 0;
+  prm.d_vec = aligned16(op.D) && (op.d_ld % 8) == 0 && (op.d_bs % 8) == 0 &&
+              (!op.D2 || (aligned16(op.D2) && (op.d2_ld % 8) == 0 && (op.d2_bs % 8) == 0));
+  prm.tiles_m = (op.M + BM - 1) / BM;
+  prm.tiles_n = (op.N + BN - 1) / BN;
+  if (op.sym) {
+    int cnt = 0;
+    for (int tm = 0; tm < prm.tiles_m; ++tm) cnt += std::min(prm.tiles_n, (tm * BM + BM - 1) / BN + 1);
+    prm.tiles_per_mat = cnt;
+  } else {
+    prm.tiles_per_mat = prm.tiles_m * prm.tiles_n;
+  }
+  const int64_t total = (int64_t)prm.tiles_per_mat * op.batch;
+  if (total > (int64_t)INT32_MAX) return THORN_ERR_ARG;
+  prm.total_tiles = (int)total;
+  prm.num_kb = (op.K + BK - 1) / BK;
+  prm.err = err;
+  const int grid = (int)min64(total, (int64_t)di.sms);
+  const double dense = 2.0 * op.M * (double)op.N * op.K * op.batch;
+  const double exec = 2.0 * BM * (double)BN * (prm.num_kb * (double)BK) * total;
+  g_flops_dense.fetch_add((uint64_t)dense);
+  g_flops_exec.fetch_add((uint64_t)exec);
+  const bool bf = dtype == THORN_BF16;
+  if (BN == 256) {
+    if (op.b_mn) return bf ? launch_gemm<256, true, __nv_bfloat16>(prm, grid, st) : launch_gemm<256, true, __half>(prm, grid, st);
+    return bf ? launch_gemm<256, false, __nv_bfloat16>(prm, grid, st) : launch_gemm<256, false, __half>(prm, grid, st);
+  }
+  if (op.b_mn) return bf ? launch_gemm<128, true, __nv_bfloat16>(prm, grid, st) : launch_gemm<128, true, __half>(prm, grid, st);
+  return bf ? launch_gemm<128, false, __nv_bfloat16>(prm, grid, st) : launch_gemm<128, false, __half>(prm, grid, st);
+}
+
+}  // namespace thorn
+
+using namespace thorn;
+
+// ===========================================================================
+// Newton-Schulz sequencer (thorn.py:626-662)
+// ===========================================================================
+namespace {
+struct NsLayout {
+  int64_t m, n, ldm, ldn;
+  bool gram;
+  int64_t xs, ms;  // bytes of one [batch, m, ldn] / [batch, m, ldm] buffer (256-aligned)
+  int64_t total;
+};
+NsLayout ns_layout(int64_t batch, int64_t rows, int64_t cols) {
+  NsLayout L;
+  L.m = std::min(rows, cols);
+  L.n = std::max(rows, cols);
+  L.ldm = thorn_ns_ld(L.m);
+  L.ldn = thorn_ns_ld(L.n);
+  L.gram = L.m != L.n;
+  auto al = [](int64_t x) { return (x + 255) / 256 * 256; };
+  L.xs = al(batch * L.m * L.ldn * 2);
+  L.ms = al(batch * L.m * L.ldm * 2);
+  L.total = L.gram ? (2 * L.xs + 5 * L.ms) : (4 * L.ms);
+  return L;
+}
+}  // namespace
+
+extern "C" int64_t thorn_ns_workspace_bytes(int64_t batch, int64_t rows, int64_t cols) {
+  if (batch <= 0 || rows <= 0 || cols <= 0) return 0;
+  return ns_layout(batch, rows, cols).total;
+}
+
+extern "C" int thorn_ns_batched(const void* x, void* out, void* workspace, int64_t workspace_bytes, int64_t batch,
+                                int64_t rows, int64_t cols, int ns_dtype, const double* coeffs, int iters,
+                                const int32_t* restarts, int n_restarts, int* err_flag, void* stream) {
+  if (batch < 0 || rows < 0 || cols < 0 || iters < 0 || n_restarts < 0) return THORN_ERR_ARG;
+  if (batch == 0 || rows == 0 || cols == 0) return THORN_OK;
+  if (!x || !out || !workspace || (iters > 0 && !coeffs) || (n_restarts > 0 && !restarts)) return THORN_ERR_ARG;
+  if (ns_dtype != THORN_F16 && ns_dtype != THORN_BF16) return THORN_ERR_ARG;
+  if (batch > INT32_MAX || rows > INT32_MAX || cols > INT32_MAX) return THORN_ERR_ARG;
+  const NsLayout L = ns_layout(batch, rows, cols);
+  if (workspace_bytes < L.total) return THORN_ERR_ARG;
+  if (!aligned16(x) || !aligned16(workspace)) return THORN_ERR_ALIGN;
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool tall = rows > cols;
+  const int m = (int)L.m, n = (int)L.n, B = (int)batch;
+  const int64_t ldm = L.ldm, ldn = L.ldn;
+  auto in_restarts = [&](int i) {
+    for (int k = 0; k < n_restarts; ++k)
+      if (restarts[k] == i) return true;
+    return false;
+  };
+  uint8_t* ws = (uint8_t*)workspace;
+  int rc = THORN_OK;
+  // product of two m x m matrices (second operand symmetric or K-major)
+  auto mm = [&](const void* A, const void* Bm, const void* C, void* D, void* D2, float alpha, float beta,
+                float diag2) {
+    GemmOp op;
+    op.A = A; op.a_ld = ldm; op.a_bs = m * ldm;
+    op.B = Bm; op.b_ld = ldm; op.b_bs = m * ldm; op.b_mn = false;
+    op.C = C; op.c_ld = ldm; op.c_bs = m * ldm;
+    op.D = D; op.d_ld = ldm; op.d_bs = m * ldm;
+    op.D2 = D2; op.d2_ld = ldm; op.d2_bs = m * ldm;
+    op.M = m; op.N = m; op.K = m; op.batch = B;
+    op.alpha = alpha; op.beta = beta; op.diag2 = diag2; op.sym = true;
+    return run_gemm(op, ns_dtype, err_flag, st);
+  };
+  // Gram matrix X X^T of a [m, n] matrix with leading dim ld
+  auto gramm = [&](const void* X, int64_t ld, int K, void* D) {
+    GemmOp op;
+    op.A = X; op.a_ld = ld; op.a_bs = m * ld;
+    op.B = X; op.b_ld = ld; op.b_bs = m * ld; op.b_mn = false;
+    op.D = D; op.d_ld = ldm; op.d_bs = m * ldm;
+    op.M = m; op.N = m; op.K = K; op.batch = B;
+    op.sym = true;
+    return run_gemm(op, ns_dtype, err_flag, st);
+  };
+  // Q @ X with X [m, N] (MN-major second operand), optional C = X
+  auto qx = [&](const void* Q, const void* X, int64_t ldx, int N, const void* C, float beta, void* D, int64_t d_ld,
+                int64_t d_bs, bool trans) {
+    GemmOp op;
+    op.A = Q; op.a_ld = ldm; op.a_bs = m * ldm;
+    op.B = X; op.b_ld = ldx; op.b_bs = m * ldx; op.b_mn = true;
+    op.C = C; op.c_ld = ldx; op.c_bs = m * ldx;
+    op.D = D; op.d_ld = d_ld; op.d_bs = d_bs;
+    op.M = m; op.N = N; op.K = m; op.batch = B;
+    op.beta = beta; op.trans_out = trans;
+    return run_gemm(op, ns_dtype, err_flag, st);
+  };
+#define NS_TRY(expr)          \
+  do {                        \
+    rc = (expr);              \
+    if (rc) return rc;        \
+  } while (0)
+
+  if (L.gram) {
+    void* Xb[2] = {ws, ws + L.xs};
+    uint8_t* mbase = ws + 2 * L.xs;
+    void* R = mbase;
+    void* Z = mbase + L.ms;
+    void* Qb[2] = {mbase + 2 * L.ms, mbase + 3 * L.ms};
+    void* RZ = mbase + 4 * L.ms;
+    const void* X = x;
+    int xi = 0, qi = 0;
+    NS_TRY(gramm(X, ldn, n, R));
+    for (int i = 0; i < iters; ++i) {
+      const float a = (float)coeffs[3 * i], b = (float)coeffs[3 * i + 1], c = (float)coeffs[3 * i + 2];
+      const bool rs = in_restarts(i);
+      if (rs && i != 0) {
+        NS_TRY(qx(Qb[qi], X, ldn, n, nullptr, 0.f, Xb[xi], ldn, m * ldn, false));
+        X = Xb[xi];
+        xi ^= 1;
+        NS_TRY(gramm(X, ldn, n, R));
+      }
+      if (i != 0 && !rs) {
+        NS_TRY(mm(R, R, R, Z, nullptr, c, b, 0.f));                   // Z = c R R + b R
+        NS_TRY(mm(Qb[qi], Z, Qb[qi], Qb[qi ^ 1], nullptr, 1.f, a, 0.f));  // Q = Q Z + a Q
+        qi ^= 1;
+      } else {
+        NS_TRY(mm(R, R, R, Z, Qb[qi], c, b, a));  // Z = c R R + b R ; Q = Z + a I
+      }
+      if (i < iters - 1 && !in_restarts(i + 1)) {
+        NS_TRY(mm(R, Z, R, RZ, nullptr, 1.f, a, 0.f));   // RZ = R Z + a R
+        NS_TRY(mm(Z, RZ, RZ, R, nullptr, 1.f, a, 0.f));  // R = Z RZ + a RZ
+      }
+    }
+    if (iters == 0) return THORN_ERR_ARG;
+    // out = Q @ X ; stored transposed for tall inputs (X.mT @ Q)
+    NS_TRY(qx(Qb[qi], X, ldn, n, nullptr, 0.f, out, tall ? (int64_t)m : (int64_t)n, (int64_t)m * n, tall));
+  } else {
+    void* Xb[2] = {ws, ws + L.ms};
+    void* A = ws + 2 * L.ms;
+    void* Bm = ws + 3 * L.ms;
+    const void* X = x;
+    int xi = 0;
+    if (iters == 0) return THORN_ERR_ARG;
+    for (int i = 0; i < iters; ++i) {
+      const float a = (float)coeffs[3 * i], b = (float)coeffs[3 * i + 1], c = (float)coeffs[3 * i + 2];
+      NS_TRY(gramm(X, ldm, m, A));                         // A = X X^T
+      NS_TRY(mm(A, A, A, Bm, nullptr, c, b, 0.f));         // B = c A A + b A
+      const bool last = i == iters - 1;
+      void* D = last ? out : Xb[xi];
+      NS_TRY(qx(Bm, X, ldm, m, X, a, D, last ? (int64_t)m : ldm, last ? (int64_t)m * m : m * ldm, false));  // X = a X + B X
+      X = D;
+      xi ^= 1;
+    }
+  }
+#undef NS_TRY
+  return THORN_OK;
+}
+
+extern "C" int thorn_sym_addmm(const void* A, const void* B, const void* C, void* O, int64_t batch, int64_t M,
+                               int64_t K, int c_batched, float alpha, float beta, int dtype, int* err_flag,
+                               void* stream) {
+  if (batch < 0 || M < 0 || K < 0) return THORN_ERR_ARG;
+  if (batch == 0 || M == 0) return THORN_OK;
+  if (batch > INT32_MAX || M > INT32_MAX || K > INT32_MAX) return THORN_ERR_ARG;
+  if ((M % 8) || (K % 8)) return THORN_ERR_ALIGN;
+  GemmOp op;
+  op.A = A; op.a_ld = K; op.a_bs = M * K;
+  op.B = B; op.b_ld = M; op.b_bs = K * M; op.b_mn = true;
+  op.C = C; op.c_ld = M; op.c_bs = c_batched ? M * M : 0;
+  op.D = O; op.d_ld = M; op.d_bs = M * M;
+  op.M = (int)M; op.N = (int)M; op.K = (int)K; op.batch = (int)batch;
+  op.alpha = alpha; op.beta = C ? beta : 0.f; op.sym = true;
+  if (K == 0) return THORN_ERR_ARG;
+  return run_gemm(op, dtype, err_flag, (cudaStream_t)stream);
+}
+
+// Dense-equivalent and executed tensor-core FLOPs issued so far (for roofline reports).
+extern "C" void thorn_gemm_flops(double* dense, double* executed) {
+  if (dense) *dense = (double)g_flops_dense.load();
+  if (executed) *executed = (double)g_flops_exec.load();
+}

@@ -1,0 +1,627 @@
+"""Drop-in ``THORN`` optimizer whose step runs on the sm_100a kernels.
+
+Public surface follows the reference ``thorn.THORN`` (thorn/thorn.py of
+pykeio/THORN v3.1.1): the constructor (thorn.py:1271-1300), the group keys and
+defaults of ``_THORNParameterGroup`` (thorn.py:535-612), ``step(closure=None, *,
+param=None)`` (thorn.py:1738-1753), ``setup_gradient_release``
+(thorn.py:1755-1776), ``polar_decomp_batch_size`` (thorn.py:1237) and the
+optimizer-state layout (thorn.py:1591-1634), so ``state_dict`` /
+``load_state_dict`` round-trip between the two.
+
+Every numeric operation of the step is a kernel of ``libthorn_b200.so`` called
+through its C ABI; host code only plans launches and allocates scratch from
+the torch caching allocator.  Parameters must live on a CUDA device; there is
+no CPU path.
+
+Extensions (all optional, off by default):
+* group key ``state_dtype``: dtype of the optimizer state (the reference keeps
+  it in the parameter dtype);
+* attribute ``ns_dtype``: operand type of the Newton-Schulz GEMMs,
+  ``torch.float16`` (the reference's choice, thorn.py:634-635) or
+  ``torch.bfloat16``.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import MISSING, dataclass, field, fields
+from functools import partial
+from math import prod
+from typing import Any, Callable, Literal, Optional, Union
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+import torch.nn.functional as F
+from torch.distributed.tensor import DTensor, Replicate
+from torch.nn import Parameter
+from torch.optim import Optimizer
+
+from . import _native as N
+from .coeffs import gram_ns_restarts, optimal_composition
+
+__all__ = ["THORN", "THORNOrthoGroup", "THORNNonOrthoGroup", "THORNGroup"]
+
+_TargetNorm = Union[Literal["init", "min", "max"], Callable[[torch.Tensor], Union[torch.Tensor, float]]]
+LN_E_SUB_1 = 0.5413248546  # softplus(LN_E_SUB_1) == 1 (thorn.py:1602)
+
+
+@dataclass
+class GroupConfig:
+    """Per-group settings; same fields and defaults as thorn.py:535-561."""
+
+    orthogonalize: bool
+    params: list
+    lr: float
+    base_lr: float = field(init=False)
+    none_grad: bool = field(default=True)
+    weight_decay: float = field(default=0.1)
+    betas: tuple = field(default_factory=lambda: (0.9, 0.95))
+    scaling_mode: Optional[str] = field(default=None)
+    target_rms: float = field(default=0.2)
+    target_norm: Optional[_TargetNorm] = field(default=None)
+    iters: int = field(default=5)
+    rectify: bool = field(default=False)
+    eps: float = field(default=0)
+    lower_bound: float = field(default=1e-3)
+    safety_factor: float = field(default=0.03)
+    cushion: float = field(default=0.02)
+    momentum_align: bool = field(default=False)
+    coeffs: list = field(init=False)
+    restarts: list = field(init=False)
+    decouple_md: bool = field(default=False)
+    gain_lr: float = field(default=1e-3)
+    gain_betas: tuple = field(default_factory=lambda: (0.9, 0.95))
+    norm_axis: Optional[Any] = field(default=None)
+    split_gain: bool = field(default=True)
+    force_per_neuron_norm: bool = field(default=False)
+
+    @classmethod
+    def from_kwargs(cls, **kw) -> "GroupConfig":
+        return cls(**{k: kw[k] for k in kw if k in cls.__dataclass_fields__})
+
+    def __post_init__(self):
+        # validation messages as in thorn.py:567-573
+        if self.lr < 0.0:
+            raise ValueError(f"Invalid learning rate `{self.lr}`; should be >= 0")
+        if not (0.0 <= self.betas[0] < 1.0):
+            raise ValueError(f"Invalid beta1 `{self.betas[0]}`; should be in [0, 1)")
+        if not (0.0 <= self.betas[1] < 1.0):
+            raise ValueError(f"Invalid beta2 `{self.betas[1]}`; should be in [0, 1)")
+        self.base_lr = self.lr
+        self.coeffs = optimal_composition(self.lower_bound, self.iters, self.safety_factor, self.cushion)
+        self.restarts = gram_ns_restarts(*self.coeffs)
+
+    @property
+    def scaling_mode_(self) -> str:
+        if self.scaling_mode is None:
+            return "md" if self.decouple_md else "moonlight"
+        return self.scaling_mode
+
+    @property
+    def gain_lr_(self) -> float:
+        return self.gain_lr * (float(self.lr) / self.base_lr) if self.base_lr else self.gain_lr
+
+    def norm_axis_(self, p) -> Any:
+        return self.norm_axis if self.norm_axis is not None else ((-2, -1) if p.ndim > 1 else -1)
+
+    def needs_pnn(self, rows: int, cols: int) -> bool:
+        """Per-neuron norm only for tall matrices unless forced (thorn.py:704-707)."""
+        return self.betas[1] > 0 and (rows > cols or self.force_per_neuron_norm)
+
+    def lr_scale(self, rows: int, cols: int) -> float:
+        """thorn.py:768-780."""
+        mode = self.scaling_mode_
+        if mode == "md":
+            return max(rows / cols, cols / rows) ** 0.5
+        if mode == "moonlight":
+            assert self.target_rms > 0
+            return self.target_rms * (max(1, rows, cols) ** 0.5)
+        if mode == "jordan":
+            return max(1, rows / cols) ** 0.5
+        raise ValueError(f"unknown scaling_mode {mode!r}")
+
+    def rect(self, step) -> float:
+        """RAdam rectification (thorn.py:782-798)."""
+        beta2 = self.betas[1]
+        if beta2 > 0.0:
+            rho_inf = 2 / (1 - beta2) - 1
+            rho = rho_inf - 2 * step * (beta2 ** step) / (1 - beta2 ** step)
+            r = ((rho - 4) * (rho - 2) * rho_inf / ((rho_inf - 4) * (rho_inf - 2) * rho)) ** 0.5 if rho > 4.0 else 0.0
+            return r ** float(self.rectify)
+        return 1.0
+
+    def target_norm_(self, p: torch.Tensor) -> torch.Tensor:
+        """thorn.py:597-612 (run once, at state creation)."""
+        tn = self.target_norm
+        if tn is None:
+            tn = "max" if self.orthogonalize else "init"
+        if callable(tn):
+            tn = tn(p)
+        elif tn == "init":
+            tn = p.norm(dim=self.norm_axis_(p), keepdim=True)
+        elif tn == "min":
+            tn = min(p.size(-2), p.size(-1)) ** 0.5
+        elif tn == "max":
+            tn = max(p.size(-2), p.size(-1)) ** 0.5
+        if isinstance(tn, (float, int)):
+            return torch.full((), tn, dtype=p.dtype, device=p.device)
+        return tn.to(dtype=p.dtype, device=p.device)
+
+
+THORNOrthoGroup = dict
+THORNNonOrthoGroup = dict
+THORNGroup = dict
+
+
+def _local(t):
+    return t.to_local() if isinstance(t, DTensor) else t
+
+
+def _mat_view(shape) -> tuple[int, int, int]:
+    """(batch, rows, cols) view of a tensor: leading dims are a batch (thorn.py:628-633)."""
+    if len(shape) >= 2:
+        return int(prod(shape[:-2])), int(shape[-2]), int(shape[-1])
+    if len(shape) == 1:
+        return 1, 1, int(shape[0])
+    return 1, 1, 1
+
+
+class _Arena:
+    """Carves fp32 scratch views out of two buffers: one zeroed, one not."""
+
+    def __init__(self):
+        self.zero_n = 0
+        self.raw_n = 0
+        self.req = []
+
+    def zeros(self, n):
+        off = self.zero_n
+        self.zero_n += (n + 3) // 4 * 4
+        return ("z", off, n)
+
+    def empty(self, n):
+        off = self.raw_n
+        self.raw_n += (n + 3) // 4 * 4
+        return ("r", off, n)
+
+    def materialize(self, device):
+        self.zbuf = torch.zeros(max(4, self.zero_n), dtype=torch.float32, device=device)
+        self.rbuf = torch.empty(max(4, self.raw_n), dtype=torch.float32, device=device)
+
+    def get(self, h):
+        if h is None:
+            return None
+        kind, off, n = h
+        buf = self.zbuf if kind == "z" else self.rbuf
+        return buf[off:off + n]
+
+    def ptr(self, h):
+        t = self.get(h)
+        return None if t is None else t.data_ptr()
+
+
+class _Item:
+    __slots__ = ("p", "g", "state", "B", "R", "C", "apply", "pdt", "sdt", "normsq", "rs", "cs", "sig_r", "sig_c",
+                 "rgs", "cgs", "rs_new", "cs_new", "pnorm", "scalar", "ggrad_r", "ggrad_c", "split")
+
+
+class THORN(Optimizer):
+    """THORN optimizer (see module docstring)."""
+
+    polar_decomp_batch_size: int = 32 * 1024 * 1024
+    ns_dtype: torch.dtype = torch.float16
+
+    def __init__(self, params, *, backend=torch.cuda, **conf):
+        self._update_rate = 1
+        self.backend = backend
+        param_groups = THORN._auto_assign(params, **conf) if isinstance(params, nn.Module) else list(params)
+        for group in param_groups:
+            assert "orthogonalize" in group
+            if group["orthogonalize"]:
+                assert all(map(lambda x: x.ndim >= 2, group["params"])), \
+                    "Only parameters with ndim >= 2 can be orthogonalized"
+        self.is_distributed = dist.is_available() and dist.is_initialized()
+        self.rank = dist.get_rank() if self.is_distributed else None
+        self.comm_stream = None
+        self.compute_stream = None
+        defaults = dict()
+        for f in fields(GroupConfig):
+            if f.default is not MISSING:
+                defaults[f.name] = f.default
+            elif f.default_factory is not MISSING:
+                defaults[f.name] = f.default_factory()
+        super().__init__(param_groups, defaults)
+        self._param_to_group: dict[int, dict[str, Any]] = {}
+        for group in self.param_groups:
+            for p in group["params"]:
+                self._param_to_group[id(p)] = group
+        self._err = {}
+        if isinstance(params, nn.Module) and conf.get("gradient_release", False):
+            self.setup_gradient_release(params)
+
+    # ------------------------------------------------------------------ API
+    @staticmethod
+    def _auto_assign(module: nn.Module, **keys) -> list:
+        """thorn.py:1302-1331: ndim>=2 params outside embeddings and lm_head are orthogonalized."""
+        emb = set()
+        module.apply(lambda m: emb.add(id(m.weight)) if isinstance(m, nn.Embedding) else None)
+        ortho, regular = [], []
+        for name, param in module.named_parameters():
+            if param.ndim >= 2 and "lm_head" not in name and id(param) not in emb:
+                ortho.append(param)
+            else:
+                regular.append(param)
+        return [{"orthogonalize": True, "params": ortho, **keys}, {"orthogonalize": False, "params": regular, **keys}]
+
+    @torch.no_grad()
+    def step(self, closure=None, *, param=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        if param is None:
+            for group in self.param_groups:
+                self._step_params(group["params"], GroupConfig.from_kwargs(**group), group)
+        else:
+            group = self._param_to_group[id(param)]
+            self._step_params([param], GroupConfig.from_kwargs(**group), group)
+        return loss
+
+    def setup_gradient_release(self, model: nn.Module, update_rate: int = 1, ignore_existing_hooks: bool = False):
+        """thorn.py:1755-1776: step each parameter from its post-accumulate-grad hook."""
+        def hook(param, optimizer):
+            optimizer.step(param=param)
+            param.grad = None
+
+        hooks = []
+        for p in model.parameters():
+            if p.requires_grad:
+                if p._post_accumulate_grad_hooks and not ignore_existing_hooks:
+                    for h in hooks:
+                        h.remove()
+                    raise ValueError("Model already has post_accumulate_grad_hooks. If this is expected, pass "
+                                     "`ignore_existing_hooks=True`.")
+                hooks.append(p.register_post_accumulate_grad_hook(partial(hook, optimizer=self)))
+        model._gradient_release_hooks = hooks
+        self._update_rate = update_rate
+
+    def device_error(self) -> bool:
+        """True if a bounded device-side wait of a kernel gave up (reads a device flag; syncs)."""
+        return any(int(t.item()) != 0 for t in self._err.values())
+
+    # ------------------------------------------------------------- routing
+    def _init_state(self, p, state, cfg: GroupConfig, gdict):
+        state["step"] = 1
+        sdt = gdict.get("state_dtype") or p.dtype
+        state["moment"] = torch.zeros_like(p, dtype=sdt)
+        if not cfg.orthogonalize:
+            state["variance"] = torch.zeros_like(p, dtype=sdt)
+        if cfg.decouple_md:
+            if p.ndim > 1 and cfg.split_gain:
+                state["row_gain"] = torch.full((*p.shape[:-1], 1), LN_E_SUB_1, dtype=p.dtype, device=p.device)
+                state["col_gain"] = torch.full((*p.shape[:-2], 1, *p.shape[-1:]), LN_E_SUB_1, dtype=p.dtype,
+                                               device=p.device)
+                for k in ("row_gain", "col_gain"):
+                    state[f"{k}_moment"] = torch.zeros_like(state[k])
+                    state[f"{k}_variance"] = torch.zeros_like(state[k])
+            else:
+                state["gain"] = torch.full((), LN_E_SUB_1, dtype=p.dtype, device=p.device)
+                state["gain_moment"] = torch.zeros((), dtype=p.dtype, device=p.device)
+                state["gain_variance"] = torch.zeros((), dtype=p.dtype, device=p.device)
+            state["target_norm"] = cfg.target_norm_(p)
+
+    def _step_params(self, params, cfg: GroupConfig, gdict):
+        if cfg.momentum_align:
+            raise NotImplementedError("momentum_align (Magma) is not implemented by thorn_b200")
+        sharded, local = [], []
+        for p in params:
+            if p is None or p.grad is None:
+                continue
+            if p.grad.is_sparse:
+                raise NotImplementedError("sparse gradients are not implemented by thorn_b200")
+            state = self.state[p]
+            if "step" not in state:
+                self._init_state(p, state, cfg, gdict)
+            if isinstance(p.data, DTensor) and cfg.orthogonalize and \
+                    not all(isinstance(pl, Replicate) for pl in p.placements):
+                sharded.append(p)
+            else:
+                local.append(p)
+        if sharded:
+            from .sharded import sharded_ortho_step
+            sharded_ortho_step(self, sharded, cfg)
+        by_dev: dict = {}
+        for p in local:
+            by_dev.setdefault(_local(p).device, []).append(p)
+        for dev, ps in by_dev.items():
+            if dev.type != "cuda":
+                raise RuntimeError(f"thorn_b200 runs its step on CUDA devices only; got a parameter on {dev}")
+            with torch.cuda.device(dev):
+                if cfg.orthogonalize:
+                    self._ortho_local(ps, cfg)
+                else:
+                    self._adam_local(ps, cfg)
+
+    def _err_flag(self, dev):
+        t = self._err.get(dev)
+        if t is None:
+            t = torch.zeros(1, dtype=torch.int32, device=dev)
+            self._err[dev] = t
+        return t
+
+    # ------------------------------------------------------ shared helpers
+    def _items(self, params, cfg, arena: _Arena, ortho: bool):
+        items = []
+        for p in params:
+            st = self.state[p]
+            it = _Item()
+            it.p = _local(p)
+            g = _local(p.grad)
+            if not g.is_contiguous():
+                g = g.contiguous()
+            it.g = g
+            if not it.p.is_contiguous():
+                raise ValueError("thorn_b200 needs contiguous parameters")
+            it.state = st
+            it.B, it.R, it.C = _mat_view(it.p.shape)
+            it.apply = (st["step"] + 1) % self._update_rate == 0
+            it.pdt = it.p.dtype
+            it.sdt = _local(st["moment"]).dtype
+            N.dtype_code(it.pdt), N.dtype_code(it.sdt)
+            if g.dtype != it.pdt:
+                raise TypeError(f"gradient dtype {g.dtype} differs from parameter dtype {it.pdt}")
+            it.normsq = arena.zeros(it.B) if ortho else None
+            it.split = "row_gain" in st
+            it.scalar = "gain" in st
+            if cfg.decouple_md:
+                nr, nc = (it.B * it.R, it.B * it.C) if it.split else (1, 1)
+                it.rs, it.sig_r, it.rs_new = arena.empty(nr), arena.empty(nr), arena.empty(nr)
+                it.rgs = arena.zeros(nr)
+                if it.split:
+                    it.cs, it.sig_c, it.cs_new = arena.empty(nc), arena.empty(nc), arena.empty(nc)
+                    it.cgs = arena.zeros(nc)
+                else:
+                    it.cs = it.sig_c = it.cs_new = it.cgs = None
+                it.pnorm = arena.zeros(it.B)
+            items.append(it)
+        return items
+
+    def _md_prep(self, items, arena, new: bool, stream):
+        lib = N.load()
+        for it in items:
+            st = it.state
+            pc = N.dtype_code(it.pdt)
+            if it.split:
+                pairs = [(st["row_gain"], it.rs_new if new else it.rs, None if new else it.sig_r),
+                         (st["col_gain"], it.cs_new if new else it.cs, None if new else it.sig_c)]
+            else:
+                pairs = [(st["gain"], it.rs_new if new else it.rs, None if new else it.sig_r)]
+            for gain, sp, sig in pairs:
+                gl = _local(gain)
+                N.check(lib.thorn_md_prep(gl.data_ptr(), gl.numel(), arena.ptr(sp), arena.ptr(sig), pc, stream),
+                        "md_prep")
+
+    def _md_gains(self, items, cfg, arena, stream):
+        """Gradient of the gains and their Adam step (thorn.py:910-967)."""
+        lib = N.load()
+        by_dt: dict = {}
+        for it in items:
+            if not it.apply:
+                continue
+            st = it.state
+            pc = N.dtype_code(it.pdt)
+            keys = [("row_gain", it.rgs, it.sig_r), ("col_gain", it.cgs, it.sig_c)] if it.split else \
+                [("gain", it.rgs, it.sig_r)]
+            step = st["step"]
+            bc1 = 1 / (1 - cfg.gain_betas[0] ** step)
+            bc2 = 1 / (1 - cfg.gain_betas[1] ** step)
+            for key, gsum, sig in keys:
+                gain = _local(st[key])
+                grad = torch.empty_like(gain)
+                N.check(lib.thorn_md_gain_grad(arena.ptr(gsum), arena.ptr(sig), grad.data_ptr(), gain.numel(), pc,
+                                               stream), "md_gain_grad")
+                mom, var = _local(st[key + "_moment"]), _local(st[key + "_variance"])
+                t = N.AdamTensor(gain.data_ptr(), grad.data_ptr(), mom.data_ptr(), var.data_ptr(), gain.numel(),
+                                 cfg.gain_lr_, bc1, bc2, 0)
+                by_dt.setdefault((pc, N.dtype_code(mom.dtype)), []).append((t, grad))
+        for (pc, sc), ts in by_dt.items():
+            arr = N.array(N.AdamTensor, [t for t, _ in ts])
+            N.check(lib.thorn_adamw_multi(arr, len(ts), pc, sc, cfg.gain_betas[0], cfg.gain_betas[1], 0.0,
+                                          float(cfg.eps), stream), "adamw_multi(gains)")
+
+    def _md_finalize(self, items, arena, renorm_of, stream):
+        lib = N.load()
+        by_dt: dict = {}
+        keep = []
+        for it in items:
+            st = it.state
+            normsq = arena.ptr(it.pnorm) if (it.apply and renorm_of(it)) else None
+            tgt = _local(st["target_norm"]).reshape(-1).float()
+            keep.append(tgt)
+            stride = 0 if tgt.numel() == 1 else 1
+            if stride and tgt.numel() != it.B:
+                raise NotImplementedError("target_norm must be a scalar or one value per matrix")
+            t = N.MdFinalTensor(it.p.data_ptr(), normsq, tgt.data_ptr(), stride, arena.ptr(it.rs_new),
+                                arena.ptr(it.cs_new), 0 if it.split else 1, it.B, it.R, it.C)
+            by_dt.setdefault(N.dtype_code(it.pdt), []).append(t)
+        for pc, ts in by_dt.items():
+            N.check(lib.thorn_md_finalize_multi(N.array(N.MdFinalTensor, ts), len(ts), pc, stream), "md_finalize")
+        return keep
+
+    def _finish(self, params, cfg):
+        for p in params:
+            if cfg.none_grad:
+                p.grad = None
+            self.state[p]["step"] += 1
+
+    # ------------------------------------------- orthogonalized group (1 GPU)
+    def _ortho_local(self, params, cfg: GroupConfig):
+        """thorn.py:1376-1457 on the kernels: momentum -> NS input -> NS -> pnn -> apply (-> md)."""
+        lib = N.load()
+        dev = _local(params[0]).device
+        stream = N.stream_of(dev)
+        err = self._err_flag(dev)
+        md = cfg.decouple_md
+        arena = _Arena()
+        items = self._items(params, cfg, arena, ortho=True)
+        b1 = float(cfg.betas[0])
+        ns_code = N.dtype_code(self.ns_dtype)
+        # NS batches: bucket by (rows, cols, p dtype, state dtype)
+        buckets: dict = {}
+        for it in items:
+            if it.apply:
+                buckets.setdefault((it.R, it.C, it.pdt, it.sdt), []).append(it)
+        chunks = []
+        for (R, C, pdt, sdt), its in buckets.items():
+            cap = max(1, self.polar_decomp_batch_size // max(1, R * C)) if self.polar_decomp_batch_size > 0 else 1
+            cur, n = [], 0
+            for it in its:
+                if cur and n + it.B > cap:
+                    chunks.append((R, C, pdt, sdt, cur))
+                    cur, n = [], 0
+                cur.append(it)
+                n += it.B
+            if cur:
+                chunks.append((R, C, pdt, sdt, cur))
+        pnn_h = {}
+        for ci, (R, C, pdt, sdt, its) in enumerate(chunks):
+            if cfg.needs_pnn(R, C):
+                nb = sum(it.B for it in its)
+                pnn_h[ci] = (arena.empty(nb * R), arena.zeros(2 * nb))
+        arena.materialize(dev)
+
+        if md:
+            self._md_prep(items, arena, new=False, stream=stream)
+        write_grad = 1 if (md and not cfg.none_grad) else 0
+        by_dt: dict = {}
+        for it in items:
+            t = N.OrthoPreTensor(it.p.data_ptr() if md else None, it.g.data_ptr(), _local(it.state["moment"]).data_ptr(),
+                                 arena.ptr(it.normsq), it.B, it.R, it.C,
+                                 arena.ptr(it.rs) if md else None, arena.ptr(it.cs) if md else None,
+                                 1 if (md and not it.split) else 0,
+                                 arena.ptr(it.rgs) if md else None, arena.ptr(it.cgs) if md else None)
+            by_dt.setdefault((it.pdt, it.sdt), []).append(t)
+        for (pdt, sdt), ts in by_dt.items():
+            udt = pdt if pdt == sdt else torch.float32
+            N.check(lib.thorn_ortho_pre_multi(N.array(N.OrthoPreTensor, ts), len(ts), N.dtype_code(pdt),
+                                              N.dtype_code(sdt), N.dtype_code(udt), b1, 1 if md else 0, write_grad,
+                                              stream), "ortho_pre_multi")
+        if md:
+            self._md_gains(items, cfg, arena, stream)
+
+        coeffs = (ctypes.c_double * (3 * max(1, cfg.iters)))(*[x for abc in cfg.coeffs[:cfg.iters] for x in abc])
+        rs = list(cfg.restarts)
+        restarts = (ctypes.c_int32 * max(1, len(rs)))(*rs)
+        for ci, (R, C, pdt, sdt, its) in enumerate(chunks):
+            nb = sum(it.B for it in its)
+            m, n = min(R, C), max(R, C)
+            ldn = int(lib.thorn_ns_ld(n))
+            X = torch.empty((nb, m, ldn), dtype=self.ns_dtype, device=dev)
+            U = torch.empty((nb, R, C), dtype=self.ns_dtype, device=dev)
+            casts, off = [], 0
+            esz = X.element_size()
+            for it in its:
+                casts.append(N.NsCastTensor(it.g.data_ptr(), _local(it.state["moment"]).data_ptr(), arena.ptr(it.normsq),
+                                            X.data_ptr() + off * m * ldn * esz, it.B, it.R, it.C,
+                                            arena.ptr(it.rs) if md else None, arena.ptr(it.cs) if md else None,
+                                            1 if (md and not it.split) else 0, 1 if (md and not write_grad) else 0))
+                off += it.B
+            udt = pdt if pdt == sdt else torch.float32
+            N.check(lib.thorn_ns_cast_multi(N.array(N.NsCastTensor, casts), len(casts), N.dtype_code(pdt),
+                                            N.dtype_code(sdt), N.dtype_code(udt), ns_code, b1, stream), "ns_cast_multi")
+            wsb = int(lib.thorn_ns_workspace_bytes(nb, R, C))
+            ws = torch.empty(max(256, wsb), dtype=torch.uint8, device=dev)
+            N.check(lib.thorn_ns_batched(X.data_ptr(), U.data_ptr(), ws.data_ptr(), wsb, nb, R, C, ns_code, coeffs,
+                                         cfg.iters, restarts, len(rs), err.data_ptr(), stream), "ns_batched")
+            del X, ws
+            row_scale = mat_stats = None
+            if ci in pnn_h:
+                rsh, msh = pnn_h[ci]
+                row_scale, mat_stats = arena.get(rsh), arena.get(msh)
+                pt = N.PnnTensor(U.data_ptr(), row_scale.data_ptr(), mat_stats.data_ptr(), nb, R, C)
+                N.check(lib.thorn_pnn_stats_multi(N.array(N.PnnTensor, [pt]), 1, ns_code, N.dtype_code(pdt), stream),
+                        "pnn_stats_multi")
+            posts, off = [], 0
+            usz = U.element_size()
+            lr_eff = float(cfg.lr) * cfg.lr_scale(R, C)
+            for it in its:
+                posts.append(N.OrthoPostTensor(
+                    U.data_ptr() + off * R * C * usz, it.p.data_ptr(),
+                    None if row_scale is None else row_scale.data_ptr() + off * R * 4,
+                    None if mat_stats is None else mat_stats.data_ptr() + off * 2 * 4,
+                    arena.ptr(it.pnorm) if md else None, it.B, it.R, it.C, lr_eff))
+                off += it.B
+            N.check(lib.thorn_ortho_post_multi(N.array(N.OrthoPostTensor, posts), len(posts), ns_code,
+                                               N.dtype_code(pdt), float(cfg.weight_decay), stream), "ortho_post_multi")
+            del U
+        keep = None
+        if md:
+            self._md_prep(items, arena, new=True, stream=stream)
+            keep = self._md_finalize(items, arena, lambda it: True, stream)
+        self._finish(params, cfg)
+        del keep
+
+    # ------------------------------------------------------- (R)AdamW group
+    def _adam_local(self, params, cfg: GroupConfig):
+        """thorn.py:1659-1727 on the multi-tensor kernel."""
+        lib = N.load()
+        dev = _local(params[0]).device
+        stream = N.stream_of(dev)
+        md = cfg.decouple_md
+        arena = _Arena()
+        items = self._items(params, cfg, arena, ortho=False)
+        if md:
+            for it in items:
+                ax = cfg.norm_axis_(it.p)
+                if ax not in ((-2, -1), -1) or (ax == -1 and it.p.ndim > 1):
+                    raise NotImplementedError("decouple_md with a custom norm_axis is not implemented by thorn_b200")
+        arena.materialize(dev)
+        b1, b2 = cfg.betas
+        if md:
+            self._md_prep(items, arena, new=False, stream=stream)
+            by_dt: dict = {}
+            for it in items:
+                t = N.OrthoPreTensor(it.p.data_ptr(), it.g.data_ptr(), None, None, it.B, it.R, it.C,
+                                     arena.ptr(it.rs), arena.ptr(it.cs), 0 if it.split else 1,
+                                     arena.ptr(it.rgs), arena.ptr(it.cgs))
+                by_dt.setdefault((it.pdt, it.sdt), []).append(t)
+            for (pdt, sdt), ts in by_dt.items():
+                N.check(lib.thorn_ortho_pre_multi(N.array(N.OrthoPreTensor, ts), len(ts), N.dtype_code(pdt),
+                                                  N.dtype_code(sdt), N.dtype_code(pdt), float(b1), 1, 1, stream),
+                        "md recover_direction")
+        by_dt = {}
+        for it in items:
+            step = it.state["step"]
+            rect = cfg.rect(step)
+            bc1 = 1 / (1 - b1 ** step)
+            bc2 = 1 / (1 - b2 ** step)
+            t = N.AdamTensor(it.p.data_ptr() if it.apply else None, it.g.data_ptr(),
+                             _local(it.state["moment"]).data_ptr(), _local(it.state["variance"]).data_ptr(),
+                             it.p.numel(), float(cfg.lr) * rect, bc1, bc2, 1 if rect == 0.0 else 0)
+            by_dt.setdefault((it.pdt, it.sdt), []).append(t)
+        for (pdt, sdt), ts in by_dt.items():
+            N.check(lib.thorn_adamw_multi(N.array(N.AdamTensor, ts), len(ts), N.dtype_code(pdt), N.dtype_code(sdt),
+                                          float(b1), float(b2), float(cfg.weight_decay), float(cfg.eps), stream),
+                    "adamw_multi")
+        keep = None
+        if md:
+            self._md_gains(items, cfg, arena, stream)
+            app = [it for it in items if it.apply]
+            if app:
+                xs = (ctypes.c_void_p * len(app))(*[it.p.data_ptr() for it in app])
+                outs = (ctypes.c_void_p * len(app))(*[arena.ptr(it.pnorm) for it in app])
+                bs = (ctypes.c_int64 * len(app))(*[it.B for it in app])
+                per = (ctypes.c_int64 * len(app))(*[it.R * it.C for it in app])
+                for pdt in {it.pdt for it in app}:
+                    sel = [i for i, it in enumerate(app) if it.pdt == pdt]
+                    xs2 = (ctypes.c_void_p * len(sel))(*[xs[i] for i in sel])
+                    outs2 = (ctypes.c_void_p * len(sel))(*[outs[i] for i in sel])
+                    bs2 = (ctypes.c_int64 * len(sel))(*[bs[i] for i in sel])
+                    per2 = (ctypes.c_int64 * len(sel))(*[per[i] for i in sel])
+                    N.check(lib.thorn_sumsq_multi(xs2, outs2, bs2, per2, len(sel), N.dtype_code(pdt), stream),
+                            "sumsq_multi")
+            self._md_prep(items, arena, new=True, stream=stream)
+            keep = self._md_finalize(items, arena, lambda it: True, stream)
+        self._finish(params, cfg)
+        del keep
