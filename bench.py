@@ -1,0 +1,407 @@
+#!/usr/bin/env python
+"""THORN.step benchmark on the Llama-3-8B-shaped parameter set.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl thorn_b200|reference]
+
+For N > 1 launch one process per GPU with torch.distributed.run; parameters
+are then DTensors sharded Shard(0) over the ranks (FSDP2 layout) and the
+orthogonalized group takes the sharded path.
+
+Workload: 32 layers, hidden 4096; per layer q/o
+4096x4096, k/v 1024x4096, gate/up 14336x4096, down 4096x14336 in the
+orthogonalized group (decouple_md=True, lr=8e-3); embedding and lm_head
+128256x4096 plus 65 RMSNorm weights of 4096 in the (R)AdamW group.  bf16
+params ~N(0, 0.02), bf16 grads ~N(0, 1e-4), fp32 optimizer state.  Synthetic
+data; every input is far larger than L2, so no L2 flush is needed.
+
+One line of JSON on rank 0:
+* value / ms_per_step: device time of one full optimizer step (CUDA events,
+  max over ranks), inputs resident in HBM;
+* e2e: the same step through THORN.step with the grads copied in from pinned
+  host memory and the updated params copied back out, inside the timed region;
+* roofline: Newton-Schulz GEMM phase, dense-equivalent FLOPs / event time,
+  against the measured sustained bf16 peak;
+* cpu_baseline: the CPU oracle's step on a bounded sample (one q, k and gate
+  matrix, an embedding slice and a norm vector), extrapolated to the full set.
+``--impl reference`` times that CPU oracle alone (rank 0; other ranks exit).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+LAYERS, HIDDEN, KV, FFN, VOCAB = 32, 4096, 1024, 14336, 128256
+LAYER_SHAPES = [(HIDDEN, HIDDEN), (KV, HIDDEN), (KV, HIDDEN), (HIDDEN, HIDDEN), (FFN, HIDDEN), (FFN, HIDDEN),
+                (HIDDEN, FFN)]
+ORTHO_LR, ADAM_LR = 8e-3, 8e-3
+METRIC = "THORN.step ms, Llama-3-8B shapes"
+# DRAM bytes per launch of the NS GEMM kernel, from the ncu capture summarised
+# in profiles/ns_gemm_llama8b.md (None until a capture exists)
+NS_GEMM_TRAFFIC = None
+
+
+def shapes():
+    ortho = [s for _ in range(LAYERS) for s in LAYER_SHAPES]
+    adamw = [(VOCAB, HIDDEN), (VOCAB, HIDDEN)] + [(HIDDEN,)] * (2 * LAYERS + 1)
+    return ortho, adamw
+
+
+def dense_ns_flops(r, c, iters=5):
+    m, n = min(r, c), max(r, c)
+    if m == n:
+        return iters * (4 * m * m * n + 2 * m ** 3)
+    return 28 * m ** 3 + 8 * m * m * n
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return pk["hbm_gbs"], pk["bf16_tflops"], pk["bf16_tflops_sustained"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, ids):
+        self.ids = ids
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        if self.ids:
+            cmd += ["-i", ",".join(self.ids)]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------- CPU baseline
+def cpu_oracle_sample():
+    """Time the CPU oracle on a bounded sample and extrapolate to one full step (ms)."""
+    import numpy as np
+
+    from oracle.thorn_oracle import OracleTHORN
+
+    rng = np.random.default_rng(0)
+    ortho_lr, adam_lr = ORTHO_LR, ADAM_LR
+
+    def timed(group, shapes_):
+        params = [(rng.standard_normal(s, dtype=np.float32) * 0.02) for s in shapes_]
+        grads = [(rng.standard_normal(s, dtype=np.float32) * 1e-4) for s in shapes_]
+        g = dict(group)
+        g["params"] = params
+        orc = OracleTHORN([g])
+        for i in range(len(params)):  # state creation outside the timed region
+            orc._init_state(orc.groups[0], i)
+        t0 = time.perf_counter()
+        orc.step([grads])
+        return time.perf_counter() - t0
+
+    og = {"orthogonalize": True, "lr": ortho_lr, "decouple_md": True, "dtype": "bf16", "state_dtype": "f32"}
+    ag = {"orthogonalize": False, "lr": adam_lr, "dtype": "bf16", "state_dtype": "f32"}
+    t_sq = timed(og, [(HIDDEN, HIDDEN)])
+    t_kv = timed(og, [(KV, HIDDEN)])
+    t_ffn = timed(og, [(FFN, HIDDEN)])
+    emb_rows = 4096
+    t_emb = timed(ag, [(emb_rows, HIDDEN)])
+    t_norm = timed(ag, [(HIDDEN,)])
+    total = (LAYERS * (2 * t_sq + 2 * t_kv + 3 * t_ffn) + 2 * (VOCAB / emb_rows) * t_emb
+             + (2 * LAYERS + 1) * t_norm)
+    sample = (f"one {HIDDEN}x{HIDDEN}, one {KV}x{HIDDEN} and one {FFN}x{HIDDEN} orthogonalized matrix "
+              f"(decouple_md), a {emb_rows}x{HIDDEN} embedding slice and one norm vector; "
+              f"sum scaled to 32 layers + 2 x {VOCAB}-row embeddings + 65 norms (extrapolated)")
+    return total * 1e3, sample, (t_sq + t_kv + t_ffn + t_emb + t_norm)
+
+
+def reference_arm(args, rank):
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    vals = []
+    sample = ""
+    for i in range(args.warmup + args.steps):
+        v, sample, _ = cpu_oracle_sample()
+        if i >= args.warmup:
+            vals.append(v)
+    v = statistics.median(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "ms", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v, 3), "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "llama3-8b-fsdp2 (BASELINE configs[3])", "sample": "bounded, extrapolated"},
+            "cpu_baseline": {"value": round(v, 3), "unit": "ms", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": round(v, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------- GPU arm
+def build_params(torch, dev, rank, world, mesh):
+    """Llama-8B-shaped params (bf16 ~N(0, 0.02)) and grads (bf16 ~N(0, 1e-4)) on `dev`."""
+    ortho_s, adam_s = shapes()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+
+    def make(shape, std):
+        if world == 1:
+            t = torch.randn(shape, device=dev, dtype=torch.bfloat16, generator=gen) * std
+            return t
+        from torch.distributed.tensor import DTensor, Shard
+        local = (shape[0] // world,) + tuple(shape[1:])
+        t = torch.randn(local, device=dev, dtype=torch.bfloat16, generator=gen) * std
+        return DTensor.from_local(t, mesh, [Shard(0)], run_check=False, shape=shape,
+                                  stride=torch.empty(shape, device="meta").stride())
+
+    ortho = [torch.nn.Parameter(make(s, 0.02)) for s in ortho_s]
+    adamw = [torch.nn.Parameter(make(s, 0.02)) for s in adam_s]
+    g_ortho = [make(s, 1e-4) for s in ortho_s]
+    g_adam = [make(s, 1e-4) for s in adam_s]
+    return ortho, adamw, g_ortho, g_adam
+
+
+def gpu_arm(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from thorn_b200 import THORN, _native
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    mesh = None
+    if world > 1:
+        from torch.distributed.device_mesh import init_device_mesh
+        mesh = init_device_mesh("cuda", (world,))
+    ortho, adamw, g_ortho, g_adam = build_params(torch, dev, rank, world, mesh)
+    params = ortho + adamw
+    grads = g_ortho + g_adam
+    opt = THORN([
+        {"orthogonalize": True, "params": ortho, "lr": ORTHO_LR, "decouple_md": True, "state_dtype": torch.float32},
+        {"orthogonalize": False, "params": adamw, "lr": ADAM_LR, "state_dtype": torch.float32},
+    ])
+
+    def local(t):
+        return t.to_local() if hasattr(t, "to_local") else t
+
+    def feed():
+        for p, g in zip(params, grads):
+            p.grad = g
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        feed()
+        opt.step()
+    torch.cuda.synchronize()
+
+    # ---------------- device-timed steps (inputs resident in HBM)
+    clocks = None
+    sampler = None
+    if rank == 0:
+        ids = []
+        try:
+            for i in range(torch.cuda.device_count()):
+                u = getattr(torch.cuda.get_device_properties(i), "uuid", None)
+                if u is not None:
+                    ids.append("GPU-" + str(u) if not str(u).startswith("GPU-") else str(u))
+        except Exception:
+            ids = []
+        sampler = ClockSampler(ids if len(ids) == world else [])
+        sampler.start()
+        time.sleep(0.3)
+    opt.profile_ns = []
+    launches0 = _native.launch_count()
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        feed()
+        opt.step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    launches = _native.launch_count() - launches0
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    prof = opt.profile_ns
+    opt.profile_ns = None
+    ns_ms = sum(a.elapsed_time(b) for a, b, *_ in prof) / args.steps
+    ns_dense = sum(d for _, _, d, _, _ in prof) / args.steps
+    ns_exec = sum(x for _, _, _, x, _ in prof) / args.steps
+    ns_launch_ms = max_over_ranks(ns_ms)
+    # whole-job NS throughput: FLOPs of all ranks / the slowest rank's NS time
+    if world > 1:
+        t = torch.tensor([ns_dense, ns_exec], device=dev, dtype=torch.float64)
+        dist.all_reduce(t)
+        ns_dense_all, ns_exec_all = float(t[0]), float(t[1])
+    else:
+        ns_dense_all, ns_exec_all = ns_dense, ns_exec
+    if sampler is not None:
+        time.sleep(0.2)
+        clocks = sampler.stop()
+
+    # ---------------- end to end: grads in from pinned host memory, params back out
+    e2e = None
+    if not args.no_e2e:
+        h_grads = [torch.empty(local(g).shape, dtype=local(g).dtype, pin_memory=True) for g in grads]
+        for h, g in zip(h_grads, grads):
+            h.copy_(local(g))
+        h_params = [torch.empty(local(p).shape, dtype=local(p).dtype, pin_memory=True) for p in params]
+        bi = sum(h.numel() * h.element_size() for h in h_grads)
+        bo = sum(h.numel() * h.element_size() for h in h_params)
+        d_grads = [torch.empty_like(g) for g in grads]
+
+        def e2e_step():
+            for dg, h in zip(d_grads, h_grads):
+                local(dg).copy_(h, non_blocking=True)
+            for p, dg in zip(params, d_grads):
+                p.grad = dg
+            opt.step()
+            for h, p in zip(h_params, params):
+                h.copy_(local(p).detach(), non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        t1.record()
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
+        if world > 1:
+            t = torch.tensor([bi, bo], device=dev, dtype=torch.float64)
+            dist.all_reduce(t)
+            bi, bo = int(t[0]), int(t[1])
+        e2e = {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo}
+        del h_grads, h_params, d_grads
+
+    if rank != 0:
+        return
+    hbm, peak_burst, peak_sus, peak_src = load_peaks()
+    achieved = ns_dense_all / (ns_launch_ms * 1e-3) / 1e12 if ns_launch_ms > 0 else None
+    achieved_exec = ns_exec_all / (ns_launch_ms * 1e-3) / 1e12 if ns_launch_ms > 0 else None
+    cpu = None
+    if not args.no_cpu_baseline and world == 1:
+        v, sample, secs = cpu_oracle_sample()
+        cpu = {"value": round(v, 3), "unit": "ms", "cores": os.cpu_count() or 1, "kind": "port", "sample": sample,
+               "sample_cpu_seconds": round(secs, 2)}
+    ortho_s, adam_s = shapes()
+    line = {
+        "metric": METRIC, "value": round(ms, 3), "unit": "ms", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "llama3-8b-fsdp2 (BASELINE configs[3])" + (" sharded Shard(0)" if world > 1 else ""),
+                   "ortho_matrices": len(ortho_s), "adamw_tensors": len(adam_s),
+                   "params": sum(math.prod(s) for s in ortho_s + adam_s), "param_dtype": "bf16",
+                   "state_dtype": "f32", "ns_dtype": "f16", "decouple_md": True, "lr": ORTHO_LR,
+                   "parallelism": f"fsdp{world}" if world > 1 else "single",
+                   "l2": "no flush: every step reads params, grads and state (~70 GB) >> 126 MB L2"},
+        "roofline": {"bound": "tensor", "kernel": "ns_gemm_kernel (Newton-Schulz phase)",
+                     "achieved": round(achieved, 1) if achieved else None, "peak": peak_sus, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak_sus, 3) if achieved else None, "traffic": NS_GEMM_TRAFFIC,
+                     "flops": "dense-equivalent (2MNK per reference GEMM)",
+                     "achieved_executed": round(achieved_exec, 1) if achieved_exec else None,
+                     "peak_source": f"{peak_src} sustained bf16 (MEASURED_PEAKS.json); burst {peak_burst}",
+                     "ns_ms_per_step": round(ns_launch_ms, 3),
+                     "ns_dense_tflop_per_step": round(ns_dense_all / 1e12, 2)},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": int(launches),
+        "gpu_launches_per_step": round(launches / args.steps, 1),
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="thorn_b200", choices=["thorn_b200", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank)
+        return
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be at least 3")
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        gpu_arm(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -79,36 +79,48 @@ THORN_API int thorn_adamw_multi(const thorn_adam_tensor* tensors, int n, int p_d
                       float beta1, float beta2, float weight_decay, float eps, void* stream);
 
 /* --------------------------------------------------------------------------
+ * Deterministic reductions.  Kernels that reduce (sums of squares, gain
+ * gradients, per-neuron-norm statistics) never accumulate floats with
+ * atomics: each block writes its partial sum to a caller-provided scratch
+ * buffer, and the last block of each segment (found with an integer counter)
+ * adds the partials in a fixed order.  Results are therefore bitwise
+ * reproducible run to run.  A scratch buffer must be zero when first used;
+ * every call leaves its counters at zero again, so the same buffer can be
+ * reused without clearing (partials are always overwritten).
+ * ------------------------------------------------------------------------ */
+
+/* --------------------------------------------------------------------------
  * Orthogonalized group, before Newton-Schulz: momentum + Nesterov, and the
- * per-matrix sum of squares needed to normalise the NS input.  With m == NULL
- * only the md part runs (no momentum, normsq unused): the direction recovery
- * of the (R)AdamW group with decouple_md (thorn.py:1704-1705).
+ * per-matrix sum of squares needed to normalise the NS input.
  * Replaces _update_momentum (thorn.py:1376-1381):  m <- beta1 m + g;
  * u = g + beta1 m (rounded to u_dtype; u itself is not stored -- the NS
  * input pass recomputes it from g and the new m).  With md != 0 it also does
  * _recover_direction (thorn.py:890-908): gain = row_sp col_sp (or the scalar
- * gain); p <- p / gain; g <- g gain (stored back when write_grad != 0) and
- * accumulates the gain-gradient sums of _update_magnitude (thorn.py:910-932):
- *   row_gsum[i] += sum_j round(round(p_dir g_raw) col_sp[j])
- *   col_gsum[j] += sum_i round(round(p_dir g_raw) row_sp[i])
- * (or row_gsum[0] += sum of round(p_dir g_raw) for a scalar gain).
- * Accumulators (normsq, *_gsum) must be zeroed by the caller.
+ * gain); p <- p / gain; g <- g gain (stored back when write_grad != 0), and
+ * the gain-gradient sums of _update_magnitude (thorn.py:910-932):
+ *   row_gsum[i] = sum_j round(round(p_dir g_raw) col_sp[j])
+ *   col_gsum[j] = sum_i round(round(p_dir g_raw) row_sp[i])
+ * (or row_gsum[0] = sum of round(p_dir g_raw) for a scalar gain).  With
+ * m == NULL only the md part runs (no momentum, normsq unused): the direction
+ * recovery of the (R)AdamW group with decouple_md (thorn.py:1704-1705).
  * ------------------------------------------------------------------------ */
 typedef struct {
   void* p;
   void* g;
   void* m;
-  float* normsq;      /* out (+=): per sub-matrix sum of u^2, [batch] */
+  float* normsq;        /* out: per sub-matrix sum of u^2, [batch] */
   int64_t batch, rows, cols;
   const float* row_sp;  /* md: softplus(row_gain) rounded to p dtype, [batch*rows] (scalar gain: [1]) */
   const float* col_sp;  /* md: softplus(col_gain) rounded to p dtype, [batch*cols] (scalar gain: unused) */
   int32_t scalar_gain;  /* md: nonzero when the gain is one scalar, row_sp[0] */
-  float* row_gsum;      /* md out (+=): [batch*rows] (scalar gain: [1]) */
-  float* col_gsum;      /* md out (+=): [batch*cols] (unused for a scalar gain) */
+  float* row_gsum;      /* md out: [batch*rows] (scalar gain: [1]) */
+  float* col_gsum;      /* md out: [batch*cols] (unused for a scalar gain) */
+  void* scratch;        /* thorn_ortho_pre_scratch_bytes(batch, rows, cols, md) bytes (see above) */
 } thorn_ortho_pre_tensor;
 
+THORN_API int64_t thorn_ortho_pre_scratch_bytes(int64_t batch, int64_t rows, int64_t cols, int md);
 THORN_API int thorn_ortho_pre_multi(const thorn_ortho_pre_tensor* tensors, int n, int p_dtype, int s_dtype,
-                          int u_dtype, float beta1, int md, int write_grad, void* stream);
+                                    int u_dtype, float beta1, int md, int write_grad, void* stream);
 
 /* --------------------------------------------------------------------------
  * Newton-Schulz input: X = ns(u / (||u||_F + 1e-8)), transposed to the wide
@@ -167,18 +179,21 @@ THORN_API int thorn_sym_addmm(const void* A, const void* B, const void* C, void*
  * Replaces _pnn_row_stats_kernel (thorn.py:205-228) and _pnn_reduce_kernel
  * (thorn.py:230-253) of _per_neuron_norm_update (thorn.py:709-757):
  *   sumsq_r = sum_j u_rj^2;  s_r = rsqrt(max(sumsq_r / N, eps))
- *   stats[b] += {sumsq_r, s_r^2 sumsq_r}  (gscale = sqrt(.0) / max(sqrt(.1), eps))
+ *   stats[b] = {sum_r sumsq_r, sum_r s_r^2 sumsq_r}
+ *   (gscale_b = sqrt(stats[b][0]) / max(sqrt(stats[b][1]), eps))
  * u is the NS output rounded to p_dtype; eps = finfo(p_dtype).eps.
- * mat_stats must be zeroed by the caller.
  * ------------------------------------------------------------------------ */
 typedef struct {
-  const void* U;        /* ns_dtype [batch, rows, cols] */
+  const void* U;        /* u_dtype [batch, rows, cols] */
   float* row_scale;     /* out: s_r, [batch*rows] */
-  float* mat_stats;     /* out (+=): [batch][2] */
+  float* mat_stats;     /* out: [batch][2] */
   int64_t batch, rows, cols;
+  void* scratch;        /* thorn_pnn_scratch_bytes(batch, rows) bytes */
 } thorn_pnn_tensor;
 
-THORN_API int thorn_pnn_stats_multi(const thorn_pnn_tensor* tensors, int n, int u_dtype, int p_dtype, void* stream);
+THORN_API int64_t thorn_pnn_scratch_bytes(int64_t batch, int64_t rows);
+THORN_API int thorn_pnn_stats_multi(const thorn_pnn_tensor* tensors, int n, int u_dtype, int p_dtype,
+                                    void* stream);
 
 /* --------------------------------------------------------------------------
  * Orthogonalized group, after Newton-Schulz: scale and apply.
@@ -187,21 +202,22 @@ THORN_API int thorn_pnn_stats_multi(const thorn_pnn_tensor* tensors, int n, int 
  * _pnn_apply_kernel (thorn.py:255-280):
  *   u = round_p(U) * s_r * gscale_b   (pnn; or * row_scale[r] when mat_stats is NULL)
  *   u <- u + wd p where u p >= 0;  p <- p - lr u
- * With p_normsq != NULL also accumulates ||p_new||^2 per sub-matrix (for
- * the decouple_md renorm).  U may be ns_dtype (bf16/f16) or f32.
+ * With p_normsq != NULL it also writes ||p_new||^2 per sub-matrix (for the
+ * decouple_md renorm; needs scratch).  U may be ns_dtype (bf16/f16) or f32.
  * ------------------------------------------------------------------------ */
 typedef struct {
   const void* U;
   void* p;
   const float* row_scale;  /* NULL: no row scaling */
   const float* mat_stats;  /* NULL: row_scale is the final factor */
-  float* p_normsq;         /* NULL or out (+=) [batch] */
+  float* p_normsq;         /* NULL or out [batch] */
   int64_t batch, rows, cols;
   float lr;                /* lr * lr_scale (thorn.py:768-780) * magma scale */
+  void* scratch;           /* with p_normsq: thorn_sumsq_scratch_bytes(batch, rows, cols) bytes */
 } thorn_ortho_post_tensor;
 
 THORN_API int thorn_ortho_post_multi(const thorn_ortho_post_tensor* tensors, int n, int u_dtype, int p_dtype,
-                           float weight_decay, void* stream);
+                                     float weight_decay, void* stream);
 
 /* --------------------------------------------------------------------------
  * Magnitude-direction decoupling helpers (thorn.py:910-977, 1414-1421).
@@ -228,10 +244,17 @@ typedef struct {
 
 THORN_API int thorn_md_finalize_multi(const thorn_md_final_tensor* tensors, int n, int p_dtype, void* stream);
 
-/* Sum of squares per sub-matrix (for renorm on paths that do not run
- * thorn_ortho_post_multi): out[b] += sum x^2 over batch b.  out zeroed by caller. */
-THORN_API int thorn_sumsq_multi(const void* const* x, float* const* out, const int64_t* batch,
-                      const int64_t* per_batch, int n, int dtype, void* stream);
+/* Sum of squares per sub-matrix: out[b] = sum of x^2 over sub-matrix b (the
+ * renorm of the (R)AdamW group with decouple_md, thorn.py:1716-1717). */
+typedef struct {
+  const void* x;
+  float* out;            /* [batch] */
+  int64_t batch, rows, cols;
+  void* scratch;         /* thorn_sumsq_scratch_bytes(batch, rows, cols) bytes */
+} thorn_sumsq_tensor;
+
+THORN_API int64_t thorn_sumsq_scratch_bytes(int64_t batch, int64_t rows, int64_t cols);
+THORN_API int thorn_sumsq_multi(const thorn_sumsq_tensor* tensors, int n, int dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -37,11 +37,44 @@ EPS = {"f32": float(np.finfo(np.float32).eps), "bf16": 0.0078125, "f16": float(n
 
 
 def to_bf16(x) -> np.ndarray:
-    """Round float32 values to bfloat16 (round-to-nearest-even); returns float32."""
+    """Round float32 values to bfloat16 (round-to-nearest-even); returns float32.
+
+    uint32 arithmetic: only NaN bit patterns can wrap, and those are restored.
+    """
     x = np.ascontiguousarray(np.asarray(x, dtype=F32))
-    b = x.view(np.uint32).astype(np.uint64)
-    r = ((b + 0x7FFF + ((b >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
-    out = r.view(F32).copy()
+    b = x.view(np.uint32)
+    r = (b >> 16) & np.uint32(1)
+    r += np.uint32(0x7FFF)
+    r += b
+    r &= np.uint32(0xFFFF0000)
+    out = r.view(F32)
+    nan = np.isnan(x)
+    if nan.any():
+        out[nan] = np.nan
+    return out
+
+
+def to_f16(x) -> np.ndarray:
+    """Round float32 values to float16 (round-to-nearest-even); returns float32.
+
+    Same result as ``x.astype(float16).astype(float32)`` without numpy's slow
+    per-element path for fp16 subnormals: the 10-bit mantissa rounding is done
+    on the float32 bits, subnormals are rounded to multiples of 2**-24 and
+    overflow goes to +-inf.
+    """
+    x = np.ascontiguousarray(np.asarray(x, dtype=F32))
+    b = x.view(np.uint32)
+    r = (b >> 13) & np.uint32(1)
+    r += np.uint32(0xFFF)
+    r += b
+    r &= np.uint32(0xFFFFE000)
+    out = r.view(F32)
+    sub = np.rint(x * F32(2.0 ** 24))
+    sub *= F32(2.0 ** -24)
+    out = np.where(np.abs(x) < F32(2.0 ** -14), sub, out)
+    big = np.abs(out) >= F32(65520.0)
+    if big.any():
+        out[big] = np.copysign(np.inf, x[big]).astype(F32)
     nan = np.isnan(x)
     if nan.any():
         out[nan] = np.nan
@@ -54,7 +87,7 @@ def rnd(x, dt: str) -> np.ndarray:
     if dt == "f32":
         return x
     if dt == "f16":
-        return x.astype(np.float16).astype(F32)
+        return to_f16(x)
     if dt == "bf16":
         return to_bf16(x)
     raise ValueError(dt)
@@ -179,11 +212,11 @@ NS_DTYPE = "f16"
 
 def _mm16(a, b, c=None, alpha=1.0, beta=1.0):
     """16-bit GEMM with fp32 accumulation, one rounding: out = alpha*a@b + beta*c."""
-    acc = np.matmul(a, b, dtype=F32)
+    acc = np.matmul(a, b)
     if alpha != 1.0:
-        acc = acc * F32(alpha)
+        acc *= F32(alpha)
     if c is not None:
-        acc = acc + F32(beta) * c
+        acc += F32(beta) * c
     return rnd(acc, NS_DTYPE)
 
 

@@ -49,12 +49,13 @@ def test_library_exports_every_declared_symbol(lib):
 STRUCTS = {
     "thorn_adam_tensor": (N.AdamTensor, ["p", "g", "m", "v", "numel", "lr", "bc1", "bc2", "degenerate"]),
     "thorn_ortho_pre_tensor": (N.OrthoPreTensor, ["p", "g", "m", "normsq", "batch", "rows", "cols", "row_sp",
-                                                  "col_sp", "scalar_gain", "row_gsum", "col_gsum"]),
+                                                  "col_sp", "scalar_gain", "row_gsum", "col_gsum", "scratch"]),
     "thorn_ns_cast_tensor": (N.NsCastTensor, ["g", "m", "normsq", "x", "batch", "rows", "cols", "row_sp", "col_sp",
                                               "scalar_gain", "md"]),
-    "thorn_pnn_tensor": (N.PnnTensor, ["U", "row_scale", "mat_stats", "batch", "rows", "cols"]),
+    "thorn_pnn_tensor": (N.PnnTensor, ["U", "row_scale", "mat_stats", "batch", "rows", "cols", "scratch"]),
     "thorn_ortho_post_tensor": (N.OrthoPostTensor, ["U", "p", "row_scale", "mat_stats", "p_normsq", "batch",
-                                                    "rows", "cols", "lr"]),
+                                                    "rows", "cols", "lr", "scratch"]),
+    "thorn_sumsq_tensor": (N.SumsqTensor, ["x", "out", "batch", "rows", "cols", "scratch"]),
     "thorn_md_final_tensor": (N.MdFinalTensor, ["p", "normsq", "target", "target_stride", "row_sp", "col_sp",
                                                 "scalar_gain", "batch", "rows", "cols"]),
 }
@@ -93,6 +94,11 @@ def test_host_only_entry_points(lib):
     assert lib.thorn_ns_workspace_bytes(3, 512, 512) == 4 * 3 * 512 * 512 * 2
     assert lib.thorn_ns_workspace_bytes(2, 96, 32) == lib.thorn_ns_workspace_bytes(2, 32, 96)
     assert lib.thorn_ns_workspace_bytes(0, 8, 8) == 0
+    # scratch: counters + one partial per 64x256 tile (+ md row/col partials)
+    assert lib.thorn_sumsq_scratch_bytes(1, 64, 256) == (4 + 1) * 4
+    assert lib.thorn_ortho_pre_scratch_bytes(2, 128, 512, 0) > 0
+    assert lib.thorn_ortho_pre_scratch_bytes(2, 128, 512, 1) > lib.thorn_ortho_pre_scratch_bytes(2, 128, 512, 0)
+    assert lib.thorn_pnn_scratch_bytes(3, 100) == (4 + 2 * 300) * 4
 
 
 def test_argument_validation_without_gpu(lib):
@@ -110,6 +116,7 @@ def test_argument_validation_without_gpu(lib):
     assert lib.thorn_ns_batched(1024, 2048, 4096, 1 << 30, 1, 8, 8, 0, co, 1, rs, 0, None, None) == 1  # f32 NS
     # symmetric GEMM needs 8-element leading dimensions
     assert lib.thorn_sym_addmm(16, 16, None, 16, 1, 12, 16, 0, 1.0, 0.0, 2, None, None) == 2
-    pre = N.array(N.OrthoPreTensor, [N.OrthoPreTensor(None, None, None, None, 1, 4, 4, None, None, 0, None, None)])
+    pre = N.array(N.OrthoPreTensor, [N.OrthoPreTensor(None, None, None, None, 1, 4, 4, None, None, 0, None, None,
+                                                       None)])
     assert lib.thorn_ortho_pre_multi(pre, 1, 0, 0, 0, 0.9, 0, 0, None) == 1
     assert lib.thorn_md_prep(None, 4, None, None, 0, None) == 1

@@ -29,7 +29,7 @@ class OrthoPreTensor(Structure):
     _fields_ = [("p", c_void_p), ("g", c_void_p), ("m", c_void_p), ("normsq", c_void_p),
                 ("batch", c_int64), ("rows", c_int64), ("cols", c_int64),
                 ("row_sp", c_void_p), ("col_sp", c_void_p), ("scalar_gain", c_int32),
-                ("row_gsum", c_void_p), ("col_gsum", c_void_p)]
+                ("row_gsum", c_void_p), ("col_gsum", c_void_p), ("scratch", c_void_p)]
 
 
 class NsCastTensor(Structure):
@@ -40,12 +40,18 @@ class NsCastTensor(Structure):
 
 class PnnTensor(Structure):
     _fields_ = [("U", c_void_p), ("row_scale", c_void_p), ("mat_stats", c_void_p),
-                ("batch", c_int64), ("rows", c_int64), ("cols", c_int64)]
+                ("batch", c_int64), ("rows", c_int64), ("cols", c_int64), ("scratch", c_void_p)]
 
 
 class OrthoPostTensor(Structure):
     _fields_ = [("U", c_void_p), ("p", c_void_p), ("row_scale", c_void_p), ("mat_stats", c_void_p),
-                ("p_normsq", c_void_p), ("batch", c_int64), ("rows", c_int64), ("cols", c_int64), ("lr", c_float)]
+                ("p_normsq", c_void_p), ("batch", c_int64), ("rows", c_int64), ("cols", c_int64), ("lr", c_float),
+                ("scratch", c_void_p)]
+
+
+class SumsqTensor(Structure):
+    _fields_ = [("x", c_void_p), ("out", c_void_p), ("batch", c_int64), ("rows", c_int64), ("cols", c_int64),
+                ("scratch", c_void_p)]
 
 
 class MdFinalTensor(Structure):
@@ -63,6 +69,7 @@ _PROTOS = {
     "thorn_gemm_flops": (None, [POINTER(c_double), POINTER(c_double)]),
     "thorn_adamw_multi": (c_int, [POINTER(AdamTensor), c_int, c_int, c_int, c_float, c_float, c_float, c_float,
                                   c_void_p]),
+    "thorn_ortho_pre_scratch_bytes": (c_int64, [c_int64, c_int64, c_int64, c_int]),
     "thorn_ortho_pre_multi": (c_int, [POINTER(OrthoPreTensor), c_int, c_int, c_int, c_int, c_float, c_int, c_int,
                                       c_void_p]),
     "thorn_ns_ld": (c_int64, [c_int64]),
@@ -72,13 +79,14 @@ _PROTOS = {
                                  POINTER(c_double), c_int, POINTER(c_int32), c_int, c_void_p, c_void_p]),
     "thorn_sym_addmm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_float,
                                 c_float, c_int, c_void_p, c_void_p]),
+    "thorn_pnn_scratch_bytes": (c_int64, [c_int64, c_int64]),
     "thorn_pnn_stats_multi": (c_int, [POINTER(PnnTensor), c_int, c_int, c_int, c_void_p]),
     "thorn_ortho_post_multi": (c_int, [POINTER(OrthoPostTensor), c_int, c_int, c_int, c_float, c_void_p]),
     "thorn_md_prep": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p]),
     "thorn_md_gain_grad": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p]),
     "thorn_md_finalize_multi": (c_int, [POINTER(MdFinalTensor), c_int, c_int, c_void_p]),
-    "thorn_sumsq_multi": (c_int, [POINTER(c_void_p), POINTER(c_void_p), POINTER(c_int64), POINTER(c_int64), c_int,
-                                  c_int, c_void_p]),
+    "thorn_sumsq_scratch_bytes": (c_int64, [c_int64, c_int64, c_int64]),
+    "thorn_sumsq_multi": (c_int, [POINTER(SumsqTensor), c_int, c_int, c_void_p]),
 }
 
 _lock = threading.Lock()

@@ -165,6 +165,89 @@ __global__ void __launch_bounds__(kThreads) adam_kernel(const __grid_constant__ 
 }
 
 // ===========================================================================
+// deterministic segment reductions
+// ===========================================================================
+// True (in every thread) for the block that arrives last on `cnt` out of
+// `total` blocks.  Partials written before the call by any thread of any
+// block are visible to the last block afterwards.  The last block resets the
+// counter, so scratch buffers stay reusable.
+__device__ __forceinline__ bool last_block(unsigned* cnt, unsigned total) {
+  __shared__ int is_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned old = atomicAdd(cnt, 1u);
+    is_last = (old == total - 1) ? 1 : 0;
+    if (is_last) *cnt = 0u;
+  }
+  __syncthreads();
+  const bool last = is_last != 0;
+  if (last) __threadfence();
+  return last;
+}
+
+// Fixed-order block sum of n partials (strided per thread, then a fixed tree).
+__device__ __forceinline__ float ordered_sum(const float* x, int64_t n, float* red) {
+  float s = 0.f;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s += __ldcg(x + i);
+  return block_sum(s, red);
+}
+
+static inline int64_t al16(int64_t b) { return (b + 15) / 16 * 16; }
+
+// Scratch of the momentum pass: counters first, then partial sums.
+struct PreLayout {
+  int64_t tr, tc, T;
+  int64_t cnt_norm, cnt_all, cnt_row, cnt_col;  // uint32 offsets
+  int64_t pn, ps, pr, pc;                        // float offsets
+  int64_t bytes;
+};
+__host__ __device__ inline PreLayout pre_layout(int64_t B, int64_t R, int64_t C, bool md) {
+  PreLayout L;
+  L.tr = (R + kTR - 1) / kTR;
+  L.tc = (C + kTC - 1) / kTC;
+  L.T = B * L.tr * L.tc;
+  L.cnt_norm = 0;
+  L.cnt_all = B;
+  L.cnt_row = B + 1;
+  L.cnt_col = L.cnt_row + (md ? B * L.tr : 0);
+  const int64_t ncnt = L.cnt_col + (md ? B * L.tc : 0);
+  const int64_t f0 = (ncnt + 3) / 4 * 4;  // float offset after counters (16-byte aligned)
+  L.pn = f0;
+  L.ps = L.pn + (L.T + 3) / 4 * 4;
+  L.pr = L.ps + (md ? (L.T + 3) / 4 * 4 : 0);
+  L.pc = L.pr + (md ? (B * R * L.tc + 3) / 4 * 4 : 0);
+  const int64_t nf = L.pc + (md ? B * L.tr * C : 0);
+  L.bytes = nf * 4;
+  return L;
+}
+
+// Scratch of a per-sub-matrix sum over 2-D tiles (post / sumsq).
+__host__ __device__ inline int64_t tiles_per_mat(int64_t R, int64_t C) {
+  return ((R + kTR - 1) / kTR) * ((C + kTC - 1) / kTC);
+}
+__host__ __device__ inline int64_t sq_pf(int64_t B) { return (B + 3) / 4 * 4; }  // float offset of partials
+__host__ __device__ inline int64_t sq_bytes(int64_t B, int64_t R, int64_t C) {
+  return (sq_pf(B) + B * tiles_per_mat(R, C)) * 4;
+}
+
+// Partials of one value per 2-D tile, then the last tile block of each
+// sub-matrix writes the fixed-order sum (used by post and sumsq).
+__device__ __forceinline__ void tile_sum_to(float* out, void* scratch, const Tile& t, int64_t B, int64_t R,
+                                            int64_t C, float v, float* red) {
+  unsigned* cnt = (unsigned*)scratch;
+  float* part = (float*)scratch + sq_pf(B);
+  const int64_t tpm = tiles_per_mat(R, C);
+  const int64_t lt = (t.r0 / kTR) * ((C + kTC - 1) / kTC) + t.c0 / kTC;
+  const float tot = block_sum(v, red);
+  if (threadIdx.x == 0) part[t.b * tpm + lt] = tot;
+  if (last_block(cnt + t.b, (unsigned)tpm)) {
+    const float s = ordered_sum(part + t.b * tpm, tpm, red);
+    if (threadIdx.x == 0) out[t.b] = s;
+  }
+}
+
+// ===========================================================================
 // momentum + Nesterov (+ MD direction recovery)  (thorn.py:1376-1381, 890-908)
 // ===========================================================================
 // u = g + beta1 * m, evaluated identically by the momentum pass (for the norm)
@@ -186,17 +269,22 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
   const int ti = find_tensor(a.pk, blockIdx.x);
   const thorn_ortho_pre_tensor& e = a.pk.t[ti];
   const bool vec = a.pk.vec[ti];
-  const Tile t = tile_of(int64_t(blockIdx.x) - a.pk.start[ti], e.rows, e.cols);
+  const int64_t local = int64_t(blockIdx.x) - a.pk.start[ti];
+  const Tile t = tile_of(local, e.rows, e.cols);
+  const PreLayout L = pre_layout(e.batch, e.rows, e.cols, MD);
+  const int64_t rt = t.r0 / kTR, ct = t.c0 / kTC;
+  unsigned* cnt = (unsigned*)e.scratch;
+  float* sf = (float*)e.scratch;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t c = t.c0 + lane * 8;
   const int nc = (int)max64(0, min64(8, e.cols - c));
   const float b1 = a.beta1;
+  const bool scalar_gain = MD && e.scalar_gain;
+  const bool momentum = e.m != nullptr;
   float sq = 0.f;
   float csum[8];
 #pragma unroll
   for (int k = 0; k < 8; ++k) csum[k] = 0.f;
-  const bool scalar_gain = MD && e.scalar_gain;
-  const bool momentum = e.m != nullptr;
   float csp[8];
   if (MD && !scalar_gain) {
 #pragma unroll
@@ -220,9 +308,9 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           if (k >= nc) continue;
-          float gain = scalar_gain ? rsp : rnd<P>(rsp * csp[k]);
-          float pd = rnd<P>(pv[k] / gain);
-          float pg = rnd<P>(pd * gv[k]);
+          const float gain = scalar_gain ? rsp : rnd<P>(rsp * csp[k]);
+          const float pd = rnd<P>(pv[k] / gain);
+          const float pg = rnd<P>(pd * gv[k]);
           if (scalar_gain) {
             part += pg;
           } else {
@@ -250,18 +338,18 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
     if (MD) {
       rs = warp_sum(rs);
       if (scalar_gain) rsum_scalar += rs;
-      else if (lane == 0) atomicAdd(e.row_gsum + t.b * e.rows + r, rs);
+      else if (lane == 0) sf[L.pr + (t.b * e.rows + r) * L.tc + ct] = rs;
     }
   }
+  const int64_t gt = (t.b * L.tr + rt) * L.tc + ct;  // tile index within the tensor
   if (momentum) {
-    float tot = block_sum(sq, red);
-    if (threadIdx.x == 0 && tot != 0.f) atomicAdd(e.normsq + t.b, tot);
+    const float tot = block_sum(sq, red);
+    if (threadIdx.x == 0) sf[L.pn + gt] = tot;
   }
   if (MD) {
     if (scalar_gain) {
-      __syncthreads();
-      float s2 = block_sum(lane == 0 ? rsum_scalar : 0.f, red);
-      if (threadIdx.x == 0) atomicAdd(e.row_gsum, s2);
+      const float s2 = block_sum(lane == 0 ? rsum_scalar : 0.f, red);
+      if (threadIdx.x == 0) sf[L.ps + gt] = s2;
     } else {
 #pragma unroll
       for (int k = 0; k < 8; ++k) colacc[warp][lane * 8 + k] = csum[k];
@@ -271,7 +359,38 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
         float s = 0.f;
 #pragma unroll
         for (int w = 0; w < 8; ++w) s += colacc[w][cc];
-        atomicAdd(e.col_gsum + t.b * e.cols + t.c0 + cc, s);
+        sf[L.pc + (t.b * L.tr + rt) * e.cols + t.c0 + cc] = s;
+      }
+    }
+  }
+  // -------- last blocks reduce their segment in a fixed order --------
+  if (momentum && last_block(cnt + L.cnt_norm + t.b, (unsigned)(L.tr * L.tc))) {
+    const float s = ordered_sum(sf + L.pn + t.b * L.tr * L.tc, L.tr * L.tc, red);
+    if (threadIdx.x == 0) e.normsq[t.b] = s;
+  }
+  if (MD && scalar_gain) {
+    if (last_block(cnt + L.cnt_all, (unsigned)L.T)) {
+      const float s = ordered_sum(sf + L.ps, L.T, red);
+      if (threadIdx.x == 0) e.row_gsum[0] = s;
+    }
+  } else if (MD) {
+    if (last_block(cnt + L.cnt_row + t.b * L.tr + rt, (unsigned)L.tc)) {
+      for (int rr = warp; rr < kTR; rr += 8) {
+        const int64_t r = t.r0 + rr;
+        if (r >= e.rows) break;
+        const float* src = sf + L.pr + (t.b * e.rows + r) * L.tc;
+        float s = 0.f;
+        for (int64_t k = lane; k < L.tc; k += 32) s += __ldcg(src + k);
+        s = warp_sum(s);
+        if (lane == 0) e.row_gsum[t.b * e.rows + r] = s;
+      }
+    }
+    if (last_block(cnt + L.cnt_col + t.b * L.tc + ct, (unsigned)L.tr)) {
+      const int64_t cc = t.c0 + threadIdx.x;
+      if (cc < e.cols) {
+        float s = 0.f;
+        for (int64_t k = 0; k < L.tr; ++k) s += __ldcg(sf + L.pc + (t.b * L.tr + k) * e.cols + cc);
+        e.col_gsum[t.b * e.cols + cc] = s;
       }
     }
   }
@@ -362,35 +481,51 @@ struct PnnArgs {
   float eps;
 };
 constexpr int kPnnRowsPerBlock = 8;
+__host__ __device__ inline int64_t pnn_pf(int64_t B) { return (B + 3) / 4 * 4; }
 
 template <class U, class P>
 __global__ void __launch_bounds__(kThreads) pnn_stats_kernel(const __grid_constant__ PnnArgs a) {
+  __shared__ float red[32];
   const int ti = find_tensor(a.pk, blockIdx.x);
   const thorn_pnn_tensor& e = a.pk.t[ti];
   const bool vec = a.pk.vec[ti];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t grow = (int64_t(blockIdx.x) - a.pk.start[ti]) * kPnnRowsPerBlock + warp;  // b*rows + r
-  if (grow >= e.batch * e.rows) return;
-  const U* row = (const U*)e.U + grow * e.cols;
-  float s = 0.f;
-  for (int64_t c = lane * 8; c < e.cols; c += 256) {
-    const int n = (int)min64(8, e.cols - c);
-    float v[8];
-    load_n(row + c, v, n, vec);
+  const int64_t nrb = (e.rows + kPnnRowsPerBlock - 1) / kPnnRowsPerBlock;  // row blocks per matrix
+  const int64_t local = int64_t(blockIdx.x) - a.pk.start[ti];
+  const int64_t b = local / nrb, rb = local - b * nrb;
+  const int64_t r = rb * kPnnRowsPerBlock + warp;
+  unsigned* cnt = (unsigned*)e.scratch;
+  float* rsq = (float*)e.scratch + pnn_pf(e.batch);  // [batch*rows] sumsq_r
+  float* rss = rsq + e.batch * e.rows;                 // [batch*rows] s_r^2 sumsq_r
+  if (r < e.rows) {
+    const U* row = (const U*)e.U + (b * e.rows + r) * e.cols;
+    float s = 0.f;
+    for (int64_t c = lane * 8; c < e.cols; c += 256) {
+      const int n = (int)min64(8, e.cols - c);
+      float v[8];
+      load_n(row + c, v, n, vec);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      float x = rnd<P>(v[k]);
-      if (k < n) s += x * x;
+      for (int k = 0; k < 8; ++k) {
+        const float x = rnd<P>(v[k]);
+        if (k < n) s += x * x;
+      }
+    }
+    s = warp_sum(s);
+    if (lane == 0) {
+      const float inv_n = 1.f / (float)e.cols;
+      const float sc = rsqrtf(fmaxf(s * inv_n, a.eps));
+      e.row_scale[b * e.rows + r] = sc;
+      rsq[b * e.rows + r] = s;
+      rss[b * e.rows + r] = sc * sc * s;
     }
   }
-  s = warp_sum(s);
-  if (lane == 0) {
-    const float inv_n = 1.f / (float)e.cols;
-    const float sc = rsqrtf(fmaxf(s * inv_n, a.eps));
-    e.row_scale[grow] = sc;
-    const int64_t b = grow / e.rows;
-    atomicAdd(e.mat_stats + 2 * b, s);
-    atomicAdd(e.mat_stats + 2 * b + 1, sc * sc * s);
+  if (last_block(cnt + b, (unsigned)nrb)) {
+    const float s0 = ordered_sum(rsq + b * e.rows, e.rows, red);
+    const float s1 = ordered_sum(rss + b * e.rows, e.rows, red);
+    if (threadIdx.x == 0) {
+      e.mat_stats[2 * b] = s0;
+      e.mat_stats[2 * b + 1] = s1;
+    }
   }
 }
 
@@ -436,10 +571,7 @@ __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_const
     }
     store_n((P*)e.p + off, pv, nc, vec);
   }
-  if (e.p_normsq != nullptr) {
-    float tot = block_sum(sq, red);
-    if (threadIdx.x == 0) atomicAdd(e.p_normsq + t.b, tot);
-  }
+  if (e.p_normsq != nullptr) tile_sum_to(e.p_normsq, e.scratch, t, e.batch, e.rows, e.cols, sq, red);
 }
 
 // ===========================================================================
@@ -508,50 +640,31 @@ __global__ void __launch_bounds__(kThreads) md_finalize_kernel(const __grid_cons
   }
 }
 
-constexpr int kSqChunk = kThreads * 8 * 4;
-struct SumsqEntry {
-  const void* x;
-  float* out;
-  int64_t batch, per;
-};
 struct SumsqArgs {
-  Pack<SumsqEntry> pk;
+  Pack<thorn_sumsq_tensor> pk;
 };
 
 template <class T>
 __global__ void __launch_bounds__(kThreads) sumsq_kernel(const __grid_constant__ SumsqArgs a) {
+  __shared__ float red[32];
   const int ti = find_tensor(a.pk, blockIdx.x);
-  const SumsqEntry& e = a.pk.t[ti];
-  const int64_t numel = e.batch * e.per;
-  const int64_t base = (int64_t(blockIdx.x) - a.pk.start[ti]) * kSqChunk;
-  const int lane = threadIdx.x & 31;
-  for (int it = 0; it < 4; ++it) {
-    const int64_t i0 = base + int64_t(it) * (kThreads * 8) + threadIdx.x * 8;
-    float s = 0.f;
-    int64_t b = -1;
-    if (i0 < numel) {
-      const T* x = (const T*)e.x;
-      for (int k = 0; k < 8 && i0 + k < numel; ++k) {
-        int64_t bk = (i0 + k) / e.per;
-        float v = to_f(x[i0 + k]);
-        if (b != bk && b >= 0) {
-          atomicAdd(e.out + b, s);
-          s = 0.f;
-        }
-        b = bk;
-        s += v * v;
-      }
-    }
-    // warp-aggregate when the whole warp is in one sub-matrix
-    const int64_t b0 = __shfl_sync(0xffffffffu, b, 0);
-    const bool uni = __all_sync(0xffffffffu, b == b0) && b0 >= 0;
-    if (uni) {
-      s = warp_sum(s);
-      if (lane == 0) atomicAdd(e.out + b0, s);
-    } else if (b >= 0) {
-      atomicAdd(e.out + b, s);
-    }
+  const thorn_sumsq_tensor& e = a.pk.t[ti];
+  const bool vec = a.pk.vec[ti];
+  const Tile t = tile_of(int64_t(blockIdx.x) - a.pk.start[ti], e.rows, e.cols);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t c = t.c0 + lane * 8;
+  const int nc = (int)max64(0, min64(8, e.cols - c));
+  float sq = 0.f;
+  for (int rr = warp; rr < kTR; rr += 8) {
+    const int64_t r = t.r0 + rr;
+    if (r >= e.rows || nc == 0) break;
+    float v[8];
+    load_n((const T*)e.x + (t.b * e.rows + r) * e.cols + c, v, nc, vec);
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (k < nc) sq += v[k] * v[k];
   }
+  tile_sum_to(e.out, e.scratch, t, e.batch, e.rows, e.cols, sq, red);
 }
 
 // ---------------------------------------------------------------------------
@@ -639,7 +752,7 @@ extern "C" int thorn_ortho_pre_multi(const thorn_ortho_pre_tensor* ts, int n, in
   for (int i = 0; i < n; ++i) {
     const auto& e = ts[i];
     if (e.batch < 0 || e.rows < 0 || e.cols < 0) return THORN_ERR_ARG;
-    if (e.batch * e.rows * e.cols > 0 && (!e.g || (e.m && !e.normsq) || (!e.m && !md) || (md && !e.p)))
+    if (e.batch * e.rows * e.cols > 0 && (!e.g || (e.m && !e.normsq) || (!e.m && !md) || (md && !e.p) || !e.scratch))
       return THORN_ERR_ARG;
     if (md && (!e.row_gsum || !e.row_sp || (!e.scalar_gain && (!e.col_sp || !e.col_gsum)))) return THORN_ERR_ARG;
   }
@@ -716,14 +829,14 @@ extern "C" int thorn_ns_cast_multi(const thorn_ns_cast_tensor* ts, int n, int p_
 extern "C" int thorn_pnn_stats_multi(const thorn_pnn_tensor* ts, int n, int u_dtype, int p_dtype, void* stream) {
   if (n < 0 || (n > 0 && ts == nullptr) || !valid_dt(u_dtype) || !valid_dt(p_dtype)) return THORN_ERR_ARG;
   for (int i = 0; i < n; ++i)
-    if (ts[i].batch * ts[i].rows * ts[i].cols > 0 && (!ts[i].U || !ts[i].row_scale || !ts[i].mat_stats))
+    if (ts[i].batch * ts[i].rows * ts[i].cols > 0 && (!ts[i].U || !ts[i].row_scale || !ts[i].mat_stats || !ts[i].scratch))
       return THORN_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   int rc = THORN_OK;
   const float eps = dt_eps(p_dtype);
   auto blocks = [](const thorn_pnn_tensor& e) -> int64_t {
     if (e.batch <= 0 || e.rows <= 0 || e.cols <= 0) return 0;
-    return cdiv(e.batch * e.rows, kPnnRowsPerBlock);
+    return e.batch * cdiv(e.rows, kPnnRowsPerBlock);
   };
   auto vec = [](const thorn_pnn_tensor& e) { return (e.cols % 8) == 0 && aligned16(e.U); };
   int d = dispatch2(u_dtype, p_dtype, [&](auto* pu, auto* pp) {
@@ -743,7 +856,8 @@ extern "C" int thorn_ortho_post_multi(const thorn_ortho_post_tensor* ts, int n, 
                                       float weight_decay, void* stream) {
   if (n < 0 || (n > 0 && ts == nullptr) || !valid_dt(u_dtype) || !valid_dt(p_dtype)) return THORN_ERR_ARG;
   for (int i = 0; i < n; ++i)
-    if (ts[i].batch * ts[i].rows * ts[i].cols > 0 && (!ts[i].U || !ts[i].p)) return THORN_ERR_ARG;
+    if (ts[i].batch * ts[i].rows * ts[i].cols > 0 && (!ts[i].U || !ts[i].p || (ts[i].p_normsq && !ts[i].scratch)))
+      return THORN_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   int rc = THORN_OK;
   const float eps = dt_eps(p_dtype);
@@ -813,33 +927,40 @@ extern "C" int thorn_md_finalize_multi(const thorn_md_final_tensor* ts, int n, i
   return d ? d : rc;
 }
 
-extern "C" int thorn_sumsq_multi(const void* const* x, float* const* out, const int64_t* batch,
-                                 const int64_t* per_batch, int n, int dtype, void* stream) {
-  if (n < 0 || (n > 0 && (!x || !out || !batch || !per_batch)) || !valid_dt(dtype)) return THORN_ERR_ARG;
-  SumsqEntry es[kMaxT];
+extern "C" int64_t thorn_sumsq_scratch_bytes(int64_t batch, int64_t rows, int64_t cols) {
+  if (batch <= 0 || rows <= 0 || cols <= 0) return 0;
+  return sq_bytes(batch, rows, cols);
+}
+
+extern "C" int64_t thorn_ortho_pre_scratch_bytes(int64_t batch, int64_t rows, int64_t cols, int md) {
+  if (batch <= 0 || rows <= 0 || cols <= 0) return 0;
+  return pre_layout(batch, rows, cols, md != 0).bytes;
+}
+
+extern "C" int64_t thorn_pnn_scratch_bytes(int64_t batch, int64_t rows) {
+  if (batch <= 0 || rows <= 0) return 0;
+  return (pnn_pf(batch) + 2 * batch * rows) * 4;
+}
+
+extern "C" int thorn_sumsq_multi(const thorn_sumsq_tensor* ts, int n, int dtype, void* stream) {
+  if (n < 0 || (n > 0 && ts == nullptr) || !valid_dt(dtype)) return THORN_ERR_ARG;
+  for (int i = 0; i < n; ++i) {
+    const auto& e = ts[i];
+    if (e.batch < 0 || e.rows < 0 || e.cols < 0) return THORN_ERR_ARG;
+    if (e.batch * e.rows * e.cols > 0 && (!e.x || !e.out || !e.scratch)) return THORN_ERR_ARG;
+  }
   cudaStream_t st = (cudaStream_t)stream;
   int rc = THORN_OK;
-  for (int i0 = 0; i0 < n; i0 += kMaxT) {
-    int m = n - i0 < kMaxT ? n - i0 : kMaxT;
-    for (int i = 0; i < m; ++i) {
-      es[i] = SumsqEntry{x[i0 + i], out[i0 + i], batch[i0 + i], per_batch[i0 + i]};
-      if (es[i].batch < 0 || es[i].per < 0 || (es[i].batch * es[i].per > 0 && (!es[i].x || !es[i].out)))
-        return THORN_ERR_ARG;
-    }
-    int d = dispatch1(dtype, [&](auto* px) {
-      using T = std::remove_pointer_t<decltype(px)>;
-      rc = launch_packed(
-          es, m, [](const SumsqEntry& e) { return cdiv(e.batch * e.per, kSqChunk); },
-          [](const SumsqEntry&) { return false; },
-          [&](const Pack<SumsqEntry>& pk, int64_t nb) {
-            SumsqArgs a;
-            a.pk = pk;
-            sumsq_kernel<T><<<(unsigned)nb, kThreads, 0, st>>>(a);
-          });
+  auto blocks = [](const thorn_sumsq_tensor& e) { return tiles_of(e.batch, e.rows, e.cols); };
+  auto vec = [](const thorn_sumsq_tensor& e) { return (e.cols % 8) == 0 && aligned16(e.x); };
+  int d = dispatch1(dtype, [&](auto* px) {
+    using T = std::remove_pointer_t<decltype(px)>;
+    rc = launch_packed(ts, n, blocks, vec, [&](const Pack<thorn_sumsq_tensor>& pk, int64_t nb) {
+      SumsqArgs a;
+      a.pk = pk;
+      sumsq_kernel<T><<<(unsigned)nb, kThreads, 0, st>>>(a);
     });
-    if (d) return d;
-    if (rc) return rc;
-  }
+  });
   (void)dt_size;
-  return rc;
+  return d ? d : rc;
 }

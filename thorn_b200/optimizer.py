@@ -211,6 +211,9 @@ class THORN(Optimizer):
 
     polar_decomp_batch_size: int = 32 * 1024 * 1024
     ns_dtype: torch.dtype = torch.float16
+    # when a list: each Newton-Schulz call appends (start event, end event, dense-equivalent
+    # FLOPs, executed FLOPs, (batch, rows, cols)); events are recorded on the launching stream
+    profile_ns: Optional[list] = None
 
     def __init__(self, params, *, backend=torch.cuda, **conf):
         self._update_rate = 1
@@ -237,6 +240,7 @@ class THORN(Optimizer):
             for p in group["params"]:
                 self._param_to_group[id(p)] = group
         self._err = {}
+        self._scratch_bufs = {}
         if isinstance(params, nn.Module) and conf.get("gradient_release", False):
             self.setup_gradient_release(params)
 
@@ -343,6 +347,23 @@ class THORN(Optimizer):
                 else:
                     self._adam_local(ps, cfg)
 
+    def _scratch(self, dev, sizes):
+        """Pointers to disjoint regions of a per-device scratch buffer (zeroed once).
+
+        The kernels leave the counters of their scratch at zero, so the buffer is
+        reused by every call without clearing; calls on one stream run in order.
+        """
+        offs, total = [], 0
+        for sz in sizes:
+            offs.append(total)
+            total += (int(sz) + 255) // 256 * 256
+        buf = self._scratch_bufs.get(dev)
+        if buf is None or buf.numel() < total:
+            buf = torch.zeros(max(total, 1 << 20), dtype=torch.uint8, device=dev)
+            self._scratch_bufs[dev] = buf
+        base = buf.data_ptr()
+        return [base + o for o in offs]
+
     def _err_flag(self, dev):
         t = self._err.get(dev)
         if t is None:
@@ -371,19 +392,19 @@ class THORN(Optimizer):
             N.dtype_code(it.pdt), N.dtype_code(it.sdt)
             if g.dtype != it.pdt:
                 raise TypeError(f"gradient dtype {g.dtype} differs from parameter dtype {it.pdt}")
-            it.normsq = arena.zeros(it.B) if ortho else None
+            it.normsq = arena.empty(it.B) if ortho else None
             it.split = "row_gain" in st
             it.scalar = "gain" in st
             if cfg.decouple_md:
                 nr, nc = (it.B * it.R, it.B * it.C) if it.split else (1, 1)
                 it.rs, it.sig_r, it.rs_new = arena.empty(nr), arena.empty(nr), arena.empty(nr)
-                it.rgs = arena.zeros(nr)
+                it.rgs = arena.empty(nr)
                 if it.split:
                     it.cs, it.sig_c, it.cs_new = arena.empty(nc), arena.empty(nc), arena.empty(nc)
-                    it.cgs = arena.zeros(nc)
+                    it.cgs = arena.empty(nc)
                 else:
                     it.cs = it.sig_c = it.cs_new = it.cgs = None
-                it.pnorm = arena.zeros(it.B)
+                it.pnorm = arena.empty(it.B)
             items.append(it)
         return items
 
@@ -488,19 +509,20 @@ class THORN(Optimizer):
         for ci, (R, C, pdt, sdt, its) in enumerate(chunks):
             if cfg.needs_pnn(R, C):
                 nb = sum(it.B for it in its)
-                pnn_h[ci] = (arena.empty(nb * R), arena.zeros(2 * nb))
+                pnn_h[ci] = (arena.empty(nb * R), arena.empty(2 * nb))
         arena.materialize(dev)
 
         if md:
             self._md_prep(items, arena, new=False, stream=stream)
         write_grad = 1 if (md and not cfg.none_grad) else 0
         by_dt: dict = {}
-        for it in items:
+        scr = self._scratch(dev, [lib.thorn_ortho_pre_scratch_bytes(it.B, it.R, it.C, 1 if md else 0) for it in items])
+        for it, sp in zip(items, scr):
             t = N.OrthoPreTensor(it.p.data_ptr() if md else None, it.g.data_ptr(), _local(it.state["moment"]).data_ptr(),
                                  arena.ptr(it.normsq), it.B, it.R, it.C,
                                  arena.ptr(it.rs) if md else None, arena.ptr(it.cs) if md else None,
                                  1 if (md and not it.split) else 0,
-                                 arena.ptr(it.rgs) if md else None, arena.ptr(it.cgs) if md else None)
+                                 arena.ptr(it.rgs) if md else None, arena.ptr(it.cgs) if md else None, sp)
             by_dt.setdefault((it.pdt, it.sdt), []).append(t)
         for (pdt, sdt), ts in by_dt.items():
             udt = pdt if pdt == sdt else torch.float32
@@ -532,25 +554,36 @@ class THORN(Optimizer):
                                             N.dtype_code(sdt), N.dtype_code(udt), ns_code, b1, stream), "ns_cast_multi")
             wsb = int(lib.thorn_ns_workspace_bytes(nb, R, C))
             ws = torch.empty(max(256, wsb), dtype=torch.uint8, device=dev)
+            if self.profile_ns is not None:
+                ev0 = torch.cuda.Event(enable_timing=True)
+                ev0.record()
+                f0 = N.gemm_flops()
             N.check(lib.thorn_ns_batched(X.data_ptr(), U.data_ptr(), ws.data_ptr(), wsb, nb, R, C, ns_code, coeffs,
                                          cfg.iters, restarts, len(rs), err.data_ptr(), stream), "ns_batched")
+            if self.profile_ns is not None:
+                ev1 = torch.cuda.Event(enable_timing=True)
+                ev1.record()
+                f1 = N.gemm_flops()
+                self.profile_ns.append((ev0, ev1, f1[0] - f0[0], f1[1] - f0[1], (nb, R, C)))
             del X, ws
             row_scale = mat_stats = None
             if ci in pnn_h:
                 rsh, msh = pnn_h[ci]
                 row_scale, mat_stats = arena.get(rsh), arena.get(msh)
-                pt = N.PnnTensor(U.data_ptr(), row_scale.data_ptr(), mat_stats.data_ptr(), nb, R, C)
+                (sp,) = self._scratch(dev, [lib.thorn_pnn_scratch_bytes(nb, R)])
+                pt = N.PnnTensor(U.data_ptr(), row_scale.data_ptr(), mat_stats.data_ptr(), nb, R, C, sp)
                 N.check(lib.thorn_pnn_stats_multi(N.array(N.PnnTensor, [pt]), 1, ns_code, N.dtype_code(pdt), stream),
                         "pnn_stats_multi")
             posts, off = [], 0
             usz = U.element_size()
             lr_eff = float(cfg.lr) * cfg.lr_scale(R, C)
-            for it in its:
+            scr = self._scratch(dev, [lib.thorn_sumsq_scratch_bytes(it.B, R, C) if md else 0 for it in its])
+            for it, sp in zip(its, scr):
                 posts.append(N.OrthoPostTensor(
                     U.data_ptr() + off * R * C * usz, it.p.data_ptr(),
                     None if row_scale is None else row_scale.data_ptr() + off * R * 4,
                     None if mat_stats is None else mat_stats.data_ptr() + off * 2 * 4,
-                    arena.ptr(it.pnorm) if md else None, it.B, it.R, it.C, lr_eff))
+                    arena.ptr(it.pnorm) if md else None, it.B, it.R, it.C, lr_eff, sp if md else None))
                 off += it.B
             N.check(lib.thorn_ortho_post_multi(N.array(N.OrthoPostTensor, posts), len(posts), ns_code,
                                                N.dtype_code(pdt), float(cfg.weight_decay), stream), "ortho_post_multi")
@@ -581,10 +614,11 @@ class THORN(Optimizer):
         if md:
             self._md_prep(items, arena, new=False, stream=stream)
             by_dt: dict = {}
-            for it in items:
+            scr = self._scratch(dev, [lib.thorn_ortho_pre_scratch_bytes(it.B, it.R, it.C, 1) for it in items])
+            for it, sp in zip(items, scr):
                 t = N.OrthoPreTensor(it.p.data_ptr(), it.g.data_ptr(), None, None, it.B, it.R, it.C,
                                      arena.ptr(it.rs), arena.ptr(it.cs), 0 if it.split else 1,
-                                     arena.ptr(it.rgs), arena.ptr(it.cgs))
+                                     arena.ptr(it.rgs), arena.ptr(it.cgs), sp)
                 by_dt.setdefault((it.pdt, it.sdt), []).append(t)
             for (pdt, sdt), ts in by_dt.items():
                 N.check(lib.thorn_ortho_pre_multi(N.array(N.OrthoPreTensor, ts), len(ts), N.dtype_code(pdt),
@@ -609,17 +643,11 @@ class THORN(Optimizer):
             self._md_gains(items, cfg, arena, stream)
             app = [it for it in items if it.apply]
             if app:
-                xs = (ctypes.c_void_p * len(app))(*[it.p.data_ptr() for it in app])
-                outs = (ctypes.c_void_p * len(app))(*[arena.ptr(it.pnorm) for it in app])
-                bs = (ctypes.c_int64 * len(app))(*[it.B for it in app])
-                per = (ctypes.c_int64 * len(app))(*[it.R * it.C for it in app])
+                scr = self._scratch(dev, [lib.thorn_sumsq_scratch_bytes(it.B, it.R, it.C) for it in app])
                 for pdt in {it.pdt for it in app}:
-                    sel = [i for i, it in enumerate(app) if it.pdt == pdt]
-                    xs2 = (ctypes.c_void_p * len(sel))(*[xs[i] for i in sel])
-                    outs2 = (ctypes.c_void_p * len(sel))(*[outs[i] for i in sel])
-                    bs2 = (ctypes.c_int64 * len(sel))(*[bs[i] for i in sel])
-                    per2 = (ctypes.c_int64 * len(sel))(*[per[i] for i in sel])
-                    N.check(lib.thorn_sumsq_multi(xs2, outs2, bs2, per2, len(sel), N.dtype_code(pdt), stream),
+                    ts = [N.SumsqTensor(it.p.data_ptr(), arena.ptr(it.pnorm), it.B, it.R, it.C, sp)
+                          for it, sp in zip(app, scr) if it.pdt == pdt]
+                    N.check(lib.thorn_sumsq_multi(N.array(N.SumsqTensor, ts), len(ts), N.dtype_code(pdt), stream),
                             "sumsq_multi")
             self._md_prep(items, arena, new=True, stream=stream)
             keep = self._md_finalize(items, arena, lambda it: True, stream)
