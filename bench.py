@@ -370,6 +370,54 @@ def gpu_arm(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def ns_only(args):
+    """Time thorn_ns_batched alone on one batch shape (profiling entry point)."""
+    import ctypes
+
+    import torch
+
+    from thorn_b200 import _native as N
+    from thorn_b200.coeffs import gram_ns_restarts, optimal_composition
+
+    B, R, C = (int(x) for x in args.ns_only.lower().split("x"))
+    lib = N.load()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    co = optimal_composition(1e-3, 5, 0.03, 0.02)
+    rs = gram_ns_restarts(*co)
+    cc = (ctypes.c_double * 15)(*[v for t in co for v in t])
+    rr = (ctypes.c_int32 * max(1, len(rs)))(*rs)
+    m, n = min(R, C), max(R, C)
+    ldn = int(lib.thorn_ns_ld(n))
+    X = (torch.randn(B, m, ldn, device=dev) / math.sqrt(m * n)).half()
+    U = torch.empty(B, R, C, dtype=torch.float16, device=dev)
+    wsb = int(lib.thorn_ns_workspace_bytes(B, R, C))
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    st = N.stream_of(dev)
+
+    def run():
+        N.check(lib.thorn_ns_batched(X.data_ptr(), U.data_ptr(), ws.data_ptr(), wsb, B, R, C, N.F16, cc, 5, rr,
+                                     len(rs), err.data_ptr(), st), "ns_batched")
+
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    d0, x0 = N.gemm_flops()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    d1, x1 = N.gemm_flops()
+    ms = e0.elapsed_time(e1) / args.steps
+    dense = B * dense_ns_flops(R, C)
+    print(json.dumps({"ns_only": f"{B}x{R}x{C}", "ms": round(ms, 4), "dense_tflops": round(dense / ms / 1e9, 1),
+                      "executed_tflops": round((x1 - x0) / args.steps / ms / 1e9, 1), "err_flag": int(err.item()),
+                      "finite": bool(torch.isfinite(U).all())}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -378,7 +426,11 @@ def main():
     ap.add_argument("--impl", default="thorn_b200", choices=["thorn_b200", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ns-only", default=None, help="BxRxC: time thorn_ns_batched alone on this batch (profiling)")
     args = ap.parse_args()
+    if args.ns_only:
+        ns_only(args)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -75,8 +75,10 @@ typedef struct {
   int32_t degenerate; /* nonzero: u = m (rect == 0) */
 } thorn_adam_tensor;
 
+/* beta1 and beta2 are doubles: the kernel uses fp32 (1 - beta) formed in double,
+ * as the reference passes 1.0 - float(beta) to its kernel (thorn.py:868). */
 THORN_API int thorn_adamw_multi(const thorn_adam_tensor* tensors, int n, int p_dtype, int s_dtype,
-                      float beta1, float beta2, float weight_decay, float eps, void* stream);
+                                double beta1, double beta2, float weight_decay, float eps, void* stream);
 
 /* --------------------------------------------------------------------------
  * Deterministic reductions.  Kernels that reduce (sums of squares, gain
@@ -84,9 +86,11 @@ THORN_API int thorn_adamw_multi(const thorn_adam_tensor* tensors, int n, int p_d
  * atomics: each block writes its partial sum to a caller-provided scratch
  * buffer, and the last block of each segment (found with an integer counter)
  * adds the partials in a fixed order.  Results are therefore bitwise
- * reproducible run to run.  A scratch buffer must be zero when first used;
- * every call leaves its counters at zero again, so the same buffer can be
- * reused without clearing (partials are always overwritten).
+ * reproducible run to run.  A scratch buffer must be all zero on entry; the
+ * kernels zero every counter and partial they used before they finish, so it
+ * is all zero again on return and may be reused by any later call on the
+ * same stream without clearing.  Calls that overlap in time need disjoint
+ * scratch.
  * ------------------------------------------------------------------------ */
 
 /* --------------------------------------------------------------------------
@@ -221,15 +225,29 @@ THORN_API int thorn_ortho_post_multi(const thorn_ortho_post_tensor* tensors, int
 
 /* --------------------------------------------------------------------------
  * Magnitude-direction decoupling helpers (thorn.py:910-977, 1414-1421).
- * thorn_md_prep:   sp = round_p(softplus(gain)), sig = round_p(sigmoid(gain)) as fp32
- * thorn_md_gain_grad: grad = round_p(round_p(gsum) * sig)  (p_dtype output)
+ * thorn_md_prep_multi: sp = round_p(softplus(gain)), sig = round_p(sigmoid(gain))
+ *   as fp32 (sig may be NULL)
+ * thorn_md_gain_grad_multi: grad = round_p(round_p(gsum) * sig)  (p_dtype output)
  * thorn_md_finalize_multi: renorm to the target norm, then multiply by the
  *   new gains:  p <- round(round(round(p * round(target / round(round(||p||) + 1e-8)))
  *                 * row_sp) * col_sp)   (scalar gain: one multiply)
  * ------------------------------------------------------------------------ */
-THORN_API int thorn_md_prep(const void* gain, int64_t n, float* sp, float* sig, int p_dtype, void* stream);
-THORN_API int thorn_md_gain_grad(const float* gsum, const float* sig, void* grad, int64_t n, int p_dtype,
-                       void* stream);
+typedef struct {
+  const void* gain;  /* p_dtype [n] */
+  float* sp;         /* out [n] */
+  float* sig;        /* out [n] or NULL */
+  int64_t n;
+} thorn_md_prep_tensor;
+
+typedef struct {
+  const float* gsum;  /* [n] */
+  const float* sig;   /* [n] */
+  void* grad;         /* out, p_dtype [n] */
+  int64_t n;
+} thorn_md_grad_tensor;
+
+THORN_API int thorn_md_prep_multi(const thorn_md_prep_tensor* tensors, int n, int p_dtype, void* stream);
+THORN_API int thorn_md_gain_grad_multi(const thorn_md_grad_tensor* tensors, int n, int p_dtype, void* stream);
 
 typedef struct {
   void* p;

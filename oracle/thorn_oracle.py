@@ -97,16 +97,21 @@ def h16(x) -> np.ndarray:
     return rnd(x, "f16")
 
 
-# torch's CPU kernels for ``add(..., alpha=a)`` / ``sub_(..., alpha=a)`` round the
-# scalar ``a`` to the tensor's dtype before using it (bf16: 0.9 -> 0.8984375);
-# its CUDA kernels, and the reference's Triton kernels, keep it in fp32.  The
-# golden vectors come from the CPU path, so the pin tests turn this on; the GPU
-# parity tests compare against the fp32-scalar (CUDA) semantics.
-CPU_ALPHA_ROUNDING = False
+# Which of the reference's two execution paths the oracle models.
+#
+# CPU_EAGER = True: the reference on CPU (how the golden vectors were made):
+#   every torch op rounds to the tensor dtype, and torch's CPU kernels for
+#   ``add(..., alpha=a)`` / ``sub_(..., alpha=a)`` round the scalar ``a`` to
+#   the tensor's dtype first (bf16: 0.9 -> 0.8984375).
+# CPU_EAGER = False: the reference on CUDA: scalars stay fp32, and the Adam
+#   update (thorn.py:147-185), the cautious-WD apply (thorn.py:187-203) and
+#   per-neuron norm (thorn.py:205-280) are fused Triton kernels that compute
+#   in fp32 and round once per stored value.  The GPU parity tests use this.
+CPU_EAGER = False
 
 
 def alpha(a: float, dt: str) -> np.float32:
-    return F32(rnd(F32(a), dt)) if CPU_ALPHA_ROUNDING else F32(a)
+    return F32(rnd(F32(a), dt)) if CPU_EAGER else F32(a)
 
 
 # ---------------------------------------------------------------------------
@@ -245,7 +250,7 @@ def polar_decomp_2d(X: np.ndarray, coeffs, restarts, src_dtype: str) -> np.ndarr
                 # Z + a*I (thorn.py:648); on CPU a*I first rounds a to fp16
                 Q = Z.copy()
                 d = np.arange(Q.shape[0])
-                a16 = rnd(F32(a), NS_DTYPE) if CPU_ALPHA_ROUNDING else F32(a)
+                a16 = rnd(F32(a), NS_DTYPE) if CPU_EAGER else F32(a)
                 Q[d, d] = rnd(Q[d, d] + a16, NS_DTYPE)
             if i < last and (i + 1) not in restarts:
                 RZ = _mm16(R, Z, R, beta=a)
@@ -296,6 +301,12 @@ def weight_decay_update(p, u, wd: float, lr: float, dt: str, udt: str | None = N
     ``udt`` the update's dtype (defaults to ``dt``).
     """
     udt = udt or dt
+    if not CPU_EAGER:
+        # Triton _wd_update_helper: fp32 throughout, one rounding of p
+        u = np.asarray(u, F32)
+        if wd > 0.0:
+            u = np.where(u * p >= 0, u + F32(wd) * p, u).astype(F32)
+        return rnd(p - F32(lr) * u, dt), u
     if wd > 0.0:
         mdt = _promote(dt, udt)
         mask = (rnd(u * p, mdt) >= 0).astype(F32)
@@ -304,8 +315,22 @@ def weight_decay_update(p, u, wd: float, lr: float, dt: str, udt: str | None = N
 
 
 def per_neuron_norm(u, dt: str):
-    """Per-row normalisation, eager path (thorn.py:709-762). u: (..., M, N)."""
+    """Per-row normalisation (thorn.py:709-762). u: (..., M, N).
+
+    CUDA path: the Triton kernels (thorn.py:205-280) in fp32 -- row sums of
+    squares, s = rsqrt(max(sumsq/N, eps)), gscale = sqrt(sum sumsq) /
+    max(sqrt(sum s^2 sumsq), eps) per matrix, u * s * gscale (left in fp32 for
+    the fused apply).  CPU path: eager torch ops rounding to ``dt``.
+    """
     eps = F32(EPS[dt])
+    if not CPU_EAGER:
+        u = np.asarray(u, F32)
+        sumsq = np.sum(u.astype(np.float64) ** 2, axis=-1, keepdims=True).astype(F32)
+        s = (1.0 / np.sqrt(np.maximum(sumsq * F32(1.0 / u.shape[-1]), eps))).astype(F32)
+        tot = np.sum(sumsq.astype(np.float64), axis=(-2, -1), keepdims=True)
+        new = np.sum((s.astype(np.float64) ** 2) * sumsq, axis=(-2, -1), keepdims=True)
+        gscale = (np.sqrt(tot) / np.maximum(np.sqrt(new), eps)).astype(F32)
+        return (u * (s * gscale)).astype(F32)
     v_norm = rnd(np.sqrt(np.sum(u.astype(np.float64) ** 2, axis=(-2, -1), keepdims=True)), dt)
     v_mean = rnd(np.mean(rnd(u * u, dt), axis=-1, keepdims=True, dtype=np.float64), dt)
     s = rnd(1.0 / np.sqrt(np.maximum(v_mean, eps)), dt)
@@ -347,6 +372,24 @@ def adam_update(p, g, m, v, step, beta1, beta2, lr, wd, eps, dt, degenerate=Fals
     bc1 = 1 / (1 - beta1 ** step)
     bc2 = 1 / (1 - beta2 ** step)
     w = F32(1 - beta1)
+    if not CPU_EAGER:
+        # Triton _adam_update_kernel: fp32 math on the loaded values; m and v
+        # round only when stored; u and the apply use the fp32 values
+        # (g - m) * w + m contracts to one fma on the GPU; float64 emulates it
+        mf = (m.astype(np.float64) + (g - m).astype(np.float64) * np.float64(w)).astype(F32)
+        vf = v * F32(beta2) + (g * g) * F32(1 - beta2)
+        m_out, v_out = rnd(mf, sdt), rnd(vf, sdt)
+        if p is None:
+            return None, m_out, v_out
+        if degenerate:
+            u = mf
+        elif eps == 0.0:
+            u = np.arctan2(mf * F32(bc1), np.sqrt(vf * F32(bc2))).astype(F32)
+        else:
+            u = ((mf * F32(bc1)) / (np.sqrt(vf * F32(bc2)) + F32(eps))).astype(F32)
+        if wd > 0.0:
+            u = np.where(u * p >= 0, u + F32(wd) * p, u).astype(F32)
+        return rnd(p - F32(lr) * u, dt), m_out, v_out
     # torch lerp: weight < 0.5 -> self + w*(end-self), else end - (end-self)*(1-w)
     if (1 - beta1) < 0.5:
         m = rnd(m + w * (g - m), sdt)

@@ -16,13 +16,14 @@ def load_golden(path: str) -> dict:
 def run_oracle(name: str, steps: int | None = None, state_dtype: str | None = None, cpu_quirks: bool = False):
     """Step the CPU oracle on a case; returns (oracle, snapshots{tag: (params, states)}).
 
-    ``cpu_quirks`` reproduces torch-CPU scalar rounding (used to pin the oracle
-    against the golden vectors, which were produced on CPU).
+    ``cpu_quirks`` models the reference's eager CPU path (used to pin the oracle
+    against the golden vectors, which were produced on CPU); otherwise the
+    oracle models the reference's CUDA path (fused fp32 Triton kernels).
     """
     from oracle import thorn_oracle as O
     from oracle.thorn_oracle import OracleTHORN
 
-    O.CPU_ALPHA_ROUNDING = cpu_quirks
+    O.CPU_EAGER = cpu_quirks
 
     case = C.CASES[name]
     params = C.build_params(case)

@@ -29,8 +29,8 @@ def declared_functions():
 def test_header_declares_entry_points():
     names = declared_functions()
     for must in ["thorn_adamw_multi", "thorn_ortho_pre_multi", "thorn_ns_cast_multi", "thorn_ns_batched",
-                 "thorn_sym_addmm", "thorn_pnn_stats_multi", "thorn_ortho_post_multi", "thorn_md_prep",
-                 "thorn_md_gain_grad", "thorn_md_finalize_multi", "thorn_sumsq_multi"]:
+                 "thorn_sym_addmm", "thorn_pnn_stats_multi", "thorn_ortho_post_multi", "thorn_md_prep_multi",
+                 "thorn_md_gain_grad_multi", "thorn_md_finalize_multi", "thorn_sumsq_multi"]:
         assert must in names
 
 
@@ -56,6 +56,8 @@ STRUCTS = {
     "thorn_ortho_post_tensor": (N.OrthoPostTensor, ["U", "p", "row_scale", "mat_stats", "p_normsq", "batch",
                                                     "rows", "cols", "lr", "scratch"]),
     "thorn_sumsq_tensor": (N.SumsqTensor, ["x", "out", "batch", "rows", "cols", "scratch"]),
+    "thorn_md_prep_tensor": (N.MdPrepTensor, ["gain", "sp", "sig", "n"]),
+    "thorn_md_grad_tensor": (N.MdGradTensor, ["gsum", "sig", "grad", "n"]),
     "thorn_md_final_tensor": (N.MdFinalTensor, ["p", "normsq", "target", "target_stride", "row_sp", "col_sp",
                                                 "scalar_gain", "batch", "rows", "cols"]),
 }
@@ -119,4 +121,5 @@ def test_argument_validation_without_gpu(lib):
     pre = N.array(N.OrthoPreTensor, [N.OrthoPreTensor(None, None, None, None, 1, 4, 4, None, None, 0, None, None,
                                                        None)])
     assert lib.thorn_ortho_pre_multi(pre, 1, 0, 0, 0, 0.9, 0, 0, None) == 1
-    assert lib.thorn_md_prep(None, 4, None, None, 0, None) == 1
+    mp = N.array(N.MdPrepTensor, [N.MdPrepTensor(None, None, None, 4)])
+    assert lib.thorn_md_prep_multi(mp, 1, 0, None) == 1

@@ -8,9 +8,11 @@ golden-pinned CPU quirks are off).  Inputs are the seeded cases of
   params (north_star); 5e-2 for bf16 params, whose per-step update is only 1-2
   bf16 ulps so rounding flips dominate (the oracle itself sits at 2.7e-2 from
   the reference there);
-* (R)AdamW / vector params and all fp32 optimizer state: 1e-5;
+* (R)AdamW / vector params and all fp32 optimizer state: 1e-5 (2e-3 when
+  stored in bf16: one 1-ulp rounding flip in 4096 elements is 6e-5);
 * MD gains (their gradients are sums over the orthogonalized update): 1e-3.
 """
+import copy
 import ctypes
 import math
 
@@ -26,6 +28,9 @@ pytestmark = pytest.mark.gpu
 
 ORTHO_TOL = {"f32": 2e-2, "bf16": 5e-2}
 VEC_TOL = 1e-5
+# bf16-stored vectors: a single 1-ulp bf16 rounding flip (from fp32 fma ordering)
+# in a 4096-element tensor is already 6e-5 relative
+VEC_TOL_BF16 = 2e-3
 GAIN_TOL = 1e-3
 
 
@@ -75,6 +80,8 @@ def _tol(name, gi, key):
         return GAIN_TOL
     if key == "param" and grp["opts"].get("decouple_md"):
         return 1e-4  # renorm/gain multiplies: a few fp32 roundings in another order
+    if grp["dtype"] != "f32":
+        return VEC_TOL_BF16
     return VEC_TOL
 
 
@@ -282,7 +289,7 @@ def test_state_dict_roundtrip():
     for s in range(2):
         feed(tp1, s)
         o1.step()
-    sd = o1.state_dict()
+    sd = copy.deepcopy(o1.state_dict())  # what a checkpoint on disk holds
     st0 = sd["state"][0]
     assert set(st0) == {"step", "moment", "row_gain", "col_gain", "row_gain_moment", "row_gain_variance",
                         "col_gain_moment", "col_gain_variance", "target_norm"}

@@ -54,6 +54,14 @@ class SumsqTensor(Structure):
                 ("scratch", c_void_p)]
 
 
+class MdPrepTensor(Structure):
+    _fields_ = [("gain", c_void_p), ("sp", c_void_p), ("sig", c_void_p), ("n", c_int64)]
+
+
+class MdGradTensor(Structure):
+    _fields_ = [("gsum", c_void_p), ("sig", c_void_p), ("grad", c_void_p), ("n", c_int64)]
+
+
 class MdFinalTensor(Structure):
     _fields_ = [("p", c_void_p), ("normsq", c_void_p), ("target", c_void_p), ("target_stride", c_int64),
                 ("row_sp", c_void_p), ("col_sp", c_void_p), ("scalar_gain", c_int32),
@@ -67,7 +75,7 @@ _PROTOS = {
     "thorn_launch_count": (c_uint64, []),
     "thorn_last_cuda_error": (c_int, []),
     "thorn_gemm_flops": (None, [POINTER(c_double), POINTER(c_double)]),
-    "thorn_adamw_multi": (c_int, [POINTER(AdamTensor), c_int, c_int, c_int, c_float, c_float, c_float, c_float,
+    "thorn_adamw_multi": (c_int, [POINTER(AdamTensor), c_int, c_int, c_int, c_double, c_double, c_float, c_float,
                                   c_void_p]),
     "thorn_ortho_pre_scratch_bytes": (c_int64, [c_int64, c_int64, c_int64, c_int]),
     "thorn_ortho_pre_multi": (c_int, [POINTER(OrthoPreTensor), c_int, c_int, c_int, c_int, c_float, c_int, c_int,
@@ -82,8 +90,8 @@ _PROTOS = {
     "thorn_pnn_scratch_bytes": (c_int64, [c_int64, c_int64]),
     "thorn_pnn_stats_multi": (c_int, [POINTER(PnnTensor), c_int, c_int, c_int, c_void_p]),
     "thorn_ortho_post_multi": (c_int, [POINTER(OrthoPostTensor), c_int, c_int, c_int, c_float, c_void_p]),
-    "thorn_md_prep": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p]),
-    "thorn_md_gain_grad": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p]),
+    "thorn_md_prep_multi": (c_int, [POINTER(MdPrepTensor), c_int, c_int, c_void_p]),
+    "thorn_md_gain_grad_multi": (c_int, [POINTER(MdGradTensor), c_int, c_int, c_void_p]),
     "thorn_md_finalize_multi": (c_int, [POINTER(MdFinalTensor), c_int, c_int, c_void_p]),
     "thorn_sumsq_scratch_bytes": (c_int64, [c_int64, c_int64, c_int64]),
     "thorn_sumsq_multi": (c_int, [POINTER(SumsqTensor), c_int, c_int, c_void_p]),

@@ -113,7 +113,7 @@ static inline int64_t tiles_of(int64_t batch, int64_t rows, int64_t cols) {
 constexpr int kAdamChunk = kThreads * 8 * 4;  // elements per block
 
 struct AdamScalars {
-  float beta1, beta2, wd, eps;
+  float w1, beta2, w2, wd, eps;  // w1 = 1 - beta1, w2 = 1 - beta2 (formed in double)
 };
 struct AdamArgs {
   Pack<thorn_adam_tensor> pk;
@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(kThreads) adam_kernel(const __grid_constant__ 
   const thorn_adam_tensor& e = a.pk.t[ti];
   const bool vec = a.pk.vec[ti];
   const int64_t base = (int64_t(blockIdx.x) - a.pk.start[ti]) * kAdamChunk;
-  const float w1 = 1.f - a.s.beta1, w2 = 1.f - a.s.beta2;
+  const float w1 = a.s.w1, w2 = a.s.w2;
   const P* g = (const P*)e.g;
   S* M = (S*)e.m;
   S* V = (S*)e.v;
@@ -187,9 +187,14 @@ __device__ __forceinline__ bool last_block(unsigned* cnt, unsigned total) {
 }
 
 // Fixed-order block sum of n partials (strided per thread, then a fixed tree).
-__device__ __forceinline__ float ordered_sum(const float* x, int64_t n, float* red) {
+// The partials are zeroed after they are read, so a scratch buffer is all
+// zero again once its kernel finishes and any later call may reuse it.
+__device__ __forceinline__ float ordered_sum(float* x, int64_t n, float* red) {
   float s = 0.f;
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s += __ldcg(x + i);
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    s += __ldcg(x + i);
+    x[i] = 0.f;
+  }
   return block_sum(s, red);
 }
 
@@ -378,9 +383,12 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
       for (int rr = warp; rr < kTR; rr += 8) {
         const int64_t r = t.r0 + rr;
         if (r >= e.rows) break;
-        const float* src = sf + L.pr + (t.b * e.rows + r) * L.tc;
+        float* src = sf + L.pr + (t.b * e.rows + r) * L.tc;
         float s = 0.f;
-        for (int64_t k = lane; k < L.tc; k += 32) s += __ldcg(src + k);
+        for (int64_t k = lane; k < L.tc; k += 32) {
+          s += __ldcg(src + k);
+          src[k] = 0.f;
+        }
         s = warp_sum(s);
         if (lane == 0) e.row_gsum[t.b * e.rows + r] = s;
       }
@@ -389,7 +397,11 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
       const int64_t cc = t.c0 + threadIdx.x;
       if (cc < e.cols) {
         float s = 0.f;
-        for (int64_t k = 0; k < L.tr; ++k) s += __ldcg(sf + L.pc + (t.b * L.tr + k) * e.cols + cc);
+        for (int64_t k = 0; k < L.tr; ++k) {
+          float* q = sf + L.pc + (t.b * L.tr + k) * e.cols + cc;
+          s += __ldcg(q);
+          *q = 0.f;
+        }
         e.col_gsum[t.b * e.cols + cc] = s;
       }
     }
@@ -577,21 +589,32 @@ __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_const
 // ===========================================================================
 // MD helpers (thorn.py:910-977, 1414-1421)
 // ===========================================================================
+struct MdPrepArgs {
+  Pack<thorn_md_prep_tensor> pk;
+};
+struct MdGradArgs {
+  Pack<thorn_md_grad_tensor> pk;
+};
+
 template <class P>
-__global__ void md_prep_kernel(const P* gain, int64_t n, float* sp, float* sig) {
-  int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  float x = to_f(gain[i]);
-  float s = x > 20.f ? x : log1pf(expf(x));
-  sp[i] = rnd<P>(s);
-  if (sig) sig[i] = rnd<P>(1.f / (1.f + expf(-x)));
+__global__ void __launch_bounds__(kThreads) md_prep_kernel(const __grid_constant__ MdPrepArgs a) {
+  const int ti = find_tensor(a.pk, blockIdx.x);
+  const thorn_md_prep_tensor& e = a.pk.t[ti];
+  const int64_t i = (int64_t(blockIdx.x) - a.pk.start[ti]) * kThreads + threadIdx.x;
+  if (i >= e.n) return;
+  const float x = to_f(((const P*)e.gain)[i]);
+  const float s = x > 20.f ? x : log1pf(expf(x));  // F.softplus(beta=1, threshold=20)
+  e.sp[i] = rnd<P>(s);
+  if (e.sig) e.sig[i] = rnd<P>(1.f / (1.f + expf(-x)));
 }
 
 template <class P>
-__global__ void md_gain_grad_kernel(const float* gsum, const float* sig, P* grad, int64_t n) {
-  int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  grad[i] = from_f<P>(rnd<P>(gsum[i]) * sig[i]);
+__global__ void __launch_bounds__(kThreads) md_gain_grad_kernel(const __grid_constant__ MdGradArgs a) {
+  const int ti = find_tensor(a.pk, blockIdx.x);
+  const thorn_md_grad_tensor& e = a.pk.t[ti];
+  const int64_t i = (int64_t(blockIdx.x) - a.pk.start[ti]) * kThreads + threadIdx.x;
+  if (i >= e.n) return;
+  ((P*)e.grad)[i] = from_f<P>(rnd<P>(e.gsum[i]) * e.sig[i]);
 }
 
 struct FinalArgs {
@@ -719,12 +742,12 @@ extern "C" const char* thorn_status_string(int s) {
 extern "C" uint64_t thorn_launch_count(void) { return g_launches.load(); }
 extern "C" int thorn_last_cuda_error(void) { return g_last_cuda_error.load(); }
 
-extern "C" int thorn_adamw_multi(const thorn_adam_tensor* ts, int n, int p_dtype, int s_dtype, float beta1,
-                                 float beta2, float weight_decay, float eps, void* stream) {
+extern "C" int thorn_adamw_multi(const thorn_adam_tensor* ts, int n, int p_dtype, int s_dtype, double beta1,
+                                 double beta2, float weight_decay, float eps, void* stream) {
   if (n < 0 || (n > 0 && ts == nullptr) || !valid_dt(p_dtype) || !valid_dt(s_dtype)) return THORN_ERR_ARG;
   for (int i = 0; i < n; ++i)
     if (ts[i].numel < 0 || (ts[i].numel > 0 && (!ts[i].g || !ts[i].m || !ts[i].v))) return THORN_ERR_ARG;
-  AdamScalars sc{beta1, beta2, weight_decay, eps};
+  AdamScalars sc{(float)(1.0 - beta1), (float)beta2, (float)(1.0 - beta2), weight_decay, eps};
   cudaStream_t st = (cudaStream_t)stream;
   int rc = THORN_OK;
   int d = dispatch2(p_dtype, s_dtype, [&](auto* pp, auto* ps) {
@@ -877,31 +900,44 @@ extern "C" int thorn_ortho_post_multi(const thorn_ortho_post_tensor* ts, int n, 
   return d ? d : rc;
 }
 
-extern "C" int thorn_md_prep(const void* gain, int64_t n, float* sp, float* sig, int p_dtype, void* stream) {
-  if (n < 0 || (n > 0 && (!gain || !sp)) || !valid_dt(p_dtype)) return THORN_ERR_ARG;
-  if (n == 0) return THORN_OK;
+extern "C" int thorn_md_prep_multi(const thorn_md_prep_tensor* ts, int n, int p_dtype, void* stream) {
+  if (n < 0 || (n > 0 && ts == nullptr) || !valid_dt(p_dtype)) return THORN_ERR_ARG;
+  for (int i = 0; i < n; ++i)
+    if (ts[i].n < 0 || (ts[i].n > 0 && (!ts[i].gain || !ts[i].sp))) return THORN_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
+  int rc = THORN_OK;
   int d = dispatch1(p_dtype, [&](auto* pp) {
     using P = std::remove_pointer_t<decltype(pp)>;
-    md_prep_kernel<P><<<(unsigned)cdiv(n, 256), 256, 0, st>>>((const P*)gain, n, sp, sig);
+    rc = launch_packed(
+        ts, n, [](const thorn_md_prep_tensor& e) { return cdiv(e.n, kThreads); },
+        [](const thorn_md_prep_tensor&) { return false; },
+        [&](const Pack<thorn_md_prep_tensor>& pk, int64_t nb) {
+          MdPrepArgs a;
+          a.pk = pk;
+          md_prep_kernel<P><<<(unsigned)nb, kThreads, 0, st>>>(a);
+        });
   });
-  if (d) return d;
-  count_launch();
-  return check_launch();
+  return d ? d : rc;
 }
 
-extern "C" int thorn_md_gain_grad(const float* gsum, const float* sig, void* grad, int64_t n, int p_dtype,
-                                  void* stream) {
-  if (n < 0 || (n > 0 && (!gsum || !sig || !grad)) || !valid_dt(p_dtype)) return THORN_ERR_ARG;
-  if (n == 0) return THORN_OK;
+extern "C" int thorn_md_gain_grad_multi(const thorn_md_grad_tensor* ts, int n, int p_dtype, void* stream) {
+  if (n < 0 || (n > 0 && ts == nullptr) || !valid_dt(p_dtype)) return THORN_ERR_ARG;
+  for (int i = 0; i < n; ++i)
+    if (ts[i].n < 0 || (ts[i].n > 0 && (!ts[i].gsum || !ts[i].sig || !ts[i].grad))) return THORN_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
+  int rc = THORN_OK;
   int d = dispatch1(p_dtype, [&](auto* pp) {
     using P = std::remove_pointer_t<decltype(pp)>;
-    md_gain_grad_kernel<P><<<(unsigned)cdiv(n, 256), 256, 0, st>>>(gsum, sig, (P*)grad, n);
+    rc = launch_packed(
+        ts, n, [](const thorn_md_grad_tensor& e) { return cdiv(e.n, kThreads); },
+        [](const thorn_md_grad_tensor&) { return false; },
+        [&](const Pack<thorn_md_grad_tensor>& pk, int64_t nb) {
+          MdGradArgs a;
+          a.pk = pk;
+          md_gain_grad_kernel<P><<<(unsigned)nb, kThreads, 0, st>>>(a);
+        });
   });
-  if (d) return d;
-  count_launch();
-  return check_launch();
+  return d ? d : rc;
 }
 
 extern "C" int thorn_md_finalize_multi(const thorn_md_final_tensor* ts, int n, int p_dtype, void* stream) {

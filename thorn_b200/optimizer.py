@@ -209,7 +209,10 @@ class _Item:
 class THORN(Optimizer):
     """THORN optimizer (see module docstring)."""
 
-    polar_decomp_batch_size: int = 32 * 1024 * 1024
+    # elements per Newton-Schulz batch (thorn.py:1237; 0 disables batching).  The
+    # reference defaults to 32 Mi; with 180 GB of HBM and 148 SMs the B200 path
+    # defaults to 256 Mi, so large matrices batch by 4+ and fill whole GEMM waves.
+    polar_decomp_batch_size: int = 256 * 1024 * 1024
     ns_dtype: torch.dtype = torch.float16
     # when a list: each Newton-Schulz call appends (start event, end event, dense-equivalent
     # FLOPs, executed FLOPs, (batch, rows, cols)); events are recorded on the launching stream
@@ -409,10 +412,11 @@ class THORN(Optimizer):
         return items
 
     def _md_prep(self, items, arena, new: bool, stream):
+        """softplus (and sigmoid) of the gains as fp32, one launch per dtype."""
         lib = N.load()
+        by_dt: dict = {}
         for it in items:
             st = it.state
-            pc = N.dtype_code(it.pdt)
             if it.split:
                 pairs = [(st["row_gain"], it.rs_new if new else it.rs, None if new else it.sig_r),
                          (st["col_gain"], it.cs_new if new else it.cs, None if new else it.sig_c)]
@@ -420,13 +424,17 @@ class THORN(Optimizer):
                 pairs = [(st["gain"], it.rs_new if new else it.rs, None if new else it.sig_r)]
             for gain, sp, sig in pairs:
                 gl = _local(gain)
-                N.check(lib.thorn_md_prep(gl.data_ptr(), gl.numel(), arena.ptr(sp), arena.ptr(sig), pc, stream),
-                        "md_prep")
+                by_dt.setdefault(N.dtype_code(it.pdt), []).append(
+                    N.MdPrepTensor(gl.data_ptr(), arena.ptr(sp), arena.ptr(sig), gl.numel()))
+        for pc, ts in by_dt.items():
+            N.check(lib.thorn_md_prep_multi(N.array(N.MdPrepTensor, ts), len(ts), pc, stream), "md_prep_multi")
 
     def _md_gains(self, items, cfg, arena, stream):
         """Gradient of the gains and their Adam step (thorn.py:910-967)."""
         lib = N.load()
-        by_dt: dict = {}
+        grads_by_dt: dict = {}
+        adam_by_dt: dict = {}
+        keep = []
         for it in items:
             if not it.apply:
                 continue
@@ -440,16 +448,20 @@ class THORN(Optimizer):
             for key, gsum, sig in keys:
                 gain = _local(st[key])
                 grad = torch.empty_like(gain)
-                N.check(lib.thorn_md_gain_grad(arena.ptr(gsum), arena.ptr(sig), grad.data_ptr(), gain.numel(), pc,
-                                               stream), "md_gain_grad")
+                keep.append(grad)
+                grads_by_dt.setdefault(pc, []).append(
+                    N.MdGradTensor(arena.ptr(gsum), arena.ptr(sig), grad.data_ptr(), gain.numel()))
                 mom, var = _local(st[key + "_moment"]), _local(st[key + "_variance"])
-                t = N.AdamTensor(gain.data_ptr(), grad.data_ptr(), mom.data_ptr(), var.data_ptr(), gain.numel(),
-                                 cfg.gain_lr_, bc1, bc2, 0)
-                by_dt.setdefault((pc, N.dtype_code(mom.dtype)), []).append((t, grad))
-        for (pc, sc), ts in by_dt.items():
-            arr = N.array(N.AdamTensor, [t for t, _ in ts])
-            N.check(lib.thorn_adamw_multi(arr, len(ts), pc, sc, cfg.gain_betas[0], cfg.gain_betas[1], 0.0,
-                                          float(cfg.eps), stream), "adamw_multi(gains)")
+                adam_by_dt.setdefault((pc, N.dtype_code(mom.dtype)), []).append(
+                    N.AdamTensor(gain.data_ptr(), grad.data_ptr(), mom.data_ptr(), var.data_ptr(), gain.numel(),
+                                 cfg.gain_lr_, bc1, bc2, 0))
+        for pc, ts in grads_by_dt.items():
+            N.check(lib.thorn_md_gain_grad_multi(N.array(N.MdGradTensor, ts), len(ts), pc, stream),
+                    "md_gain_grad_multi")
+        for (pc, sc), ts in adam_by_dt.items():
+            N.check(lib.thorn_adamw_multi(N.array(N.AdamTensor, ts), len(ts), pc, sc, cfg.gain_betas[0],
+                                          cfg.gain_betas[1], 0.0, float(cfg.eps), stream), "adamw_multi(gains)")
+        del keep
 
     def _md_finalize(self, items, arena, renorm_of, stream):
         lib = N.load()
