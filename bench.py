@@ -45,9 +45,11 @@ LAYER_SHAPES = [(HIDDEN, HIDDEN), (KV, HIDDEN), (KV, HIDDEN), (HIDDEN, HIDDEN), 
                 (HIDDEN, FFN)]
 ORTHO_LR, ADAM_LR = 8e-3, 8e-3
 METRIC = "THORN.step ms, Llama-3-8B shapes"
-# DRAM bytes per launch of the NS GEMM kernel, from the ncu capture summarised
-# in profiles/ns_gemm_llama8b.md (None until a capture exists)
-NS_GEMM_TRAFFIC = None
+# DRAM bytes (read + write) of one ns_gemm_kernel launch from the ncu capture in
+# profiles/ns_gemm_2x4096.md: X X^T on two 4096x4096 matrices (K = 4096), whose
+# compulsory traffic is 67 MB read + 67 MB written.
+NS_GEMM_TRAFFIC = 98.6e6
+NS_GEMM_TRAFFIC_CASE = "one X X^T launch on 2 x 4096x4096 (K=4096); compulsory 67 MB read + 67 MB write"
 
 
 def shapes():
@@ -356,6 +358,7 @@ def gpu_arm(args, rank, world, local_rank):
         "roofline": {"bound": "tensor", "kernel": "ns_gemm_kernel (Newton-Schulz phase)",
                      "achieved": round(achieved, 1) if achieved else None, "peak": peak_sus, "unit": "TFLOP/s",
                      "frac": round(achieved / peak_sus, 3) if achieved else None, "traffic": NS_GEMM_TRAFFIC,
+                     "traffic_case": NS_GEMM_TRAFFIC_CASE,
                      "flops": "dense-equivalent (2MNK per reference GEMM)",
                      "achieved_executed": round(achieved_exec, 1) if achieved_exec else None,
                      "peak_source": f"{peak_src} sustained bf16 (MEASURED_PEAKS.json); burst {peak_burst}",
