@@ -37,6 +37,7 @@ extern "C" {
 #define THORN_ERR_ALIGN 2        /* pointer or leading dimension not aligned as required */
 #define THORN_ERR_CUDA 3         /* a CUDA runtime call or kernel launch failed */
 #define THORN_ERR_UNSUPPORTED 4  /* no device / wrong architecture / missing driver entry point */
+#define THORN_ERR_TOO_LARGE 5    /* problem needs more than THORN_NS_STATIC_WORKSPACE_BYTES */
 
 /* --------------------------------------------------------------------------
  * Library information
@@ -168,6 +169,25 @@ THORN_API int thorn_ns_batched(const void* x, void* out, void* workspace, int64_
                      int64_t batch, int64_t rows, int64_t cols, int ns_dtype,
                      const double* coeffs, int iters, const int32_t* restarts, int n_restarts,
                      int* err_flag, void* stream);
+
+/* Same as thorn_ns_batched, but allocates nothing and takes no workspace: for
+ * callers that cannot allocate device memory, such as a custom call inside a
+ * host framework that passes only operands and offers no allocator, or code
+ * that must not call cudaMalloc after start-up.  It has no counterpart in the
+ * reference.  The workspace is a fixed 64 MiB device array built into the
+ * library, held on every GPU that loads the library's kernels until the
+ * process exits.  Problems whose thorn_ns_workspace_bytes(batch, rows, cols)
+ * exceed THORN_NS_STATIC_WORKSPACE_BYTES are rejected with
+ * THORN_ERR_TOO_LARGE (e.g. one 2896x2896 or 1024x8192 matrix fits).
+ * The first call on a device looks up the array's device address (once per
+ * device, with that device current); make that first call before any CUDA
+ * stream capture.  All calls on a device share the one array and nothing in it
+ * needs to start at zero, so calls that overlap on the GPU (two streams, two
+ * host threads) race on it and must be serialised by the caller. */
+#define THORN_NS_STATIC_WORKSPACE_BYTES (64ll * 1024 * 1024)
+THORN_API int thorn_ns_batched_static(const void* x, void* out, int64_t batch, int64_t rows, int64_t cols,
+                                      int ns_dtype, const double* coeffs, int iters, const int32_t* restarts,
+                                      int n_restarts, int* err_flag, void* stream);
 
 /* O = alpha A@B + beta C for symmetric A@B and C: the thorn::sym_addmm
  * contract (thorn.py:298-363).  A [batch, M, K], B [batch, K, M],

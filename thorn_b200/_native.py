@@ -17,7 +17,8 @@ from . import build as _build
 F32, BF16, F16 = 0, 1, 2
 DTYPE_CODE = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
 STATUS = {0: "ok", 1: "invalid argument", 2: "misaligned pointer or leading dimension", 3: "CUDA error",
-          4: "unsupported device or configuration"}
+          4: "unsupported device or configuration", 5: "problem needs more than the 64 MiB static NS workspace"}
+NS_STATIC_WORKSPACE_BYTES = 64 * 1024 * 1024
 
 
 class AdamTensor(Structure):
@@ -87,6 +88,8 @@ _PROTOS = {
                                  POINTER(c_double), c_int, POINTER(c_int32), c_int, c_void_p, c_void_p]),
     "thorn_sym_addmm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_float,
                                 c_float, c_int, c_void_p, c_void_p]),
+    "thorn_ns_batched_static": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, POINTER(c_double),
+                                        c_int, POINTER(c_int32), c_int, c_void_p, c_void_p]),
     "thorn_pnn_scratch_bytes": (c_int64, [c_int64, c_int64]),
     "thorn_pnn_stats_multi": (c_int, [POINTER(PnnTensor), c_int, c_int, c_int, c_void_p]),
     "thorn_ortho_post_multi": (c_int, [POINTER(OrthoPostTensor), c_int, c_int, c_int, c_float, c_void_p]),

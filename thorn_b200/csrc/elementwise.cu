@@ -735,6 +735,7 @@ extern "C" const char* thorn_status_string(int s) {
     case THORN_ERR_ALIGN: return "misaligned pointer or leading dimension";
     case THORN_ERR_CUDA: return "CUDA error";
     case THORN_ERR_UNSUPPORTED: return "unsupported device or configuration";
+    case THORN_ERR_TOO_LARGE: return "problem needs more than the 64 MiB static NS workspace";
   }
   return "unknown status";
 }

@@ -732,3 +732,56 @@ extern "C" void thorn_gemm_flops(double* dense, double* executed) {
   if (dense) *dense = (double)g_flops_dense.load();
   if (executed) *executed = (double)g_flops_exec.load();
 }
+
+// ===========================================================================
+// Newton-Schulz without any device allocation
+// ===========================================================================
+// Some callers cannot hand this library a workspace: a custom call inside a
+// host framework (an XLA/JAX FFI handler, for instance) receives only its
+// operands and no allocator, and code that must not allocate after start-up
+// cannot call cudaMalloc (it synchronises the device and can fail under memory
+// pressure).  For them the NS workspace lives in this fixed device array.  It
+// is part of the module image: every GPU on which the library's kernels are
+// loaded holds it until the process exits.
+static __device__ __align__(256) unsigned char g_ns_static_workspace[THORN_NS_STATIC_WORKSPACE_BYTES];
+
+namespace {
+// Device address of g_ns_static_workspace on the current device.  The symbol's
+// name in host code is only a host-side stand-in; the address is looked up once
+// per device (with that device current) and cached.
+int static_workspace(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return THORN_ERR_CUDA;
+  }
+  static std::mutex mu;
+  static void* addr[64] = {};
+  std::lock_guard<std::mutex> lk(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_ns_static_workspace);
+    if (e != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return THORN_ERR_CUDA;
+    }
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return THORN_OK;
+}
+}  // namespace
+
+extern "C" int thorn_ns_batched_static(const void* x, void* out, int64_t batch, int64_t rows, int64_t cols,
+                                       int ns_dtype, const double* coeffs, int iters, const int32_t* restarts,
+                                       int n_restarts, int* err_flag, void* stream) {
+  if (batch < 0 || rows < 0 || cols < 0) return THORN_ERR_ARG;
+  if (batch == 0 || rows == 0 || cols == 0) return THORN_OK;
+  if (thorn_ns_workspace_bytes(batch, rows, cols) > (int64_t)THORN_NS_STATIC_WORKSPACE_BYTES)
+    return THORN_ERR_TOO_LARGE;
+  void* ws = nullptr;
+  const int rc = static_workspace(&ws);
+  if (rc) return rc;
+  return thorn_ns_batched(x, out, ws, (int64_t)THORN_NS_STATIC_WORKSPACE_BYTES, batch, rows, cols, ns_dtype, coeffs,
+                          iters, restarts, n_restarts, err_flag, stream);
+}
