@@ -390,9 +390,8 @@ def ns_only(args):
     rs = gram_ns_restarts(*co)
     cc = (ctypes.c_double * 15)(*[v for t in co for v in t])
     rr = (ctypes.c_int32 * max(1, len(rs)))(*rs)
-    m, n = min(R, C), max(R, C)
-    ldn = int(lib.thorn_ns_ld(n))
-    X = (torch.randn(B, m, ldn, device=dev) / math.sqrt(m * n)).half()
+    ldc = int(lib.thorn_ns_ld(C))
+    X = (torch.randn(B, R, ldc, device=dev) / math.sqrt(R * C)).half()
     U = torch.empty(B, R, C, dtype=torch.float16, device=dev)
     wsb = int(lib.thorn_ns_workspace_bytes(B, R, C))
     ws = torch.empty(wsb, dtype=torch.uint8, device=dev)

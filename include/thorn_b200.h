@@ -128,13 +128,13 @@ THORN_API int thorn_ortho_pre_multi(const thorn_ortho_pre_tensor* tensors, int n
                                     int u_dtype, float beta1, int md, int write_grad, void* stream);
 
 /* --------------------------------------------------------------------------
- * Newton-Schulz input: X = ns(u / (||u||_F + 1e-8)), transposed to the wide
- * orientation (rows <= cols) when the sub-matrix is tall.  Replaces
- * thorn.py:629-635.  u = round_u(fma(beta1, m, g_eff)) is recomputed from the
+ * Newton-Schulz input: X = ns(u / (||u||_F + 1e-8)) in the matrix's own
+ * orientation (the NS GEMMs read a tall input transposed, so no transpose
+ * pass is needed).  Replaces thorn.py:629-635.  u = round_u(fma(beta1, m, g_eff)) is recomputed from the
  * gradient and the moment written by thorn_ortho_pre_multi, with
  * g_eff = round_p(g * gain) when md != 0 (g still holds the raw gradient,
  * i.e. the pre pass ran with write_grad == 0) and g_eff = g otherwise.
- * x is [batch, min(r,c), ld] with ld = thorn_ns_ld(max(r,c)).
+ * x is [batch, rows, ld] with ld = thorn_ns_ld(cols).
  * ------------------------------------------------------------------------ */
 typedef struct {
   const void* g;
@@ -156,9 +156,9 @@ THORN_API int thorn_ns_cast_multi(const thorn_ns_cast_tensor* tensors, int n, in
  * Newton-Schulz polar factor of a batch of same-shape matrices.
  * Replaces _polar_decomp_impl (thorn.py:626-662) with its custom op
  * thorn::sym_addmm (thorn.py:298-377) and torch.bmm/baddbmm (thorn.py:614-624,
- * 653).  x: normalised input from thorn_ns_cast_multi, [batch, m, ld(n)] with
- * m = min(rows, cols), n = max(rows, cols).  out: [batch, rows, cols] in the
- * original orientation, ns_dtype.  Runs the standard quintic for square
+ * 653).  x: normalised input from thorn_ns_cast_multi, [batch, rows,
+ * thorn_ns_ld(cols)] (a tall matrix is not transposed; the GEMMs read it as
+ * X = x^T).  out: [batch, rows, cols], ns_dtype.  Runs the standard quintic for square
  * matrices and Gram Newton-Schulz (restarts at the listed iterations) for
  * rectangular ones, with the reference's recurrences and coefficients.
  * err_flag: device int set nonzero if a bounded wait in a kernel gave up
@@ -209,10 +209,11 @@ THORN_API int thorn_sym_addmm(const void* A, const void* B, const void* C, void*
  * ------------------------------------------------------------------------ */
 typedef struct {
   const void* U;        /* u_dtype [batch, rows, cols] */
-  float* row_scale;     /* out: s_r, [batch*rows] */
+  float* row_scale;     /* out: s_r, [batch*rows] (s_r * gscale_b when fold != 0) */
   float* mat_stats;     /* out: [batch][2] */
   int64_t batch, rows, cols;
   void* scratch;        /* thorn_pnn_scratch_bytes(batch, rows) bytes */
+  int32_t fold;         /* nonzero: fold gscale_b into row_scale (one factor per row) */
 } thorn_pnn_tensor;
 
 THORN_API int64_t thorn_pnn_scratch_bytes(int64_t batch, int64_t rows);
@@ -238,6 +239,8 @@ typedef struct {
   int64_t batch, rows, cols;
   float lr;                /* lr * lr_scale (thorn.py:768-780) * magma scale */
   void* scratch;           /* with p_normsq: thorn_sumsq_scratch_bytes(batch, rows, cols) bytes */
+  int32_t round_u;         /* nonzero: round U to the param dtype first (thorn.py:1404);
+                              zero: use it as is (the sharded path's fp32 u, thorn.py:1079-1081, 1143) */
 } thorn_ortho_post_tensor;
 
 THORN_API int thorn_ortho_post_multi(const thorn_ortho_post_tensor* tensors, int n, int u_dtype, int p_dtype,

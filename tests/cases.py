@@ -83,6 +83,14 @@ CASES = {
         dict(orthogonalize=False, shapes=[(64,), (40, 24)], init=("normal", 0.1), dtype="f32",
              opts=dict(lr=1e-3, rectify=True, eps=1e-8, weight_decay=0.1, betas=(0.9, 0.95))),
     ]),
+    # decouple_md on the orthogonalized group with 2-D matrices whose rows split over 2 ranks
+    # (the FSDP2 tests), next to a plain (R)AdamW vector group.
+    "md_shard": dict(steps=3, grad_std=1e-3, groups=[
+        dict(orthogonalize=True, shapes=[(64, 64), (96, 64), (64, 160), (128, 128)],
+             init=("normal", 0.02), dtype="f32", opts=dict(lr=8e-3, decouple_md=True)),
+        dict(orthogonalize=False, shapes=[(64,), (32,)], init=("normal", 0.5), dtype="f32",
+             opts=dict(lr=1e-3, weight_decay=0.05)),
+    ]),
     # BASELINE config 2 shapes (flattened conv kernels) -- the many-tiny-matrices case.
     "vad": dict(steps=3, grad_std=1e-3, groups=_vad_groups(flatten=True)),
 }

@@ -1,0 +1,72 @@
+"""Run a seeded case with FSDP2-style DTensor Shard(0) parameters on every rank.
+
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \\
+        --master-port P tests/sharded_worker.py --case NAME --out FILE.npz
+
+Rank 0 writes the full (gathered) parameters and optimizer state after step 1
+and after the last step, in the layout of the GPU parity tests.
+"""
+import argparse
+import datetime
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+sys.path.insert(0, os.path.dirname(HERE))
+
+import cases as C  # noqa: E402
+
+
+def full(t):
+    from torch.distributed.tensor import DTensor
+    t = t.full_tensor() if isinstance(t, DTensor) else t
+    return t.detach().float().cpu().numpy()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", required=True)
+    ap.add_argument("--out", required=True)
+    args = ap.parse_args()
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local_rank))
+    from torch.distributed.device_mesh import init_device_mesh
+    from torch.distributed.tensor import Shard, distribute_tensor
+
+    from thorn_b200 import THORN
+
+    mesh = init_device_mesh("cuda", (dist.get_world_size(),))
+    case = C.CASES[args.case]
+    params = C.build_params(case)
+    tp = [[torch.nn.Parameter(distribute_tensor(t.cuda(), mesh, [Shard(0)])) for t in ps] for ps in params]
+    opt = THORN(C.group_dicts(case, tp))
+    out = {}
+    for s in range(case["steps"]):
+        for ps, gs in zip(tp, C.build_grads(case, s)):
+            for p, g in zip(ps, gs):
+                p.grad = distribute_tensor(g.cuda(), mesh, [Shard(0)])
+        opt.step()
+        if s == 0 or s == case["steps"] - 1:
+            tag = "step1" if s == 0 else "final"
+            for gi, ps in enumerate(tp):
+                for pi, p in enumerate(ps):
+                    out[f"{tag}/g{gi}/p{pi}/param"] = full(p)
+                    for k, v in opt.state[p].items():
+                        out[f"{tag}/g{gi}/p{pi}/{k}"] = full(v) if isinstance(v, torch.Tensor) else np.asarray(v)
+    torch.cuda.synchronize()
+    assert not opt.device_error()
+    if dist.get_rank() == 0:
+        np.savez(args.out, **out)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -52,9 +52,9 @@ STRUCTS = {
                                                   "col_sp", "scalar_gain", "row_gsum", "col_gsum", "scratch"]),
     "thorn_ns_cast_tensor": (N.NsCastTensor, ["g", "m", "normsq", "x", "batch", "rows", "cols", "row_sp", "col_sp",
                                               "scalar_gain", "md"]),
-    "thorn_pnn_tensor": (N.PnnTensor, ["U", "row_scale", "mat_stats", "batch", "rows", "cols", "scratch"]),
+    "thorn_pnn_tensor": (N.PnnTensor, ["U", "row_scale", "mat_stats", "batch", "rows", "cols", "scratch", "fold"]),
     "thorn_ortho_post_tensor": (N.OrthoPostTensor, ["U", "p", "row_scale", "mat_stats", "p_normsq", "batch",
-                                                    "rows", "cols", "lr", "scratch"]),
+                                                    "rows", "cols", "lr", "scratch", "round_u"]),
     "thorn_sumsq_tensor": (N.SumsqTensor, ["x", "out", "batch", "rows", "cols", "scratch"]),
     "thorn_md_prep_tensor": (N.MdPrepTensor, ["gain", "sp", "sig", "n"]),
     "thorn_md_grad_tensor": (N.MdGradTensor, ["gsum", "sig", "grad", "n"]),

@@ -137,14 +137,11 @@ def _ns_gpu(u: torch.Tensor, ns_dtype=torch.float16, iters=5):
 
     lib = N.load()
     Bn, R, Cc = u.shape
-    m, n = min(R, Cc), max(R, Cc)
-    ldn = int(lib.thorn_ns_ld(n))
+    ldc = int(lib.thorn_ns_ld(Cc))
     x = u.float()
-    if R > Cc:
-        x = x.mT
     x = x / (x.norm(dim=(-2, -1), keepdim=True) + 1e-8)
-    X = torch.zeros((Bn, m, ldn), dtype=ns_dtype, device="cuda")
-    X[:, :, :n] = x.to(ns_dtype)
+    X = torch.zeros((Bn, R, ldc), dtype=ns_dtype, device="cuda")
+    X[:, :, :Cc] = x.to(ns_dtype)  # original orientation, also for tall matrices
     out = torch.empty((Bn, R, Cc), dtype=ns_dtype, device="cuda")
     wsb = int(lib.thorn_ns_workspace_bytes(Bn, R, Cc))
     ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")

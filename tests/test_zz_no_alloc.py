@@ -29,12 +29,11 @@ def _normalised_input(u):
     from thorn_b200 import _native as N
 
     B, R, Cc = u.shape
-    m, n = min(R, Cc), max(R, Cc)
-    ld = int(N.load().thorn_ns_ld(n))
-    x = u.float().mT if R > Cc else u.float()
+    ld = int(N.load().thorn_ns_ld(Cc))
+    x = u.float()
     x = x / (x.norm(dim=(-2, -1), keepdim=True) + 1e-8)
-    X = torch.zeros((B, m, ld), dtype=torch.float16, device="cuda")
-    X[:, :, :n] = x.half()
+    X = torch.zeros((B, R, ld), dtype=torch.float16, device="cuda")
+    X[:, :, :Cc] = x.half()  # original orientation, also for tall matrices
     return X
 
 

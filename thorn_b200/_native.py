@@ -41,13 +41,13 @@ class NsCastTensor(Structure):
 
 class PnnTensor(Structure):
     _fields_ = [("U", c_void_p), ("row_scale", c_void_p), ("mat_stats", c_void_p),
-                ("batch", c_int64), ("rows", c_int64), ("cols", c_int64), ("scratch", c_void_p)]
+                ("batch", c_int64), ("rows", c_int64), ("cols", c_int64), ("scratch", c_void_p), ("fold", c_int32)]
 
 
 class OrthoPostTensor(Structure):
     _fields_ = [("U", c_void_p), ("p", c_void_p), ("row_scale", c_void_p), ("mat_stats", c_void_p),
                 ("p_normsq", c_void_p), ("batch", c_int64), ("rows", c_int64), ("cols", c_int64), ("lr", c_float),
-                ("scratch", c_void_p)]
+                ("scratch", c_void_p), ("round_u", c_int32)]
 
 
 class SumsqTensor(Structure):

@@ -198,8 +198,6 @@ __device__ __forceinline__ float ordered_sum(float* x, int64_t n, float* red) {
   return block_sum(s, red);
 }
 
-static inline int64_t al16(int64_t b) { return (b + 15) / 16 * 16; }
-
 // Scratch of the momentum pass: counters first, then partial sums.
 struct PreLayout {
   int64_t tr, tc, T;
@@ -430,58 +428,28 @@ __device__ __forceinline__ float cast_u(const thorn_ns_cast_tensor& e, float g, 
 
 template <class P, class S, class U, class X>
 __global__ void __launch_bounds__(kThreads) ns_cast_kernel(const __grid_constant__ CastArgs a) {
-  __shared__ float tile[32][33];
   const int ti = find_tensor(a.pk, blockIdx.x);
   const thorn_ns_cast_tensor& e = a.pk.t[ti];
-  const int64_t local = int64_t(blockIdx.x) - a.pk.start[ti];
-  const bool tall = e.rows > e.cols;
+  const bool vec = a.pk.vec[ti];
+  const Tile t = tile_of(int64_t(blockIdx.x) - a.pk.start[ti], e.rows, e.cols);
+  const float d = sqrtf(e.normsq[t.b]) + 1e-8f;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t c = t.c0 + lane * 8;
+  const int nc = (int)max64(0, min64(8, e.cols - c));
+  if (nc == 0) return;
+  const int64_t ld = ns_ld(e.cols);
   const P* G = (const P*)e.g;
   const S* M = (const S*)e.m;
-  if (!tall) {
-    const bool vec = a.pk.vec[ti];
-    const Tile t = tile_of(local, e.rows, e.cols);
-    const float d = sqrtf(e.normsq[t.b]) + 1e-8f;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t c = t.c0 + lane * 8;
-    const int nc = (int)max64(0, min64(8, e.cols - c));
-    if (nc == 0) return;
-    const int64_t ld = ns_ld(e.cols);
-    for (int rr = warp; rr < kTR; rr += 8) {
-      const int64_t r = t.r0 + rr;
-      if (r >= e.rows) break;
-      const int64_t off = (t.b * e.rows + r) * e.cols + c;
-      float gv[8], mv[8], v[8];
-      load_n(G + off, gv, nc, vec);
-      load_n(M + off, mv, nc, vec);
+  for (int rr = warp; rr < kTR; rr += 8) {
+    const int64_t r = t.r0 + rr;
+    if (r >= e.rows) break;
+    const int64_t off = (t.b * e.rows + r) * e.cols + c;
+    float gv[8], mv[8], v[8];
+    load_n(G + off, gv, nc, vec);
+    load_n(M + off, mv, nc, vec);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) v[k] = (k < nc ? cast_u<P, U>(e, gv[k], mv[k], a.beta1, t.b, r, c + k) : 0.f) / d;
-      store_n((X*)e.x + (t.b * e.rows + r) * ld + c, v, nc, vec);
-    }
-  } else {
-    // 32x32 tiles through shared memory: read rows of u, write rows of u^T
-    const int64_t tr = (e.rows + 31) / 32, tc = (e.cols + 31) / 32;
-    const int64_t b = local / (tr * tc);
-    const int64_t rem = local - b * tr * tc;
-    const int64_t r0 = (rem / tc) * 32, c0 = (rem % tc) * 32;
-    const float d = sqrtf(e.normsq[b]) + 1e-8f;
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-    const int64_t base = b * e.rows * e.cols;
-    for (int k = ty; k < 32; k += 8) {
-      const int64_t r = r0 + k, cc = c0 + tx;
-      float v = 0.f;
-      if (r < e.rows && cc < e.cols) {
-        const int64_t off = base + r * e.cols + cc;
-        v = cast_u<P, U>(e, to_f(G[off]), to_f(M[off]), a.beta1, b, r, cc) / d;
-      }
-      tile[k][tx] = v;
-    }
-    __syncthreads();
-    const int64_t ld = ns_ld(e.rows);
-    X* x = (X*)e.x + b * e.cols * ld;
-    for (int k = ty; k < 32; k += 8) {
-      const int64_t cc = c0 + k, r = r0 + tx;
-      if (cc < e.cols && r < e.rows) x[cc * ld + r] = from_f<X>(tile[tx][k]);
-    }
+    for (int k = 0; k < 8; ++k) v[k] = (k < nc ? cast_u<P, U>(e, gv[k], mv[k], a.beta1, t.b, r, c + k) : 0.f) / d;
+    store_n((X*)e.x + (t.b * e.rows + r) * ld + c, v, nc, vec);
   }
 }
 
@@ -538,6 +506,13 @@ __global__ void __launch_bounds__(kThreads) pnn_stats_kernel(const __grid_consta
       e.mat_stats[2 * b] = s0;
       e.mat_stats[2 * b + 1] = s1;
     }
+    if (e.fold) {
+      const float gscale = sqrtf(s0) / fmaxf(sqrtf(s1), a.eps);
+      for (int64_t i = threadIdx.x; i < e.rows; i += blockDim.x) {
+        float* q = e.row_scale + b * e.rows + i;
+        *q = __ldcg(q) * gscale;
+      }
+    }
   }
 }
 
@@ -575,7 +550,7 @@ __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_const
     load_n((const P*)e.p + off, pv, nc, vec);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      float u = rnd<P>(uv[k]);
+      float u = e.round_u ? rnd<P>(uv[k]) : uv[k];
       if (e.row_scale != nullptr) u = u * scale;
       if (a.wd > 0.f && u * pv[k] >= 0.f) u = u + a.wd * pv[k];
       pv[k] = rnd<P>(pv[k] - e.lr * u);
@@ -820,11 +795,7 @@ extern "C" int thorn_ns_cast_multi(const thorn_ns_cast_tensor* ts, int n, int p_
   }
   cudaStream_t st = (cudaStream_t)stream;
   int rc = THORN_OK;
-  auto blocks = [](const thorn_ns_cast_tensor& e) -> int64_t {
-    if (e.batch <= 0 || e.rows <= 0 || e.cols <= 0) return 0;
-    if (e.rows > e.cols) return e.batch * cdiv(e.rows, 32) * cdiv(e.cols, 32);
-    return tiles_of(e.batch, e.rows, e.cols);
-  };
+  auto blocks = [](const thorn_ns_cast_tensor& e) { return tiles_of(e.batch, e.rows, e.cols); };
   auto vec = [](const thorn_ns_cast_tensor& e) {
     return (e.cols % 8) == 0 && aligned16(e.g) && aligned16(e.m) && aligned16(e.x);
   };

@@ -3,8 +3,9 @@
 // One persistent kernel serves every product of the NS iteration:
 //   D = alpha * A @ op(B) + beta * C          (fp32 accumulate in TMEM)
 //   D2 = D + diag2 * I                         (optional second output)
-// A is K-major ([rows, K] row-major).  B is either K-major ([N, K], used for
-// X X^T and for products with a symmetric right operand) or MN-major
+// A is K-major ([M, K] row-major) or MN-major ([K, M], the Gram product of a
+// tall input kept in its original orientation).  B is either K-major ([N, K],
+// used for X X^T and for products with a symmetric right operand) or MN-major
 // ([K, N], used for Q @ X and B @ X).  With `sym`, only 128x BN tiles that
 // touch the lower triangle are computed; each lower element is stored at
 // (r, c) and mirrored to (c, r), so the output is exactly symmetric.  With
@@ -158,10 +159,10 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t
   return d;
 }
 
-// Instruction descriptor: kind::f16, fp32 accumulate, A K-major.
-__host__ __device__ constexpr uint32_t idesc_f16(int bn, bool bf16, bool b_mn) {
-  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((b_mn ? 1u : 0u) << 16) |
-         ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+// Instruction descriptor: kind::f16, fp32 accumulate; A/B K-major (0) or MN-major (1).
+__host__ __device__ constexpr uint32_t idesc_f16(int bn, bool bf16, bool a_mn, bool b_mn) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((a_mn ? 1u : 0u) << 15) |
+         ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
 template <int BN>
@@ -188,7 +189,7 @@ __device__ __forceinline__ void decode_tile(const Params& p, int t, int& b, int&
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int BN, bool B_MN, class T>
+template <int BN, bool A_MN, bool B_MN, class T>
 __global__ void __launch_bounds__(kThreadsG, 1) ns_gemm_kernel(const __grid_constant__ Params p) {
   using C_ = Cfg<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -243,7 +244,14 @@ __global__ void __launch_bounds__(kThreadsG, 1) ns_gemm_kernel(const __grid_cons
           if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.err)) break;
           const uint32_t fb = smem_u32(&full[stage]);
           mbar_expect_tx(fb, C_::kStageBytes);
-          tma_load_3d(smem_u32(sA + stage * C_::kABytes), &p.tmA, fb, kb * BK, tm * BM, b);
+          if (!A_MN) {
+            tma_load_3d(smem_u32(sA + stage * C_::kABytes), &p.tmA, fb, kb * BK, tm * BM, b);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BM / 64; ++c)
+              tma_load_3d(smem_u32(sA + stage * C_::kABytes + c * (64 * BK * 2)), &p.tmA, fb, tm * BM + c * 64,
+                          kb * BK, b);
+          }
           if (!B_MN) {
             tma_load_3d(smem_u32(sB + stage * C_::kBBytes), &p.tmB, fb, kb * BK, tn * BN, b);
           } else {
@@ -262,7 +270,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) ns_gemm_kernel(const __grid_cons
   } else if (warp == 1) {
     // ------------------------------ MMA issuer -----------------------------
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(BN, sizeof(T) == 2 && !std::is_same<T, __half>::value, B_MN);
+      constexpr uint32_t idesc = idesc_f16(BN, sizeof(T) == 2 && !std::is_same<T, __half>::value, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -283,7 +291,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) ns_gemm_kernel(const __grid_cons
           const uint32_t b0 = smem_u32(sB + stage * C_::kBBytes);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t ad = sdesc(a0 + kk * 32, 16, 1024);
+            const uint64_t ad = A_MN ? sdesc(a0 + kk * 2048, 64 * BK * 2, 1024) : sdesc(a0 + kk * 32, 16, 1024);
             const uint64_t bd = B_MN ? sdesc(b0 + kk * 2048, 64 * BK * 2, 1024) : sdesc(b0 + kk * 32, 16, 1024);
             umma(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
@@ -457,6 +465,7 @@ static int make_map(CUtensorMap* m, const void* base, int dtype, int64_t inner, 
 struct GemmOp {
   const void* A = nullptr;
   int64_t a_ld = 0, a_bs = 0;
+  bool a_mn = false;
   const void* B = nullptr;
   int64_t b_ld = 0, b_bs = 0;
   bool b_mn = false;
@@ -474,18 +483,33 @@ struct GemmOp {
 // Algorithmic work of the GEMMs issued so far (for roofline reporting).
 static std::atomic<uint64_t> g_flops_dense{0}, g_flops_exec{0};
 
-template <int BN, bool BMN, class T>
+template <int BN, bool AMN, bool BMN, class T>
 static int launch_gemm(gemm::Params& prm, int grid, cudaStream_t st) {
   using C_ = gemm::Cfg<BN>;
   static std::once_flag attr_once[64];
   int dev = 0;
   cudaGetDevice(&dev);
   std::call_once(attr_once[dev & 63], []() {
-    cudaFuncSetAttribute(gemm::ns_gemm_kernel<BN, BMN, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::kSmem);
+    cudaFuncSetAttribute(gemm::ns_gemm_kernel<BN, AMN, BMN, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         C_::kSmem);
   });
-  gemm::ns_gemm_kernel<BN, BMN, T><<<grid, gemm::kThreadsG, C_::kSmem, st>>>(prm);
+  gemm::ns_gemm_kernel<BN, AMN, BMN, T><<<grid, gemm::kThreadsG, C_::kSmem, st>>>(prm);
   count_launch();
   return check_launch();
+}
+
+template <class T>
+static int launch_any(const GemmOp& op, int BN, gemm::Params& prm, int grid, cudaStream_t st) {
+  // instantiated operand layouts: (A K, B K), (A K, B MN), (A MN, B MN)
+  if (op.a_mn && !op.b_mn) return THORN_ERR_ARG;
+  if (BN == 256) {
+    if (op.a_mn) return launch_gemm<256, true, true, T>(prm, grid, st);
+    if (op.b_mn) return launch_gemm<256, false, true, T>(prm, grid, st);
+    return launch_gemm<256, false, false, T>(prm, grid, st);
+  }
+  if (op.a_mn) return launch_gemm<128, true, true, T>(prm, grid, st);
+  if (op.b_mn) return launch_gemm<128, false, true, T>(prm, grid, st);
+  return launch_gemm<128, false, false, T>(prm, grid, st);
 }
 
 int run_gemm(const GemmOp& op, int dtype, int* err, cudaStream_t st) {
@@ -502,7 +526,8 @@ int run_gemm(const GemmOp& op, int dtype, int* err, cudaStream_t st) {
   Params prm;
   memset(&prm, 0, sizeof(prm));
   const int BN = (op.N > 128) ? 256 : 128;
-  int rc = make_map(&prm.tmA, op.A, dtype, op.K, op.M, op.batch, op.a_ld, op.a_bs, BK, BM);
+  int rc = op.a_mn ? make_map(&prm.tmA, op.A, dtype, op.M, op.K, op.batch, op.a_ld, op.a_bs, 64, BK)
+                   : make_map(&prm.tmA, op.A, dtype, op.K, op.M, op.batch, op.a_ld, op.a_bs, BK, BM);
   if (rc) return rc;
   if (op.b_mn) rc = make_map(&prm.tmB, op.B, dtype, op.N, op.K, op.batch, op.b_ld, op.b_bs, 64, BK);
   else rc = make_map(&prm.tmB, op.B, dtype, op.K, op.N, op.batch, op.b_ld, op.b_bs, BK, BN);
@@ -547,13 +572,8 @@ int run_gemm(const GemmOp& op, int dtype, int* err, cudaStream_t st) {
   const double exec = 2.0 * BM * (double)BN * (prm.num_kb * (double)BK) * total;
   g_flops_dense.fetch_add((uint64_t)dense);
   g_flops_exec.fetch_add((uint64_t)exec);
-  const bool bf = dtype == THORN_BF16;
-  if (BN == 256) {
-    if (op.b_mn) return bf ? launch_gemm<256, true, __nv_bfloat16>(prm, grid, st) : launch_gemm<256, true, __half>(prm, grid, st);
-    return bf ? launch_gemm<256, false, __nv_bfloat16>(prm, grid, st) : launch_gemm<256, false, __half>(prm, grid, st);
-  }
-  if (op.b_mn) return bf ? launch_gemm<128, true, __nv_bfloat16>(prm, grid, st) : launch_gemm<128, true, __half>(prm, grid, st);
-  return bf ? launch_gemm<128, false, __nv_bfloat16>(prm, grid, st) : launch_gemm<128, false, __half>(prm, grid, st);
+  return dtype == THORN_BF16 ? launch_any<__nv_bfloat16>(op, BN, prm, grid, st)
+                             : launch_any<__half>(op, BN, prm, grid, st);
 }
 
 }  // namespace thorn
@@ -647,6 +667,27 @@ extern "C" int thorn_ns_batched(const void* x, void* out, void* workspace, int64
     op.beta = beta; op.trans_out = trans;
     return run_gemm(op, ns_dtype, err_flag, st);
   };
+  // The same two products for a tall input kept in its original orientation:
+  // u is [n, m] (ld ldm) and X = u^T.  X X^T = u^T u reads u MN-major for both
+  // operands; Q @ X = Q u^T reads u as a K-major second operand.
+  auto gramm_tall = [&](const void* U, void* D) {
+    GemmOp op;
+    op.A = U; op.a_ld = ldm; op.a_bs = n * ldm; op.a_mn = true;
+    op.B = U; op.b_ld = ldm; op.b_bs = n * ldm; op.b_mn = true;
+    op.D = D; op.d_ld = ldm; op.d_bs = m * ldm;
+    op.M = m; op.N = m; op.K = n; op.batch = B;
+    op.sym = true;
+    return run_gemm(op, ns_dtype, err_flag, st);
+  };
+  auto qx_tall = [&](const void* Q, const void* U, void* D, int64_t d_ld, int64_t d_bs, bool trans) {
+    GemmOp op;
+    op.A = Q; op.a_ld = ldm; op.a_bs = m * ldm;
+    op.B = U; op.b_ld = ldm; op.b_bs = n * ldm; op.b_mn = false;
+    op.D = D; op.d_ld = d_ld; op.d_bs = d_bs;
+    op.M = m; op.N = n; op.K = m; op.batch = B;
+    op.trans_out = trans;
+    return run_gemm(op, ns_dtype, err_flag, st);
+  };
 #define NS_TRY(expr)          \
   do {                        \
     rc = (expr);              \
@@ -661,14 +702,17 @@ extern "C" int thorn_ns_batched(const void* x, void* out, void* workspace, int64
     void* Qb[2] = {mbase + 2 * L.ms, mbase + 3 * L.ms};
     void* RZ = mbase + 4 * L.ms;
     const void* X = x;
+    bool x_is_input_tall = tall;  // X is still the caller's tall input (original orientation)
     int xi = 0, qi = 0;
-    NS_TRY(gramm(X, ldn, n, R));
+    NS_TRY(tall ? gramm_tall(X, R) : gramm(X, ldn, n, R));
     for (int i = 0; i < iters; ++i) {
       const float a = (float)coeffs[3 * i], b = (float)coeffs[3 * i + 1], c = (float)coeffs[3 * i + 2];
       const bool rs = in_restarts(i);
       if (rs && i != 0) {
-        NS_TRY(qx(Qb[qi], X, ldn, n, nullptr, 0.f, Xb[xi], ldn, m * ldn, false));
+        if (x_is_input_tall) NS_TRY(qx_tall(Qb[qi], X, Xb[xi], ldn, m * ldn, false));
+        else NS_TRY(qx(Qb[qi], X, ldn, n, nullptr, 0.f, Xb[xi], ldn, m * ldn, false));
         X = Xb[xi];
+        x_is_input_tall = false;
         xi ^= 1;
         NS_TRY(gramm(X, ldn, n, R));
       }
@@ -686,7 +730,8 @@ extern "C" int thorn_ns_batched(const void* x, void* out, void* workspace, int64
     }
     if (iters == 0) return THORN_ERR_ARG;
     // out = Q @ X ; stored transposed for tall inputs (X.mT @ Q)
-    NS_TRY(qx(Qb[qi], X, ldn, n, nullptr, 0.f, out, tall ? (int64_t)m : (int64_t)n, (int64_t)m * n, tall));
+    if (x_is_input_tall) NS_TRY(qx_tall(Qb[qi], X, out, (int64_t)m, (int64_t)m * n, true));
+    else NS_TRY(qx(Qb[qi], X, ldn, n, nullptr, 0.f, out, tall ? (int64_t)m : (int64_t)n, (int64_t)m * n, tall));
   } else {
     void* Xb[2] = {ws, ws + L.ms};
     void* A = ws + 2 * L.ms;

@@ -158,6 +158,25 @@ def _local(t):
     return t.to_local() if isinstance(t, DTensor) else t
 
 
+def _sharded_gains(p: DTensor):
+    """Magnitude gains of a Shard(0) parameter as DTensors."""
+    mesh, pl = p.device_mesh, p.placements
+    loc = p.to_local()
+    row_shape = (*p.shape[:-1], 1)
+    rg = torch.full((*loc.shape[:-1], 1), LN_E_SUB_1, dtype=p.dtype, device=loc.device)
+    row = DTensor.from_local(rg, mesh, pl, run_check=False, shape=row_shape,
+                             stride=torch.empty(row_shape, device="meta").stride())
+    col_shape = (*p.shape[:-2], 1, p.shape[-1])
+    if p.ndim == 2:
+        cg = torch.full(col_shape, LN_E_SUB_1, dtype=p.dtype, device=loc.device)
+        col = DTensor.from_local(cg, mesh, [Replicate()] * mesh.ndim, run_check=False)
+    else:  # batch dimension split: each rank holds whole matrices and their column gains
+        cg = torch.full((*loc.shape[:-2], 1, p.shape[-1]), LN_E_SUB_1, dtype=p.dtype, device=loc.device)
+        col = DTensor.from_local(cg, mesh, pl, run_check=False, shape=col_shape,
+                                 stride=torch.empty(col_shape, device="meta").stride())
+    return row, col
+
+
 def _mat_view(shape) -> tuple[int, int, int]:
     """(batch, rows, cols) view of a tensor: leading dims are a batch (thorn.py:628-633)."""
     if len(shape) >= 2:
@@ -168,33 +187,41 @@ def _mat_view(shape) -> tuple[int, int, int]:
 
 
 class _Arena:
-    """Carves fp32 scratch views out of two buffers: one zeroed, one not."""
+    """Carves fp32 scratch views out of a few buffers ("regions").
+
+    Region "z" is zero-filled; every other region is uninitialised.  Values
+    that are all-reduced together are allocated from one region so a single
+    collective covers them.
+    """
 
     def __init__(self):
-        self.zero_n = 0
-        self.raw_n = 0
-        self.req = []
+        self.sizes: dict = {}
+        self.bufs: dict = {}
 
-    def zeros(self, n):
-        off = self.zero_n
-        self.zero_n += (n + 3) // 4 * 4
-        return ("z", off, n)
+    def alloc(self, n, region="r"):
+        off = self.sizes.get(region, 0)
+        self.sizes[region] = off + (n + 3) // 4 * 4
+        return (region, off, n)
 
     def empty(self, n):
-        off = self.raw_n
-        self.raw_n += (n + 3) // 4 * 4
-        return ("r", off, n)
+        return self.alloc(n, "r")
+
+    def zeros(self, n):
+        return self.alloc(n, "z")
 
     def materialize(self, device):
-        self.zbuf = torch.zeros(max(4, self.zero_n), dtype=torch.float32, device=device)
-        self.rbuf = torch.empty(max(4, self.raw_n), dtype=torch.float32, device=device)
+        for reg, n in self.sizes.items():
+            make = torch.zeros if reg == "z" else torch.empty
+            self.bufs[reg] = make(max(4, n), dtype=torch.float32, device=device)
+
+    def region(self, name):
+        return self.bufs[name][:self.sizes[name]]
 
     def get(self, h):
         if h is None:
             return None
-        kind, off, n = h
-        buf = self.zbuf if kind == "z" else self.rbuf
-        return buf[off:off + n]
+        reg, off, n = h
+        return self.bufs[reg][off:off + n]
 
     def ptr(self, h):
         t = self.get(h)
@@ -306,9 +333,14 @@ class THORN(Optimizer):
             state["variance"] = torch.zeros_like(p, dtype=sdt)
         if cfg.decouple_md:
             if p.ndim > 1 and cfg.split_gain:
-                state["row_gain"] = torch.full((*p.shape[:-1], 1), LN_E_SUB_1, dtype=p.dtype, device=p.device)
-                state["col_gain"] = torch.full((*p.shape[:-2], 1, *p.shape[-1:]), LN_E_SUB_1, dtype=p.dtype,
-                                               device=p.device)
+                if isinstance(p, DTensor) and not all(isinstance(pl, Replicate) for pl in p.placements):
+                    # Shard(0): row gains are split like the rows; column gains of a 2-D matrix are
+                    # replicated (the reference creates them at the global shape, thorn.py:1604-1605)
+                    state["row_gain"], state["col_gain"] = _sharded_gains(p)
+                else:
+                    state["row_gain"] = torch.full((*p.shape[:-1], 1), LN_E_SUB_1, dtype=p.dtype, device=p.device)
+                    state["col_gain"] = torch.full((*p.shape[:-2], 1, *p.shape[-1:]), LN_E_SUB_1, dtype=p.dtype,
+                                                   device=p.device)
                 for k in ("row_gain", "col_gain"):
                     state[f"{k}_moment"] = torch.zeros_like(state[k])
                     state[f"{k}_variance"] = torch.zeros_like(state[k])
@@ -330,9 +362,12 @@ class THORN(Optimizer):
             state = self.state[p]
             if "step" not in state:
                 self._init_state(p, state, cfg, gdict)
-            if isinstance(p.data, DTensor) and cfg.orthogonalize and \
-                    not all(isinstance(pl, Replicate) for pl in p.placements):
+            is_sharded = isinstance(p.data, DTensor) and not all(isinstance(pl, Replicate) for pl in p.placements)
+            if is_sharded and cfg.orthogonalize:
                 sharded.append(p)
+            elif is_sharded and cfg.decouple_md:
+                raise NotImplementedError("decouple_md on sharded (R)AdamW parameters is not implemented by "
+                                          "thorn_b200")
             else:
                 local.append(p)
         if sharded:
@@ -375,7 +410,12 @@ class THORN(Optimizer):
         return t
 
     # ------------------------------------------------------ shared helpers
-    def _items(self, params, cfg, arena: _Arena, ortho: bool):
+    def _items(self, params, cfg, arena: _Arena, ortho: bool, reduce_regions: bool = False):
+        """Per-parameter launch records.  With ``reduce_regions`` the values the
+        sharded path all-reduces (sums of squares, column-gain and scalar-gain
+        gradients) are laid out contiguously in regions "red1" / "red2"."""
+        red1 = "red1" if reduce_regions else "r"
+        red2 = "red2" if reduce_regions else "r"
         items = []
         for p in params:
             st = self.state[p]
@@ -395,19 +435,20 @@ class THORN(Optimizer):
             N.dtype_code(it.pdt), N.dtype_code(it.sdt)
             if g.dtype != it.pdt:
                 raise TypeError(f"gradient dtype {g.dtype} differs from parameter dtype {it.pdt}")
-            it.normsq = arena.empty(it.B) if ortho else None
+            it.normsq = arena.alloc(it.B, red1) if ortho else None
             it.split = "row_gain" in st
             it.scalar = "gain" in st
             if cfg.decouple_md:
                 nr, nc = (it.B * it.R, it.B * it.C) if it.split else (1, 1)
                 it.rs, it.sig_r, it.rs_new = arena.empty(nr), arena.empty(nr), arena.empty(nr)
-                it.rgs = arena.empty(nr)
+                # row-gain gradients are local to the rows a rank holds; a scalar gain sums everything
+                it.rgs = arena.empty(nr) if it.split else arena.alloc(1, red1)
                 if it.split:
                     it.cs, it.sig_c, it.cs_new = arena.empty(nc), arena.empty(nc), arena.empty(nc)
-                    it.cgs = arena.empty(nc)
+                    it.cgs = arena.alloc(nc, red1)
                 else:
                     it.cs = it.sig_c = it.cs_new = it.cgs = None
-                it.pnorm = arena.empty(it.B)
+                it.pnorm = arena.alloc(it.B, red2)
             items.append(it)
         return items
 
@@ -549,15 +590,14 @@ class THORN(Optimizer):
         restarts = (ctypes.c_int32 * max(1, len(rs)))(*rs)
         for ci, (R, C, pdt, sdt, its) in enumerate(chunks):
             nb = sum(it.B for it in its)
-            m, n = min(R, C), max(R, C)
-            ldn = int(lib.thorn_ns_ld(n))
-            X = torch.empty((nb, m, ldn), dtype=self.ns_dtype, device=dev)
+            ldc = int(lib.thorn_ns_ld(C))
+            X = torch.empty((nb, R, ldc), dtype=self.ns_dtype, device=dev)
             U = torch.empty((nb, R, C), dtype=self.ns_dtype, device=dev)
             casts, off = [], 0
             esz = X.element_size()
             for it in its:
                 casts.append(N.NsCastTensor(it.g.data_ptr(), _local(it.state["moment"]).data_ptr(), arena.ptr(it.normsq),
-                                            X.data_ptr() + off * m * ldn * esz, it.B, it.R, it.C,
+                                            X.data_ptr() + off * R * ldc * esz, it.B, it.R, it.C,
                                             arena.ptr(it.rs) if md else None, arena.ptr(it.cs) if md else None,
                                             1 if (md and not it.split) else 0, 1 if (md and not write_grad) else 0))
                 off += it.B
@@ -583,7 +623,7 @@ class THORN(Optimizer):
                 rsh, msh = pnn_h[ci]
                 row_scale, mat_stats = arena.get(rsh), arena.get(msh)
                 (sp,) = self._scratch(dev, [lib.thorn_pnn_scratch_bytes(nb, R)])
-                pt = N.PnnTensor(U.data_ptr(), row_scale.data_ptr(), mat_stats.data_ptr(), nb, R, C, sp)
+                pt = N.PnnTensor(U.data_ptr(), row_scale.data_ptr(), mat_stats.data_ptr(), nb, R, C, sp, 0)
                 N.check(lib.thorn_pnn_stats_multi(N.array(N.PnnTensor, [pt]), 1, ns_code, N.dtype_code(pdt), stream),
                         "pnn_stats_multi")
             posts, off = [], 0
@@ -595,7 +635,7 @@ class THORN(Optimizer):
                     U.data_ptr() + off * R * C * usz, it.p.data_ptr(),
                     None if row_scale is None else row_scale.data_ptr() + off * R * 4,
                     None if mat_stats is None else mat_stats.data_ptr() + off * 2 * 4,
-                    arena.ptr(it.pnorm) if md else None, it.B, it.R, it.C, lr_eff, sp if md else None))
+                    arena.ptr(it.pnorm) if md else None, it.B, it.R, it.C, lr_eff, sp if md else None, 1))
                 off += it.B
             N.check(lib.thorn_ortho_post_multi(N.array(N.OrthoPostTensor, posts), len(posts), ns_code,
                                                N.dtype_code(pdt), float(cfg.weight_decay), stream), "ortho_post_multi")

@@ -1,0 +1,322 @@
+"""FSDP2 / DTensor ``Shard(0)`` path of the orthogonalized group.
+
+Replaces the reference's ``_DistributedTHORNState`` (thorn.py:979-1186),
+``_assign_params`` (thorn.py:1333-1374) and ``_sharded_ortho_step``
+(thorn.py:1459-1581).  The reference gathers each matrix's fp32 momentum rows
+to an owner rank with one ``dist.gather`` per matrix, runs Newton-Schulz there
+and scatters fp32 results back.  Here, per step:
+
+1. every rank runs the momentum pass on its own rows (one multi-tensor launch)
+   and the per-matrix partial sums of u^2 (plus the decouple_md column-gain
+   partials) are added with a single all-reduce;
+2. every rank normalises its rows by the global norm and casts them to the NS
+   operand type, writing straight into the owner's NS input buffer when it is
+   the owner, else into a send slab;
+3. one batched NCCL point-to-point exchange moves all slabs to their owners
+   (half the bytes of the reference's fp32 gather);
+4. owners run batched Newton-Schulz (+ per-neuron-norm statistics with the
+   row scale folded into one factor per row);
+5. one batched exchange returns the 16-bit result rows and the fp32 row
+   factors;
+6. every rank applies the update to its own rows (and, with decouple_md,
+   all-reduces ||p||^2 for the renorm).
+
+Owners are chosen by longest-processing-time over the reference's NS FLOP
+estimate (thorn.py:1001-1007), deterministically on every rank.  Parameters of
+rank > 2 (conv kernels) split along their batch dimension hold whole matrices
+on each rank and take the local path.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+from torch.distributed.tensor import DTensor, Replicate, Shard
+
+from . import _native as N
+
+
+def shard_group(p: DTensor, rank: int):
+    """Ranks (in shard order) and process group of a sharded parameter (thorn.py:1009-1021)."""
+    if p.placements == (Shard(dim=0),):
+        return [int(r) for r in p.device_mesh.mesh.tolist()], p.device_mesh.get_group(mesh_dim=0)
+    if p.placements == (Replicate(), Shard(dim=0)):
+        for row in p.device_mesh.mesh:
+            if rank in row.tolist():
+                return [int(r) for r in row.tolist()], p.device_mesh.get_group(mesh_dim=1)
+        raise ValueError("rank not found in the shard mesh")
+    raise ValueError(f"Unsupported placements {p.placements}")
+
+
+def ns_flops(rows: int, cols: int, iters: int) -> int:
+    """The reference's per-matrix NS cost estimate (thorn.py:1001-1007)."""
+    m, n = min(rows, cols), max(rows, cols)
+    return iters * ((m ** 3) * 2 + (m ** 2 * n) * 4 + m * n * 2 + m ** 2 * 3)
+
+
+def assign_owners(flops: list[int], world: int) -> list[int]:
+    """Longest-processing-time assignment: heaviest matrix first, to the least-loaded rank.
+
+    Ties go to the lower matrix index and the lower rank, so every rank computes
+    the same assignment.  (The reference deals sorted matrices round-robin,
+    thorn.py:1348-1372; both balance the Llama sets exactly.)
+    """
+    order = sorted(range(len(flops)), key=lambda j: (-flops[j], j))
+    load = [0] * world
+    owner = [0] * len(flops)
+    for j in order:
+        r = min(range(world), key=lambda k: (load[k], k))
+        owner[j] = r
+        load[r] += flops[j]
+    return owner
+
+
+@dataclass
+class Slab:
+    """One point-to-point message: ``tensor`` goes to / comes from shard index ``peer``."""
+
+    tensor: torch.Tensor
+    peer: int
+
+
+def exchange(sends: list[Slab], recvs: list[Slab], ranks: list[int], group) -> None:
+    """All messages of one exchange in a single batched P2P call.
+
+    Callers list messages in a canonical order (matrix index ascending, then
+    peer ascending), so the sends from rank a to rank b and b's receives from a
+    appear in the same order on both sides, which is how NCCL matches them.
+    """
+    ops = [dist.P2POp(dist.isend, s.tensor, ranks[s.peer], group) for s in sends]
+    ops += [dist.P2POp(dist.irecv, r.tensor, ranks[r.peer], group) for r in recvs]
+    if ops:
+        for w in dist.batch_isend_irecv(ops):
+            w.wait()
+
+
+def plan_gather(owners: list[int], me: int, world: int, my_rows, owner_rows):
+    """Messages that bring every matrix's row slabs to its owner.
+
+    ``my_rows(j)``: this rank's slab of matrix j (a send buffer, for j it does
+    not own); ``owner_rows(j, s)``: where slab s of an owned matrix j lands.
+    """
+    sends = [Slab(my_rows(j), owners[j]) for j in range(len(owners)) if owners[j] != me]
+    recvs = [Slab(owner_rows(j, s), s) for j in range(len(owners)) if owners[j] == me
+             for s in range(world) if s != me]
+    return sends, recvs
+
+
+def plan_scatter(owners: list[int], me: int, world: int, owner_parts, my_parts):
+    """Messages that return result slabs from owners.
+
+    ``owner_parts(j, s)``: list of tensors of owned matrix j destined for shard
+    s; ``my_parts(j)``: matching receive buffers for a matrix this rank does
+    not own.
+    """
+    sends = [Slab(t, s) for j in range(len(owners)) if owners[j] == me
+             for s in range(world) if s != me for t in owner_parts(j, s)]
+    recvs = [Slab(t, owners[j]) for j in range(len(owners)) if owners[j] != me for t in my_parts(j)]
+    return sends, recvs
+
+
+def sharded_ortho_step(opt, params, cfg) -> None:
+    """One step of the orthogonalized group for DTensor ``Shard(0)`` parameters."""
+    from .optimizer import _Arena, _local
+
+    rank = dist.get_rank()
+    ranks, group = shard_group(params[0], rank)
+    mesh0 = params[0].device_mesh
+    for p in params:
+        if p.device_mesh != mesh0:
+            raise ValueError("All parameters must be on the same mesh.")
+        shard_group(p, rank)
+    world, me = len(ranks), ranks.index(rank)
+    mats, batched = [], []
+    for p in params:
+        if p.ndim == 2:
+            if p.shape[0] % world:
+                raise NotImplementedError(f"uneven Shard(0) split: {p.shape[0]} rows over {world} ranks")
+            mats.append(p)
+        else:
+            batched.append(p)  # whole (in, k) matrices on every rank
+    if batched:
+        with torch.cuda.device(_local(batched[0]).device):
+            opt._ortho_local(batched, cfg)
+    if not mats:
+        return
+    dev = _local(mats[0]).device
+    with torch.cuda.device(dev):
+        _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, _Arena, _local)
+
+
+def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local):
+    lib = N.load()
+    stream = N.stream_of(dev)
+    err = opt._err_flag(dev)
+    md = cfg.decouple_md
+    arena = Arena()
+    items = opt._items(mats, cfg, arena, ortho=True, reduce_regions=True)
+    b1 = float(cfg.betas[0])
+    ns_dt = opt.ns_dtype
+    ns_code = N.dtype_code(ns_dt)
+    esz = torch.empty((), dtype=ns_dt).element_size()
+    rows_g = [it.R * world for it in items]  # global rows
+    for it in items:
+        if it.C % 8:
+            raise NotImplementedError("sharded NS needs a column count that is a multiple of 8")
+        if not it.apply:
+            raise NotImplementedError("update_rate > 1 is not implemented for sharded parameters")
+    owners = assign_owners([ns_flops(rows_g[j], it.C, cfg.iters) for j, it in enumerate(items)], world)
+
+    # owned matrices, batched by (global shape, dtypes)
+    buckets: dict = {}
+    for j, it in enumerate(items):
+        if owners[j] == me:
+            buckets.setdefault((rows_g[j], it.C, it.pdt, it.sdt), []).append(j)
+    chunks = []
+    for (R, C, pdt, sdt), js in buckets.items():
+        cap = max(1, opt.polar_decomp_batch_size // max(1, R * C)) if opt.polar_decomp_batch_size > 0 else 1
+        for i in range(0, len(js), cap):
+            chunks.append((R, C, pdt, sdt, js[i:i + cap]))
+    pnn_h = {}
+    for ci, (R, C, pdt, sdt, js) in enumerate(chunks):
+        if cfg.needs_pnn(R, C):
+            pnn_h[ci] = (arena.empty(len(js) * R), arena.empty(2 * len(js)))
+    arena.materialize(dev)
+
+    # 1. momentum pass on local rows, then one all-reduce of the partial sums
+    if md:
+        opt._md_prep(items, arena, new=False, stream=stream)
+    write_grad = 1 if (md and not cfg.none_grad) else 0
+    scr = opt._scratch(dev, [lib.thorn_ortho_pre_scratch_bytes(it.B, it.R, it.C, 1 if md else 0) for it in items])
+    by_dt: dict = {}
+    for it, sp in zip(items, scr):
+        by_dt.setdefault((it.pdt, it.sdt), []).append(N.OrthoPreTensor(
+            it.p.data_ptr() if md else None, it.g.data_ptr(), _local(it.state["moment"]).data_ptr(),
+            arena.ptr(it.normsq), it.B, it.R, it.C, arena.ptr(it.rs) if md else None,
+            arena.ptr(it.cs) if md else None, 1 if (md and not it.split) else 0,
+            arena.ptr(it.rgs) if md else None, arena.ptr(it.cgs) if md else None, sp))
+    for (pdt, sdt), ts in by_dt.items():
+        udt = pdt if pdt == sdt else torch.float32
+        N.check(lib.thorn_ortho_pre_multi(N.array(N.OrthoPreTensor, ts), len(ts), N.dtype_code(pdt),
+                                          N.dtype_code(sdt), N.dtype_code(udt), b1, 1 if md else 0, write_grad,
+                                          stream), "ortho_pre_multi")
+    dist.all_reduce(arena.region("red1"), group=group)
+    if md:
+        opt._md_gains(items, cfg, arena, stream)
+
+    # 2. normalised rows -> owner buffers / send slabs
+    X = {}
+    U = {}
+    slot = {}  # j -> (chunk index, position in chunk)
+    for ci, (R, C, pdt, sdt, js) in enumerate(chunks):
+        X[ci] = torch.empty((len(js), R, C), dtype=ns_dt, device=dev)
+        U[ci] = torch.empty((len(js), R, C), dtype=ns_dt, device=dev)
+        for k, j in enumerate(js):
+            slot[j] = (ci, k)
+    send_rows = {}
+    n_send = sum(it.R * it.C for j, it in enumerate(items) if owners[j] != me)
+    send_buf = torch.empty(max(1, n_send), dtype=ns_dt, device=dev)
+    off = 0
+    for j, it in enumerate(items):
+        if owners[j] != me:
+            send_rows[j] = send_buf[off:off + it.R * it.C].view(it.R, it.C)
+            off += it.R * it.C
+
+    def owner_rows(j, s):
+        ci, k = slot[j]
+        r = items[j].R
+        return X[ci][k, s * r:(s + 1) * r]
+
+    casts: dict = {}
+    for j, it in enumerate(items):
+        dst = owner_rows(j, me) if owners[j] == me else send_rows[j]
+        casts.setdefault((it.pdt, it.sdt), []).append(N.NsCastTensor(
+            it.g.data_ptr(), _local(it.state["moment"]).data_ptr(), arena.ptr(it.normsq), dst.data_ptr(),
+            it.B, it.R, it.C, arena.ptr(it.rs) if md else None, arena.ptr(it.cs) if md else None,
+            1 if (md and not it.split) else 0, 1 if (md and not write_grad) else 0))
+    for (pdt, sdt), ts in casts.items():
+        udt = pdt if pdt == sdt else torch.float32
+        N.check(lib.thorn_ns_cast_multi(N.array(N.NsCastTensor, ts), len(ts), N.dtype_code(pdt), N.dtype_code(sdt),
+                                        N.dtype_code(udt), ns_code, b1, stream), "ns_cast_multi")
+
+    # 3. slabs to owners
+    sends, recvs = plan_gather(owners, me, world, lambda j: send_rows[j], owner_rows)
+    exchange(sends, recvs, ranks, group)
+    del send_buf, send_rows
+
+    # 4. Newton-Schulz (+ pnn factors) on owned matrices
+    coeffs = (N.ctypes.c_double * (3 * max(1, cfg.iters)))(*[x for abc in cfg.coeffs[:cfg.iters] for x in abc])
+    rs_ = list(cfg.restarts)
+    restarts = (N.ctypes.c_int32 * max(1, len(rs_)))(*rs_)
+    factors = {}
+    for ci, (R, C, pdt, sdt, js) in enumerate(chunks):
+        nb = len(js)
+        wsb = int(lib.thorn_ns_workspace_bytes(nb, R, C))
+        ws = torch.empty(max(256, wsb), dtype=torch.uint8, device=dev)
+        if opt.profile_ns is not None:
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev0.record()
+            f0 = N.gemm_flops()
+        N.check(lib.thorn_ns_batched(X[ci].data_ptr(), U[ci].data_ptr(), ws.data_ptr(), wsb, nb, R, C, ns_code,
+                                     coeffs, cfg.iters, restarts, len(rs_), err.data_ptr(), stream), "ns_batched")
+        if opt.profile_ns is not None:
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev1.record()
+            f1 = N.gemm_flops()
+            opt.profile_ns.append((ev0, ev1, f1[0] - f0[0], f1[1] - f0[1], (nb, R, C)))
+        del ws
+        if ci in pnn_h:
+            rsh, msh = pnn_h[ci]
+            (sp,) = opt._scratch(dev, [lib.thorn_pnn_scratch_bytes(nb, R)])
+            # the sharded reference runs pnn on fp32 u (thorn.py:1079-1081): no rounding, fp32 eps
+            pt = N.PnnTensor(U[ci].data_ptr(), arena.ptr(rsh), arena.ptr(msh), nb, R, C, sp, 1)
+            N.check(lib.thorn_pnn_stats_multi(N.array(N.PnnTensor, [pt]), 1, ns_code, N.F32, stream), "pnn_stats")
+            factors[ci] = arena.get(rsh).view(nb, R)
+    del X
+
+    # 5. result rows (+ row factors) back to every shard
+    u_loc, f_loc = {}, {}
+    for j, it in enumerate(items):
+        if owners[j] != me:
+            u_loc[j] = torch.empty((it.R, it.C), dtype=ns_dt, device=dev)
+            if cfg.needs_pnn(rows_g[j], it.C):
+                f_loc[j] = torch.empty(it.R, dtype=torch.float32, device=dev)
+
+    def owner_parts(j, s):
+        ci, k = slot[j]
+        r = items[j].R
+        parts = [U[ci][k, s * r:(s + 1) * r]]
+        if ci in factors:
+            parts.append(factors[ci][k, s * r:(s + 1) * r])
+        return parts
+
+    def my_parts(j):
+        return [u_loc[j]] + ([f_loc[j]] if j in f_loc else [])
+
+    sends, recvs = plan_scatter(owners, me, world, owner_parts, my_parts)
+    exchange(sends, recvs, ranks, group)
+
+    # 6. apply on local rows
+    scr = opt._scratch(dev, [lib.thorn_sumsq_scratch_bytes(it.B, it.R, it.C) if md else 0 for it in items])
+    posts: dict = {}
+    for j, (it, sp) in enumerate(zip(items, scr)):
+        if owners[j] == me:
+            ci, k = slot[j]
+            uj = U[ci][k, me * it.R:(me + 1) * it.R]
+            fj = factors[ci][k, me * it.R:(me + 1) * it.R] if ci in factors else None
+        else:
+            uj, fj = u_loc[j], f_loc.get(j)
+        lr_eff = float(cfg.lr) * cfg.lr_scale(rows_g[j], it.C)
+        posts.setdefault(it.pdt, []).append(N.OrthoPostTensor(
+            uj.data_ptr(), it.p.data_ptr(), None if fj is None else fj.data_ptr(), None,
+            arena.ptr(it.pnorm) if md else None, it.B, it.R, it.C, lr_eff, sp if md else None, 0))
+    for pdt, ts in posts.items():
+        N.check(lib.thorn_ortho_post_multi(N.array(N.OrthoPostTensor, ts), len(ts), ns_code, N.dtype_code(pdt),
+                                           float(cfg.weight_decay), stream), "ortho_post_multi")
+    if md:
+        dist.all_reduce(arena.region("red2"), group=group)
+        opt._md_prep(items, arena, new=True, stream=stream)
+        opt._md_finalize(items, arena, lambda it: True, stream)
+    del U, u_loc, f_loc
+    opt._finish(mats, cfg)
