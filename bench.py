@@ -52,9 +52,9 @@ NS_GEMM_TRAFFIC = 98.6e6
 NS_GEMM_TRAFFIC_CASE = "one X X^T launch on 2 x 4096x4096 (K=4096); compulsory 67 MB read + 67 MB write"
 
 
-def shapes():
-    ortho = [s for _ in range(LAYERS) for s in LAYER_SHAPES]
-    adamw = [(VOCAB, HIDDEN), (VOCAB, HIDDEN)] + [(HIDDEN,)] * (2 * LAYERS + 1)
+def shapes(layers=LAYERS):
+    ortho = [s for _ in range(layers) for s in LAYER_SHAPES]
+    adamw = [(VOCAB, HIDDEN), (VOCAB, HIDDEN)] + [(HIDDEN,)] * (2 * layers + 1)
     return ortho, adamw
 
 
@@ -181,9 +181,9 @@ def reference_arm(args, rank):
 
 
 # ------------------------------------------------------------- GPU arm
-def build_params(torch, dev, rank, world, mesh):
+def build_params(torch, dev, rank, world, mesh, layers=LAYERS):
     """Llama-8B-shaped params (bf16 ~N(0, 0.02)) and grads (bf16 ~N(0, 1e-4)) on `dev`."""
-    ortho_s, adam_s = shapes()
+    ortho_s, adam_s = shapes(layers)
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
 
@@ -216,7 +216,7 @@ def gpu_arm(args, rank, world, local_rank):
     if world > 1:
         from torch.distributed.device_mesh import init_device_mesh
         mesh = init_device_mesh("cuda", (world,))
-    ortho, adamw, g_ortho, g_adam = build_params(torch, dev, rank, world, mesh)
+    ortho, adamw, g_ortho, g_adam = build_params(torch, dev, rank, world, mesh, args.layers)
     params = ortho + adamw
     grads = g_ortho + g_adam
     opt = THORN([
@@ -344,12 +344,13 @@ def gpu_arm(args, rank, world, local_rank):
         v, sample, secs = cpu_oracle_sample()
         cpu = {"value": round(v, 3), "unit": "ms", "cores": os.cpu_count() or 1, "kind": "port", "sample": sample,
                "sample_cpu_seconds": round(secs, 2)}
-    ortho_s, adam_s = shapes()
+    ortho_s, adam_s = shapes(args.layers)
     line = {
         "metric": METRIC, "value": round(ms, 3), "unit": "ms", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False,
         "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": "llama3-8b-fsdp2 (BASELINE configs[3])" + (" sharded Shard(0)" if world > 1 else ""),
+        "config": {"workload": "llama3-8b-fsdp2 (BASELINE configs[3])" + (" sharded Shard(0)" if world > 1 else "")
+                   + ("" if args.layers == LAYERS else f" REDUCED to {args.layers} layers (profiling only)"),
                    "ortho_matrices": len(ortho_s), "adamw_tensors": len(adam_s),
                    "params": sum(math.prod(s) for s in ortho_s + adam_s), "param_dtype": "bf16",
                    "state_dtype": "f32", "ns_dtype": "f16", "decouple_md": True, "lr": ORTHO_LR,
@@ -429,6 +430,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ns-only", default=None, help="BxRxC: time thorn_ns_batched alone on this batch (profiling)")
+    ap.add_argument("--layers", type=int, default=LAYERS, help="transformer layers (profiling runs use fewer)")
     args = ap.parse_args()
     if args.ns_only:
         ns_only(args)

@@ -201,8 +201,7 @@ __device__ __forceinline__ float ordered_sum(float* x, int64_t n, float* red) {
 // Scratch of the momentum pass: counters first, then partial sums.
 struct PreLayout {
   int64_t tr, tc, T;
-  int64_t cnt_norm, cnt_all, cnt_row, cnt_col;  // uint32 offsets
-  int64_t pn, ps, pr, pc;                        // float offsets
+  int64_t pn, ps, pr, pc;  // float offsets: [b][tile], [b][tile], [b][ct][r], [b][rt][c]
   int64_t bytes;
 };
 __host__ __device__ inline PreLayout pre_layout(int64_t B, int64_t R, int64_t C, bool md) {
@@ -210,16 +209,10 @@ __host__ __device__ inline PreLayout pre_layout(int64_t B, int64_t R, int64_t C,
   L.tr = (R + kTR - 1) / kTR;
   L.tc = (C + kTC - 1) / kTC;
   L.T = B * L.tr * L.tc;
-  L.cnt_norm = 0;
-  L.cnt_all = B;
-  L.cnt_row = B + 1;
-  L.cnt_col = L.cnt_row + (md ? B * L.tr : 0);
-  const int64_t ncnt = L.cnt_col + (md ? B * L.tc : 0);
-  const int64_t f0 = (ncnt + 3) / 4 * 4;  // float offset after counters (16-byte aligned)
-  L.pn = f0;
+  L.pn = 0;
   L.ps = L.pn + (L.T + 3) / 4 * 4;
   L.pr = L.ps + (md ? (L.T + 3) / 4 * 4 : 0);
-  L.pc = L.pr + (md ? (B * R * L.tc + 3) / 4 * 4 : 0);
+  L.pc = L.pr + (md ? (B * L.tc * R + 3) / 4 * 4 : 0);
   const int64_t nf = L.pc + (md ? B * L.tr * C : 0);
   L.bytes = nf * 4;
   return L;
@@ -253,6 +246,18 @@ __device__ __forceinline__ void tile_sum_to(float* out, void* scratch, const Til
 // ===========================================================================
 // momentum + Nesterov (+ MD direction recovery)  (thorn.py:1376-1381, 890-908)
 // ===========================================================================
+// 8 consecutive fp32 values (two 16-byte loads when aligned), zero past n
+__device__ __forceinline__ void load8f(const float* p, float* v, int n, bool vec) {
+  if (vec && n == 8) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    return;
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) v[k] = k < n ? p[k] : 0.f;
+}
+
 // u = g + beta1 * m, evaluated identically by the momentum pass (for the norm)
 // and by the NS-input pass (for X), so both see the same u.
 template <class U>
@@ -276,7 +281,6 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
   const Tile t = tile_of(local, e.rows, e.cols);
   const PreLayout L = pre_layout(e.batch, e.rows, e.cols, MD);
   const int64_t rt = t.r0 / kTR, ct = t.c0 / kTC;
-  unsigned* cnt = (unsigned*)e.scratch;
   float* sf = (float*)e.scratch;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t c = t.c0 + lane * 8;
@@ -289,10 +293,7 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
 #pragma unroll
   for (int k = 0; k < 8; ++k) csum[k] = 0.f;
   float csp[8];
-  if (MD && !scalar_gain) {
-#pragma unroll
-    for (int k = 0; k < 8; ++k) csp[k] = k < nc ? e.col_sp[t.b * e.cols + c + k] : 0.f;
-  }
+  if (MD && !scalar_gain) load8f(e.col_sp + t.b * e.cols + c, csp, nc, vec);
   float rsum_scalar = 0.f;
   for (int rr = warp; rr < kTR; rr += 8) {
     const int64_t r = t.r0 + rr;
@@ -312,7 +313,8 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
         for (int k = 0; k < 8; ++k) {
           if (k >= nc) continue;
           const float gain = scalar_gain ? rsp : rnd<P>(rsp * csp[k]);
-          const float pd = rnd<P>(pv[k] / gain);
+          // fast division (<= 2 fp32 ulp) before the rounding to the param dtype
+          const float pd = rnd<P>(__fdividef(pv[k], gain));
           const float pg = rnd<P>(pd * gv[k]);
           if (scalar_gain) {
             part += pg;
@@ -341,7 +343,7 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
     if (MD) {
       rs = warp_sum(rs);
       if (scalar_gain) rsum_scalar += rs;
-      else if (lane == 0) sf[L.pr + (t.b * e.rows + r) * L.tc + ct] = rs;
+      else if (lane == 0) sf[L.pr + (t.b * L.tc + ct) * e.rows + r] = rs;
     }
   }
   const int64_t gt = (t.b * L.tr + rt) * L.tc + ct;  // tile index within the tensor
@@ -366,43 +368,69 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
       }
     }
   }
-  // -------- last blocks reduce their segment in a fixed order --------
-  if (momentum && last_block(cnt + L.cnt_norm + t.b, (unsigned)(L.tr * L.tc))) {
-    const float s = ordered_sum(sf + L.pn + t.b * L.tr * L.tc, L.tr * L.tc, red);
-    if (threadIdx.x == 0) e.normsq[t.b] = s;
-  }
-  if (MD && scalar_gain) {
-    if (last_block(cnt + L.cnt_all, (unsigned)L.T)) {
+}
+
+// Fixed-order sums of the momentum pass's partials (no atomics in the pass
+// itself).  Blocks per tensor and batch: one for the sum of squares (and a
+// scalar gain), ceil(rows/256) for row-gain sums, ceil(cols/256) for
+// column-gain sums.  Every partial read is zeroed again.
+struct PreRedArgs {
+  Pack<thorn_ortho_pre_tensor> pk;
+  int md;
+};
+__host__ __device__ inline int64_t pre_red_blocks(int64_t B, int64_t R, int64_t C, bool split) {
+  return B * (1 + (split ? (R + 255) / 256 + (C + 255) / 256 : 0));
+}
+
+__global__ void __launch_bounds__(kThreads) pre_reduce_kernel(const __grid_constant__ PreRedArgs a) {
+  __shared__ float red[32];
+  const int ti = find_tensor(a.pk, blockIdx.x);
+  const thorn_ortho_pre_tensor& e = a.pk.t[ti];
+  const bool md = a.md != 0;
+  const bool split = md && !e.scalar_gain;
+  const PreLayout L = pre_layout(e.batch, e.rows, e.cols, md);
+  float* sf = (float*)e.scratch;
+  const int64_t per_b = pre_red_blocks(1, e.rows, e.cols, split);
+  const int64_t local = int64_t(blockIdx.x) - a.pk.start[ti];
+  const int64_t b = local / per_b;
+  int64_t k = local - b * per_b;
+  const int64_t tpm = L.tr * L.tc;
+  if (k == 0) {
+    if (e.m != nullptr) {
+      const float s = ordered_sum(sf + L.pn + b * tpm, tpm, red);
+      if (threadIdx.x == 0) e.normsq[b] = s;
+    }
+    if (md && !split && b == 0) {  // a scalar gain sums over the whole tensor
       const float s = ordered_sum(sf + L.ps, L.T, red);
       if (threadIdx.x == 0) e.row_gsum[0] = s;
     }
-  } else if (MD) {
-    if (last_block(cnt + L.cnt_row + t.b * L.tr + rt, (unsigned)L.tc)) {
-      for (int rr = warp; rr < kTR; rr += 8) {
-        const int64_t r = t.r0 + rr;
-        if (r >= e.rows) break;
-        float* src = sf + L.pr + (t.b * e.rows + r) * L.tc;
-        float s = 0.f;
-        for (int64_t k = lane; k < L.tc; k += 32) {
-          s += __ldcg(src + k);
-          src[k] = 0.f;
-        }
-        s = warp_sum(s);
-        if (lane == 0) e.row_gsum[t.b * e.rows + r] = s;
+    return;
+  }
+  k -= 1;
+  const int64_t nrb = (e.rows + 255) / 256;
+  if (k < nrb) {
+    const int64_t r = k * 256 + threadIdx.x;
+    if (r < e.rows) {
+      float s = 0.f;
+      for (int64_t c = 0; c < L.tc; ++c) {
+        float* q = sf + L.pr + (b * L.tc + c) * e.rows + r;
+        s += __ldcg(q);
+        *q = 0.f;
       }
+      e.row_gsum[b * e.rows + r] = s;
     }
-    if (last_block(cnt + L.cnt_col + t.b * L.tc + ct, (unsigned)L.tr)) {
-      const int64_t cc = t.c0 + threadIdx.x;
-      if (cc < e.cols) {
-        float s = 0.f;
-        for (int64_t k = 0; k < L.tr; ++k) {
-          float* q = sf + L.pc + (t.b * L.tr + k) * e.cols + cc;
-          s += __ldcg(q);
-          *q = 0.f;
-        }
-        e.col_gsum[t.b * e.cols + cc] = s;
-      }
+    return;
+  }
+  k -= nrb;
+  const int64_t cc = k * 256 + threadIdx.x;
+  if (cc < e.cols) {
+    float s = 0.f;
+    for (int64_t r = 0; r < L.tr; ++r) {
+      float* q = sf + L.pc + (b * L.tr + r) * e.cols + cc;
+      s += __ldcg(q);
+      *q = 0.f;
     }
+    e.col_gsum[b * e.cols + cc] = s;
   }
 }
 
@@ -415,14 +443,11 @@ struct CastArgs {
 };
 
 
-// u for element (b, r, c) exactly as the momentum pass computed it
+// u for one element exactly as the momentum pass computed it; `gain` is the
+// element's magnitude gain (used when the raw gradient is still in g)
 template <class P, class U>
-__device__ __forceinline__ float cast_u(const thorn_ns_cast_tensor& e, float g, float m, float b1, int64_t b,
-                                        int64_t r, int64_t c) {
-  if (e.md) {
-    const float gain = e.scalar_gain ? e.row_sp[0] : rnd<P>(e.row_sp[b * e.rows + r] * e.col_sp[b * e.cols + c]);
-    g = rnd<P>(g * gain);
-  }
+__device__ __forceinline__ float cast_u(bool md, float g, float m, float b1, float gain) {
+  if (md) g = rnd<P>(g * gain);
   return nesterov_u<U>(g, m, b1);
 }
 
@@ -440,6 +465,13 @@ __global__ void __launch_bounds__(kThreads) ns_cast_kernel(const __grid_constant
   const int64_t ld = ns_ld(e.cols);
   const P* G = (const P*)e.g;
   const S* M = (const S*)e.m;
+  // multiply by the reciprocal of (||u|| + 1e-8): <= 1 fp32 ulp from the
+  // reference's division, before the rounding to the 16-bit NS type
+  const float inv = 1.f / d;
+  const bool md = e.md != 0;
+  const bool split = md && !e.scalar_gain;
+  float csp[8];
+  if (split) load8f(e.col_sp + t.b * e.cols + c, csp, nc, vec);
   for (int rr = warp; rr < kTR; rr += 8) {
     const int64_t r = t.r0 + rr;
     if (r >= e.rows) break;
@@ -447,8 +479,12 @@ __global__ void __launch_bounds__(kThreads) ns_cast_kernel(const __grid_constant
     float gv[8], mv[8], v[8];
     load_n(G + off, gv, nc, vec);
     load_n(M + off, mv, nc, vec);
+    const float rsp = md ? (split ? e.row_sp[t.b * e.rows + r] : e.row_sp[0]) : 1.f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) v[k] = (k < nc ? cast_u<P, U>(e, gv[k], mv[k], a.beta1, t.b, r, c + k) : 0.f) / d;
+    for (int k = 0; k < 8; ++k) {
+      const float gain = split ? rnd<P>(rsp * csp[k]) : rsp;
+      v[k] = cast_u<P, U>(md, gv[k], mv[k], a.beta1, gain) * inv;
+    }
     store_n((X*)e.x + (t.b * e.rows + r) * ld + c, v, nc, vec);
   }
 }
@@ -615,10 +651,7 @@ __global__ void __launch_bounds__(kThreads) md_finalize_kernel(const __grid_cons
   }
   const bool split = !e.scalar_gain;
   float csp[8];
-  if (split) {
-#pragma unroll
-    for (int k = 0; k < 8; ++k) csp[k] = k < nc ? e.col_sp[t.b * e.cols + c + k] : 0.f;
-  }
+  if (split) load8f(e.col_sp + t.b * e.cols + c, csp, nc, vec);
   for (int rr = warp; rr < kTR; rr += 8) {
     const int64_t r = t.r0 + rr;
     if (r >= e.rows) break;
@@ -776,6 +809,21 @@ extern "C" int thorn_ortho_pre_multi(const thorn_ortho_pre_tensor* ts, int n, in
         if (md) ortho_pre_kernel<P, S, U, true><<<(unsigned)nb, kThreads, 0, st>>>(a);
         else ortho_pre_kernel<P, S, U, false><<<(unsigned)nb, kThreads, 0, st>>>(a);
       });
+      if (rc == THORN_OK) {
+        rc = launch_packed(
+            ts, n,
+            [md](const thorn_ortho_pre_tensor& e) -> int64_t {
+              if (e.batch <= 0 || e.rows <= 0 || e.cols <= 0) return 0;
+              return pre_red_blocks(e.batch, e.rows, e.cols, md && !e.scalar_gain);
+            },
+            [](const thorn_ortho_pre_tensor&) { return false; },
+            [&](const Pack<thorn_ortho_pre_tensor>& pk, int64_t nb) {
+              PreRedArgs a;
+              a.pk = pk;
+              a.md = md;
+              pre_reduce_kernel<<<(unsigned)nb, kThreads, 0, st>>>(a);
+            });
+      }
     });
     if (d2) rc = d2;
   });
