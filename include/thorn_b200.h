@@ -52,6 +52,12 @@ THORN_API int thorn_last_cuda_error(void);
  * dense-equivalent FLOPs (2 M N K per product) and FLOPs of the tiles
  * actually executed (lower-triangle tiles only for symmetric products). */
 THORN_API void thorn_gemm_flops(double* dense, double* executed);
+/* GEMM tiling of the NS products: nonzero (default) uses 2-CTA 256x256 cluster
+ * tiles (tcgen05.mma.cta_group::2) whenever both output dimensions are >= 256;
+ * zero keeps every product on single-CTA 128x256 tiles.  Returns the previous
+ * setting.  Process-wide; both settings give the same results up to
+ * floating-point summation order. */
+THORN_API int thorn_set_gemm_pair(int enable);
 
 /* --------------------------------------------------------------------------
  * (R)Adam(-atan2)W over many tensors in one launch per dtype pair.

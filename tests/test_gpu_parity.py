@@ -317,3 +317,24 @@ def test_launch_counter_and_no_fallback():
     opt.step()
     torch.cuda.synchronize()
     assert N.launch_count() - before >= 5
+
+
+@pytest.mark.parametrize("shape", [(1, 512, 512), (2, 1024, 512), (1, 512, 1024), (1, 300, 700), (3, 640, 384)])
+def test_pair_tiles_match_single_cta(shape):
+    """2-CTA (cta_group::2) 256x256 tiles and single-CTA tiles give the same NS result."""
+    from thorn_b200 import _native as N
+
+    lib = N.load()
+    torch.manual_seed(11)
+    u = (torch.randn(shape) * 1e-3).cuda()
+    prev = lib.thorn_set_gemm_pair(1)
+    try:
+        pair, co, rs = _ns_gpu(u)
+        lib.thorn_set_gemm_pair(0)
+        single, _, _ = _ns_gpu(u)
+    finally:
+        lib.thorn_set_gemm_pair(prev)
+    assert np.isfinite(pair).all()
+    assert C.rel_fro(pair, single) <= 1e-3, C.rel_fro(pair, single)
+    want = np.stack([O.polar_decomp_2d(x, co, rs, "f32") for x in u.cpu().numpy()])
+    assert C.rel_fro(pair, want) <= 2e-2

@@ -186,6 +186,68 @@ __device__ __forceinline__ void decode_tile(const Params& p, int t, int& b, int&
   }
 }
 
+// Epilogue of one 32-column chunk of a thread's accumulator row: alpha/beta/C,
+// one rounding, optional second output D + diag2 I, and plain, transposed or
+// mirrored (symmetric) stores with bounds checks.
+template <class T>
+__device__ __forceinline__ void epilogue_chunk(const Params& p, float* v, int row, bool row_ok, int col0,
+                                               int warp_row_max, T* D, T* D2, const T* Cb) {
+  const bool full = row_ok && col0 + 32 <= p.N;
+  if (Cb != nullptr) {
+    float cv[32];
+    if (full && p.c_vec) {
+      load_n(Cb + (int64_t)row * p.c_ld + col0, cv, 8, true);
+      load_n(Cb + (int64_t)row * p.c_ld + col0 + 8, cv + 8, 8, true);
+      load_n(Cb + (int64_t)row * p.c_ld + col0 + 16, cv + 16, 8, true);
+      load_n(Cb + (int64_t)row * p.c_ld + col0 + 24, cv + 24, 8, true);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        cv[j] = (row_ok && col0 + j < p.N) ? to_f(Cb[(int64_t)row * p.c_ld + col0 + j]) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = p.alpha * v[j] + p.beta * cv[j];
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = p.alpha * v[j];
+  }
+  // round once to the output type
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = rnd<T>(v[j]);
+
+  for (int out = 0; out < (D2 ? 2 : 1); ++out) {
+    T* O = out == 0 ? D : D2;
+    const int64_t ld = out == 0 ? p.d_ld : p.d2_ld;
+    float w[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) w[j] = (out == 1 && row == col0 + j) ? rnd<T>(v[j] + p.diag2) : v[j];
+    if (p.trans_out) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (row_ok && col0 + j < p.N) O[(int64_t)(col0 + j) * ld + row] = from_f<T>(w[j]);
+      continue;
+    }
+    const bool lower_full = !p.sym || row >= col0 + 31;
+    if (full && p.d_vec && lower_full) {
+      T* dst = O + (int64_t)row * ld + col0;
+      store_n(dst, w, 8, true);
+      store_n(dst + 8, w + 8, 8, true);
+      store_n(dst + 16, w + 16, 8, true);
+      store_n(dst + 24, w + 24, 8, true);
+    } else if (row_ok) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.N && (!p.sym || row >= col0 + j)) O[(int64_t)row * ld + col0 + j] = from_f<T>(w[j]);
+    }
+    if (p.sym && warp_row_max > col0) {
+      // mirror strictly-lower elements: lanes hold consecutive rows -> coalesced
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (row_ok && col0 + j < p.N && row > col0 + j) O[(int64_t)(col0 + j) * ld + row] = from_f<T>(w[j]);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
@@ -333,60 +395,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) ns_gemm_kernel(const __grid_cons
         if (p.sym && warp_row_max < col0) continue;  // whole warp above the diagonal
         float v[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + ch * 32), v);
-        const bool full = row_ok && col0 + 32 <= p.N;
-        if (Cb != nullptr) {
-          float cv[32];
-          if (full && p.c_vec) {
-            load_n(Cb + (int64_t)row * p.c_ld + col0, cv, 8, true);
-            load_n(Cb + (int64_t)row * p.c_ld + col0 + 8, cv + 8, 8, true);
-            load_n(Cb + (int64_t)row * p.c_ld + col0 + 16, cv + 16, 8, true);
-            load_n(Cb + (int64_t)row * p.c_ld + col0 + 24, cv + 24, 8, true);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              cv[j] = (row_ok && col0 + j < p.N) ? to_f(Cb[(int64_t)row * p.c_ld + col0 + j]) : 0.f;
-          }
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = p.alpha * v[j] + p.beta * cv[j];
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = p.alpha * v[j];
-        }
-        // round once to the output type
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = rnd<T>(v[j]);
-
-        for (int out = 0; out < (D2 ? 2 : 1); ++out) {
-          T* O = out == 0 ? D : D2;
-          const int64_t ld = out == 0 ? p.d_ld : p.d2_ld;
-          float w[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) w[j] = (out == 1 && row == col0 + j) ? rnd<T>(v[j] + p.diag2) : v[j];
-          if (p.trans_out) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (row_ok && col0 + j < p.N) O[(int64_t)(col0 + j) * ld + row] = from_f<T>(w[j]);
-            continue;
-          }
-          const bool lower_full = !p.sym || row >= col0 + 31;
-          if (full && p.d_vec && lower_full) {
-            T* dst = O + (int64_t)row * ld + col0;
-            store_n(dst, w, 8, true);
-            store_n(dst + 8, w + 8, 8, true);
-            store_n(dst + 16, w + 16, 8, true);
-            store_n(dst + 24, w + 24, 8, true);
-          } else if (row_ok) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < p.N && (!p.sym || row >= col0 + j)) O[(int64_t)row * ld + col0 + j] = from_f<T>(w[j]);
-          }
-          if (p.sym && warp_row_max > col0) {
-            // mirror strictly-lower elements: lanes hold consecutive rows -> coalesced
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (row_ok && col0 + j < p.N && row > col0 + j) O[(int64_t)(col0 + j) * ld + row] = from_f<T>(w[j]);
-          }
-        }
+        epilogue_chunk(p, v, row, row_ok, col0, warp_row_max, D, D2, Cb);
       }
       tc_fence_before();
       mbar_arrive(smem_u32(&tempty[acc]));
@@ -400,6 +409,251 @@ __global__ void __launch_bounds__(kThreadsG, 1) ns_gemm_kernel(const __grid_cons
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                  "r"((uint32_t)C_::kTmemCols)
                  : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 2-CTA variant: a cluster of two CTAs computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2.  Each CTA loads its own 128 rows of A and its own
+// 128 rows (columns of the tile) of B; the MMA of the leader CTA (cluster rank
+// 0) reads both CTAs' shared memory and accumulates rows 0-127 in the leader's
+// TMEM and rows 128-255 in the peer's.  Per SM this halves the B operand bytes
+// that TMA moves for the same tensor-core work.
+//   full[s]   leader only: both CTAs' TMA loads complete on it (leader expects
+//             all 64 KB); the peer reaches it through its cluster address
+//   empty[s]  both CTAs: the leader's MMA commits to each CTA's copy
+//   tfull[a]  both CTAs: the leader commits to each CTA's copy
+//   tempty[a] leader only: 256 arrivals, the peer's epilogue arrives remotely
+// ---------------------------------------------------------------------------
+constexpr int BM2 = 256;  // rows of a cluster tile (128 per CTA)
+constexpr int kStages2 = 6;
+constexpr int kHalfBytes = 128 * BK * 2;  // 16 KB: one CTA's A (or B) slab per stage
+constexpr int kSmem2 = kStages2 * 2 * kHalfBytes + 256 + 1024;
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* tm, uint32_t bar_cluster, int x, int y,
+                                                 int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void umma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+
+__host__ __device__ constexpr uint32_t idesc_f16_m256(bool bf16, bool a_mn, bool b_mn) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((a_mn ? 1u : 0u) << 15) |
+         ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(BM2 >> 4) << 24);
+}
+
+__device__ __forceinline__ void decode_tile2(const Params& p, int t, int& b, int& tm, int& tn) {
+  b = t / p.tiles_per_mat;
+  int l = t - b * p.tiles_per_mat;
+  if (!p.sym) {
+    tm = l / p.tiles_n;
+    tn = l - tm * p.tiles_n;
+    return;
+  }
+  tm = 0;
+  for (;;) {
+    const int cnt = min(p.tiles_n, tm + 1);  // square 256 x 256 tiles on or below the diagonal
+    if (l < cnt || tm + 1 >= p.tiles_m) {
+      tn = l;
+      return;
+    }
+    l -= cnt;
+    ++tm;
+  }
+}
+
+template <bool A_MN, bool B_MN, class T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
+    ns_gemm2_kernel(const __grid_constant__ Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kStages2 * kHalfBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kStages2 * kHalfBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kStages2;
+  uint64_t* tfull = bars + 2 * kStages2;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cid = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages2; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), 2 * 4 * 32);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tmA)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tmB)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(512u)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs are initialised before any remote signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------ producer (both CTAs) -------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      const int row_off = (int)rank * 128;
+      for (int t = cid; t < p.total_tiles && !*abort_flag; t += nclusters) {
+        int b, tm, tn;
+        decode_tile2(p, t, b, tm, tn);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.err)) break;
+          const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+          if (leader) mbar_expect_tx(smem_u32(&full[stage]), 4 * kHalfBytes);
+          const uint32_t a_dst = smem_u32(sA + stage * kHalfBytes);
+          const uint32_t b_dst = smem_u32(sB + stage * kHalfBytes);
+          if (!A_MN) {
+            tma_load_3d_pair(a_dst, &p.tmA, fb, kb * BK, tm * BM2 + row_off, b);
+          } else {
+            tma_load_3d_pair(a_dst, &p.tmA, fb, tm * BM2 + row_off, kb * BK, b);
+            tma_load_3d_pair(a_dst + 64 * BK * 2, &p.tmA, fb, tm * BM2 + row_off + 64, kb * BK, b);
+          }
+          if (!B_MN) {
+            tma_load_3d_pair(b_dst, &p.tmB, fb, kb * BK, tn * 256 + row_off, b);
+          } else {
+            tma_load_3d_pair(b_dst, &p.tmB, fb, tn * 256 + row_off, kb * BK, b);
+            tma_load_3d_pair(b_dst + 64 * BK * 2, &p.tmB, fb, tn * 256 + row_off + 64, kb * BK, b);
+          }
+          if (++stage == kStages2) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer (leader) --------------------
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_m256(sizeof(T) == 2 && !std::is_same<T, __half>::value, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int t = cid; t < p.total_tiles && !*abort_flag; t += nclusters, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
+        if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag, p.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * 256);
+        bool ok = true;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * kHalfBytes);
+          const uint32_t b0 = smem_u32(sB + stage * kHalfBytes);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? sdesc(a0 + kk * 2048, 64 * BK * 2, 1024) : sdesc(a0 + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc(b0 + kk * 2048, 64 * BK * 2, 1024) : sdesc(b0 + kk * 32, 16, 1024);
+            umma_pair(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 0));
+          umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 1));
+          if (++stage == kStages2) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(mapa_shared(smem_u32(&tfull[acc]), 0));
+        umma_commit_pair(mapa_shared(smem_u32(&tfull[acc]), 1));
+      }
+    }
+  } else {
+    // ------------------------------ epilogue (both CTAs) -------------------
+    const int q = warp & 3;
+    const int rloc = (int)rank * 128 + q * 32 + lane;
+    const T* Cp = reinterpret_cast<const T*>(p.C);
+    T* Dp = reinterpret_cast<T*>(p.D);
+    T* D2p = reinterpret_cast<T*>(p.D2);
+    int it = 0;
+    for (int t = cid; t < p.total_tiles; t += nclusters, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
+      if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag, p.err)) break;
+      tc_fence_after();
+      int b, tm, tn;
+      decode_tile2(p, t, b, tm, tn);
+      const int row = tm * BM2 + rloc;
+      const bool row_ok = row < p.M;
+      const int warp_row_max = tm * BM2 + (int)rank * 128 + q * 32 + 31;
+      T* D = Dp + (int64_t)b * p.d_bs;
+      T* D2 = D2p ? D2p + (int64_t)b * p.d2_bs : nullptr;
+      const T* Cb = Cp ? Cp + (int64_t)b * p.c_bs : nullptr;
+#pragma unroll 1
+      for (int ch = 0; ch < 256 / 32; ++ch) {
+        const int col0 = tn * 256 + ch * 32;
+        if (col0 >= p.N) break;
+        if (p.sym && warp_row_max < col0) continue;
+        float v[32];
+        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 256 + ch * 32), v);
+        epilogue_chunk(p, v, row, row_ok, col0, warp_row_max, D, D2, Cb);
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+    }
+  }
+
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal it
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(512u) : "memory");
   }
 }
 
@@ -498,6 +752,50 @@ static int launch_gemm(gemm::Params& prm, int grid, cudaStream_t st) {
   return check_launch();
 }
 
+template <bool AMN, bool BMN, class T>
+static int launch_gemm2(gemm::Params& prm, int64_t total, int sms, cudaStream_t st) {
+  static std::once_flag attr_once[64];
+  static int max_clusters[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(attr_once[dev & 63], [sms, dev]() {
+    auto k = gemm::ns_gemm2_kernel<AMN, BMN, T>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kSmem2);
+    // persistent grid: as many CTA pairs as can be resident at once
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
+    cfg.blockDim = dim3(gemm::kThreadsG, 1, 1);
+    cfg.dynamicSmemBytes = gemm::kSmem2;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sms / 2;
+    }
+    max_clusters[dev & 63] = n;
+  });
+  const int clusters = (int)min64(total, (int64_t)std::max(1, max_clusters[dev & 63]));
+  gemm::ns_gemm2_kernel<AMN, BMN, T><<<2 * clusters, gemm::kThreadsG, gemm::kSmem2, st>>>(prm);
+  count_launch();
+  return check_launch();
+}
+
+template <class T>
+static int launch_any2(const GemmOp& op, gemm::Params& prm, int64_t total, int sms, cudaStream_t st) {
+  if (op.a_mn && !op.b_mn) return THORN_ERR_ARG;
+  if (op.a_mn) return launch_gemm2<true, true, T>(prm, total, sms, st);
+  if (op.b_mn) return launch_gemm2<false, true, T>(prm, total, sms, st);
+  return launch_gemm2<false, false, T>(prm, total, sms, st);
+}
+
+static std::atomic<int> g_pair_tiles{1};
+
 template <class T>
 static int launch_any(const GemmOp& op, int BN, gemm::Params& prm, int grid, cudaStream_t st) {
   // instantiated operand layouts: (A K, B K), (A K, B MN), (A MN, B MN)
@@ -525,12 +823,17 @@ int run_gemm(const GemmOp& op, int dtype, int* err, cudaStream_t st) {
   if (di.major != 10) return THORN_ERR_UNSUPPORTED;
   Params prm;
   memset(&prm, 0, sizeof(prm));
-  const int BN = (op.N > 128) ? 256 : 128;
+  // 2-CTA 256 x 256 cluster tiles when both output dimensions fill them
+  const bool pair = g_pair_tiles.load() != 0 && op.M >= 256 && op.N >= 256 && di.sms >= 2;
+  const int BN = pair ? 256 : ((op.N > 128) ? 256 : 128);
+  const int BMt = pair ? BM2 : BM;
+  const int a_box_rows = 128;  // rows of A one CTA loads per stage (half of a pair tile)
+  const int b_box_rows = pair ? 128 : BN;
   int rc = op.a_mn ? make_map(&prm.tmA, op.A, dtype, op.M, op.K, op.batch, op.a_ld, op.a_bs, 64, BK)
-                   : make_map(&prm.tmA, op.A, dtype, op.K, op.M, op.batch, op.a_ld, op.a_bs, BK, BM);
+                   : make_map(&prm.tmA, op.A, dtype, op.K, op.M, op.batch, op.a_ld, op.a_bs, BK, a_box_rows);
   if (rc) return rc;
   if (op.b_mn) rc = make_map(&prm.tmB, op.B, dtype, op.N, op.K, op.batch, op.b_ld, op.b_bs, 64, BK);
-  else rc = make_map(&prm.tmB, op.B, dtype, op.K, op.N, op.batch, op.b_ld, op.b_bs, BK, BN);
+  else rc = make_map(&prm.tmB, op.B, dtype, op.K, op.N, op.batch, op.b_ld, op.b_bs, BK, b_box_rows);
   if (rc) return rc;
   prm.C = op.C;
   prm.D = op.D;
@@ -553,11 +856,12 @@ int run_gemm(const GemmOp& op, int dtype, int* err, cudaStream_t st) {
   prm.c_vec = op.C && aligned16(op.C) && (op.c_ld % 8) == 0 && (op.c_bs % 8) == 0;
   prm.d_vec = aligned16(op.D) && (op.d_ld % 8) == 0 && (op.d_bs % 8) == 0 &&
               (!op.D2 || (aligned16(op.D2) && (op.d2_ld % 8) == 0 && (op.d2_bs % 8) == 0));
-  prm.tiles_m = (op.M + BM - 1) / BM;
+  prm.tiles_m = (op.M + BMt - 1) / BMt;
   prm.tiles_n = (op.N + BN - 1) / BN;
   if (op.sym) {
     int cnt = 0;
-    for (int tm = 0; tm < prm.tiles_m; ++tm) cnt += std::min(prm.tiles_n, (tm * BM + BM - 1) / BN + 1);
+    for (int tm = 0; tm < prm.tiles_m; ++tm)
+      cnt += pair ? std::min(prm.tiles_n, tm + 1) : std::min(prm.tiles_n, (tm * BM + BM - 1) / BN + 1);
     prm.tiles_per_mat = cnt;
   } else {
     prm.tiles_per_mat = prm.tiles_m * prm.tiles_n;
@@ -569,9 +873,12 @@ int run_gemm(const GemmOp& op, int dtype, int* err, cudaStream_t st) {
   prm.err = err;
   const int grid = (int)min64(total, (int64_t)di.sms);
   const double dense = 2.0 * op.M * (double)op.N * op.K * op.batch;
-  const double exec = 2.0 * BM * (double)BN * (prm.num_kb * (double)BK) * total;
+  const double exec = 2.0 * BMt * (double)BN * (prm.num_kb * (double)BK) * total;
   g_flops_dense.fetch_add((uint64_t)dense);
   g_flops_exec.fetch_add((uint64_t)exec);
+  if (pair)
+    return dtype == THORN_BF16 ? launch_any2<__nv_bfloat16>(op, prm, total, di.sms, st)
+                               : launch_any2<__half>(op, prm, total, di.sms, st);
   return dtype == THORN_BF16 ? launch_any<__nv_bfloat16>(op, BN, prm, grid, st)
                              : launch_any<__half>(op, BN, prm, grid, st);
 }
@@ -771,6 +1078,8 @@ extern "C" int thorn_sym_addmm(const void* A, const void* B, const void* C, void
   if (K == 0) return THORN_ERR_ARG;
   return run_gemm(op, dtype, err_flag, (cudaStream_t)stream);
 }
+
+extern "C" int thorn_set_gemm_pair(int enable) { return g_pair_tiles.exchange(enable ? 1 : 0); }
 
 // Dense-equivalent and executed tensor-core FLOPs issued so far (for roofline reports).
 extern "C" void thorn_gemm_flops(double* dense, double* executed) {
