@@ -251,15 +251,15 @@ def gpu_arm(args, rank, world, local_rank):
     clocks = None
     sampler = None
     if rank == 0:
+        # the GPUs of this job: local ranks 0..world-1 (one node)
         ids = []
         try:
-            for i in range(torch.cuda.device_count()):
-                u = getattr(torch.cuda.get_device_properties(i), "uuid", None)
-                if u is not None:
-                    ids.append("GPU-" + str(u) if not str(u).startswith("GPU-") else str(u))
+            for i in range(min(world, torch.cuda.device_count())):
+                u = str(torch.cuda.get_device_properties(i).uuid)
+                ids.append(u if u.startswith("GPU-") else "GPU-" + u)
         except Exception:
-            ids = []
-        sampler = ClockSampler(ids if len(ids) == world else [])
+            ids = [str(i) for i in range(world)]
+        sampler = ClockSampler(ids)
         sampler.start()
         time.sleep(0.3)
     opt.profile_ns = []
@@ -269,14 +269,24 @@ def gpu_arm(args, rank, world, local_rank):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
+    h0 = time.perf_counter()
     for _ in range(args.steps):
         feed()
         opt.step()
+    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps  # host time to enqueue one step
     e1.record()
     torch.cuda.synchronize()
     barrier()
     launches = _native.launch_count() - launches0
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    # host cost of one step on an idle GPU (nothing blocks on a full launch queue)
+    feed()
+    torch.cuda.synchronize()
+    barrier()
+    h1 = time.perf_counter()
+    opt.step()
+    host_enqueue_ms = max_over_ranks((time.perf_counter() - h1) * 1e3)
+    torch.cuda.synchronize()
     prof = opt.profile_ns
     opt.profile_ns = None
     ns_ms = sum(a.elapsed_time(b) for a, b, *_ in prof) / args.steps
@@ -337,6 +347,7 @@ def gpu_arm(args, rank, world, local_rank):
     if rank != 0:
         return
     hbm, peak_burst, peak_sus, peak_src = load_peaks()
+    peak_job = peak_sus * world  # whole-job peak: the NS work is spread over all ranks
     achieved = ns_dense_all / (ns_launch_ms * 1e-3) / 1e12 if ns_launch_ms > 0 else None
     achieved_exec = ns_exec_all / (ns_launch_ms * 1e-3) / 1e12 if ns_launch_ms > 0 else None
     cpu = None
@@ -357,16 +368,20 @@ def gpu_arm(args, rank, world, local_rank):
                    "parallelism": f"fsdp{world}" if world > 1 else "single",
                    "l2": "no flush: every step reads params, grads and state (~70 GB) >> 126 MB L2"},
         "roofline": {"bound": "tensor", "kernel": "ns_gemm_kernel (Newton-Schulz phase)",
-                     "achieved": round(achieved, 1) if achieved else None, "peak": peak_sus, "unit": "TFLOP/s",
-                     "frac": round(achieved / peak_sus, 3) if achieved else None, "traffic": NS_GEMM_TRAFFIC,
+                     "achieved": round(achieved, 1) if achieved else None, "peak": round(peak_job, 1),
+                     "unit": "TFLOP/s", "frac": round(achieved / peak_job, 3) if achieved else None,
+                     "traffic": NS_GEMM_TRAFFIC,
                      "traffic_case": NS_GEMM_TRAFFIC_CASE,
                      "flops": "dense-equivalent (2MNK per reference GEMM)",
                      "achieved_executed": round(achieved_exec, 1) if achieved_exec else None,
-                     "peak_source": f"{peak_src} sustained bf16 (MEASURED_PEAKS.json); burst {peak_burst}",
+                     "peak_source": f"{peak_src} sustained bf16 (MEASURED_PEAKS.json) x {world} GPU(s); "
+                                    f"burst {peak_burst} per GPU",
                      "ns_ms_per_step": round(ns_launch_ms, 3),
                      "ns_dense_tflop_per_step": round(ns_dense_all / 1e12, 2)},
         "cpu_baseline": cpu,
         "e2e": e2e,
+        "host_ms_per_step": round(host_ms, 2),
+        "host_enqueue_ms_idle_gpu": round(host_enqueue_ms, 2),
         "gpu_launches": int(launches),
         "gpu_launches_per_step": round(launches / args.steps, 1),
         "clocks": clocks,

@@ -271,6 +271,7 @@ class THORN(Optimizer):
                 self._param_to_group[id(p)] = group
         self._err = {}
         self._scratch_bufs = {}
+        self._targets = {}
         if isinstance(params, nn.Module) and conf.get("gradient_release", False):
             self.setup_gradient_release(params)
 
@@ -488,21 +489,44 @@ class THORN(Optimizer):
             bc2 = 1 / (1 - cfg.gain_betas[1] ** step)
             for key, gsum, sig in keys:
                 gain = _local(st[key])
-                grad = torch.empty_like(gain)
-                keep.append(grad)
-                grads_by_dt.setdefault(pc, []).append(
-                    N.MdGradTensor(arena.ptr(gsum), arena.ptr(sig), grad.data_ptr(), gain.numel()))
-                mom, var = _local(st[key + "_moment"]), _local(st[key + "_variance"])
-                adam_by_dt.setdefault((pc, N.dtype_code(mom.dtype)), []).append(
-                    N.AdamTensor(gain.data_ptr(), grad.data_ptr(), mom.data_ptr(), var.data_ptr(), gain.numel(),
-                                 cfg.gain_lr_, bc1, bc2, 0))
+                keep.append((gain, gsum, sig, pc, key, st, bc1, bc2))
+        # gain gradients: one buffer per dtype for all gains of the group
+        sizes: dict = {}
+        for gain, *_rest in keep:
+            sizes[gain.dtype] = sizes.get(gain.dtype, 0) + (gain.numel() + 7) // 8 * 8
+        bufs = {dt: torch.empty(max(8, n), dtype=dt, device=keep[0][0].device) for dt, n in sizes.items()} \
+            if keep else {}
+        offs = {dt: 0 for dt in bufs}
+        for gain, gsum, sig, pc, key, st, bc1, bc2 in keep:
+            n = gain.numel()
+            grad = bufs[gain.dtype][offs[gain.dtype]:offs[gain.dtype] + n]
+            offs[gain.dtype] += (n + 7) // 8 * 8
+            grads_by_dt.setdefault(pc, []).append(
+                N.MdGradTensor(arena.ptr(gsum), arena.ptr(sig), grad.data_ptr(), n))
+            mom, var = _local(st[key + "_moment"]), _local(st[key + "_variance"])
+            adam_by_dt.setdefault((pc, N.dtype_code(mom.dtype)), []).append(
+                N.AdamTensor(gain.data_ptr(), grad.data_ptr(), mom.data_ptr(), var.data_ptr(), n,
+                             cfg.gain_lr_, bc1, bc2, 0))
         for pc, ts in grads_by_dt.items():
             N.check(lib.thorn_md_gain_grad_multi(N.array(N.MdGradTensor, ts), len(ts), pc, stream),
                     "md_gain_grad_multi")
         for (pc, sc), ts in adam_by_dt.items():
             N.check(lib.thorn_adamw_multi(N.array(N.AdamTensor, ts), len(ts), pc, sc, cfg.gain_betas[0],
                                           cfg.gain_betas[1], 0.0, float(cfg.eps), stream), "adamw_multi(gains)")
+        keep.append(bufs)
         del keep
+
+    def _target_f32(self, st):
+        """fp32 copy of a parameter's target norm, cached while the state tensor is unchanged
+        (same object, same in-place version counter)."""
+        t = st["target_norm"]
+        loc = _local(t)
+        hit = self._targets.get(id(t))
+        if hit is not None and hit[0] is t and hit[1] == loc._version:
+            return hit[2]
+        f = loc.reshape(-1).float().contiguous()
+        self._targets[id(t)] = (t, loc._version, f)
+        return f
 
     def _md_finalize(self, items, arena, renorm_of, stream):
         lib = N.load()
@@ -511,7 +535,7 @@ class THORN(Optimizer):
         for it in items:
             st = it.state
             normsq = arena.ptr(it.pnorm) if (it.apply and renorm_of(it)) else None
-            tgt = _local(st["target_norm"]).reshape(-1).float()
+            tgt = self._target_f32(st)
             keep.append(tgt)
             stride = 0 if tgt.numel() == 1 else 1
             if stride and tgt.numel() != it.B:
