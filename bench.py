@@ -279,6 +279,8 @@ def gpu_arm(args, rank, world, local_rank):
     barrier()
     launches = _native.launch_count() - launches0
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    prof = opt.profile_ns
+    opt.profile_ns = None
     # host cost of one step on an idle GPU (nothing blocks on a full launch queue)
     feed()
     torch.cuda.synchronize()
@@ -287,8 +289,6 @@ def gpu_arm(args, rank, world, local_rank):
     opt.step()
     host_enqueue_ms = max_over_ranks((time.perf_counter() - h1) * 1e3)
     torch.cuda.synchronize()
-    prof = opt.profile_ns
-    opt.profile_ns = None
     ns_ms = sum(a.elapsed_time(b) for a, b, *_ in prof) / args.steps
     ns_dense = sum(d for _, _, d, _, _ in prof) / args.steps
     ns_exec = sum(x for _, _, _, x, _ in prof) / args.steps

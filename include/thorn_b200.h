@@ -58,6 +58,13 @@ THORN_API void thorn_gemm_flops(double* dense, double* executed);
  * setting.  Process-wide; both settings give the same results up to
  * floating-point summation order. */
 THORN_API int thorn_set_gemm_pair(int enable);
+/* Epilogue of the 2-CTA tiles: nonzero (default) stages each 32x32 output block
+ * in shared memory and writes it (and its mirror or transpose) with TMA bulk
+ * stores, with C blocks TMA-loaded one block ahead; zero stores from registers.
+ * Applies when D, D2 and C are 16-byte aligned with leading dimensions and batch
+ * strides that are multiples of 8.  Returns the previous setting.  Both settings
+ * give bit-identical results. */
+THORN_API int thorn_set_gemm_staged_epilogue(int enable);
 
 /* --------------------------------------------------------------------------
  * (R)Adam(-atan2)W over many tensors in one launch per dtype pair.

@@ -338,3 +338,62 @@ def test_pair_tiles_match_single_cta(shape):
     assert C.rel_fro(pair, single) <= 1e-3, C.rel_fro(pair, single)
     want = np.stack([O.polar_decomp_2d(x, co, rs, "f32") for x in u.cpu().numpy()])
     assert C.rel_fro(pair, want) <= 2e-2
+
+
+@pytest.mark.parametrize("shape,dt", [((2, 512, 512), torch.float16), ((1, 1024, 512), torch.float16),
+                                      ((2, 512, 1024), torch.float16), ((1, 300, 700), torch.float16),
+                                      ((1, 520, 1000), torch.float16), ((2, 1000, 520), torch.float16),
+                                      ((1, 768, 768), torch.bfloat16), ((1, 1536, 512), torch.bfloat16)])
+def test_staged_epilogue_bitwise(shape, dt):
+    """The shared-memory/TMA-store epilogue of the 2-CTA tiles writes exactly what the
+    register epilogue writes (mirrored symmetric blocks, D + aI, C operand, transposed output)."""
+    from thorn_b200 import _native as N
+
+    lib = N.load()
+    torch.manual_seed(12)
+    u = (torch.randn(shape) * 1e-3).cuda()
+    prev = lib.thorn_set_gemm_staged_epilogue(1)
+    try:
+        staged, co, rs = _ns_gpu(u, ns_dtype=dt)
+        lib.thorn_set_gemm_staged_epilogue(0)
+        plain, _, _ = _ns_gpu(u, ns_dtype=dt)
+    finally:
+        lib.thorn_set_gemm_staged_epilogue(prev)
+    assert np.isfinite(staged).all()
+    assert np.array_equal(staged, plain)
+
+
+@pytest.mark.parametrize("batch,m,k,c_batched", [(3, 512, 264, 1), (2, 520, 128, 0), (1, 768, 1024, 1)])
+def test_staged_epilogue_sym_addmm(batch, m, k, c_batched):
+    """sym_addmm with a per-matrix or a broadcast C: staged and register epilogues agree
+    bit for bit, and both match torch within fp16 rounding."""
+    from thorn_b200 import _native as N
+
+    lib = N.load()
+    torch.manual_seed(13)
+    a = (torch.randn(batch, m, k, device="cuda") / k ** 0.5).half()
+    bt = a.transpose(1, 2).contiguous()
+    c = torch.randn(batch if c_batched else 1, m, m, device="cuda")
+    c = ((c + c.transpose(1, 2)) / 2).half()
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    st = N.stream_of(torch.device("cuda"))
+
+    def run():
+        o = torch.empty(batch, m, m, dtype=torch.float16, device="cuda")
+        N.check(lib.thorn_sym_addmm(a.data_ptr(), bt.data_ptr(), c.data_ptr(), o.data_ptr(), batch, m, k, c_batched,
+                                    0.75, -0.5, N.F16, err.data_ptr(), st), "sym_addmm")
+        torch.cuda.synchronize()
+        return o
+
+    prev = lib.thorn_set_gemm_staged_epilogue(1)
+    try:
+        staged = run()
+        lib.thorn_set_gemm_staged_epilogue(0)
+        plain = run()
+    finally:
+        lib.thorn_set_gemm_staged_epilogue(prev)
+    assert int(err.item()) == 0
+    assert torch.equal(staged, plain)
+    assert torch.equal(staged, staged.transpose(1, 2))
+    want = 0.75 * (a.float() @ bt.float()) - 0.5 * c.float().expand(batch, m, m)
+    assert (staged.float() - want).abs().max().item() <= 2e-2 * want.abs().max().item()

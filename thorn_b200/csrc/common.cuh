@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <type_traits>
 #include <stdint.h>
 
 #include "thorn_b200.h"
@@ -50,18 +51,51 @@ template <> struct Vec8<float> {
     *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
   }
 };
+// Two fp32 values -> one packed pair of 16-bit values, one conversion
+// instruction (cvt.rn.bf16x2.f32 / cvt.rn.f16x2.f32), round-to-nearest-even
+// per element exactly like the scalar conversions.
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, __nv_bfloat16*) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, __half*) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ void unpack2(uint32_t u, float& lo, float& hi, __nv_bfloat16*) {
+  lo = __uint_as_float(u << 16);
+  hi = __uint_as_float(u & 0xFFFF0000u);
+}
+__device__ __forceinline__ void unpack2(uint32_t u, float& lo, float& hi, __half*) {
+  const __half2 h = *reinterpret_cast<const __half2*>(&u);
+  const float2 f = __half22float2(h);
+  lo = f.x;
+  hi = f.y;
+}
+
+// Round 8 fp32 values to T and back (T = float: no-op), two per instruction.
+template <class T>
+__device__ __forceinline__ void rnd8(float* v) {
+  if constexpr (!std::is_same<T, float>::value) {
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) unpack2(pack2(v[i], v[i + 1], (T*)nullptr), v[i], v[i + 1], (T*)nullptr);
+  }
+}
+
 template <class H> struct Vec8Half {
   static __device__ __forceinline__ void load(const H* p, float* v) {
-    uint4 r = *reinterpret_cast<const uint4*>(p);
-    const H* h = reinterpret_cast<const H*>(&r);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = to_f(h[i]);
+    const uint4 r = *reinterpret_cast<const uint4*>(p);
+    unpack2(r.x, v[0], v[1], (H*)nullptr);
+    unpack2(r.y, v[2], v[3], (H*)nullptr);
+    unpack2(r.z, v[4], v[5], (H*)nullptr);
+    unpack2(r.w, v[6], v[7], (H*)nullptr);
   }
   static __device__ __forceinline__ void store(H* p, const float* v) {
     uint4 r;
-    H* h = reinterpret_cast<H*>(&r);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) h[i] = from_f<H>(v[i]);
+    r.x = pack2(v[0], v[1], (H*)nullptr);
+    r.y = pack2(v[2], v[3], (H*)nullptr);
+    r.z = pack2(v[4], v[5], (H*)nullptr);
+    r.w = pack2(v[6], v[7], (H*)nullptr);
     *reinterpret_cast<uint4*>(p) = r;
   }
 };

@@ -258,11 +258,13 @@ __device__ __forceinline__ void load8f(const float* p, float* v, int n, bool vec
   for (int k = 0; k < 8; ++k) v[k] = k < n ? p[k] : 0.f;
 }
 
-// u = g + beta1 * m, evaluated identically by the momentum pass (for the norm)
-// and by the NS-input pass (for X), so both see the same u.
+// u = g + beta1 * m rounded to the NS input type U for 8 elements, evaluated
+// identically by the momentum pass (for the norm) and by the NS-input pass (for X).
 template <class U>
-__device__ __forceinline__ float nesterov_u(float g, float m, float b1) {
-  return rnd<U>(__fmaf_rn(b1, m, g));
+__device__ __forceinline__ void nesterov_u8(const float* g, const float* m, float b1, float* u) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) u[k] = __fmaf_rn(b1, m[k], g[k]);
+  rnd8<U>(u);
 }
 struct PreArgs {
   Pack<thorn_ortho_pre_tensor> pk;
@@ -305,38 +307,62 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
       load_n((const P*)e.g + off, gv, nc, vec);
       if (momentum) load_n((const S*)e.m + off, mv, nc, vec);
       if (MD) {
-        float pv[8];
+        // every step below rounds 8 values to the param dtype at once (packed
+        // conversions); lanes k >= nc hold padding and are neither summed nor stored
+        float pv[8], gain[8], pg[8];
         load_n((const P*)e.p + off, pv, nc, vec);
         const float rsp = scalar_gain ? e.row_sp[0] : e.row_sp[t.b * e.rows + r];
-        float part = 0.f;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          if (k >= nc) continue;
-          const float gain = scalar_gain ? rsp : rnd<P>(rsp * csp[k]);
-          // fast division (<= 2 fp32 ulp) before the rounding to the param dtype
-          const float pd = rnd<P>(__fdividef(pv[k], gain));
-          const float pg = rnd<P>(pd * gv[k]);
-          if (scalar_gain) {
-            part += pg;
-          } else {
-            part += rnd<P>(pg * csp[k]);
-            csum[k] += rnd<P>(pg * rsp);
+        for (int k = 0; k < 8; ++k) gain[k] = scalar_gain ? rsp : __fmul_rn(rsp, csp[k]);
+        if (!scalar_gain) rnd8<P>(gain);
+        // fast division (<= 2 fp32 ulp) before the rounding to the param dtype
+#pragma unroll
+        for (int k = 0; k < 8; ++k) pv[k] = __fdividef(pv[k], gain[k]);
+        rnd8<P>(pv);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) pg[k] = __fmul_rn(pv[k], gv[k]);
+        rnd8<P>(pg);
+        float part = 0.f;
+        if (scalar_gain) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            if (k < nc) part = __fadd_rn(part, pg[k]);
+        } else {
+          float pc[8], pr[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            pc[k] = __fmul_rn(pg[k], csp[k]);
+            pr[k] = __fmul_rn(pg[k], rsp);
           }
-          pv[k] = pd;
-          gv[k] = rnd<P>(gv[k] * gain);
+          rnd8<P>(pc);
+          rnd8<P>(pr);
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            if (k < nc) {
+              part = __fadd_rn(part, pc[k]);
+              csum[k] = __fadd_rn(csum[k], pr[k]);
+            }
         }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) gv[k] = __fmul_rn(gv[k], gain[k]);
+        rnd8<P>(gv);
         rs = part;
         store_n((P*)e.p + off, pv, nc, vec);
         if (a.write_grad) store_n((P*)e.g + off, gv, nc, vec);
       }
       if (momentum) {
+        float u[8];
+        // m = m * beta1 + g as two rounded torch ops (thorn.py:1376-1381): no fma
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float m1 = rnd<S>(mv[k] * b1);
-          mv[k] = rnd<S>(m1 + gv[k]);
-          const float u = nesterov_u<U>(gv[k], mv[k], b1);
-          if (k < nc) sq += u * u;
-        }
+        for (int k = 0; k < 8; ++k) mv[k] = __fmul_rn(mv[k], b1);
+        rnd8<S>(mv);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mv[k] = __fadd_rn(mv[k], gv[k]);
+        rnd8<S>(mv);
+        nesterov_u8<U>(gv, mv, b1, u);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (k < nc) sq = __fmaf_rn(u[k], u[k], sq);
         store_n((S*)e.m + off, mv, nc, vec);
       }
     }
@@ -382,6 +408,28 @@ __host__ __device__ inline int64_t pre_red_blocks(int64_t B, int64_t R, int64_t 
   return B * (1 + (split ? (R + 255) / 256 + (C + 255) / 256 : 0));
 }
 
+// Sequential sum of x[0], x[stride], ..., x[(n-1)*stride] (each zeroed after it
+// is read), with eight loads in flight per thread.
+__device__ __forceinline__ float strided_sum(float* x, int64_t stride, int64_t n) {
+  float s = 0.f;
+  int64_t i = 0;
+  for (; i + 8 <= n; i += 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __ldcg(x + (i + j) * stride);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      x[(i + j) * stride] = 0.f;
+      s += v[j];
+    }
+  }
+  for (; i < n; ++i) {
+    s += __ldcg(x + i * stride);
+    x[i * stride] = 0.f;
+  }
+  return s;
+}
+
 __global__ void __launch_bounds__(kThreads) pre_reduce_kernel(const __grid_constant__ PreRedArgs a) {
   __shared__ float red[32];
   const int ti = find_tensor(a.pk, blockIdx.x);
@@ -410,28 +458,12 @@ __global__ void __launch_bounds__(kThreads) pre_reduce_kernel(const __grid_const
   const int64_t nrb = (e.rows + 255) / 256;
   if (k < nrb) {
     const int64_t r = k * 256 + threadIdx.x;
-    if (r < e.rows) {
-      float s = 0.f;
-      for (int64_t c = 0; c < L.tc; ++c) {
-        float* q = sf + L.pr + (b * L.tc + c) * e.rows + r;
-        s += __ldcg(q);
-        *q = 0.f;
-      }
-      e.row_gsum[b * e.rows + r] = s;
-    }
+    if (r < e.rows) e.row_gsum[b * e.rows + r] = strided_sum(sf + L.pr + b * L.tc * e.rows + r, e.rows, L.tc);
     return;
   }
   k -= nrb;
   const int64_t cc = k * 256 + threadIdx.x;
-  if (cc < e.cols) {
-    float s = 0.f;
-    for (int64_t r = 0; r < L.tr; ++r) {
-      float* q = sf + L.pc + (b * L.tr + r) * e.cols + cc;
-      s += __ldcg(q);
-      *q = 0.f;
-    }
-    e.col_gsum[b * e.cols + cc] = s;
-  }
+  if (cc < e.cols) e.col_gsum[b * e.cols + cc] = strided_sum(sf + L.pc + b * L.tr * e.cols + cc, e.cols, L.tr);
 }
 
 // ===========================================================================
@@ -442,14 +474,6 @@ struct CastArgs {
   float beta1;
 };
 
-
-// u for one element exactly as the momentum pass computed it; `gain` is the
-// element's magnitude gain (used when the raw gradient is still in g)
-template <class P, class U>
-__device__ __forceinline__ float cast_u(bool md, float g, float m, float b1, float gain) {
-  if (md) g = rnd<P>(g * gain);
-  return nesterov_u<U>(g, m, b1);
-}
 
 template <class P, class S, class U, class X>
 __global__ void __launch_bounds__(kThreads) ns_cast_kernel(const __grid_constant__ CastArgs a) {
@@ -480,11 +504,18 @@ __global__ void __launch_bounds__(kThreads) ns_cast_kernel(const __grid_constant
     load_n(G + off, gv, nc, vec);
     load_n(M + off, mv, nc, vec);
     const float rsp = md ? (split ? e.row_sp[t.b * e.rows + r] : e.row_sp[0]) : 1.f;
+    if (md) {  // the gradient times its magnitude gain, as the momentum pass formed it
+      float gain[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float gain = split ? rnd<P>(rsp * csp[k]) : rsp;
-      v[k] = cast_u<P, U>(md, gv[k], mv[k], a.beta1, gain) * inv;
+      for (int k = 0; k < 8; ++k) gain[k] = split ? __fmul_rn(rsp, csp[k]) : rsp;
+      if (split) rnd8<P>(gain);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) gv[k] = __fmul_rn(gv[k], gain[k]);
+      rnd8<P>(gv);
     }
+    nesterov_u8<U>(gv, mv, a.beta1, v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(v[k], inv);
     store_n((X*)e.x + (t.b * e.rows + r) * ld + c, v, nc, vec);
   }
 }
@@ -520,11 +551,10 @@ __global__ void __launch_bounds__(kThreads) pnn_stats_kernel(const __grid_consta
       const int n = (int)min64(8, e.cols - c);
       float v[8];
       load_n(row + c, v, n, vec);
+      rnd8<P>(v);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float x = rnd<P>(v[k]);
-        if (k < n) s += x * x;
-      }
+      for (int k = 0; k < 8; ++k)
+        if (k < n) s += v[k] * v[k];
     }
     s = warp_sum(s);
     if (lane == 0) {
@@ -584,14 +614,18 @@ __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_const
     float uv[8], pv[8];
     load_n((const U*)e.U + off, uv, nc, vec);
     load_n((const P*)e.p + off, pv, nc, vec);
+    if (e.round_u) rnd8<P>(uv);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      float u = e.round_u ? rnd<P>(uv[k]) : uv[k];
+      float u = uv[k];
       if (e.row_scale != nullptr) u = u * scale;
       if (a.wd > 0.f && u * pv[k] >= 0.f) u = u + a.wd * pv[k];
-      pv[k] = rnd<P>(pv[k] - e.lr * u);
-      if (k < nc) sq += pv[k] * pv[k];
+      pv[k] = pv[k] - e.lr * u;
     }
+    rnd8<P>(pv);
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (k < nc) sq += pv[k] * pv[k];
     store_n((P*)e.p + off, pv, nc, vec);
   }
   if (e.p_normsq != nullptr) tile_sum_to(e.p_normsq, e.scratch, t, e.batch, e.rows, e.cols, sq, red);
@@ -659,13 +693,18 @@ __global__ void __launch_bounds__(kThreads) md_finalize_kernel(const __grid_cons
     float pv[8];
     load_n((const P*)e.p + off, pv, nc, vec);
     const float rsp = split ? e.row_sp[t.b * e.rows + r] : e.row_sp[0];
+    if (renorm) {
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      float x = pv[k];
-      if (renorm) x = rnd<P>(x * f);
-      x = rnd<P>(x * rsp);
-      if (split) x = rnd<P>(x * csp[k]);
-      pv[k] = x;
+      for (int k = 0; k < 8; ++k) pv[k] = __fmul_rn(pv[k], f);
+      rnd8<P>(pv);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) pv[k] = __fmul_rn(pv[k], rsp);
+    rnd8<P>(pv);
+    if (split) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) pv[k] = __fmul_rn(pv[k], csp[k]);
+      rnd8<P>(pv);
     }
     store_n((P*)e.p + off, pv, nc, vec);
   }

@@ -53,13 +53,17 @@ struct Cfg {
 struct Params {
   CUtensorMap tmA;
   CUtensorMap tmB;
+  // staged epilogue (2-CTA kernel, `tma_epi`): 32 x 32 blocks, 64-byte swizzle
+  CUtensorMap tmC;   // C operand, [batch or 1][M][N]
+  CUtensorMap tmD;   // D, [batch][M][N], or [batch][N][M] with trans_out
+  CUtensorMap tmD2;  // D2, [batch][M][N]
   const void* C;
   void* D;
   void* D2;
   int64_t c_bs, c_ld, d_bs, d_ld, d2_bs, d2_ld;
   int M, N, K, batch;
   float alpha, beta, diag2;
-  int sym, trans_out, c_vec, d_vec;
+  int sym, trans_out, c_vec, d_vec, tma_epi, c_bcast;
   int tiles_m, tiles_n, tiles_per_mat, total_tiles, num_kb;
   int* err;
 };
@@ -103,7 +107,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   for (uint32_t it = 1;; ++it) {
     if (mbar_try(bar, parity)) return true;
     if ((it & 255u) == 0) {
-      if (*abort) return false;
+      if (abort && *abort) return false;
       if (global_ns() - t0 > kTimeoutNs) {
         if (err) atomicExch(err, 1);
         *abort = 1;
@@ -119,6 +123,24 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* tm,
       "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
+// TMA bulk store of a shared-memory block (bulk async-group of the issuing thread).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* tm, uint32_t src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tm)),
+               "r"(src), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// all but the newest N bulk groups of this thread have finished reading shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
@@ -428,7 +450,22 @@ __global__ void __launch_bounds__(kThreadsG, 1) ns_gemm_kernel(const __grid_cons
 constexpr int BM2 = 256;  // rows of a cluster tile (128 per CTA)
 constexpr int kStages2 = 6;
 constexpr int kHalfBytes = 128 * BK * 2;  // 16 KB: one CTA's A (or B) slab per stage
-constexpr int kSmem2 = kStages2 * 2 * kHalfBytes + 256 + 1024;
+// Staged epilogue: per epilogue warp two buffer pairs, each a 32 x 32 block of
+// the output (2 KB, also the landing place of the C block) and its transpose.
+constexpr int kEpiBlock = 32 * 32 * 2;
+constexpr int kEpiWarpBytes = 4 * kEpiBlock;
+constexpr int kEpiBytes = 4 * kEpiWarpBytes;
+constexpr int kSmem2 = kStages2 * 2 * kHalfBytes + kEpiBytes + 256 + 1024;
+static_assert(kSmem2 <= 232448, "2-CTA kernel exceeds 227 KB of shared memory");
+
+// Byte offset of element (r, c) in a 32 x 32 block of 16-bit values stored in
+// the layout of a CU_TENSOR_MAP_SWIZZLE_64B box: 64-byte rows whose four
+// 16-byte chunks are permuted by chunk ^= (r / 2) % 4.  Rows written this way
+// (one row per lane) and columns (one element per lane) are both free of bank
+// conflicts.
+__device__ __forceinline__ uint32_t sw64_off(int r, int c) {
+  return (uint32_t)(r * 64 + ((((c >> 3) ^ (r >> 1)) & 3) << 4) + ((c & 7) << 1));
+}
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -493,6 +530,35 @@ __device__ __forceinline__ void decode_tile2(const Params& p, int t, int& b, int
   }
 }
 
+// Number of 32-column blocks of tile t that the epilogue warp with rows
+// [row_base, row_base + 32) of the tile stores (a prefix of the tile's 8).
+__device__ __forceinline__ int warp_blocks(const Params& p, int t, int row_base, int& b, int& tm, int& tn) {
+  decode_tile2(p, t, b, tm, tn);
+  const int row0 = tm * BM2 + row_base;
+  if (row0 >= p.M) return 0;
+  int nv = min(8, (p.N - tn * 256 + 31) >> 5);
+  if (p.sym) nv = min(nv, ((row0 + 31 - tn * 256) >> 5) + 1);  // blocks on or below the diagonal
+  return max(nv, 0);
+}
+
+// Position (t2, ch2) of the block after (t, ch) in the warp's processing order.
+__device__ __forceinline__ bool next_block(const Params& p, int t, int ch, int nv, int step, int row_base, int& t2,
+                                           int& ch2, int& b2, int& tm2, int& tn2) {
+  if (ch + 1 < nv) {
+    t2 = t;
+    ch2 = ch + 1;
+    decode_tile2(p, t, b2, tm2, tn2);
+    return true;
+  }
+  for (t2 = t + step; t2 < p.total_tiles; t2 += step) {
+    if (warp_blocks(p, t2, row_base, b2, tm2, tn2) > 0) {
+      ch2 = 0;
+      return true;
+    }
+  }
+  return false;
+}
+
 template <bool A_MN, bool B_MN, class T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
     ns_gemm2_kernel(const __grid_constant__ Params p) {
@@ -500,12 +566,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages2 * kHalfBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kStages2 * kHalfBytes);
+  uint8_t* sEpi = sB + kStages2 * kHalfBytes;  // 1024-byte aligned
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sEpi + kEpiBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + kStages2;
   uint64_t* tfull = bars + 2 * kStages2;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* cbar = tempty + 2;  // [4 epilogue warps][2 buffers]: C block landed
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(cbar + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -522,6 +590,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
       mbar_init(smem_u32(&tfull[a]), 1);
       mbar_init(smem_u32(&tempty[a]), 2 * 4 * 32);
     }
+    for (int i = 0; i < 8; ++i) mbar_init(smem_u32(&cbar[i]), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -613,6 +682,152 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
         umma_commit_pair(mapa_shared(smem_u32(&tfull[acc]), 1));
       }
     }
+  } else if (p.tma_epi) {
+    // ------------------------------ staged epilogue (both CTAs) ------------
+    // Warp q stores rows [row0, row0 + 32) of each tile, 32 columns at a time:
+    // TMEM -> registers -> alpha/beta/C, one rounding -> a swizzled 2 KB block
+    // (and its transpose when the block is mirrored or the output transposed)
+    // -> TMA bulk stores.  Blocks alternate between two buffer pairs; C blocks
+    // are TMA-loaded one block ahead into the buffer the next block uses.
+    const int q = warp & 3;
+    const int row_base = (int)rank * 128 + q * 32;
+    uint8_t* gE = sEpi + q * kEpiWarpBytes;
+    const uint32_t sE = smem_u32(gE);
+    const uint32_t cb0 = smem_u32(&cbar[2 * q]);
+    const bool has_c = p.C != nullptr;
+    const bool has_d2 = p.D2 != nullptr;
+    bool c_inflight = false;  // a C load was issued and not yet waited for
+    int c_buf = 0;
+    uint32_t c_par = 0;
+    auto load_c = [&](int n_blk, int b2, int tm2, int tn2, int ch2) {
+      const int k2 = n_blk & 1;
+      if (lane == 0) {
+        bulk_wait_read<1>();  // stores of block n_blk - 2 no longer read buffer k2
+        mbar_expect_tx(cb0 + 8 * k2, kEpiBlock);
+        tma_load_3d(sE + k2 * 2 * kEpiBlock, &p.tmC, cb0 + 8 * k2, tn2 * 256 + ch2 * 32, tm2 * BM2 + row_base,
+                    p.c_bcast ? 0 : b2);
+      }
+      c_inflight = true;
+      c_buf = k2;
+      c_par = (uint32_t)(n_blk >> 1) & 1u;
+    };
+    if (has_c) {
+      int b2, tm2, tn2;
+      for (int t0 = cid; t0 < p.total_tiles; t0 += nclusters)
+        if (warp_blocks(p, t0, row_base, b2, tm2, tn2) > 0) {
+          load_c(0, b2, tm2, tn2, 0);
+          break;
+        }
+    }
+    int n = 0;  // blocks handled by this warp so far
+    int it = 0;
+    bool aborted = false;
+    for (int t = cid; t < p.total_tiles && !aborted; t += nclusters, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
+      // warp-uniform outcome: the .sync.aligned TMEM loads and __syncwarp below need all lanes
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag, p.err))) break;
+      tc_fence_after();
+      int b, tm, tn;
+      const int nv = warp_blocks(p, t, row_base, b, tm, tn);
+      const int row0 = tm * BM2 + row_base;
+      if (nv == 0) {
+        tc_fence_before();
+        mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+        continue;
+      }
+#pragma unroll 1
+      for (int ch = 0; ch < nv; ++ch, ++n) {
+        const int col0 = tn * 256 + ch * 32;
+        const int k = n & 1;
+        uint8_t* gM = gE + k * 2 * kEpiBlock;
+        uint8_t* gT = gM + kEpiBlock;
+        const uint32_t sM = sE + k * 2 * kEpiBlock;
+        const uint32_t sT = sM + kEpiBlock;
+        float v[32];
+        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 256 + ch * 32), v);
+        if (ch == nv - 1) {  // accumulator fully read: hand it back to the MMA warp
+          tc_fence_before();
+          mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+        }
+        if (has_c) {
+          if (!__all_sync(0xffffffffu, mbar_wait(cb0 + 8 * k, (uint32_t)(n >> 1) & 1u, abort_flag, p.err))) {
+            aborted = true;
+            break;
+          }
+          c_inflight = false;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint4 r = *reinterpret_cast<const uint4*>(gM + sw64_off(lane, 8 * c));
+            const T* h = reinterpret_cast<const T*>(&r);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[8 * c + i] = p.alpha * v[8 * c + i] + p.beta * to_f(h[i]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = p.alpha * v[j];
+          if (lane == 0) bulk_wait_read<1>();  // stores of block n - 2 no longer read buffer k
+        }
+        __syncwarp();
+        const bool diag = row0 == col0;
+        const bool mirror = p.sym && row0 > col0;
+        if (!p.trans_out) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint4 r;
+            T* h = reinterpret_cast<T*>(&r);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) h[i] = from_f<T>(v[8 * c + i]);
+            *reinterpret_cast<uint4*>(gM + sw64_off(lane, 8 * c)) = r;
+          }
+        }
+        if (p.sym && diag) {
+          // upper half of a diagonal block: element (j, lane) = lower element (lane, j)
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < lane) *reinterpret_cast<T*>(gM + sw64_off(j, lane)) = from_f<T>(v[j]);
+        }
+        if (mirror || p.trans_out) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) *reinterpret_cast<T*>(gT + sw64_off(j, lane)) = from_f<T>(v[j]);
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (!p.trans_out) tma_store_3d(&p.tmD, sM, col0, row0, b);
+          if (mirror || p.trans_out) tma_store_3d(&p.tmD, sT, row0, col0, b);
+          if (has_d2 && !diag) {
+            tma_store_3d(&p.tmD2, sM, col0, row0, b);
+            if (mirror) tma_store_3d(&p.tmD2, sT, row0, col0, b);
+          }
+          bulk_commit();
+        }
+        if (has_d2 && diag) {
+          // D2 = D + diag2 I: patch the block's diagonal once D's store has read it
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
+          float dv = 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j == lane) dv = v[j];
+          *reinterpret_cast<T*>(gM + sw64_off(lane, lane)) = from_f<T>(rnd<T>(dv) + p.diag2);
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&p.tmD2, sM, col0, row0, b);
+            bulk_commit();
+          }
+        }
+        if (has_c) {
+          int t2, ch2, b2, tm2, tn2;
+          if (next_block(p, t, ch, nv, nclusters, row_base, t2, ch2, b2, tm2, tn2)) load_c(n + 1, b2, tm2, tn2, ch2);
+        }
+      }
+    }
+    if (lane == 0) bulk_wait_all<0>();
+    // a C block still in flight (abort path) must land before the CTA exits
+    if (c_inflight) mbar_wait(cb0 + 8 * c_buf, c_par, nullptr, p.err);
   } else {
     // ------------------------------ epilogue (both CTAs) -------------------
     const int q = warp & 3;
@@ -699,7 +914,8 @@ static DevInfo dev_info() {
 
 // 3-D tiled tensor map over [batch][rows][inner] with 128-byte swizzle.
 static int make_map(CUtensorMap* m, const void* base, int dtype, int64_t inner, int64_t rows, int64_t batch,
-                    int64_t ld, int64_t bs, int box_inner, int box_rows) {
+                    int64_t ld, int64_t bs, int box_inner, int box_rows,
+                    CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return THORN_ERR_UNSUPPORTED;
   cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)batch};
@@ -708,8 +924,8 @@ static int make_map(CUtensorMap* m, const void* base, int dtype, int64_t inner, 
   cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(m, dtype == THORN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
-                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? THORN_OK : THORN_ERR_ARG;
 }
 
@@ -795,6 +1011,7 @@ static int launch_any2(const GemmOp& op, gemm::Params& prm, int64_t total, int s
 }
 
 static std::atomic<int> g_pair_tiles{1};
+static std::atomic<int> g_staged_epilogue{1};
 
 template <class T>
 static int launch_any(const GemmOp& op, int BN, gemm::Params& prm, int grid, cudaStream_t st) {
@@ -856,6 +1073,25 @@ int run_gemm(const GemmOp& op, int dtype, int* err, cudaStream_t st) {
   prm.c_vec = op.C && aligned16(op.C) && (op.c_ld % 8) == 0 && (op.c_bs % 8) == 0;
   prm.d_vec = aligned16(op.D) && (op.d_ld % 8) == 0 && (op.d_bs % 8) == 0 &&
               (!op.D2 || (aligned16(op.D2) && (op.d2_ld % 8) == 0 && (op.d2_bs % 8) == 0));
+  // staged epilogue (2-CTA tiles): TMA maps of C, D, D2 with 32 x 32 boxes
+  const bool c_al = !op.C || (aligned16(op.C) && (op.c_ld % 8) == 0 && (op.c_bs % 8) == 0);
+  prm.tma_epi = pair && g_staged_epilogue.load() != 0 && prm.d_vec && c_al && !(op.D2 && op.trans_out);
+  if (prm.tma_epi) {
+    const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_64B;
+    rc = op.trans_out ? make_map(&prm.tmD, op.D, dtype, op.M, op.N, op.batch, op.d_ld, op.d_bs, 32, 32, sw)
+                      : make_map(&prm.tmD, op.D, dtype, op.N, op.M, op.batch, op.d_ld, op.d_bs, 32, 32, sw);
+    if (rc) return rc;
+    if (op.D2) {
+      rc = make_map(&prm.tmD2, op.D2, dtype, op.N, op.M, op.batch, op.d2_ld, op.d2_bs, 32, 32, sw);
+      if (rc) return rc;
+    }
+    if (op.C) {
+      prm.c_bcast = op.c_bs == 0;
+      rc = make_map(&prm.tmC, op.C, dtype, op.N, op.M, prm.c_bcast ? 1 : op.batch, op.c_ld,
+                    prm.c_bcast ? op.c_ld * op.M : op.c_bs, 32, 32, sw);
+      if (rc) return rc;
+    }
+  }
   prm.tiles_m = (op.M + BMt - 1) / BMt;
   prm.tiles_n = (op.N + BN - 1) / BN;
   if (op.sym) {
@@ -1080,6 +1316,8 @@ extern "C" int thorn_sym_addmm(const void* A, const void* B, const void* C, void
 }
 
 extern "C" int thorn_set_gemm_pair(int enable) { return g_pair_tiles.exchange(enable ? 1 : 0); }
+
+extern "C" int thorn_set_gemm_staged_epilogue(int enable) { return g_staged_epilogue.exchange(enable ? 1 : 0); }
 
 // Dense-equivalent and executed tensor-core FLOPs issued so far (for roofline reports).
 extern "C" void thorn_gemm_flops(double* dense, double* executed) {
