@@ -107,7 +107,8 @@ _lib = None
 
 
 def library_path() -> str:
-    return _build.LIB
+    """The in-tree build, or the file named by THORN_B200_LIBRARY (a build kept elsewhere)."""
+    return os.environ.get("THORN_B200_LIBRARY") or _build.LIB
 
 
 def load(build_if_missing: bool = False):
