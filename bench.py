@@ -204,6 +204,37 @@ def build_params(torch, dev, rank, world, mesh, layers=LAYERS):
     return ortho, adamw, g_ortho, g_adam
 
 
+_T0 = time.time()
+_LAST = [time.time(), "start"]
+
+
+def progress(rank, msg):
+    """One line of progress on stderr (stdout carries only the result line)."""
+    _LAST[0], _LAST[1] = time.time(), msg
+    print(f"[bench rank {rank} +{time.time() - _T0:.1f}s] {msg}", file=sys.stderr, flush=True)
+
+
+def stall_watchdog(rank, limit_s):
+    """Multi-rank runs: end the process if no stage completes for `limit_s` seconds.
+
+    A rank blocked on the host inside a collective call is invisible to the
+    process group's own timeout; this turns such a stall into an exit with the
+    last completed stage in the log instead of a run that waits for its caller's
+    time limit.
+    """
+    import threading
+
+    def run():
+        while True:
+            time.sleep(5)
+            if time.time() - _LAST[0] > limit_s:
+                print(f"[bench rank {rank}] no progress for {limit_s}s after '{_LAST[1]}'; exiting",
+                      file=sys.stderr, flush=True)
+                os._exit(3)
+
+    threading.Thread(target=run, daemon=True).start()
+
+
 def gpu_arm(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -216,6 +247,7 @@ def gpu_arm(args, rank, world, local_rank):
     if world > 1:
         from torch.distributed.device_mesh import init_device_mesh
         mesh = init_device_mesh("cuda", (world,))
+        progress(rank, "device mesh ready")
     ortho, adamw, g_ortho, g_adam = build_params(torch, dev, rank, world, mesh, args.layers)
     params = ortho + adamw
     grads = g_ortho + g_adam
@@ -242,10 +274,12 @@ def gpu_arm(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    for _ in range(args.warmup):
+    progress(rank, "params built")
+    for i in range(args.warmup):
         feed()
         opt.step()
-    torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        progress(rank, f"warm-up step {i + 1} done")
 
     # ---------------- device-timed steps (inputs resident in HBM)
     clocks = None
@@ -279,6 +313,7 @@ def gpu_arm(args, rank, world, local_rank):
     barrier()
     launches = _native.launch_count() - launches0
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    progress(rank, "timed steps done")
     prof = opt.profile_ns
     opt.profile_ns = None
     # host cost of one step on an idle GPU (nothing blocks on a full launch queue)
@@ -342,6 +377,7 @@ def gpu_arm(args, rank, world, local_rank):
             dist.all_reduce(t)
             bi, bo = int(t[0]), int(t[1])
         e2e = {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo}
+        progress(rank, "end-to-end steps done")
         del h_grads, h_params, d_grads
 
     if rank != 0:
@@ -461,6 +497,10 @@ def main():
     if world > 1:
         import datetime
 
+        # the exchanges are point-to-point and the all-reduces a few KB: NVLink
+        # SHARP buys nothing here, so NCCL skips setting up its multicast buffers
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        stall_watchdog(rank, 420)
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)

@@ -1,6 +1,6 @@
 """The FSDP2 / DTensor Shard(0) path.
 
-CPU (gloo, 2 ranks): owner assignment and the slab exchange plans move every
+CPU (gloo, 2-4 ranks): owner assignment and the slab exchange plans move every
 row slab to its owner and every result slab back.  GPU: the full sharded step
 (world 1 on any box, world 2 when two GPUs are visible) against the CPU oracle
 on the full tensors -- the reference's own MD + FSDP2 path does not run on
@@ -53,7 +53,7 @@ def _exchange_worker(rank, world, port, result):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         ranks = list(range(world))
-        shapes = [(8, 3), (4, 5), (6, 2), (2, 7)]  # global rows divisible by world
+        shapes = [(24, 3), (12, 5), (36, 2), (12, 7), (48, 4)]  # global rows divisible by world
         full = [torch.arange(r * c, dtype=torch.float32).reshape(r, c) + 100 * j for j, (r, c) in enumerate(shapes)]
         owners = assign_owners([r * c for r, c in shapes], world)
         rows = [r // world for r, _ in shapes]
@@ -83,12 +83,42 @@ def _exchange_worker(rank, world, port, result):
         dist.destroy_process_group()
 
 
-def test_slab_exchange_gloo_two_ranks():
+@pytest.mark.parametrize("world", [2, 3, 4])
+def test_slab_exchange_gloo(world):
+    """Gather and scatter plans through the shifted pairwise rounds, odd world sizes included."""
     ctx = mp.get_context("spawn")
     mgr = ctx.Manager()
     result = mgr.dict()
-    mp.start_processes(_exchange_worker, args=(2, _free_port(), result), nprocs=2, join=True, start_method="spawn")
-    assert dict(result) == {0: True, 1: True}
+    mp.start_processes(_exchange_worker, args=(world, _free_port(), result), nprocs=world, join=True,
+                       start_method="spawn")
+    assert dict(result) == {r: True for r in range(world)}
+
+
+def test_exchange_rounds_pair_every_message():
+    """Llama-3-8B matrix set at 8 shards: in every round the messages i sends to i + d are, in
+    order and by shape, the messages i + d receives from i (the condition NCCL matches on)."""
+    world = 8
+    shapes = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096), (14336, 4096),
+              (4096, 14336)] * 32
+    owners = assign_owners([ns_flops(r, c, 5) for r, c in shapes], world)
+    plans = {}
+    for me in range(world):
+        g = plan_gather(owners, me, world, lambda j, me=me: ("x", j, me, shapes[j][0] // world, shapes[j][1]),
+                        lambda j, s: ("x", j, s, shapes[j][0] // world, shapes[j][1]))
+        sc = plan_scatter(owners, me, world,
+                          lambda j, s: [("u", j, s)] + ([("f", j, s)] if shapes[j][0] > shapes[j][1] else []),
+                          lambda j, me=me: [("u", j, me)] + ([("f", j, me)] if shapes[j][0] > shapes[j][1] else []))
+        plans[me] = (g, sc)
+    for k in range(2):
+        for d in range(1, world):
+            for i in range(world):
+                to = (i + d) % world
+                sent = [s.tensor for s in plans[i][k][0] if s.peer == to]
+                got = [r.tensor for r in plans[to][k][1] if r.peer == i]
+                assert sent == got
+        total_sent = sum(len(plans[i][k][0]) for i in range(world))
+        total_recv = sum(len(plans[i][k][1]) for i in range(world))
+        assert total_sent == total_recv > 0
 
 
 def _mesh_error_worker(rank, world, port, result):

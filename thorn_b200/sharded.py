@@ -12,12 +12,12 @@ and scatters fp32 results back.  Here, per step:
 2. every rank normalises its rows by the global norm and casts them to the NS
    operand type, writing straight into the owner's NS input buffer when it is
    the owner, else into a send slab;
-3. one batched NCCL point-to-point exchange moves all slabs to their owners
-   (half the bytes of the reference's fp32 gather);
+3. one NCCL point-to-point exchange (world - 1 shifted pairwise rounds) moves
+   all slabs to their owners (half the bytes of the reference's fp32 gather);
 4. owners run batched Newton-Schulz (+ per-neuron-norm statistics with the
    row scale folded into one factor per row);
-5. one batched exchange returns the 16-bit result rows and the fp32 row
-   factors;
+5. one exchange of the same form returns the 16-bit result rows and the fp32
+   row factors;
 6. every rank applies the update to its own rows (and, with decouple_md,
    all-reduces ||p||^2 for the renorm).
 
@@ -81,17 +81,27 @@ class Slab:
 
 
 def exchange(sends: list[Slab], recvs: list[Slab], ranks: list[int], group) -> None:
-    """All messages of one exchange in a single batched P2P call.
+    """All messages of one exchange, as world - 1 shifted pairwise rounds.
 
-    Callers list messages in a canonical order (matrix index ascending, then
-    peer ascending), so the sends from rank a to rank b and b's receives from a
-    appear in the same order on both sides, which is how NCCL matches them.
+    In round d every shard index i sends only to i + d and receives only from
+    i - d (mod world), one batched P2P call per round: each call pairs every
+    rank with exactly one destination and one source, the permutation pattern
+    that NVSwitch serves at full bandwidth and for which NCCL sets up at most
+    two new peer connections per call.  Callers list messages in a canonical
+    order (matrix index ascending, then peer ascending), so the sends from a to
+    b and b's receives from a appear in the same order on both sides, which is
+    how NCCL matches them.  The calls only make the current stream wait; the
+    host does not block.
     """
-    ops = [dist.P2POp(dist.isend, s.tensor, ranks[s.peer], group) for s in sends]
-    ops += [dist.P2POp(dist.irecv, r.tensor, ranks[r.peer], group) for r in recvs]
-    if ops:
-        for w in dist.batch_isend_irecv(ops):
-            w.wait()
+    world = len(ranks)
+    me = ranks.index(dist.get_rank())
+    for d in range(1, world):
+        to, frm = (me + d) % world, (me - d) % world
+        ops = [dist.P2POp(dist.isend, s.tensor, ranks[to], group) for s in sends if s.peer == to]
+        ops += [dist.P2POp(dist.irecv, r.tensor, ranks[frm], group) for r in recvs if r.peer == frm]
+        if ops:
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()
 
 
 def plan_gather(owners: list[int], me: int, world: int, my_rows, owner_rows):
