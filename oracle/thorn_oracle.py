@@ -433,8 +433,6 @@ class Group:
         self.__dict__.update(cfg)
         self.orthogonalize = bool(d["orthogonalize"])
         self.lr = float(d["lr"])
-        if self.momentum_align:
-            raise NotImplementedError("momentum_align is outside the oracle's scope")
         self.coeffs = optimal_composition(self.lower_bound, self.iters, self.safety_factor, self.cushion)
         self.restarts = gram_ns_restarts(self.coeffs)
 
@@ -464,6 +462,54 @@ class Group:
         if tn == "max":
             return rnd(F32(max(p.shape[-2], p.shape[-1]) ** 0.5), dt)
         raise NotImplementedError(tn)
+
+
+# ---------------------------------------------------------------------------
+# Magma: momentum-aligned gradient masking (thorn.py:800-836)
+# ---------------------------------------------------------------------------
+W1_C = 0xD07EBC63274654C7
+MASK64 = (1 << 64) - 1
+
+
+def w1rand(s: int) -> tuple[int, int]:
+    """The reference's 64-bit generator step (thorn.py:800-804): (new state, output)."""
+    s = (s + W1_C) & MASK64
+    t = s * (s ^ W1_C)
+    return s, ((t >> 64) ^ t) & MASK64
+
+
+def cosine_similarity(a, b) -> float:
+    """torch.nn.functional.cosine_similarity of two flat vectors (eps 1e-8), in float64."""
+    a = np.asarray(a, np.float64).reshape(-1)
+    b = np.asarray(b, np.float64).reshape(-1)
+    na = max(float(np.sqrt(np.sum(a * a))), 1e-8)
+    nb = max(float(np.sqrt(np.sum(b * b))), 1e-8)
+    return float(np.sum((a / na) * (b / nb)))
+
+
+def magma_scale(g, m, st, dt: str, tau: float = 2.0, p: float = 0.9, sharded: bool = False) -> float:
+    """LR multiplier of one Magma step (thorn.py:806-836); 0.0 means "skip this update".
+
+    ``g``: the (direction-recovered) gradient, ``m``: the moment before this
+    step's update.  ``sharded``: the statistics path of the sharded step
+    (fp32 dot / (|g| |m|) clamped at 1e-12, thorn.py:820-829).
+    """
+    if sharded:
+        g64, m64 = np.asarray(g, np.float64).reshape(-1), np.asarray(m, np.float64).reshape(-1)
+        dot = F32(np.sum(g64 * m64))
+        gsq, msq = F32(np.sum(g64 * g64)), F32(np.sum(m64 * m64))
+        cos = F32(dot / F32(max(F32(np.sqrt(gsq)) * F32(np.sqrt(msq)), F32(1e-12))))
+        s_t = F32(1.0 / (1.0 + np.exp(-np.float64(F32(cos / F32(tau))))))
+        sdt = "f32"  # a 0-d bf16 tensor plus a 0-d fp32 tensor promotes to fp32
+    else:
+        cos = rnd(F32(cosine_similarity(g, m)), dt)
+        s_t = rnd(1.0 / (1.0 + np.exp(-np.float64(rnd(cos / F32(tau), dt)))), dt)
+        sdt = dt
+    st["s"] = rnd(rnd(F32(p) * st["s"], dt) + rnd(F32(1 - p) * s_t, sdt), sdt)
+    st["random_state"], out = w1rand(int(st["random_state"]))
+    if out % 2 != 0:
+        return 0.0
+    return float(st["s"])
 
 
 def norm_axes(p):
@@ -548,7 +594,11 @@ class OracleTHORN:
     dtype, thorn.py:1596-1599).
     """
 
-    def __init__(self, groups):
+    def __init__(self, groups, seed_fn=None):
+        """``seed_fn()``: the next Magma seed, called once per momentum_align
+        parameter at state initialisation in group and parameter order -- where
+        the reference draws ``torch.randint`` (thorn.py:1616-1633)."""
+        self.seed_fn = seed_fn
         self.groups = []
         for d in groups:
             g = Group(d)
@@ -581,9 +631,13 @@ class OracleTHORN:
                 st["gain_moment"] = np.zeros((), F32)
                 st["gain_variance"] = np.zeros((), F32)
             st["target_norm"] = grp.target_norm_(p, dt)
+        if grp.momentum_align:
+            st["random_state"] = int(self.seed_fn())
+            st["s"] = rnd(np.ones((), F32), dt)
 
     def step(self, grads):
-        """``grads``: per group, a list of float32 arrays (None = no grad)."""
+        """``grads``: per group, a list of float32 arrays, ``SparseRows`` (AdamW
+        groups) or None (no grad)."""
         for grp, gl in zip(self.groups, grads):
             idx = [i for i, g in enumerate(gl) if g is not None]
             for i in idx:
@@ -604,17 +658,19 @@ class OracleTHORN:
             p_g = gains = None
             if grp.decouple_md:
                 p, g, p_g, gains = recover_direction(p, g, st, dt)
+            # Magma on the recovered gradient and the moment before this step (thorn.py:1392)
+            scale = magma_scale(g, st["moment"], st, dt) if grp.momentum_align else 1.0
             # momentum (thorn.py:1376-1381): m = m*b1 + g ; u = g + b1*m
             m = rnd(st["moment"] * b1, sdt)
             m = rnd(m + g, sdt)
             st["moment"] = m
             udt = _promote(dt, sdt)
             u = rnd(g + alpha(grp.betas[0], udt) * m, udt)
-            apply = (st["step"] + 1) % self.update_rate == 0
+            apply = scale != 0.0 and (st["step"] + 1) % self.update_rate == 0
             if apply:
                 U = polar_decomp(u, grp.coeffs[: grp.iters], grp.restarts, udt)
                 U = rnd(U, dt)
-                lr = grp.lr * lr_scale_ortho(U.shape, grp.scaling_mode_, grp.target_rms)
+                lr = grp.lr * lr_scale_ortho(U.shape, grp.scaling_mode_, grp.target_rms) * scale
                 if grp.needs_pnn(p.shape):
                     U = per_neuron_norm(U, dt)
                 p, _ = weight_decay_update(p, U, grp.weight_decay, lr, dt)
@@ -633,15 +689,24 @@ class OracleTHORN:
         for i in idx:
             st = grp.state[i]
             p = grp.params[i]
-            g = rnd(gl[i], dt)
             step = st["step"]
             rect = compute_rect(grp.betas, grp.rectify, step)
+            gi = gl[i]
+            if isinstance(gi, SparseRows) and grp.decouple_md:
+                gi = gi.dense(p.shape)  # thorn.py:1667-1668: sparse grads are densified under MD
+            if isinstance(gi, SparseRows):
+                if self._sparse_adam_step(grp, i, gi, rect):
+                    st["step"] += 1
+                continue
+            g = rnd(gi, dt)
+            # Magma on the raw gradient, before direction recovery (thorn.py:1702)
+            scale = magma_scale(g, st["moment"], st, dt) if grp.momentum_align else 1.0
             p_g = gains = None
             if grp.decouple_md:
                 p, g, p_g, gains = recover_direction(p, g, st, dt)
-            apply = (step + 1) % self.update_rate == 0
+            apply = scale != 0.0 and (step + 1) % self.update_rate == 0
             newp, m, v = adam_update(p if apply else None, g, st["moment"], st["variance"], step, b1, b2,
-                                     grp.lr * rect, grp.weight_decay, grp.eps, dt,
+                                     grp.lr * rect * scale, grp.weight_decay, grp.eps, dt,
                                      degenerate=(rect == 0.0), sdt=grp.state_dtype)
             st["moment"], st["variance"] = m, v
             if apply:
@@ -653,6 +718,55 @@ class OracleTHORN:
                 p = reassemble_md(p, st, dt)
             grp.params[i] = p
             st["step"] += 1
+
+
+class SparseRows:
+    """A row-sparse gradient (torch sparse COO with one sparse dimension):
+    ``indices`` of rows (duplicates allowed) and one value row per index."""
+
+    def __init__(self, indices, values):
+        self.indices = np.asarray(indices, dtype=np.int64).reshape(-1)
+        self.values = np.asarray(values, dtype=F32)
+
+    def coalesce(self):
+        """Sorted unique rows; duplicate rows summed (torch ``coalesce``)."""
+        uniq, inv = np.unique(self.indices, return_inverse=True)
+        vals = np.zeros((len(uniq),) + self.values.shape[1:], dtype=np.float64)
+        np.add.at(vals, inv, self.values.astype(np.float64))
+        return uniq, vals.astype(F32)
+
+    def dense(self, shape):
+        out = np.zeros(shape, dtype=np.float64)
+        np.add.at(out, self.indices, self.values.astype(np.float64))
+        return out.astype(F32)
+
+
+def _sparse_adam_step(self, grp: Group, i, gs: SparseRows, rect) -> bool:
+    """Row-sparse (R)AdamW (thorn.py:1669-1698); False when the gradient has no rows
+    (the reference then leaves the step count unchanged)."""
+    st, p, dt = grp.state[i], grp.params[i], grp.dtype
+    idx, rows = gs.coalesce()
+    if idx.size == 0:
+        return False
+    rows = rnd(rows, dt)
+    m_rows, v_rows = st["moment"][idx], st["variance"][idx]
+    scale = magma_scale(rows, m_rows, st, dt) if grp.momentum_align else 1.0
+    step = st["step"]
+    apply = scale != 0.0 and (step + 1) % self.update_rate == 0
+    newp, m_rows, v_rows = adam_update(p[idx] if apply else None, rows, m_rows, v_rows, step, grp.betas[0],
+                                       grp.betas[1], grp.lr * rect * scale, grp.weight_decay, grp.eps, dt,
+                                       degenerate=(rect == 0.0), sdt=grp.state_dtype)
+    st["moment"] = st["moment"].copy()
+    st["variance"] = st["variance"].copy()
+    st["moment"][idx], st["variance"][idx] = m_rows, v_rows
+    if apply:
+        p = p.copy()
+        p[idx] = rnd(newp, dt)
+        grp.params[i] = p
+    return True
+
+
+OracleTHORN._sparse_adam_step = _sparse_adam_step
 
 
 def _promote(a: str, b: str) -> str:

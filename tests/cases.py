@@ -93,6 +93,25 @@ CASES = {
     ]),
     # BASELINE config 2 shapes (flattened conv kernels) -- the many-tiny-matrices case.
     "vad": dict(steps=3, grad_std=1e-3, groups=_vad_groups(flatten=True)),
+    # Magma momentum-aligned masking (thorn.py:800-836) on both group kinds, with and without MD.
+    "magma_small": dict(steps=6, grad_std=1e-3, groups=[
+        dict(orthogonalize=True, shapes=[(64, 64), (96, 64), (64, 160)], init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=2e-3, weight_decay=0.1, momentum_align=True)),
+        dict(orthogonalize=True, shapes=[(64, 96)], init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=8e-3, decouple_md=True, momentum_align=True)),
+        dict(orthogonalize=False, shapes=[(64,), (40, 24)], init=("normal", 0.1), dtype="f32",
+             opts=dict(lr=1e-3, weight_decay=0.1, momentum_align=True)),
+        dict(orthogonalize=False, shapes=[(48, 16)], init=("normal", 0.5), dtype="f32",
+             opts=dict(lr=1e-3, decouple_md=True, momentum_align=True)),
+    ]),
+    # Row-sparse gradients on (R)AdamW parameters (thorn.py:1667-1698): duplicate rows, a 1-D
+    # embedding, a step whose sparse gradient has no rows, Magma on sparse rows.
+    "sparse_small": dict(steps=4, grad_std=1e-3, groups=[
+        dict(orthogonalize=False, shapes=[(100, 16), (32,), (60, 8), (40,)], init=("normal", 0.1), dtype="f32",
+             opts=dict(lr=1e-3, weight_decay=0.1), sparse={0: 24, 2: 10, 3: 6}, sparse_empty={2: [2]}),
+        dict(orthogonalize=False, shapes=[(50, 12)], init=("normal", 0.1), dtype="f32",
+             opts=dict(lr=1e-3, momentum_align=True, rectify=True, eps=1e-8), sparse={0: 16}),
+    ]),
 }
 
 
@@ -115,13 +134,33 @@ def build_params(case: dict):
 
 
 def build_grads(case: dict, s: int):
-    """Grads for step ``s`` (0-based), per group, in the group's dtype."""
+    """Grads for step ``s`` (0-based), per group, in the group's dtype.
+
+    Parameters listed in a group's ``sparse`` map get a torch sparse COO
+    gradient with one sparse dimension: ``nnz`` row indices drawn with
+    replacement (so rows repeat) and one value row each; ``sparse_empty`` lists
+    steps at which such a gradient has no rows at all."""
     torch.manual_seed(1000 + s)
     out = []
     for grp in case["groups"]:
         dt = TORCH_DTYPES[grp["dtype"]]
-        out.append([(torch.randn(shp) * case["grad_std"]).to(dt) for shp in grp["shapes"]])
+        sparse, empty = grp.get("sparse", {}), grp.get("sparse_empty", {})
+        gs = []
+        for pi, shp in enumerate(grp["shapes"]):
+            if pi in sparse:
+                nnz = 0 if s in empty.get(pi, ()) else sparse[pi]
+                idx = torch.randint(0, shp[0], (nnz,))
+                vals = (torch.randn((nnz, *shp[1:])) * case["grad_std"]).to(dt)
+                gs.append(torch.sparse_coo_tensor(idx[None], vals, shp))
+            else:
+                gs.append((torch.randn(shp) * case["grad_std"]).to(dt))
+        out.append(gs)
     return out
+
+
+def magma_seed() -> int:
+    """The reference's Magma seed draw at state initialisation (thorn.py:1616-1620)."""
+    return int(torch.randint(0, (1 << 63) - 1, (), dtype=torch.uint64).item())
 
 
 def group_dicts(case: dict, params):

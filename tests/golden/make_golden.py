@@ -35,6 +35,8 @@ LIMITS = {"vad": (256, 256)}
 
 
 def _np(t: torch.Tensor) -> np.ndarray:
+    if t.is_sparse:
+        t = t.to_dense()
     return t.detach().to(torch.float32).cpu().numpy().copy()
 
 
@@ -73,6 +75,8 @@ def run_case(THORN, name: str) -> dict:
                     for k, v in opt.state[p].items():
                         if isinstance(v, torch.Tensor):
                             _store(out, f"{base}/{k}", v, lim)
+                        elif isinstance(v, int) and v >= 1 << 63:
+                            out[f"{base}/{k}"] = np.asarray(v, dtype=np.uint64)  # Magma generator state
                         else:
                             out[f"{base}/{k}"] = np.asarray(v)
     return out

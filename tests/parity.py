@@ -34,12 +34,12 @@ def run_oracle(name: str, steps: int | None = None, state_dtype: str | None = No
             d["state_dtype"] = state_dtype
         d["params"] = [t.float().numpy() for t in ps]
         groups.append(d)
-    orc = OracleTHORN(groups)
+    orc = OracleTHORN(groups, seed_fn=C.magma_seed)
     n = case["steps"] if steps is None else steps
     snaps = {}
     for s in range(n):
         grads = C.build_grads(case, s)
-        orc.step([[t.float().numpy() for t in gs] for gs in grads])
+        orc.step([[oracle_grad(t) for t in gs] for gs in grads])
         if s == 0 or s == n - 1:
             tag = "step1" if s == 0 else "final"
             snaps[tag] = (
@@ -48,6 +48,15 @@ def run_oracle(name: str, steps: int | None = None, state_dtype: str | None = No
                   for st in g.state] for g in orc.groups],
             )
     return orc, snaps
+
+
+def oracle_grad(t):
+    """A torch gradient as the oracle takes it: float32 array, or ``SparseRows``."""
+    from oracle.thorn_oracle import SparseRows
+
+    if t.is_sparse:
+        return SparseRows(t._indices()[0].numpy(), t._values().float().numpy())
+    return t.float().numpy()
 
 
 def compare_tensor(mine: np.ndarray, gold: dict, key: str, base: np.ndarray | None = None):
@@ -84,8 +93,8 @@ def compare_run(name: str, gold: dict, snaps: dict, init_params):
                 base = f"{tag}/g{gi}/p{pi}"
                 errs[(tag, gi, pi, "param")] = compare_tensor(p, gold, base + "/param", init_params[gi][pi])
                 for k, v in st.items():
-                    if k == "step":
-                        assert int(v) == int(gold[f"{base}/{k}"]), (base, k)
+                    if k in ("step", "random_state"):  # integers: exact (Magma's generator state too)
+                        assert int(v) == int(gold[f"{base}/{k}"]), (base, k, int(v), int(gold[f"{base}/{k}"]))
                         continue
                     if isinstance(v, np.ndarray) or np.isscalar(v):
                         errs[(tag, gi, pi, k)] = compare_tensor(np.asarray(v, dtype=np.float32), gold, f"{base}/{k}")
