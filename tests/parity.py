@@ -13,12 +13,15 @@ def load_golden(path: str) -> dict:
         return {k: z[k] for k in z.files}
 
 
-def run_oracle(name: str, steps: int | None = None, state_dtype: str | None = None, cpu_quirks: bool = False):
+def run_oracle(name: str, steps: int | None = None, state_dtype: str | None = None, cpu_quirks: bool = False,
+               seeds: list | None = None):
     """Step the CPU oracle on a case; returns (oracle, snapshots{tag: (params, states)}).
 
     ``cpu_quirks`` models the reference's eager CPU path (used to pin the oracle
     against the golden vectors, which were produced on CPU); otherwise the
     oracle models the reference's CUDA path (fused fp32 Triton kernels).
+    ``seeds``: the Magma seeds in initialisation order (default: drawn from
+    torch's CPU generator exactly where the reference draws them).
     """
     from oracle import thorn_oracle as O
     from oracle.thorn_oracle import OracleTHORN
@@ -34,7 +37,8 @@ def run_oracle(name: str, steps: int | None = None, state_dtype: str | None = No
             d["state_dtype"] = state_dtype
         d["params"] = [t.float().numpy() for t in ps]
         groups.append(d)
-    orc = OracleTHORN(groups, seed_fn=C.magma_seed)
+    seed_fn = C.magma_seed if seeds is None else iter(list(seeds)).__next__
+    orc = OracleTHORN(groups, seed_fn=seed_fn)
     n = case["steps"] if steps is None else steps
     snaps = {}
     for s in range(n):

@@ -45,6 +45,21 @@ __all__ = ["THORN", "THORNOrthoGroup", "THORNNonOrthoGroup", "THORNGroup"]
 _TargetNorm = Union[Literal["init", "min", "max"], Callable[[torch.Tensor], Union[torch.Tensor, float]]]
 LN_E_SUB_1 = 0.5413248546  # softplus(LN_E_SUB_1) == 1 (thorn.py:1602)
 
+# Magma momentum-aligned masking (thorn.py:806-836): score temperature and EMA
+# weight, and the 64-bit generator that decides which steps are masked.
+MAGMA_TAU = 2.0
+MAGMA_EMA = 0.9
+_W1_C = 0xD07EBC63274654C7
+_U64 = (1 << 64) - 1
+
+
+def _w1rand(state: int) -> tuple[int, int]:
+    """One generator step (thorn.py:800-804): state += C; t = state * (state ^ C)
+    as a 128-bit product; output = high half ^ low half.  Returns (state, output)."""
+    state = (state + _W1_C) & _U64
+    t = state * (state ^ _W1_C)
+    return state, ((t >> 64) ^ t) & _U64
+
 
 @dataclass
 class GroupConfig:
@@ -230,7 +245,8 @@ class _Arena:
 
 class _Item:
     __slots__ = ("p", "g", "state", "B", "R", "C", "apply", "pdt", "sdt", "normsq", "rs", "cs", "sig_r", "sig_c",
-                 "rgs", "cgs", "rs_new", "cs_new", "pnorm", "scalar", "ggrad_r", "ggrad_c", "split")
+                 "rgs", "cgs", "rs_new", "cs_new", "pnorm", "scalar", "ggrad_r", "ggrad_c", "split", "scale",
+                 "m_rows", "v_rows")
 
 
 class THORN(Optimizer):
@@ -350,16 +366,85 @@ class THORN(Optimizer):
                 state["gain_moment"] = torch.zeros((), dtype=p.dtype, device=p.device)
                 state["gain_variance"] = torch.zeros((), dtype=p.dtype, device=p.device)
             state["target_norm"] = cfg.target_norm_(p)
+        if cfg.momentum_align:
+            # drawn from torch's generator of the gradient's device, so torch.manual_seed
+            # reproduces it (thorn.py:1616-1633): a value in [0, 2^63 - 1).  The reference
+            # asks for uint64; int64 draws the same value from the same generator state and
+            # every device type implements it.
+            g = p.grad
+            seed = int(torch.randint(0, (1 << 63) - 1, (), device=_local(g).device, dtype=torch.int64).item())
+            if isinstance(p, DTensor) and cfg.orthogonalize and \
+                    not all(isinstance(pl, Replicate) for pl in p.placements):
+                # every shard of a matrix must mask the same steps: take the first shard's seed
+                from .sharded import shard_group
+                ranks, group = shard_group(p, self.rank)
+                box = [seed]
+                dist.broadcast_object_list(box, src=ranks[0], group=group)
+                seed = int(box[0])
+            state["random_state"] = seed
+            state["s"] = torch.ones((), dtype=p.dtype, device=_local(p).device)
+
+    def _magma(self, items, cfg, recovered: bool, group=None) -> None:
+        """Magma masking (thorn.py:806-836) for a list of launch records.
+
+        Sets ``it.scale``, the LR multiplier, on every item, and clears ``it.apply``
+        where the generator masks the step.  The score compares the gradient
+        (direction-recovered under decouple_md when ``recovered``) with the moment
+        before this step's update (``it.m_rows`` when set: the gathered moment
+        rows of a sparse update).  ``group``: shard process group: the three sums
+        of all items are all-reduced in one call and the cosine is formed in fp32
+        (thorn.py:820-829).  The smoothed scores of all items are read back to the
+        host once per call (the reference reads each with ``.item()``).
+        """
+        for it in items:
+            it.scale = 1.0
+        if not cfg.momentum_align or not items:
+            return
+        flats = []
+        for it in items:
+            st = it.state
+            g = it.g
+            if recovered and cfg.decouple_md:
+                if it.split:
+                    gain = F.softplus(_local(st["row_gain"])) * F.softplus(_local(st["col_gain"]))
+                else:
+                    gain = F.softplus(_local(st["gain"]))
+                g = g * gain
+            m = getattr(it, "m_rows", None)
+            if m is None:
+                m = _local(st["moment"])
+            flats.append((g.reshape(-1), m.reshape(-1)))
+        if group is not None:
+            stats = torch.stack([torch.stack([(g * m).sum(), g.square().sum(), m.square().sum()]).float()
+                                 for g, m in flats])
+            dist.all_reduce(stats, group=group)
+            cos = [stats[i, 0] / (stats[i, 1].sqrt() * stats[i, 2].sqrt()).clamp_min(1e-12) for i in range(len(flats))]
+        else:
+            cos = [F.cosine_similarity(g, m, dim=0) for g, m in flats]
+        scores = []
+        for it, c in zip(items, cos):
+            st = it.state
+            st["s"] = MAGMA_EMA * st["s"] + (1 - MAGMA_EMA) * torch.sigmoid(c / MAGMA_TAU)
+            scores.append(st["s"].float())
+        for it, v in zip(items, torch.stack(scores).tolist()):
+            st = it.state
+            st["random_state"], out = _w1rand(int(st["random_state"]))
+            if out % 2:
+                it.scale, it.apply = 0.0, False
+            else:
+                it.scale = v
 
     def _step_params(self, params, cfg: GroupConfig, gdict):
-        if cfg.momentum_align:
-            raise NotImplementedError("momentum_align (Magma) is not implemented by thorn_b200")
         sharded, local = [], []
         for p in params:
             if p is None or p.grad is None:
                 continue
             if p.grad.is_sparse:
-                raise NotImplementedError("sparse gradients are not implemented by thorn_b200")
+                if cfg.orthogonalize or isinstance(p.data, DTensor):
+                    raise NotImplementedError("sparse gradients are implemented for (R)AdamW parameters on one "
+                                              "device only")
+                if cfg.decouple_md or p.grad.sparse_dim() != 1:
+                    p.grad = p.grad.to_dense()  # thorn.py:1667-1668
             state = self.state[p]
             if "step" not in state:
                 self._init_state(p, state, cfg, gdict)
@@ -563,6 +648,8 @@ class THORN(Optimizer):
         md = cfg.decouple_md
         arena = _Arena()
         items = self._items(params, cfg, arena, ortho=True)
+        # Magma looks at the direction-recovered gradient and the moment before this step (thorn.py:1389-1392)
+        self._magma(items, cfg, recovered=True)
         b1 = float(cfg.betas[0])
         ns_code = N.dtype_code(self.ns_dtype)
         # NS batches: bucket by (rows, cols, p dtype, state dtype)
@@ -659,7 +746,7 @@ class THORN(Optimizer):
                     U.data_ptr() + off * R * C * usz, it.p.data_ptr(),
                     None if row_scale is None else row_scale.data_ptr() + off * R * 4,
                     None if mat_stats is None else mat_stats.data_ptr() + off * 2 * 4,
-                    arena.ptr(it.pnorm) if md else None, it.B, it.R, it.C, lr_eff, sp if md else None, 1))
+                    arena.ptr(it.pnorm) if md else None, it.B, it.R, it.C, lr_eff * it.scale, sp if md else None, 1))
                 off += it.B
             N.check(lib.thorn_ortho_post_multi(N.array(N.OrthoPostTensor, posts), len(posts), ns_code,
                                                N.dtype_code(pdt), float(cfg.weight_decay), stream), "ortho_post_multi")
@@ -672,14 +759,71 @@ class THORN(Optimizer):
         del keep
 
     # ------------------------------------------------------- (R)AdamW group
+    def _sparse_rows(self, params, cfg):
+        """Launch records of row-sparse gradients (thorn.py:1669-1698): the moment,
+        variance (and, when applied, parameter) rows a gradient touches are gathered
+        into contiguous buffers, updated by the AdamW kernel and copied back by
+        ``_scatter_rows``.  Parameters whose gradient has no rows are left out: the
+        reference then keeps their step count and gradient."""
+        recs = []
+        for p in params:
+            g = p.grad.coalesce()
+            idx = g.indices()[0]
+            if idx.numel() == 0:
+                continue
+            st = self.state[p]
+            it = _Item()
+            it.g = g.values().contiguous()
+            it.state = st
+            it.apply = (st["step"] + 1) % self._update_rate == 0
+            it.pdt, it.sdt = p.dtype, st["moment"].dtype
+            it.m_rows = st["moment"].index_select(0, idx)
+            it.v_rows = st["variance"].index_select(0, idx)
+            recs.append((p, idx, it))
+        self._magma([it for _, _, it in recs], cfg, recovered=False)
+        for p, idx, it in recs:
+            it.p = p.index_select(0, idx) if it.apply else None
+        return recs
+
+    def _scatter_rows(self, recs):
+        for p, idx, it in recs:
+            st = it.state
+            st["moment"].index_copy_(0, idx, it.m_rows)
+            st["variance"].index_copy_(0, idx, it.v_rows)
+            if it.p is not None:
+                p.data.index_copy_(0, idx, it.p)
+
     def _adam_local(self, params, cfg: GroupConfig):
         """thorn.py:1659-1727 on the multi-tensor kernel."""
         lib = N.load()
         dev = _local(params[0]).device
         stream = N.stream_of(dev)
         md = cfg.decouple_md
+        sparse = [p for p in params if p.grad.is_sparse]
+        if sparse:
+            params = [p for p in params if not p.grad.is_sparse]
+            recs = self._sparse_rows(sparse, cfg)
+            by_dt: dict = {}
+            for _, _, it in recs:
+                step = it.state["step"]
+                rect = cfg.rect(step)
+                b1, b2 = cfg.betas
+                by_dt.setdefault((it.pdt, it.sdt), []).append(N.AdamTensor(
+                    None if it.p is None else it.p.data_ptr(), it.g.data_ptr(), it.m_rows.data_ptr(),
+                    it.v_rows.data_ptr(), it.g.numel(), float(cfg.lr) * rect * it.scale, 1 / (1 - b1 ** step),
+                    1 / (1 - b2 ** step), 1 if rect == 0.0 else 0))
+            for (pdt, sdt), ts in by_dt.items():
+                N.check(lib.thorn_adamw_multi(N.array(N.AdamTensor, ts), len(ts), N.dtype_code(pdt),
+                                              N.dtype_code(sdt), float(cfg.betas[0]), float(cfg.betas[1]),
+                                              float(cfg.weight_decay), float(cfg.eps), stream), "adamw_multi(rows)")
+            self._scatter_rows(recs)
+            self._finish([p for p, _, _ in recs], cfg)
+            if not params:
+                return
         arena = _Arena()
         items = self._items(params, cfg, arena, ortho=False)
+        # Magma on the raw gradient, before direction recovery (thorn.py:1702)
+        self._magma(items, cfg, recovered=False)
         if md:
             for it in items:
                 ax = cfg.norm_axis_(it.p)
@@ -708,7 +852,7 @@ class THORN(Optimizer):
             bc2 = 1 / (1 - b2 ** step)
             t = N.AdamTensor(it.p.data_ptr() if it.apply else None, it.g.data_ptr(),
                              _local(it.state["moment"]).data_ptr(), _local(it.state["variance"]).data_ptr(),
-                             it.p.numel(), float(cfg.lr) * rect, bc1, bc2, 1 if rect == 0.0 else 0)
+                             it.p.numel(), float(cfg.lr) * rect * it.scale, bc1, bc2, 1 if rect == 0.0 else 0)
             by_dt.setdefault((it.pdt, it.sdt), []).append(t)
         for (pdt, sdt), ts in by_dt.items():
             N.check(lib.thorn_adamw_multi(N.array(N.AdamTensor, ts), len(ts), N.dtype_code(pdt), N.dtype_code(sdt),

@@ -154,12 +154,33 @@ def sharded_ortho_step(opt, params, cfg) -> None:
             opt._ortho_local(batched, cfg)
     if not mats:
         return
+    scales = [1.0] * len(mats)
+    if cfg.momentum_align:
+        # Magma on the shards: the three sums are all-reduced over the shard group
+        # (thorn.py:1483-1490).  A masked matrix is left out of this step entirely:
+        # no momentum update and no step count, as in the reference's sharded path.
+        from .optimizer import _Item
+        recs = []
+        for p in mats:
+            it = _Item()
+            it.g, it.state = _local(p.grad), opt.state[p]
+            it.split, it.apply = "row_gain" in it.state, True
+            recs.append(it)
+        with torch.cuda.device(_local(mats[0]).device):
+            opt._magma(recs, cfg, recovered=True, group=group)
+        for p, it in zip(mats, recs):
+            if not it.apply:
+                p.grad = None
+        scales = [it.scale for it in recs if it.apply]
+        mats = [p for p, it in zip(mats, recs) if it.apply]
+        if not mats:
+            return
     dev = _local(mats[0]).device
     with torch.cuda.device(dev):
-        _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, _Arena, _local)
+        _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, _Arena, _local, scales)
 
 
-def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local):
+def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, scales):
     lib = N.load()
     stream = N.stream_of(dev)
     err = opt._err_flag(dev)
@@ -317,7 +338,7 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local):
             fj = factors[ci][k, me * it.R:(me + 1) * it.R] if ci in factors else None
         else:
             uj, fj = u_loc[j], f_loc.get(j)
-        lr_eff = float(cfg.lr) * cfg.lr_scale(rows_g[j], it.C)
+        lr_eff = float(cfg.lr) * cfg.lr_scale(rows_g[j], it.C) * scales[j]
         posts.setdefault(it.pdt, []).append(N.OrthoPostTensor(
             uj.data_ptr(), it.p.data_ptr(), None if fj is None else fj.data_ptr(), None,
             arena.ptr(it.pnorm) if md else None, it.B, it.R, it.C, lr_eff, sp if md else None, 0))
