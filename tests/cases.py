@@ -93,6 +93,16 @@ CASES = {
     ]),
     # BASELINE config 2 shapes (flattened conv kernels) -- the many-tiny-matrices case.
     "vad": dict(steps=3, grad_std=1e-3, groups=_vad_groups(flatten=True)),
+    # Row counts that split unevenly over 2 (and 4) shards, with and without MD, next to AdamW
+    # vectors whose shards are uneven too (the FSDP2 tests at world 1 and 2).
+    "shard_uneven": dict(steps=3, grad_std=1e-3, groups=[
+        dict(orthogonalize=True, shapes=[(66, 64), (97, 64), (64, 160)], init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=2e-3, weight_decay=0.1)),
+        dict(orthogonalize=True, shapes=[(75, 64), (33, 96)], init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=8e-3, decouple_md=True)),
+        dict(orthogonalize=False, shapes=[(65,), (33,)], init=("normal", 0.5), dtype="f32",
+             opts=dict(lr=1e-3, weight_decay=0.05)),
+    ]),
     # Magma momentum-aligned masking (thorn.py:800-836) on both group kinds, with and without MD.
     "magma_small": dict(steps=6, grad_std=1e-3, groups=[
         dict(orthogonalize=True, shapes=[(64, 64), (96, 64), (64, 160)], init=("normal", 0.02), dtype="f32",

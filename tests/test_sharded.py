@@ -19,7 +19,7 @@ import torch.multiprocessing as mp
 
 import cases as C
 import parity as P
-from thorn_b200.sharded import assign_owners, exchange, ns_flops, plan_gather, plan_scatter
+from thorn_b200.sharded import assign_owners, exchange, ns_flops, plan_gather, plan_scatter, shard_rows
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 
@@ -53,31 +53,35 @@ def _exchange_worker(rank, world, port, result):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         ranks = list(range(world))
-        shapes = [(24, 3), (12, 5), (36, 2), (12, 7), (48, 4)]  # global rows divisible by world
+        # even and uneven Shard(0) splits (torch.chunk sizes: the last shard is shorter)
+        shapes = [(24, 3), (13, 5), (36, 2), (25, 7), (49, 4), (12, 3)]
         full = [torch.arange(r * c, dtype=torch.float32).reshape(r, c) + 100 * j for j, (r, c) in enumerate(shapes)]
         owners = assign_owners([r * c for r, c in shapes], world)
-        rows = [r // world for r, _ in shapes]
-        mine = [f[rank * n:(rank + 1) * n].clone() for f, n in zip(full, rows)]
+        parts = [shard_rows(r, world) for r, _ in shapes]
+
+        def sl(j, s):
+            r0, n = parts[j][s]
+            return slice(r0, r0 + n)
+
+        mine = [f[sl(j, rank)].clone() for j, f in enumerate(full)]
         owned = {j: torch.full_like(full[j], -1.0) for j in range(len(shapes)) if owners[j] == rank}
         for j in owned:  # own slab goes in directly
-            owned[j][rank * rows[j]:(rank + 1) * rows[j]] = mine[j]
-        sends, recvs = plan_gather(owners, rank, world, lambda j: mine[j],
-                                   lambda j, s: owned[j][s * rows[j]:(s + 1) * rows[j]])
+            owned[j][sl(j, rank)] = mine[j]
+        sends, recvs = plan_gather(owners, rank, world, lambda j: mine[j], lambda j, s: owned[j][sl(j, s)])
         exchange(sends, recvs, ranks, None)
         ok = all(torch.equal(owned[j], full[j]) for j in owned)
         # owners return 2x the matrix, with a per-row factor
         res = {j: 2 * owned[j] for j in owned}
         fac = {j: torch.arange(full[j].shape[0], dtype=torch.float32) for j in owned}
-        back = {j: torch.zeros(rows[j], shapes[j][1]) for j in range(len(shapes)) if owners[j] != rank}
-        bfac = {j: torch.zeros(rows[j]) for j in back}
-        sends, recvs = plan_scatter(
-            owners, rank, world,
-            lambda j, s: [res[j][s * rows[j]:(s + 1) * rows[j]], fac[j][s * rows[j]:(s + 1) * rows[j]]],
-            lambda j: [back[j], bfac[j]])
+        back = {j: torch.zeros(parts[j][rank][1], shapes[j][1]) for j in range(len(shapes)) if owners[j] != rank}
+        bfac = {j: torch.zeros(parts[j][rank][1]) for j in back}
+        sends, recvs = plan_scatter(owners, rank, world, lambda j, s: [res[j][sl(j, s)], fac[j][sl(j, s)]],
+                                    lambda j: [back[j], bfac[j]])
         exchange(sends, recvs, ranks, None)
         for j in back:
             ok &= torch.equal(back[j], 2 * mine[j])
-            ok &= torch.equal(bfac[j], torch.arange(rank * rows[j], (rank + 1) * rows[j], dtype=torch.float32))
+            r0, n = parts[j][rank]
+            ok &= torch.equal(bfac[j], torch.arange(r0, r0 + n, dtype=torch.float32))
         result[rank] = bool(ok)
     finally:
         dist.destroy_process_group()
@@ -134,16 +138,17 @@ def _mesh_error_worker(rank, world, port, result):
         m2 = init_device_mesh("cpu", (world,), mesh_dim_names=("other",))
         a = torch.nn.Parameter(distribute_tensor(torch.randn(8, 8), m1, [Shard(0)]))
         b = torch.nn.Parameter(distribute_tensor(torch.randn(8, 8), m2, [Shard(0)]))
-        c = torch.nn.Parameter(distribute_tensor(torch.randn(9, 8), m1, [Shard(0)]))
+        c = torch.nn.Parameter(distribute_tensor(torch.randn(1, 8), m1, [Shard(0)]))  # second shard empty
+        d = torch.nn.Parameter(distribute_tensor(torch.randn(9, 8), m1, [Shard(0)]))  # uneven: 5 + 4 rows
         msgs = []
-        for ps in ([a, b], [c]):
+        for ps in ([a, b], [c], [d]):
             opt = THORN([{"orthogonalize": True, "params": ps, "lr": 1e-3}], backend=torch.cpu)
             for p in ps:
                 p.grad = distribute_tensor(torch.randn(p.shape), p.device_mesh, [Shard(0)])
             try:
                 opt.step()
                 msgs.append("no error")
-            except (ValueError, NotImplementedError) as e:
+            except (ValueError, NotImplementedError, RuntimeError) as e:
                 msgs.append(type(e).__name__ + ": " + str(e))
         result[rank] = msgs
     finally:
@@ -151,13 +156,25 @@ def _mesh_error_worker(rank, world, port, result):
 
 
 def test_mesh_and_split_checks_gloo():
-    """Host-side checks fire before any kernel: mixed meshes (thorn.py:1358-1359), uneven splits."""
+    """Host-side checks fire before any kernel: mixed meshes (thorn.py:1358-1359), a split
+    that leaves a shard empty, and parameters that are not on a CUDA device (an uneven
+    split itself is accepted)."""
     ctx = mp.get_context("spawn")
     result = ctx.Manager().dict()
     mp.start_processes(_mesh_error_worker, args=(2, _free_port(), result), nprocs=2, join=True, start_method="spawn")
     for r in (0, 1):
         assert "same mesh" in result[r][0]
-        assert "uneven Shard(0)" in result[r][1]
+        assert "empty shard" in result[r][1]
+        assert "CUDA devices only" in result[r][2]
+
+
+def test_shard_rows_follow_torch_chunk():
+    for rows in (1, 7, 8, 9, 13, 128256, 151936):
+        for world in (1, 2, 3, 4, 8):
+            want = [t.shape[0] for t in torch.arange(rows).chunk(world)]
+            got = [n for _, n in shard_rows(rows, world)]
+            assert got[:len(want)] == want and all(n == 0 for n in got[len(want):])
+            assert sum(got) == rows and shard_rows(rows, world)[0][0] == 0
 
 
 def _run_workers(n, name, tmp_path):
@@ -172,7 +189,7 @@ def _run_workers(n, name, tmp_path):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("world", [1, 2])
-@pytest.mark.parametrize("name", ["tiny", "md_shard"])
+@pytest.mark.parametrize("name", ["tiny", "md_shard", "shard_uneven"])
 def test_sharded_step_matches_oracle(world, name, tmp_path):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")

@@ -49,6 +49,14 @@ def shard_group(p: DTensor, rank: int):
     raise ValueError(f"Unsupported placements {p.placements}")
 
 
+def shard_rows(rows: int, world: int) -> list[tuple[int, int]]:
+    """(first row, row count) of every shard of a ``Shard(0)`` split: DTensor's
+    ``torch.chunk`` rule, ceil(rows / world) rows per shard and a shorter (or
+    empty) tail."""
+    c = -(-rows // world)
+    return [(min(i * c, rows), max(0, min(c, rows - i * c))) for i in range(world)]
+
+
 def ns_flops(rows: int, cols: int, iters: int) -> int:
     """The reference's per-matrix NS cost estimate (thorn.py:1001-1007)."""
     m, n = min(rows, cols), max(rows, cols)
@@ -144,11 +152,19 @@ def sharded_ortho_step(opt, params, cfg) -> None:
     mats, batched = [], []
     for p in params:
         if p.ndim == 2:
-            if p.shape[0] % world:
-                raise NotImplementedError(f"uneven Shard(0) split: {p.shape[0]} rows over {world} ranks")
+            parts = shard_rows(p.shape[0], world)
+            if any(n == 0 for _, n in parts):
+                raise NotImplementedError(f"Shard(0) split with an empty shard: {p.shape[0]} rows over {world} "
+                                          "ranks")
+            if _local(p).shape[0] != parts[me][1]:
+                raise ValueError(f"local shard of {_local(p).shape[0]} rows does not follow the Shard(0) split of "
+                                 f"{p.shape[0]} rows over {world} ranks")
             mats.append(p)
         else:
             batched.append(p)  # whole (in, k) matrices on every rank
+    dev_type = _local(params[0]).device.type
+    if dev_type != "cuda":
+        raise RuntimeError(f"thorn_b200 runs its step on CUDA devices only; got a sharded parameter on {dev_type}")
     if batched:
         with torch.cuda.device(_local(batched[0]).device):
             opt._ortho_local(batched, cfg)
@@ -191,7 +207,8 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
     ns_dt = opt.ns_dtype
     ns_code = N.dtype_code(ns_dt)
     esz = torch.empty((), dtype=ns_dt).element_size()
-    rows_g = [it.R * world for it in items]  # global rows
+    rows_g = [int(p.shape[0]) for p in mats]  # global rows
+    parts = [shard_rows(r, world) for r in rows_g]  # (first row, count) of every shard
     for it in items:
         if it.C % 8:
             raise NotImplementedError("sharded NS needs a column count that is a multiple of 8")
@@ -256,8 +273,8 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
 
     def owner_rows(j, s):
         ci, k = slot[j]
-        r = items[j].R
-        return X[ci][k, s * r:(s + 1) * r]
+        r0, n = parts[j][s]
+        return X[ci][k, r0:r0 + n]
 
     casts: dict = {}
     for j, it in enumerate(items):
@@ -316,11 +333,11 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
 
     def owner_parts(j, s):
         ci, k = slot[j]
-        r = items[j].R
-        parts = [U[ci][k, s * r:(s + 1) * r]]
+        r0, n = parts[j][s]
+        out = [U[ci][k, r0:r0 + n]]
         if ci in factors:
-            parts.append(factors[ci][k, s * r:(s + 1) * r])
-        return parts
+            out.append(factors[ci][k, r0:r0 + n])
+        return out
 
     def my_parts(j):
         return [u_loc[j]] + ([f_loc[j]] if j in f_loc else [])
@@ -334,8 +351,9 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
     for j, (it, sp) in enumerate(zip(items, scr)):
         if owners[j] == me:
             ci, k = slot[j]
-            uj = U[ci][k, me * it.R:(me + 1) * it.R]
-            fj = factors[ci][k, me * it.R:(me + 1) * it.R] if ci in factors else None
+            r0, n = parts[j][me]
+            uj = U[ci][k, r0:r0 + n]
+            fj = factors[ci][k, r0:r0 + n] if ci in factors else None
         else:
             uj, fj = u_loc[j], f_loc.get(j)
         lr_eff = float(cfg.lr) * cfg.lr_scale(rows_g[j], it.C) * scales[j]
