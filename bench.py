@@ -348,7 +348,40 @@ def gpu_arm(args, rank, world, local_rank):
         h_params = [torch.empty(local(p).shape, dtype=local(p).dtype, pin_memory=True) for p in params]
         bi = sum(h.numel() * h.element_size() for h in h_grads)
         bo = sum(h.numel() * h.element_size() for h in h_params)
-        d_grads = [torch.empty_like(g) for g in grads]
+        # the device-resident grads of the timed loop are not needed any more
+        for lst in (grads, g_ortho, g_adam):
+            lst.clear()
+        torch.cuda.synchronize()
+    if not args.no_e2e and args.e2e_mode == "pipelined":
+        from thorn_b200.host_stepper import PinnedStepper
+
+        stepper = PinnedStepper(opt, params, h_grads, h_params)
+        for _ in range(2):
+            stepper.step()
+        stepper.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        stepper.h2d.wait_stream(torch.cuda.current_stream())  # no copy starts before t0
+        for _ in range(args.steps):
+            stepper.step()
+        stepper.wait_on()
+        t1.record()
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
+        if world > 1:
+            t = torch.tensor([bi, bo], device=dev, dtype=torch.float64)
+            dist.all_reduce(t)
+            bi, bo = int(t[0]), int(t[1])
+        e2e = {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
+               "mode": "pipelined: copies overlap the steps on two copy streams (thorn_b200.PinnedStepper)"}
+        progress(rank, "end-to-end steps done")
+        del stepper, h_grads, h_params
+    elif not args.no_e2e:
+        d_grads = [torch.empty_like(p) for p in params]
 
         def e2e_step():
             for dg, h in zip(d_grads, h_grads):
@@ -479,6 +512,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="thorn_b200", choices=["thorn_b200", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-mode", default="serial", choices=["serial", "pipelined"],
+                    help="serial: copy in, step, copy out on one stream; pipelined: thorn_b200.PinnedStepper "
+                         "overlaps both copies with the steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ns-only", default=None, help="BxRxC: time thorn_ns_batched alone on this batch (profiling)")
     ap.add_argument("--layers", type=int, default=LAYERS, help="transformer layers (profiling runs use fewer)")

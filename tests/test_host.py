@@ -119,3 +119,17 @@ def test_mat_view():
     assert _mat_view((8, 4, 3)) == (8, 4, 3)
     assert _mat_view((2, 3, 4, 5)) == (6, 4, 5)
     assert _mat_view((7,)) == (1, 1, 7)
+
+
+def test_pinned_stepper_checks_buffers():
+    """PinnedStepper rejects host buffers of the wrong shape, dtype or memory kind before
+    touching a device."""
+    from thorn_b200 import PinnedStepper
+
+    p = torch.nn.Parameter(torch.zeros(4, 3))
+    with pytest.raises(ValueError, match="same length"):
+        PinnedStepper(None, [p], [], [])
+    with pytest.raises(ValueError, match="local shape"):
+        PinnedStepper(None, [p], [torch.zeros(3, 4)], [torch.zeros(4, 3)])
+    with pytest.raises(ValueError, match="pinned"):
+        PinnedStepper(None, [p], [torch.zeros(4, 3)], [torch.zeros(4, 3)])

@@ -3,7 +3,8 @@
 ``from thorn_b200 import THORN`` is a drop-in for ``from thorn import THORN``
 (pykeio/THORN v3.1.1).
 """
+from .host_stepper import PinnedStepper  # noqa: F401
 from .optimizer import THORN, THORNGroup, THORNNonOrthoGroup, THORNOrthoGroup  # noqa: F401
 
 __version__ = "0.1.0"
-__all__ = ["THORN", "THORNOrthoGroup", "THORNNonOrthoGroup", "THORNGroup"]
+__all__ = ["THORN", "THORNOrthoGroup", "THORNNonOrthoGroup", "THORNGroup", "PinnedStepper"]

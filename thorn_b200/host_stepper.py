@@ -1,0 +1,104 @@
+"""Optimizer steps fed from, and drained to, pinned host memory.
+
+A training loop that keeps gradients or a parameter mirror in host memory (host-side
+gradient accumulation, a parameter server, checkpoint shadows) pays two PCIe
+transfers per step.  Run back to back they cost more than the step itself on B200:
+an 8B-parameter bf16 model moves 16 GB each way, about 0.3 s per direction at PCIe 5
+speeds, against ~0.36 s for the whole THORN step.  ``PinnedStepper`` overlaps them
+with the optimizer's own work on two copy streams:
+
+* the gradients of step k are copied host -> device into one of two device gradient
+  buffers while step k - 1 still runs;
+* after step k the updated parameters are snapshotted device -> device (HBM speed)
+  and the snapshot is copied device -> host while step k + 1 runs.
+
+Every dependency is a CUDA event; the host blocks only in :meth:`synchronize`.  Host
+buffers must be pinned (``torch.empty(..., pin_memory=True)``) and hold the local
+shard of every parameter (its ``to_local()`` for a DTensor).  The host gradients of a
+step must be written before :meth:`step` is called for it, and the host parameter
+buffers hold the values of step k once a later :meth:`synchronize` returns.
+"""
+from __future__ import annotations
+
+import torch
+
+from .optimizer import _local
+
+
+class PinnedStepper:
+    """Run ``optimizer.step()`` with gradients from ``host_grads`` and the updated
+    parameters copied to ``host_params`` (lists in the order of ``params``)."""
+
+    def __init__(self, optimizer, params, host_grads, host_params):
+        if not (len(params) == len(host_grads) == len(host_params)):
+            raise ValueError("params, host_grads and host_params must have the same length")
+        for p, hg, hp in zip(params, host_grads, host_params):
+            loc = _local(p)
+            if hg.shape != loc.shape or hp.shape != loc.shape:
+                raise ValueError(f"host buffers must have the local shape {tuple(loc.shape)}")
+            if not (hg.is_pinned() and hp.is_pinned()):
+                raise ValueError("host buffers must be pinned (torch.empty(..., pin_memory=True))")
+            if hg.dtype != p.dtype or hp.dtype != p.dtype:
+                raise TypeError("host buffers must have the parameter dtype")
+        self.opt = optimizer
+        self.params = list(params)
+        self.host_grads = list(host_grads)
+        self.host_params = list(host_params)
+        dev = _local(self.params[0]).device
+        self.device = dev
+        self.h2d = torch.cuda.Stream(dev)
+        self.d2h = torch.cuda.Stream(dev)
+        # two gradient buffers (step k fills one while step k - 1 reads the other), one snapshot
+        self.grads = [[torch.empty_like(p) for p in self.params] for _ in range(2)]
+        self.snapshot = [torch.empty_like(_local(p)) for p in self.params]
+        self.loaded = [torch.cuda.Event(), torch.cuda.Event()]  # gradients of the slot are on the device
+        self.consumed = [None, None]  # the step that read the slot has finished
+        self.staged = torch.cuda.Event()  # the snapshot holds the latest parameters
+        self.drained = None  # the snapshot has been copied to the host
+        self.k = 0
+
+    def step(self):
+        """Enqueue one step; returns without waiting for the GPU."""
+        slot = self.k & 1
+        compute = torch.cuda.current_stream(self.device)
+        with torch.cuda.stream(self.h2d):
+            if self.consumed[slot] is not None:
+                self.h2d.wait_event(self.consumed[slot])
+            for g, h in zip(self.grads[slot], self.host_grads):
+                _local(g).copy_(h, non_blocking=True)
+            self.loaded[slot].record(self.h2d)
+        compute.wait_event(self.loaded[slot])
+        for p, g in zip(self.params, self.grads[slot]):
+            p.grad = g
+        self.opt.step()
+        done = torch.cuda.Event()
+        done.record(compute)
+        self.consumed[slot] = done
+        if self.drained is not None:
+            compute.wait_event(self.drained)  # the host copy of the previous snapshot has finished
+        for s, p in zip(self.snapshot, self.params):
+            s.copy_(_local(p).detach())
+        self.staged.record(compute)
+        with torch.cuda.stream(self.d2h):
+            self.d2h.wait_event(self.staged)
+            for h, s in zip(self.host_params, self.snapshot):
+                h.copy_(s, non_blocking=True)
+            drained = torch.cuda.Event()
+            drained.record(self.d2h)
+        self.drained = drained
+        self.k += 1
+
+    def wait_on(self, stream=None):
+        """Make ``stream`` (default: the current one) wait until every enqueued
+        transfer and step has finished, without blocking the host."""
+        stream = stream or torch.cuda.current_stream(self.device)
+        if self.drained is not None:
+            stream.wait_event(self.drained)
+        for ev in self.consumed:
+            if ev is not None:
+                stream.wait_event(ev)
+
+    def synchronize(self):
+        """Block until the host parameter buffers hold the latest step's values."""
+        self.wait_on()
+        torch.cuda.current_stream(self.device).synchronize()
