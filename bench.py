@@ -255,6 +255,7 @@ def gpu_arm(args, rank, world, local_rank):
         {"orthogonalize": True, "params": ortho, "lr": ORTHO_LR, "decouple_md": True, "state_dtype": torch.float32},
         {"orthogonalize": False, "params": adamw, "lr": ADAM_LR, "state_dtype": torch.float32},
     ])
+    opt.pipeline_exchange = bool(args.pipeline_exchange)
 
     def local(t):
         return t.to_local() if hasattr(t, "to_local") else t
@@ -512,6 +513,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="thorn_b200", choices=["thorn_b200", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--pipeline-exchange", action="store_true",
+                    help="N > 1: exchange row slabs in waves that overlap the owners' Newton-Schulz work")
     ap.add_argument("--e2e-mode", default="serial", choices=["serial", "pipelined"],
                     help="serial: copy in, step, copy out on one stream; pipelined: thorn_b200.PinnedStepper "
                          "overlaps both copies with the steps")

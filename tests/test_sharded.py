@@ -82,6 +82,18 @@ def _exchange_worker(rank, world, port, result):
             ok &= torch.equal(back[j], 2 * mine[j])
             r0, n = parts[j][rank]
             ok &= torch.equal(bfac[j], torch.arange(r0, r0 + n, dtype=torch.float32))
+        # the same gather in two waves (even / odd matrices), both queued before either is waited on
+        for j in owned:
+            owned[j].fill_(-1.0)
+            owned[j][sl(j, rank)] = mine[j]
+        works = []
+        for js in ([j for j in range(len(shapes)) if j % 2 == 0], [j for j in range(len(shapes)) if j % 2 == 1]):
+            sends, recvs = plan_gather(owners, rank, world, lambda j: mine[j], lambda j, s: owned[j][sl(j, s)],
+                                       subset=js)
+            works += exchange(sends, recvs, ranks, None, wait=False)
+        for w in works:
+            w.wait()
+        ok &= all(torch.equal(owned[j], full[j]) for j in owned)
         result[rank] = bool(ok)
     finally:
         dist.destroy_process_group()

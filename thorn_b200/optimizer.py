@@ -260,6 +260,9 @@ class THORN(Optimizer):
     # when a list: each Newton-Schulz call appends (start event, end event, dense-equivalent
     # FLOPs, executed FLOPs, (batch, rows, cols)); events are recorded on the launching stream
     profile_ns: Optional[list] = None
+    # sharded path: exchange row slabs in waves of NS batches so that transfers overlap
+    # the owners' Newton-Schulz work (False: every slab moves before any NS starts)
+    pipeline_exchange: bool = False
 
     def __init__(self, params, *, backend=torch.cuda, **conf):
         self._update_rate = 1

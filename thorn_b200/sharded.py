@@ -88,7 +88,7 @@ class Slab:
     peer: int
 
 
-def exchange(sends: list[Slab], recvs: list[Slab], ranks: list[int], group) -> None:
+def exchange(sends: list[Slab], recvs: list[Slab], ranks: list[int], group, wait: bool = True) -> list:
     """All messages of one exchange, as world - 1 shifted pairwise rounds.
 
     In round d every shard index i sends only to i + d and receives only from
@@ -98,42 +98,49 @@ def exchange(sends: list[Slab], recvs: list[Slab], ranks: list[int], group) -> N
     two new peer connections per call.  Callers list messages in a canonical
     order (matrix index ascending, then peer ascending), so the sends from a to
     b and b's receives from a appear in the same order on both sides, which is
-    how NCCL matches them.  The calls only make the current stream wait; the
-    host does not block.
+    how NCCL matches them.  Empty messages are left out on both sides.  With
+    ``wait`` the current stream waits for the exchange (the host never blocks);
+    otherwise the works are returned for the caller to wait on.
     """
     world = len(ranks)
     me = ranks.index(dist.get_rank())
+    works = []
     for d in range(1, world):
         to, frm = (me + d) % world, (me - d) % world
-        ops = [dist.P2POp(dist.isend, s.tensor, ranks[to], group) for s in sends if s.peer == to]
-        ops += [dist.P2POp(dist.irecv, r.tensor, ranks[frm], group) for r in recvs if r.peer == frm]
+        ops = [dist.P2POp(dist.isend, s.tensor, ranks[to], group) for s in sends if s.peer == to and s.tensor.numel()]
+        ops += [dist.P2POp(dist.irecv, r.tensor, ranks[frm], group) for r in recvs
+                if r.peer == frm and r.tensor.numel()]
         if ops:
-            for w in dist.batch_isend_irecv(ops):
-                w.wait()
+            works += dist.batch_isend_irecv(ops)
+    if wait:
+        for w in works:
+            w.wait()
+    return works
 
 
-def plan_gather(owners: list[int], me: int, world: int, my_rows, owner_rows):
+def plan_gather(owners: list[int], me: int, world: int, my_rows, owner_rows, subset=None):
     """Messages that bring every matrix's row slabs to its owner.
 
     ``my_rows(j)``: this rank's slab of matrix j (a send buffer, for j it does
     not own); ``owner_rows(j, s)``: where slab s of an owned matrix j lands.
+    ``subset``: ascending matrix indices to plan for (default: all).
     """
-    sends = [Slab(my_rows(j), owners[j]) for j in range(len(owners)) if owners[j] != me]
-    recvs = [Slab(owner_rows(j, s), s) for j in range(len(owners)) if owners[j] == me
-             for s in range(world) if s != me]
+    js = range(len(owners)) if subset is None else subset
+    sends = [Slab(my_rows(j), owners[j]) for j in js if owners[j] != me]
+    recvs = [Slab(owner_rows(j, s), s) for j in js if owners[j] == me for s in range(world) if s != me]
     return sends, recvs
 
 
-def plan_scatter(owners: list[int], me: int, world: int, owner_parts, my_parts):
+def plan_scatter(owners: list[int], me: int, world: int, owner_parts, my_parts, subset=None):
     """Messages that return result slabs from owners.
 
     ``owner_parts(j, s)``: list of tensors of owned matrix j destined for shard
     s; ``my_parts(j)``: matching receive buffers for a matrix this rank does
-    not own.
+    not own.  ``subset``: ascending matrix indices to plan for (default: all).
     """
-    sends = [Slab(t, s) for j in range(len(owners)) if owners[j] == me
-             for s in range(world) if s != me for t in owner_parts(j, s)]
-    recvs = [Slab(t, owners[j]) for j in range(len(owners)) if owners[j] != me for t in my_parts(j)]
+    js = range(len(owners)) if subset is None else subset
+    sends = [Slab(t, s) for j in js if owners[j] == me for s in range(world) if s != me for t in owner_parts(j, s)]
+    recvs = [Slab(t, owners[j]) for j in js if owners[j] != me for t in my_parts(j)]
     return sends, recvs
 
 
@@ -216,16 +223,35 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
             raise NotImplementedError("update_rate > 1 is not implemented for sharded parameters")
     owners = assign_owners([ns_flops(rows_g[j], it.C, cfg.iters) for j, it in enumerate(items)], world)
 
-    # owned matrices, batched by (global shape, dtypes)
-    buckets: dict = {}
-    for j, it in enumerate(items):
-        if owners[j] == me:
-            buckets.setdefault((rows_g[j], it.C, it.pdt, it.sdt), []).append(j)
-    chunks = []
-    for (R, C, pdt, sdt), js in buckets.items():
-        cap = max(1, opt.polar_decomp_batch_size // max(1, R * C)) if opt.polar_decomp_batch_size > 0 else 1
-        for i in range(0, len(js), cap):
-            chunks.append((R, C, pdt, sdt, js[i:i + cap]))
+    def owner_chunks(r):
+        """NS batches of owner r: its matrices by (global shape, dtypes), in batches of at
+        most polar_decomp_batch_size elements.  Every rank computes every owner's list."""
+        buckets: dict = {}
+        for j, it in enumerate(items):
+            if owners[j] == r:
+                buckets.setdefault((rows_g[j], it.C, it.pdt, it.sdt), []).append(j)
+        out = []
+        for (R, C, pdt, sdt), js in buckets.items():
+            cap = max(1, opt.polar_decomp_batch_size // max(1, R * C)) if opt.polar_decomp_batch_size > 0 else 1
+            for i in range(0, len(js), cap):
+                out.append((R, C, pdt, sdt, js[i:i + cap]))
+        return out
+
+    chunks = owner_chunks(me)
+    # Exchange waves.  One wave: every slab moves before any NS starts.  With
+    # pipeline_exchange, wave w holds every owner's w-th NS batch: all gathers are
+    # queued at once, so later waves' slabs move while the owners compute earlier ones,
+    # and each wave's results go back while the next wave computes.
+    wave_of = [0] * len(items)
+    n_waves = 1
+    if getattr(opt, "pipeline_exchange", False) and world > 1:
+        for r in range(world):
+            cs = chunks if r == me else owner_chunks(r)
+            n_waves = max(n_waves, len(cs))
+            for w, ch in enumerate(cs):
+                for j in ch[4]:
+                    wave_of[j] = w
+    wave_js = [[j for j in range(len(items)) if wave_of[j] == w] for w in range(n_waves)]
     pnn_h = {}
     for ci, (R, C, pdt, sdt, js) in enumerate(chunks):
         if cfg.needs_pnn(R, C):
@@ -288,48 +314,21 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
         N.check(lib.thorn_ns_cast_multi(N.array(N.NsCastTensor, ts), len(ts), N.dtype_code(pdt), N.dtype_code(sdt),
                                         N.dtype_code(udt), ns_code, b1, stream), "ns_cast_multi")
 
-    # 3. slabs to owners
-    sends, recvs = plan_gather(owners, me, world, lambda j: send_rows[j], owner_rows)
-    exchange(sends, recvs, ranks, group)
-    del send_buf, send_rows
+    # 3. slabs to owners: every wave's exchange is queued now (the NCCL stream runs them
+    # in order); each NS batch waits only for its own wave
+    gathers = []
+    for js in wave_js:
+        sends, recvs = plan_gather(owners, me, world, lambda j: send_rows[j], owner_rows, subset=js)
+        gathers.append(exchange(sends, recvs, ranks, group, wait=False))
 
-    # 4. Newton-Schulz (+ pnn factors) on owned matrices
-    coeffs = (N.ctypes.c_double * (3 * max(1, cfg.iters)))(*[x for abc in cfg.coeffs[:cfg.iters] for x in abc])
-    rs_ = list(cfg.restarts)
-    restarts = (N.ctypes.c_int32 * max(1, len(rs_)))(*rs_)
-    factors = {}
-    for ci, (R, C, pdt, sdt, js) in enumerate(chunks):
-        nb = len(js)
-        wsb = int(lib.thorn_ns_workspace_bytes(nb, R, C))
-        ws = torch.empty(max(256, wsb), dtype=torch.uint8, device=dev)
-        if opt.profile_ns is not None:
-            ev0 = torch.cuda.Event(enable_timing=True)
-            ev0.record()
-            f0 = N.gemm_flops()
-        N.check(lib.thorn_ns_batched(X[ci].data_ptr(), U[ci].data_ptr(), ws.data_ptr(), wsb, nb, R, C, ns_code,
-                                     coeffs, cfg.iters, restarts, len(rs_), err.data_ptr(), stream), "ns_batched")
-        if opt.profile_ns is not None:
-            ev1 = torch.cuda.Event(enable_timing=True)
-            ev1.record()
-            f1 = N.gemm_flops()
-            opt.profile_ns.append((ev0, ev1, f1[0] - f0[0], f1[1] - f0[1], (nb, R, C)))
-        del ws
-        if ci in pnn_h:
-            rsh, msh = pnn_h[ci]
-            (sp,) = opt._scratch(dev, [lib.thorn_pnn_scratch_bytes(nb, R)])
-            # the sharded reference runs pnn on fp32 u (thorn.py:1079-1081): no rounding, fp32 eps
-            pt = N.PnnTensor(U[ci].data_ptr(), arena.ptr(rsh), arena.ptr(msh), nb, R, C, sp, 1)
-            N.check(lib.thorn_pnn_stats_multi(N.array(N.PnnTensor, [pt]), 1, ns_code, N.F32, stream), "pnn_stats")
-            factors[ci] = arena.get(rsh).view(nb, R)
-    del X
-
-    # 5. result rows (+ row factors) back to every shard
+    # 5. (buffers) result rows (+ row factors) come back to every shard
     u_loc, f_loc = {}, {}
     for j, it in enumerate(items):
         if owners[j] != me:
             u_loc[j] = torch.empty((it.R, it.C), dtype=ns_dt, device=dev)
             if cfg.needs_pnn(rows_g[j], it.C):
                 f_loc[j] = torch.empty(it.R, dtype=torch.float32, device=dev)
+    factors = {}
 
     def owner_parts(j, s):
         ci, k = slot[j]
@@ -342,8 +341,48 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
     def my_parts(j):
         return [u_loc[j]] + ([f_loc[j]] if j in f_loc else [])
 
-    sends, recvs = plan_scatter(owners, me, world, owner_parts, my_parts)
-    exchange(sends, recvs, ranks, group)
+    # 4. Newton-Schulz (+ pnn factors) on owned matrices, wave by wave, and 5. each
+    # wave's results back to their shards
+    coeffs = (N.ctypes.c_double * (3 * max(1, cfg.iters)))(*[x for abc in cfg.coeffs[:cfg.iters] for x in abc])
+    rs_ = list(cfg.restarts)
+    restarts = (N.ctypes.c_int32 * max(1, len(rs_)))(*rs_)
+    scatters = []
+    for w, js_w in enumerate(wave_js):
+        for wk in gathers[w]:
+            wk.wait()  # the current stream waits; the host does not
+        for ci, (R, C, pdt, sdt, js) in enumerate(chunks):
+            if wave_of[js[0]] != w:
+                continue
+            nb = len(js)
+            wsb = int(lib.thorn_ns_workspace_bytes(nb, R, C))
+            ws = torch.empty(max(256, wsb), dtype=torch.uint8, device=dev)
+            if opt.profile_ns is not None:
+                ev0 = torch.cuda.Event(enable_timing=True)
+                ev0.record()
+                f0 = N.gemm_flops()
+            N.check(lib.thorn_ns_batched(X[ci].data_ptr(), U[ci].data_ptr(), ws.data_ptr(), wsb, nb, R, C, ns_code,
+                                         coeffs, cfg.iters, restarts, len(rs_), err.data_ptr(), stream), "ns_batched")
+            if opt.profile_ns is not None:
+                ev1 = torch.cuda.Event(enable_timing=True)
+                ev1.record()
+                f1 = N.gemm_flops()
+                opt.profile_ns.append((ev0, ev1, f1[0] - f0[0], f1[1] - f0[1], (nb, R, C)))
+            del ws
+            X[ci] = None
+            if ci in pnn_h:
+                rsh, msh = pnn_h[ci]
+                (sp,) = opt._scratch(dev, [lib.thorn_pnn_scratch_bytes(nb, R)])
+                # the sharded reference runs pnn on fp32 u (thorn.py:1079-1081): no rounding, fp32 eps
+                pt = N.PnnTensor(U[ci].data_ptr(), arena.ptr(rsh), arena.ptr(msh), nb, R, C, sp, 1)
+                N.check(lib.thorn_pnn_stats_multi(N.array(N.PnnTensor, [pt]), 1, ns_code, N.F32, stream),
+                        "pnn_stats")
+                factors[ci] = arena.get(rsh).view(nb, R)
+        sends, recvs = plan_scatter(owners, me, world, owner_parts, my_parts, subset=js_w)
+        scatters.append(exchange(sends, recvs, ranks, group, wait=False))
+    for works in scatters:
+        for wk in works:
+            wk.wait()
+    del X, send_buf, send_rows
 
     # 6. apply on local rows
     scr = opt._scratch(dev, [lib.thorn_sumsq_scratch_bytes(it.B, it.R, it.C) if md else 0 for it in items])
