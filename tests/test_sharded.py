@@ -86,14 +86,22 @@ def _exchange_worker(rank, world, port, result):
         for j in owned:
             owned[j].fill_(-1.0)
             owned[j][sl(j, rank)] = mine[j]
-        works = []
+        handles = []
         for js in ([j for j in range(len(shapes)) if j % 2 == 0], [j for j in range(len(shapes)) if j % 2 == 1]):
             sends, recvs = plan_gather(owners, rank, world, lambda j: mine[j], lambda j, s: owned[j][sl(j, s)],
                                        subset=js)
-            works += exchange(sends, recvs, ranks, None, wait=False)
-        for w in works:
-            w.wait()
+            handles.append(exchange(sends, recvs, ranks, None, wait=False))
+        for h in handles:
+            h.wait()
         ok &= all(torch.equal(owned[j], full[j]) for j in owned)
+        # slabs back to back in one buffer travel as a view; mixed dtypes pack as bytes
+        packed = torch.arange(12, dtype=torch.float32)
+        views = [packed[0:4], packed[4:10], packed[10:12]]
+        from thorn_b200.sharded import _bytes_of, _span
+        ok &= _span(views) is not None and _span(views).data_ptr() == packed.data_ptr()
+        ok &= _span([packed[0:4], packed[5:7]]) is None
+        mixed = _bytes_of([torch.ones(3, dtype=torch.float16), torch.full((2,), 2.0)])
+        ok &= mixed.numel() == 3 * 2 + 2 * 4
         result[rank] = bool(ok)
     finally:
         dist.destroy_process_group()

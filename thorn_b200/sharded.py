@@ -88,34 +88,84 @@ class Slab:
     peer: int
 
 
-def exchange(sends: list[Slab], recvs: list[Slab], ranks: list[int], group, wait: bool = True) -> list:
+def _span(ts: list[torch.Tensor]):
+    """A flat uint8 view covering the given tensors in order when they are contiguous
+    and back to back in one allocation, else None."""
+    if not all(t.is_contiguous() for t in ts):
+        return None
+    if len(ts) == 1:
+        return ts[0].reshape(-1).view(torch.uint8)
+    st = ts[0].untyped_storage()
+    if not all(a.data_ptr() + a.nbytes == b.data_ptr() and b.untyped_storage().data_ptr() == st.data_ptr()
+               for a, b in zip(ts, ts[1:])):
+        return None
+    span = torch.empty(0, dtype=torch.uint8, device=ts[0].device)
+    return span.set_(st, ts[0].data_ptr() - st.data_ptr(), (sum(t.nbytes for t in ts),), (1,))
+
+
+def _bytes_of(ts: list[torch.Tensor]) -> torch.Tensor:
+    """The tensors' bytes in order, as one flat uint8 tensor: a view when possible,
+    else a packed copy."""
+    span = _span(ts)
+    if span is not None:
+        return span
+    return torch.cat([t.contiguous().reshape(-1).view(torch.uint8) for t in ts])
+
+
+class Exchange:
+    """Handle of a queued exchange: ``wait()`` makes the current stream wait for it
+    and unpacks received messages that did not land in place (the host never blocks)."""
+
+    def __init__(self):
+        self.works = []
+        self.unpack = []  # (received bytes, destination tensors)
+
+    def wait(self):
+        for w in self.works:
+            w.wait()
+        for buf, dsts in self.unpack:
+            off = 0
+            for t in dsts:
+                t.reshape(-1).view(torch.uint8).copy_(buf[off:off + t.nbytes])
+                off += t.nbytes
+        self.works, self.unpack = [], []
+
+
+def exchange(sends: list[Slab], recvs: list[Slab], ranks: list[int], group, wait: bool = True) -> Exchange:
     """All messages of one exchange, as world - 1 shifted pairwise rounds.
 
     In round d every shard index i sends only to i + d and receives only from
-    i - d (mod world), one batched P2P call per round: each call pairs every
-    rank with exactly one destination and one source, the permutation pattern
-    that NVSwitch serves at full bandwidth and for which NCCL sets up at most
-    two new peer connections per call.  Callers list messages in a canonical
-    order (matrix index ascending, then peer ascending), so the sends from a to
-    b and b's receives from a appear in the same order on both sides, which is
-    how NCCL matches them.  Empty messages are left out on both sides.  With
-    ``wait`` the current stream waits for the exchange (the host never blocks);
-    otherwise the works are returned for the caller to wait on.
+    i - d (mod world).  Each round is one batched P2P call with one message per
+    direction, that peer's slabs packed in canonical order (matrix index
+    ascending, then peer ascending) -- so NCCL sets up at most two new peer
+    connections per call, the pattern is a permutation that NVSwitch serves at
+    full bandwidth, and the host posts two operations per round, not one per
+    slab.  Slabs that are back to back in memory travel without a packing copy.
+    Empty slabs are left out on both sides.  With ``wait`` the current stream
+    waits for the exchange now; otherwise the caller calls ``wait()`` on the
+    returned handle.
     """
     world = len(ranks)
     me = ranks.index(dist.get_rank())
-    works = []
+    ex = Exchange()
     for d in range(1, world):
         to, frm = (me + d) % world, (me - d) % world
-        ops = [dist.P2POp(dist.isend, s.tensor, ranks[to], group) for s in sends if s.peer == to and s.tensor.numel()]
-        ops += [dist.P2POp(dist.irecv, r.tensor, ranks[frm], group) for r in recvs
-                if r.peer == frm and r.tensor.numel()]
+        out = [s.tensor for s in sends if s.peer == to and s.tensor.numel()]
+        inc = [r.tensor for r in recvs if r.peer == frm and r.tensor.numel()]
+        ops = []
+        if out:
+            ops.append(dist.P2POp(dist.isend, _bytes_of(out), ranks[to], group))
+        if inc:
+            buf = _span(inc)  # received in place when the destinations are back to back
+            if buf is None:
+                buf = torch.empty(sum(t.nbytes for t in inc), dtype=torch.uint8, device=inc[0].device)
+                ex.unpack.append((buf, inc))
+            ops.append(dist.P2POp(dist.irecv, buf, ranks[frm], group))
         if ops:
-            works += dist.batch_isend_irecv(ops)
+            ex.works += dist.batch_isend_irecv(ops)
     if wait:
-        for w in works:
-            w.wait()
-    return works
+        ex.wait()
+    return ex
 
 
 def plan_gather(owners: list[int], me: int, world: int, my_rows, owner_rows, subset=None):
@@ -288,14 +338,16 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
         U[ci] = torch.empty((len(js), R, C), dtype=ns_dt, device=dev)
         for k, j in enumerate(js):
             slot[j] = (ci, k)
+    # send slabs grouped by owner (matrix index ascending within an owner): each
+    # round's message to one owner is then one contiguous range of this buffer
     send_rows = {}
     n_send = sum(it.R * it.C for j, it in enumerate(items) if owners[j] != me)
     send_buf = torch.empty(max(1, n_send), dtype=ns_dt, device=dev)
     off = 0
-    for j, it in enumerate(items):
-        if owners[j] != me:
-            send_rows[j] = send_buf[off:off + it.R * it.C].view(it.R, it.C)
-            off += it.R * it.C
+    for j in sorted((j for j in range(len(items)) if owners[j] != me), key=lambda j: (owners[j], j)):
+        it = items[j]
+        send_rows[j] = send_buf[off:off + it.R * it.C].view(it.R, it.C)
+        off += it.R * it.C
 
     def owner_rows(j, s):
         ci, k = slot[j]
@@ -348,8 +400,7 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
     restarts = (N.ctypes.c_int32 * max(1, len(rs_)))(*rs_)
     scatters = []
     for w, js_w in enumerate(wave_js):
-        for wk in gathers[w]:
-            wk.wait()  # the current stream waits; the host does not
+        gathers[w].wait()  # the current stream waits; the host does not
         for ci, (R, C, pdt, sdt, js) in enumerate(chunks):
             if wave_of[js[0]] != w:
                 continue
@@ -379,9 +430,8 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
                 factors[ci] = arena.get(rsh).view(nb, R)
         sends, recvs = plan_scatter(owners, me, world, owner_parts, my_parts, subset=js_w)
         scatters.append(exchange(sends, recvs, ranks, group, wait=False))
-    for works in scatters:
-        for wk in works:
-            wk.wait()
+    for ex in scatters:
+        ex.wait()
     del X, send_buf, send_rows
 
     # 6. apply on local rows
