@@ -17,8 +17,11 @@ data; every input is far larger than L2, so no L2 flush is needed.
 One line of JSON on rank 0:
 * value / ms_per_step: device time of one full optimizer step (CUDA events,
   max over ranks), inputs resident in HBM;
-* e2e: the same step through THORN.step with the grads copied in from pinned
-  host memory and the updated params copied back out, inside the timed region;
+* e2e: the same step through the public API with every step's grads copied in
+  from pinned host memory and its updated params copied back out, inside the
+  timed region; by default through thorn_b200.PinnedStepper, which overlaps the
+  copies of one step with the compute of its neighbours on two copy streams
+  (``--e2e-mode serial``: copy in, step, copy out, one after the other);
 * roofline: Newton-Schulz GEMM phase, dense-equivalent FLOPs / event time,
   against the measured sustained bf16 peak;
 * cpu_baseline: the CPU oracle's step on a bounded sample (one q, k and gate
@@ -353,10 +356,26 @@ def gpu_arm(args, rank, world, local_rank):
         for lst in (grads, g_ortho, g_adam):
             lst.clear()
         torch.cuda.synchronize()
+    e2e_note = None
     if not args.no_e2e and args.e2e_mode == "pipelined":
         from thorn_b200.host_stepper import PinnedStepper
 
-        stepper = PinnedStepper(opt, params, h_grads, h_params)
+        ok = 1.0
+        stepper = None
+        try:  # the stepper's device buffers: two gradient sets and a parameter snapshot
+            stepper = PinnedStepper(opt, params, h_grads, h_params)
+        except (RuntimeError, ValueError, TypeError) as exc:  # e.g. out of device memory
+            ok = 0.0
+            e2e_note = f"pipelined mode unavailable ({type(exc).__name__}: {str(exc)[:120]}); serial mode"
+        if world > 1:  # every rank takes the same branch before any step runs
+            t = torch.tensor([ok], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MIN)
+            if float(t.item()) == 0.0:
+                e2e_note = e2e_note or "pipelined mode unavailable on another rank; serial mode"
+        if e2e_note is not None:
+            stepper = None
+            torch.cuda.empty_cache()
+    if not args.no_e2e and args.e2e_mode == "pipelined" and e2e_note is None:
         for _ in range(2):
             stepper.step()
         stepper.synchronize()
@@ -378,7 +397,7 @@ def gpu_arm(args, rank, world, local_rank):
             dist.all_reduce(t)
             bi, bo = int(t[0]), int(t[1])
         e2e = {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
-               "mode": "pipelined: copies overlap the steps on two copy streams (thorn_b200.PinnedStepper)"}
+               "mode": "pipelined: both copies overlap the steps on two copy streams (thorn_b200.PinnedStepper)"}
         progress(rank, "end-to-end steps done")
         del stepper, h_grads, h_params
     elif not args.no_e2e:
@@ -410,7 +429,8 @@ def gpu_arm(args, rank, world, local_rank):
             t = torch.tensor([bi, bo], device=dev, dtype=torch.float64)
             dist.all_reduce(t)
             bi, bo = int(t[0]), int(t[1])
-        e2e = {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo}
+        e2e = {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
+               "mode": e2e_note or "serial: copy in, step, copy out on one stream"}
         progress(rank, "end-to-end steps done")
         del h_grads, h_params, d_grads
 
@@ -515,9 +535,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--pipeline-exchange", action="store_true",
                     help="N > 1: exchange row slabs in waves that overlap the owners' Newton-Schulz work")
-    ap.add_argument("--e2e-mode", default="serial", choices=["serial", "pipelined"],
-                    help="serial: copy in, step, copy out on one stream; pipelined: thorn_b200.PinnedStepper "
-                         "overlaps both copies with the steps")
+    ap.add_argument("--e2e-mode", default="pipelined", choices=["serial", "pipelined"],
+                    help="pipelined (default): thorn_b200.PinnedStepper overlaps both copies with the steps, "
+                         "falling back to serial if it cannot run; serial: copy in, step, copy out on one stream")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ns-only", default=None, help="BxRxC: time thorn_ns_batched alone on this batch (profiling)")
     ap.add_argument("--layers", type=int, default=LAYERS, help="transformer layers (profiling runs use fewer)")
