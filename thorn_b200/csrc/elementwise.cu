@@ -7,6 +7,7 @@
 // kernel parameter (pointer table + block prefix) so one launch covers many
 // parameters; blocks find their tensor with a short scan of the prefix.
 #include <atomic>
+#include <mutex>
 #include <math.h>
 #include <type_traits>
 
@@ -272,10 +273,53 @@ struct PreArgs {
   int write_grad;
 };
 
-template <class P, class S, class U, bool MD>
+// Async-copy staging of the momentum pass (ASYNC = true): each thread streams
+// its rows' g, m (and p) chunks into shared memory kPreAhead rows ahead with
+// cp.async, so the bytes in flight do not occupy registers.  Per stage and
+// thread the chunks are 16-byte units laid out [unit][thread]: a warp's unit
+// accesses are 512 contiguous bytes, free of bank conflicts.
+constexpr int kPreAhead = 4;
+constexpr int kPreStages = kPreAhead + 1;
+template <class P, class S>
+struct PreUnits {
+  static constexpr int g = 8 * (int)sizeof(P) / 16;  // units of g (and of p)
+  static constexpr int m = 8 * (int)sizeof(S) / 16;
+  static constexpr int all = 2 * g + m;
+  static constexpr int bytes = kPreStages * all * kThreads * 16;
+};
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
+               "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// 8 values of type T from 16-byte units at u[0] (and u[stride] for 4-byte T)
+template <class T>
+__device__ __forceinline__ void load8_units(const uint4* u, int stride, float* v) {
+  if constexpr (sizeof(T) == 4) {
+    const uint4 a = u[0], b = u[stride];
+    v[0] = __uint_as_float(a.x); v[1] = __uint_as_float(a.y); v[2] = __uint_as_float(a.z); v[3] = __uint_as_float(a.w);
+    v[4] = __uint_as_float(b.x); v[5] = __uint_as_float(b.y); v[6] = __uint_as_float(b.z); v[7] = __uint_as_float(b.w);
+  } else {
+    const uint4 a = u[0];
+    unpack2(a.x, v[0], v[1], (T*)nullptr);
+    unpack2(a.y, v[2], v[3], (T*)nullptr);
+    unpack2(a.z, v[4], v[5], (T*)nullptr);
+    unpack2(a.w, v[6], v[7], (T*)nullptr);
+  }
+}
+
+template <class P, class S, class U, bool MD, bool ASYNC = false>
 __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_constant__ PreArgs a) {
   __shared__ float red[32];
   __shared__ float colacc[MD ? 8 : 1][MD ? kTC : 1];
+  extern __shared__ uint4 pre_stage[];  // ASYNC only: [kPreStages][PreUnits::all][kThreads]
   const int ti = find_tensor(a.pk, blockIdx.x);
   const thorn_ortho_pre_tensor& e = a.pk.t[ti];
   const bool vec = a.pk.vec[ti];
@@ -297,20 +341,61 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
   float csp[8];
   if (MD && !scalar_gain) load8f(e.col_sp + t.b * e.cols + c, csp, nc, vec);
   float rsum_scalar = 0.f;
+  using UN = PreUnits<P, S>;
+  const bool staged = ASYNC && vec && nc == 8;  // this thread's chunks are whole, aligned units
+  // ASYNC: copy this thread's chunks of its i-th row (row warp + 8 i of the tile) into stage i % kPreStages;
+  // every call commits one group (possibly empty), so group counts stay uniform
+  auto issue = [&](int i) {
+    if constexpr (ASYNC) {
+      const int64_t r = t.r0 + warp + 8 * i;
+      if (staged && i < kTR / 8 && r < e.rows) {
+        const int64_t off = (t.b * e.rows + r) * e.cols + c;
+        uint4* st = pre_stage + (size_t)(i % kPreStages) * UN::all * kThreads + threadIdx.x;
+        const char* gs = reinterpret_cast<const char*>((const P*)e.g + off);
+#pragma unroll
+        for (int u = 0; u < UN::g; ++u) cp_async16(st + u * kThreads, gs + 16 * u);
+        if (momentum) {
+          const char* ms = reinterpret_cast<const char*>((const S*)e.m + off);
+#pragma unroll
+          for (int u = 0; u < UN::m; ++u) cp_async16(st + (UN::g + u) * kThreads, ms + 16 * u);
+        }
+        if (MD) {
+          const char* ps = reinterpret_cast<const char*>((const P*)e.p + off);
+#pragma unroll
+          for (int u = 0; u < UN::g; ++u) cp_async16(st + (UN::g + UN::m + u) * kThreads, ps + 16 * u);
+        }
+      }
+      cp_async_commit();
+    }
+  };
+#pragma unroll
+  for (int i = 0; i < kPreAhead; ++i) issue(i);
   for (int rr = warp; rr < kTR; rr += 8) {
     const int64_t r = t.r0 + rr;
     if (r >= e.rows) break;
     float rs = 0.f;
+    const uint4* st = nullptr;
+    if constexpr (ASYNC) {
+      const int i = rr >> 3;
+      issue(i + kPreAhead);
+      cp_async_wait<kPreAhead>();  // row i's group has landed
+      st = pre_stage + (size_t)(i % kPreStages) * UN::all * kThreads + threadIdx.x;
+    }
     if (nc > 0) {
       const int64_t off = (t.b * e.rows + r) * e.cols + c;
       float gv[8], mv[8];
-      load_n((const P*)e.g + off, gv, nc, vec);
-      if (momentum) load_n((const S*)e.m + off, mv, nc, vec);
+      if (staged) load8_units<P>(st, kThreads, gv);
+      else load_n((const P*)e.g + off, gv, nc, vec);
+      if (momentum) {
+        if (staged) load8_units<S>(st + UN::g * kThreads, kThreads, mv);
+        else load_n((const S*)e.m + off, mv, nc, vec);
+      }
       if (MD) {
         // every step below rounds 8 values to the param dtype at once (packed
         // conversions); lanes k >= nc hold padding and are neither summed nor stored
         float pv[8], gain[8], pg[8];
-        load_n((const P*)e.p + off, pv, nc, vec);
+        if (staged) load8_units<P>(st + (UN::g + UN::m) * kThreads, kThreads, pv);
+        else load_n((const P*)e.p + off, pv, nc, vec);
         const float rsp = scalar_gain ? e.row_sp[0] : e.row_sp[t.b * e.rows + r];
 #pragma unroll
         for (int k = 0; k < 8; ++k) gain[k] = scalar_gain ? rsp : __fmul_rn(rsp, csp[k]);
@@ -372,6 +457,7 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
       else if (lane == 0) sf[L.pr + (t.b * L.tc + ct) * e.rows + r] = rs;
     }
   }
+  if constexpr (ASYNC) cp_async_wait<0>();  // no copy into shared memory outlives the block
   const int64_t gt = (t.b * L.tr + rt) * L.tc + ct;  // tile index within the tensor
   if (momentum) {
     const float tot = block_sum(sq, red);
@@ -816,6 +902,11 @@ extern "C" int thorn_adamw_multi(const thorn_adam_tensor* ts, int n, int p_dtype
   return d ? d : rc;
 }
 
+// Momentum pass with cp.async row staging (1) or register loads (0, default).
+static std::atomic<int> g_async_pre{0};
+
+extern "C" int thorn_set_elementwise_async(int enable) { return g_async_pre.exchange(enable ? 1 : 0); }
+
 extern "C" int thorn_ortho_pre_multi(const thorn_ortho_pre_tensor* ts, int n, int p_dtype, int s_dtype,
                                      int u_dtype, float beta1, int md, int write_grad, void* stream) {
   if (n < 0 || (n > 0 && ts == nullptr) || !valid_dt(p_dtype) || !valid_dt(s_dtype) || !valid_dt(u_dtype))
@@ -845,8 +936,24 @@ extern "C" int thorn_ortho_pre_multi(const thorn_ortho_pre_tensor* ts, int n, in
       rc = launch_packed(ts, n, blocks, vec, [&](const Pack<thorn_ortho_pre_tensor>& pk, int64_t nb) {
         PreArgs a = base;
         a.pk = pk;
-        if (md) ortho_pre_kernel<P, S, U, true><<<(unsigned)nb, kThreads, 0, st>>>(a);
-        else ortho_pre_kernel<P, S, U, false><<<(unsigned)nb, kThreads, 0, st>>>(a);
+        if (g_async_pre.load() != 0) {
+          constexpr int smem = PreUnits<P, S>::bytes;
+          static std::once_flag once[64][2];
+          int dev = 0;
+          cudaGetDevice(&dev);
+          std::call_once(once[dev & 63][md ? 1 : 0], [md]() {
+            if (md) cudaFuncSetAttribute(ortho_pre_kernel<P, S, U, true, true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            else cudaFuncSetAttribute(ortho_pre_kernel<P, S, U, false, true>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+          });
+          if (md) ortho_pre_kernel<P, S, U, true, true><<<(unsigned)nb, kThreads, smem, st>>>(a);
+          else ortho_pre_kernel<P, S, U, false, true><<<(unsigned)nb, kThreads, smem, st>>>(a);
+        } else if (md) {
+          ortho_pre_kernel<P, S, U, true><<<(unsigned)nb, kThreads, 0, st>>>(a);
+        } else {
+          ortho_pre_kernel<P, S, U, false><<<(unsigned)nb, kThreads, 0, st>>>(a);
+        }
       });
       if (rc == THORN_OK) {
         rc = launch_packed(
