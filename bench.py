@@ -259,6 +259,8 @@ def gpu_arm(args, rank, world, local_rank):
         {"orthogonalize": False, "params": adamw, "lr": ADAM_LR, "state_dtype": torch.float32},
     ])
     opt.pipeline_exchange = bool(args.pipeline_exchange)
+    if args.elementwise_async:
+        _native.load().thorn_set_elementwise_async(1)
 
     def local(t):
         return t.to_local() if hasattr(t, "to_local") else t
@@ -533,6 +535,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="thorn_b200", choices=["thorn_b200", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--elementwise-async", action="store_true",
+                    help="momentum pass with cp.async row staging (thorn_set_elementwise_async)")
     ap.add_argument("--pipeline-exchange", action="store_true",
                     help="N > 1: exchange row slabs in waves that overlap the owners' Newton-Schulz work")
     ap.add_argument("--e2e-mode", default="pipelined", choices=["serial", "pipelined"],
