@@ -261,6 +261,8 @@ def gpu_arm(args, rank, world, local_rank):
     opt.pipeline_exchange = bool(args.pipeline_exchange)
     if args.elementwise_async:
         _native.load().thorn_set_elementwise_async(1)
+    if args.gemm_pdl:
+        _native.load().thorn_set_gemm_pdl(1)
 
     def local(t):
         return t.to_local() if hasattr(t, "to_local") else t
@@ -537,6 +539,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--elementwise-async", action="store_true",
                     help="momentum pass with cp.async row staging (thorn_set_elementwise_async)")
+    ap.add_argument("--gemm-pdl", action="store_true",
+                    help="NS GEMMs with programmatic dependent launch (thorn_set_gemm_pdl)")
     ap.add_argument("--pipeline-exchange", action="store_true",
                     help="N > 1: exchange row slabs in waves that overlap the owners' Newton-Schulz work")
     ap.add_argument("--e2e-mode", default="pipelined", choices=["serial", "pipelined"],

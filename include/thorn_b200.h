@@ -70,6 +70,12 @@ THORN_API int thorn_set_gemm_staged_epilogue(int enable);
  * zero (default) loads them into registers.  Returns the previous setting.  Both
  * settings give bit-identical results. */
 THORN_API int thorn_set_elementwise_async(int enable);
+/* NS GEMM launches: nonzero uses programmatic dependent launch, so each GEMM's
+ * set-up (barriers, TMEM, descriptor prefetch) overlaps the previous kernel's
+ * tail and its CTAs wait for that kernel to finish before touching global
+ * memory; zero (default) launches in plain stream order.  Returns the previous
+ * setting.  Both settings give bit-identical results. */
+THORN_API int thorn_set_gemm_pdl(int enable);
 
 /* --------------------------------------------------------------------------
  * (R)Adam(-atan2)W over many tensors in one launch per dtype pair.

@@ -140,6 +140,12 @@ template <int N>
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
+// Programmatic dependent launch: let the next grid on the stream be scheduled
+// now (its CTAs take SMs as this grid's CTAs exit), and wait until the previous
+// grid has completed and its memory is visible.  Without a programmatic launch
+// both are no-ops.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -315,6 +321,9 @@ __global__ void __launch_bounds__(kThreadsG, 1) ns_gemm_kernel(const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // set-up above overlaps the previous grid's tail; global memory only after it has finished
+  pdl_launch_dependents();
+  pdl_wait();
 
   if (warp == 0) {
     // ------------------------------ producer ------------------------------
@@ -607,6 +616,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
   cluster_sync_all();  // barriers of both CTAs are initialised before any remote signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // set-up above overlaps the previous grid's tail; global memory only after it has finished
+  pdl_launch_dependents();
+  pdl_wait();
 
   if (warp == 0) {
     // ------------------------------ producer (both CTAs) -------------------
@@ -953,6 +965,9 @@ struct GemmOp {
 // Algorithmic work of the GEMMs issued so far (for roofline reporting).
 static std::atomic<uint64_t> g_flops_dense{0}, g_flops_exec{0};
 
+// Programmatic dependent launch of the NS GEMMs (1) or plain stream order (0, default).
+static std::atomic<int> g_gemm_pdl{0};
+
 template <int BN, bool AMN, bool BMN, class T>
 static int launch_gemm(gemm::Params& prm, int grid, cudaStream_t st) {
   using C_ = gemm::Cfg<BN>;
@@ -963,7 +978,21 @@ static int launch_gemm(gemm::Params& prm, int grid, cudaStream_t st) {
     cudaFuncSetAttribute(gemm::ns_gemm_kernel<BN, AMN, BMN, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          C_::kSmem);
   });
-  gemm::ns_gemm_kernel<BN, AMN, BMN, T><<<grid, gemm::kThreadsG, C_::kSmem, st>>>(prm);
+  if (g_gemm_pdl.load() != 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(gemm::kThreadsG, 1, 1);
+    cfg.dynamicSmemBytes = C_::kSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, gemm::ns_gemm_kernel<BN, AMN, BMN, T>, prm);
+  } else {
+    gemm::ns_gemm_kernel<BN, AMN, BMN, T><<<grid, gemm::kThreadsG, C_::kSmem, st>>>(prm);
+  }
   count_launch();
   return check_launch();
 }
@@ -997,7 +1026,21 @@ static int launch_gemm2(gemm::Params& prm, int64_t total, int sms, cudaStream_t 
     max_clusters[dev & 63] = n;
   });
   const int clusters = (int)min64(total, (int64_t)std::max(1, max_clusters[dev & 63]));
-  gemm::ns_gemm2_kernel<AMN, BMN, T><<<2 * clusters, gemm::kThreadsG, gemm::kSmem2, st>>>(prm);
+  if (g_gemm_pdl.load() != 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.blockDim = dim3(gemm::kThreadsG, 1, 1);
+    cfg.dynamicSmemBytes = gemm::kSmem2;
+    cfg.stream = st;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, gemm::ns_gemm2_kernel<AMN, BMN, T>, prm);
+  } else {
+    gemm::ns_gemm2_kernel<AMN, BMN, T><<<2 * clusters, gemm::kThreadsG, gemm::kSmem2, st>>>(prm);
+  }
   count_launch();
   return check_launch();
 }
@@ -1318,6 +1361,8 @@ extern "C" int thorn_sym_addmm(const void* A, const void* B, const void* C, void
 extern "C" int thorn_set_gemm_pair(int enable) { return g_pair_tiles.exchange(enable ? 1 : 0); }
 
 extern "C" int thorn_set_gemm_staged_epilogue(int enable) { return g_staged_epilogue.exchange(enable ? 1 : 0); }
+
+extern "C" int thorn_set_gemm_pdl(int enable) { return g_gemm_pdl.exchange(enable ? 1 : 0); }
 
 // Dense-equivalent and executed tensor-core FLOPs issued so far (for roofline reports).
 extern "C" void thorn_gemm_flops(double* dense, double* executed) {
