@@ -133,3 +133,83 @@ def test_pinned_stepper_checks_buffers():
         PinnedStepper(None, [p], [torch.zeros(3, 4)], [torch.zeros(4, 3)])
     with pytest.raises(ValueError, match="pinned"):
         PinnedStepper(None, [p], [torch.zeros(4, 3)], [torch.zeros(4, 3)])
+
+
+def test_magma_generator_matches_oracle():
+    """The product's restatement of the reference's generator step (thorn.py:800-804)
+    equals the oracle's, which reproduces the reference's own generator states."""
+    from oracle import thorn_oracle as O
+    from thorn_b200.optimizer import _w1rand
+
+    rng = np.random.default_rng(5)
+    for s in [0, 1, (1 << 64) - 1, O.W1_C, *map(int, rng.integers(0, 1 << 63, 50))]:
+        assert _w1rand(s) == O.w1rand(s)
+
+
+@pytest.mark.parametrize("decouple_md", [False, True])
+def test_magma_scores_and_masks_match_oracle(decouple_md):
+    """THORN._magma (torch glue around the kernels) on CPU tensors against the oracle's
+    masking: same masked steps, same smoothed score, over several steps."""
+    from oracle import thorn_oracle as O
+    from thorn_b200.optimizer import _Item
+
+    torch.manual_seed(3)
+    p = nn.Parameter(torch.randn(12, 8) * 0.1)
+    opt = THORN([{"orthogonalize": True, "params": [p], "lr": 1e-3, "momentum_align": True,
+                  "decouple_md": decouple_md}])
+    cfg = GroupConfig.from_kwargs(**opt.param_groups[0])
+    p.grad = torch.randn_like(p)
+    st = opt.state[p]
+    opt._init_state(p, st, cfg, opt.param_groups[0])
+    ost = {"random_state": st["random_state"], "s": np.float32(1.0)}
+    if decouple_md:  # non-trivial gains so the recovered gradient differs from the raw one
+        st["row_gain"] = st["row_gain"] + torch.linspace(-0.5, 0.5, 12).reshape(12, 1)
+        st["col_gain"] = st["col_gain"] + torch.linspace(0.3, -0.3, 8).reshape(1, 8)
+    masked = 0
+    for k in range(12):
+        g = torch.randn(12, 8) * 1e-3
+        st["moment"] = torch.randn(12, 8) * 1e-3 if k else torch.zeros(12, 8)
+        it = _Item()
+        it.g, it.state, it.split, it.apply = g, st, "row_gain" in st, True
+        opt._magma([it], cfg, recovered=True)
+        gd = g.numpy()
+        if decouple_md:
+            sp = lambda x: np.log1p(np.exp(x.numpy().astype(np.float64))).astype(np.float32)
+            gd = (gd * (sp(st["row_gain"]) * sp(st["col_gain"]))).astype(np.float32)
+        want = O.magma_scale(gd, st["moment"].numpy(), ost, "f32")
+        assert st["random_state"] == ost["random_state"]
+        assert float(st["s"]) == pytest.approx(float(ost["s"]), rel=1e-6)
+        assert it.scale == pytest.approx(want, rel=1e-6)
+        assert it.apply == (want != 0.0)
+        masked += want == 0.0
+    assert 0 < masked < 12
+
+
+def test_sparse_row_gather_and_scatter():
+    """The row bookkeeping around the AdamW kernel for row-sparse gradients: duplicate rows
+    are summed (coalesce), only touched rows are gathered and written back, and a gradient
+    without rows is left out (the reference keeps its step count)."""
+    e = nn.Parameter(torch.randn(10, 3))
+    f = nn.Parameter(torch.randn(6, 2))
+    opt = THORN([{"orthogonalize": False, "params": [e, f], "lr": 1e-3}])
+    cfg = GroupConfig.from_kwargs(**opt.param_groups[0])
+    e.grad = torch.sparse_coo_tensor(torch.tensor([[7, 2, 7]]), torch.tensor([[1., 1, 1], [2, 2, 2], [3, 3, 3]]),
+                                     (10, 3))
+    f.grad = torch.sparse_coo_tensor(torch.zeros((1, 0), dtype=torch.long), torch.zeros((0, 2)), (6, 2))
+    for p in (e, f):
+        opt._init_state(p, opt.state[p], cfg, opt.param_groups[0])
+    recs = opt._sparse_rows([e, f], cfg)
+    assert len(recs) == 1
+    p, idx, it = recs[0]
+    assert p is e and idx.tolist() == [2, 7]
+    assert torch.equal(it.g, torch.tensor([[2., 2, 2], [4, 4, 4]]))
+    before = e.detach().clone()
+    it.m_rows += 1.0
+    it.v_rows += 2.0
+    it.p += 3.0
+    opt._scatter_rows(recs)
+    st = opt.state[e]
+    assert torch.equal(st["moment"][[2, 7]], torch.ones(2, 3)) and st["moment"][[0, 1, 3]].abs().sum() == 0
+    assert torch.equal(st["variance"][[2, 7]], torch.full((2, 3), 2.0))
+    assert torch.equal(e.detach()[[2, 7]], before[[2, 7]] + 3.0)
+    assert torch.equal(e.detach()[[0, 1, 3, 4, 5, 6, 8, 9]], before[[0, 1, 3, 4, 5, 6, 8, 9]])
