@@ -263,6 +263,8 @@ def gpu_arm(args, rank, world, local_rank):
         _native.load().thorn_set_elementwise_async(1)
     if args.gemm_pdl:
         _native.load().thorn_set_gemm_pdl(1)
+    if args.gemm_l2_hints:
+        _native.load().thorn_set_gemm_l2_hints(1)
 
     def local(t):
         return t.to_local() if hasattr(t, "to_local") else t
@@ -541,6 +543,8 @@ def main():
                     help="momentum pass with cp.async row staging (thorn_set_elementwise_async)")
     ap.add_argument("--gemm-pdl", action="store_true",
                     help="NS GEMMs with programmatic dependent launch (thorn_set_gemm_pdl)")
+    ap.add_argument("--gemm-l2-hints", action="store_true",
+                    help="L2 cache policies on the 2-CTA NS GEMM's loads and stores (thorn_set_gemm_l2_hints)")
     ap.add_argument("--pipeline-exchange", action="store_true",
                     help="N > 1: exchange row slabs in waves that overlap the owners' Newton-Schulz work")
     ap.add_argument("--e2e-mode", default="pipelined", choices=["serial", "pipelined"],
@@ -565,7 +569,7 @@ def main():
         import datetime
 
         # the exchanges are point-to-point and the all-reduces a few KB: NVLink
-        # SHARP buys nothing here, so NCCL skips setting up its multicast buffers
+        # SHARP buys nothing here, so NCCL skips setting up its NVLS buffers
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         stall_watchdog(rank, 420)
         import torch

@@ -76,6 +76,10 @@ THORN_API int thorn_set_elementwise_async(int enable);
  * memory; zero (default) launches in plain stream order.  Returns the previous
  * setting.  Both settings give bit-identical results. */
 THORN_API int thorn_set_gemm_pdl(int enable);
+/* 2-CTA NS GEMM tiles: nonzero gives operand TMA loads an L2 evict_last policy
+ * and output bulk stores an evict_first policy; zero (default) uses none.
+ * Returns the previous setting.  Both settings give bit-identical results. */
+THORN_API int thorn_set_gemm_l2_hints(int enable);
 
 /* --------------------------------------------------------------------------
  * (R)Adam(-atan2)W over many tensors in one launch per dtype pair.

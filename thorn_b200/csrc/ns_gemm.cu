@@ -63,7 +63,7 @@ struct Params {
   int64_t c_bs, c_ld, d_bs, d_ld, d2_bs, d2_ld;
   int M, N, K, batch;
   float alpha, beta, diag2;
-  int sym, trans_out, c_vec, d_vec, tma_epi, c_bcast;
+  int sym, trans_out, c_vec, d_vec, tma_epi, c_bcast, l2hint;
   int tiles_m, tiles_n, tiles_per_mat, total_tiles, num_kb;
   int* err;
 };
@@ -500,6 +500,34 @@ __device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap
       "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
+// The same loads and stores with an L2 cache policy (2-CTA kernel, `l2hint`):
+// operand tiles are re-read by other clusters and should stay (evict_last),
+// output blocks are not re-read by this kernel (evict_first).
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void tma_load_3d_pair_hint(uint32_t dst, const CUtensorMap* tm, uint32_t bar_cluster, int x,
+                                                      int y, int z, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.cta_group::2.L2::cache_hint "
+      "[%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z), "l"(pol)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_3d_hint(const CUtensorMap* tm, uint32_t src, int x, int y, int z,
+                                                  uint64_t pol) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3, %4}], [%1], %5;" ::
+                   "l"(reinterpret_cast<uint64_t>(tm)),
+               "r"(src), "r"(x), "r"(y), "r"(z), "l"(pol)
+               : "memory");
+}
 __device__ __forceinline__ void umma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                           uint32_t acc) {
   asm volatile(
@@ -626,6 +654,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
       int stage = 0;
       uint32_t phase = 0;
       const int row_off = (int)rank * 128;
+      const uint64_t pol_keep = l2_policy_evict_last();
+      auto load = [&](uint32_t dst, const CUtensorMap* tm, uint32_t bar, int x, int y, int z) {
+        if (p.l2hint) tma_load_3d_pair_hint(dst, tm, bar, x, y, z, pol_keep);
+        else tma_load_3d_pair(dst, tm, bar, x, y, z);
+      };
       for (int t = cid; t < p.total_tiles && !*abort_flag; t += nclusters) {
         int b, tm, tn;
         decode_tile2(p, t, b, tm, tn);
@@ -636,16 +669,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
           const uint32_t a_dst = smem_u32(sA + stage * kHalfBytes);
           const uint32_t b_dst = smem_u32(sB + stage * kHalfBytes);
           if (!A_MN) {
-            tma_load_3d_pair(a_dst, &p.tmA, fb, kb * BK, tm * BM2 + row_off, b);
+            load(a_dst, &p.tmA, fb, kb * BK, tm * BM2 + row_off, b);
           } else {
-            tma_load_3d_pair(a_dst, &p.tmA, fb, tm * BM2 + row_off, kb * BK, b);
-            tma_load_3d_pair(a_dst + 64 * BK * 2, &p.tmA, fb, tm * BM2 + row_off + 64, kb * BK, b);
+            load(a_dst, &p.tmA, fb, tm * BM2 + row_off, kb * BK, b);
+            load(a_dst + 64 * BK * 2, &p.tmA, fb, tm * BM2 + row_off + 64, kb * BK, b);
           }
           if (!B_MN) {
-            tma_load_3d_pair(b_dst, &p.tmB, fb, kb * BK, tn * 256 + row_off, b);
+            load(b_dst, &p.tmB, fb, kb * BK, tn * 256 + row_off, b);
           } else {
-            tma_load_3d_pair(b_dst, &p.tmB, fb, tn * 256 + row_off, kb * BK, b);
-            tma_load_3d_pair(b_dst + 64 * BK * 2, &p.tmB, fb, tn * 256 + row_off + 64, kb * BK, b);
+            load(b_dst, &p.tmB, fb, tn * 256 + row_off, kb * BK, b);
+            load(b_dst + 64 * BK * 2, &p.tmB, fb, tn * 256 + row_off + 64, kb * BK, b);
           }
           if (++stage == kStages2) {
             stage = 0;
@@ -708,6 +741,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
     const uint32_t cb0 = smem_u32(&cbar[2 * q]);
     const bool has_c = p.C != nullptr;
     const bool has_d2 = p.D2 != nullptr;
+    const uint64_t pol_out = l2_policy_evict_first();
+    auto store = [&](const CUtensorMap* tm, uint32_t src, int x, int y, int z) {
+      if (p.l2hint) tma_store_3d_hint(tm, src, x, y, z, pol_out);
+      else tma_store_3d(tm, src, x, y, z);
+    };
     bool c_inflight = false;  // a C load was issued and not yet waited for
     int c_buf = 0;
     uint32_t c_par = 0;
@@ -807,11 +845,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
         fence_async_smem();
         __syncwarp();
         if (lane == 0) {
-          if (!p.trans_out) tma_store_3d(&p.tmD, sM, col0, row0, b);
-          if (mirror || p.trans_out) tma_store_3d(&p.tmD, sT, row0, col0, b);
+          if (!p.trans_out) store(&p.tmD, sM, col0, row0, b);
+          if (mirror || p.trans_out) store(&p.tmD, sT, row0, col0, b);
           if (has_d2 && !diag) {
-            tma_store_3d(&p.tmD2, sM, col0, row0, b);
-            if (mirror) tma_store_3d(&p.tmD2, sT, row0, col0, b);
+            store(&p.tmD2, sM, col0, row0, b);
+            if (mirror) store(&p.tmD2, sT, row0, col0, b);
           }
           bulk_commit();
         }
@@ -827,7 +865,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
           fence_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_3d(&p.tmD2, sM, col0, row0, b);
+            store(&p.tmD2, sM, col0, row0, b);
             bulk_commit();
           }
         }
@@ -967,6 +1005,8 @@ static std::atomic<uint64_t> g_flops_dense{0}, g_flops_exec{0};
 
 // Programmatic dependent launch of the NS GEMMs (1) or plain stream order (0, default).
 static std::atomic<int> g_gemm_pdl{0};
+// L2 cache policies on the 2-CTA kernel's operand loads and output stores (1) or none (0, default).
+static std::atomic<int> g_l2_hints{0};
 
 template <int BN, bool AMN, bool BMN, class T>
 static int launch_gemm(gemm::Params& prm, int grid, cudaStream_t st) {
@@ -1135,6 +1175,7 @@ int run_gemm(const GemmOp& op, int dtype, int* err, cudaStream_t st) {
       if (rc) return rc;
     }
   }
+  prm.l2hint = pair && g_l2_hints.load() != 0;
   prm.tiles_m = (op.M + BMt - 1) / BMt;
   prm.tiles_n = (op.N + BN - 1) / BN;
   if (op.sym) {
@@ -1363,6 +1404,8 @@ extern "C" int thorn_set_gemm_pair(int enable) { return g_pair_tiles.exchange(en
 extern "C" int thorn_set_gemm_staged_epilogue(int enable) { return g_staged_epilogue.exchange(enable ? 1 : 0); }
 
 extern "C" int thorn_set_gemm_pdl(int enable) { return g_gemm_pdl.exchange(enable ? 1 : 0); }
+
+extern "C" int thorn_set_gemm_l2_hints(int enable) { return g_l2_hints.exchange(enable ? 1 : 0); }
 
 // Dense-equivalent and executed tensor-core FLOPs issued so far (for roofline reports).
 extern "C" void thorn_gemm_flops(double* dense, double* executed) {
