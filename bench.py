@@ -259,12 +259,7 @@ def gpu_arm(args, rank, world, local_rank):
         {"orthogonalize": False, "params": adamw, "lr": ADAM_LR, "state_dtype": torch.float32},
     ])
     opt.pipeline_exchange = bool(args.pipeline_exchange)
-    if args.elementwise_async:
-        _native.load().thorn_set_elementwise_async(1)
-    if args.gemm_pdl:
-        _native.load().thorn_set_gemm_pdl(1)
-    if args.gemm_l2_hints:
-        _native.load().thorn_set_gemm_l2_hints(1)
+    apply_switches(args)
 
     def local(t):
         return t.to_local() if hasattr(t, "to_local") else t
@@ -485,6 +480,19 @@ def gpu_arm(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def apply_switches(args):
+    """Kernel options of the library (all off by default)."""
+    from thorn_b200 import _native
+
+    lib = _native.load()
+    if args.elementwise_async:
+        lib.thorn_set_elementwise_async(1)
+    if args.gemm_pdl:
+        lib.thorn_set_gemm_pdl(1)
+    if args.gemm_l2_hints:
+        lib.thorn_set_gemm_l2_hints(1)
+
+
 def ns_only(args):
     """Time thorn_ns_batched alone on one batch shape (profiling entry point)."""
     import ctypes
@@ -496,6 +504,7 @@ def ns_only(args):
 
     B, R, C = (int(x) for x in args.ns_only.lower().split("x"))
     lib = N.load()
+    apply_switches(args)
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     co = optimal_composition(1e-3, 5, 0.03, 0.02)
