@@ -131,7 +131,13 @@ def test_bf16_params_with_fp32_state():
 
 # ---------------------------------------------------------------- NS / GEMM
 def _ns_gpu(u: torch.Tensor, ns_dtype=torch.float16, iters=5):
-    """Polar factor of each matrix of u (B, R, C) via thorn_ns_batched."""
+    """Polar factor of each matrix of u (B, R, C) via thorn_ns_batched (as numpy on the host)."""
+    out, co, rs = _ns_gpu_t(u, ns_dtype, iters)
+    return out.float().cpu().numpy(), co, rs
+
+
+def _ns_gpu_t(u: torch.Tensor, ns_dtype=torch.float16, iters=5):
+    """Polar factor of each matrix of u (B, R, C) via thorn_ns_batched (device tensor)."""
     from thorn_b200 import _native as N
     from thorn_b200.coeffs import gram_ns_restarts, optimal_composition
 
@@ -155,7 +161,28 @@ def _ns_gpu(u: torch.Tensor, ns_dtype=torch.float16, iters=5):
                                  N.stream_of(torch.device("cuda"))), "ns_batched")
     torch.cuda.synchronize()
     assert int(err.item()) == 0
-    return out.float().cpu().numpy(), co, rs
+    return out, co, rs
+
+
+@pytest.mark.parametrize("shape,kind", [((1, 14336, 4096), "rand"), ((1, 4096, 14336), "rand"),
+                                        ((2, 4096, 4096), "near_id"), ((4, 1024, 4096), "rand")])
+def test_ns_full_size_singular_values(shape, kind):
+    """At the Llama-3-8B shapes (too large for the CPU oracle), a size-independent property:
+    every singular value of the NS output lies in the band the Polar-Express composition
+    maps [1e-3, 1] into (the oracle gives [0.848, 1.153] at smaller sizes), while the
+    Frobenius-normalised inputs have singular values near 1/sqrt(min dim) ~ 0.016."""
+    torch.manual_seed(17)
+    if kind == "rand":  # rectangular Gaussian matrices are well conditioned
+        u = torch.randn(shape, device="cuda")
+    else:  # square: I + W/4 with W a scaled Gaussian keeps every singular value in [0.5, 1.5]
+        n = shape[-1]
+        u = torch.eye(n, device="cuda") + 0.25 * torch.randn(shape, device="cuda") / n ** 0.5
+    out, _, _ = _ns_gpu_t(u)
+    for U in out.float():
+        G = U.T @ U if U.shape[0] >= U.shape[1] else U @ U.T
+        ev = torch.linalg.eigvalsh(G.double())
+        s_min, s_max = float(ev.min().clamp_min(0).sqrt()), float(ev.max().sqrt())
+        assert 0.8 < s_min and s_max < 1.2, (shape, s_min, s_max)
 
 
 @pytest.mark.parametrize("shape", [(1, 64, 64), (3, 128, 64), (2, 64, 128), (1, 512, 512), (1, 1024, 512),
