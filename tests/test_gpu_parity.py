@@ -424,3 +424,33 @@ def test_staged_epilogue_sym_addmm(batch, m, k, c_batched):
     assert torch.equal(staged, staged.transpose(1, 2))
     want = 0.75 * (a.float() @ bt.float()) - 0.5 * c.float().expand(batch, m, m)
     assert (staged.float() - want).abs().max().item() <= 2e-2 * want.abs().max().item()
+
+
+def test_full_size_state_updates():
+    """Full Llama-3-8B sizes, size-independent checks of the elementwise passes: the momentum
+    of a 14336x4096 bf16 matrix with fp32 state is bit for bit torch's (m * beta1) + g, and
+    the (R)AdamW moments of the 128256x4096 embedding match torch's formulas (fp32)."""
+    from thorn_b200 import THORN
+
+    torch.manual_seed(21)
+    w = torch.nn.Parameter(torch.randn(14336, 4096, device="cuda", dtype=torch.bfloat16) * 0.02)
+    e = torch.nn.Parameter(torch.randn(128256, 4096, device="cuda", dtype=torch.bfloat16) * 0.02)
+    opt = THORN([{"orthogonalize": True, "params": [w], "lr": 1e-3, "state_dtype": torch.float32},
+                 {"orthogonalize": False, "params": [e], "lr": 1e-3, "state_dtype": torch.float32}])
+    b1, b2 = 0.9, 0.95
+    m_w = torch.zeros(w.shape, device="cuda")
+    m_e = torch.zeros(e.shape, device="cuda")
+    v_e = torch.zeros(e.shape, device="cuda")
+    for _ in range(2):
+        gw = torch.randn_like(w) * 1e-4
+        ge = torch.randn_like(e) * 1e-4
+        w.grad, e.grad = gw, ge
+        opt.step()
+        m_w = m_w * b1 + gw.float()
+        ge32 = ge.float()
+        m_e = m_e + (ge32 - m_e) * (1 - b1)
+        v_e = v_e * b2 + ge32 * ge32 * (1 - b2)
+        torch.cuda.synchronize()
+        assert torch.equal(opt.state[w]["moment"], m_w)
+        assert C.rel_fro(opt.state[e]["moment"].cpu().numpy(), m_e.cpu().numpy()) <= 1e-6
+        assert C.rel_fro(opt.state[e]["variance"].cpu().numpy(), v_e.cpu().numpy()) <= 1e-6
