@@ -541,6 +541,44 @@ def ns_only(args):
                       "finite": bool(torch.isfinite(U).all())}), flush=True)
 
 
+def ortho_only(args):
+    """Time THORN steps of one orthogonalized group of B x (R x C) bf16 matrices with
+    decouple_md and fp32 state (profiling entry point for the elementwise passes)."""
+    import torch
+
+    from thorn_b200 import THORN
+
+    B, R, C = (int(x) for x in args.ortho_only.lower().split("x"))
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    apply_switches(args)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    ps = [torch.nn.Parameter(torch.randn(R, C, device=dev, dtype=torch.bfloat16, generator=gen) * 0.02)
+          for _ in range(B)]
+    gs = [torch.randn(R, C, device=dev, dtype=torch.bfloat16, generator=gen) * 1e-4 for _ in range(B)]
+    opt = THORN([{"orthogonalize": True, "params": ps, "lr": ORTHO_LR, "decouple_md": True,
+                  "state_dtype": torch.float32}])
+
+    def step():
+        for p, g in zip(ps, gs):
+            p.grad = g
+        opt.step()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    print(json.dumps({"ortho_only": args.ortho_only, "ms": round(ms, 4), "err_flag": int(opt.device_error()),
+                      "finite": bool(all(torch.isfinite(p).all() for p in ps))}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -562,9 +600,14 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ns-only", default=None, help="BxRxC: time thorn_ns_batched alone on this batch (profiling)")
     ap.add_argument("--layers", type=int, default=LAYERS, help="transformer layers (profiling runs use fewer)")
+    ap.add_argument("--ortho-only", default=None,
+                    help="BxRxC: time steps of one decouple_md group of B bf16 RxC matrices (profiling)")
     args = ap.parse_args()
     if args.ns_only:
         ns_only(args)
+        return
+    if args.ortho_only:
+        ortho_only(args)
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
