@@ -48,10 +48,10 @@ LAYER_SHAPES = [(HIDDEN, HIDDEN), (KV, HIDDEN), (KV, HIDDEN), (HIDDEN, HIDDEN), 
                 (HIDDEN, FFN)]
 ORTHO_LR, ADAM_LR = 8e-3, 8e-3
 METRIC = "THORN.step ms, Llama-3-8B shapes"
-# DRAM bytes (read + write) of one ns_gemm_kernel launch from the ncu capture in
+# DRAM bytes (read + write) of one ns_gemm2_kernel launch from the ncu capture in
 # profiles/ns_gemm_2x4096.md: X X^T on two 4096x4096 matrices (K = 4096), whose
 # compulsory traffic is 67 MB read + 67 MB written.
-NS_GEMM_TRAFFIC = 98.6e6
+NS_GEMM_TRAFFIC = 100.1e6
 NS_GEMM_TRAFFIC_CASE = "one X X^T launch on 2 x 4096x4096 (K=4096); compulsory 67 MB read + 67 MB write"
 
 
@@ -458,7 +458,7 @@ def gpu_arm(args, rank, world, local_rank):
                    "state_dtype": "f32", "ns_dtype": "f16", "decouple_md": True, "lr": ORTHO_LR,
                    "parallelism": f"fsdp{world}" if world > 1 else "single",
                    "l2": "no flush: every step reads params, grads and state (~70 GB) >> 126 MB L2"},
-        "roofline": {"bound": "tensor", "kernel": "ns_gemm_kernel (Newton-Schulz phase)",
+        "roofline": {"bound": "tensor", "kernel": "ns_gemm2_kernel (Newton-Schulz phase)",
                      "achieved": round(achieved, 1) if achieved else None, "peak": round(peak_job, 1),
                      "unit": "TFLOP/s", "frac": round(achieved / peak_job, 3) if achieved else None,
                      "traffic": NS_GEMM_TRAFFIC,
