@@ -594,11 +594,16 @@ class OracleTHORN:
     dtype, thorn.py:1596-1599).
     """
 
-    def __init__(self, groups, seed_fn=None):
+    def __init__(self, groups, seed_fn=None, sharded: bool = False):
         """``seed_fn()``: the next Magma seed, called once per momentum_align
         parameter at state initialisation in group and parameter order -- where
-        the reference draws ``torch.randint`` (thorn.py:1616-1633)."""
+        the reference draws ``torch.randint`` (thorn.py:1616-1633).
+        ``sharded``: orthogonalized groups follow the reference's FSDP2 step
+        (thorn.py:1459-1581): Magma statistics in fp32 from summed shard
+        partials, and a masked matrix skips the whole step (no momentum update,
+        no step count)."""
         self.seed_fn = seed_fn
+        self.sharded = sharded
         self.groups = []
         for d in groups:
             g = Group(d)
@@ -659,7 +664,9 @@ class OracleTHORN:
             if grp.decouple_md:
                 p, g, p_g, gains = recover_direction(p, g, st, dt)
             # Magma on the recovered gradient and the moment before this step (thorn.py:1392)
-            scale = magma_scale(g, st["moment"], st, dt) if grp.momentum_align else 1.0
+            scale = magma_scale(g, st["moment"], st, dt, sharded=self.sharded) if grp.momentum_align else 1.0
+            if self.sharded and scale == 0.0:
+                continue  # thorn.py:1485-1490: the masked matrix is left as it is
             # momentum (thorn.py:1376-1381): m = m*b1 + g ; u = g + b1*m
             m = rnd(st["moment"] * b1, sdt)
             m = rnd(m + g, sdt)

@@ -114,6 +114,16 @@ CASES = {
         dict(orthogonalize=False, shapes=[(48, 16)], init=("normal", 0.5), dtype="f32",
              opts=dict(lr=1e-3, decouple_md=True, momentum_align=True)),
     ]),
+    # Magma on the FSDP2 path (world 1 and 2): orthogonalized matrices, even and uneven splits,
+    # with and without MD, next to a Magma (R)AdamW vector group.
+    "magma_shard": dict(steps=6, grad_std=1e-3, groups=[
+        dict(orthogonalize=True, shapes=[(64, 64), (97, 64)], init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=2e-3, weight_decay=0.1, momentum_align=True)),
+        dict(orthogonalize=True, shapes=[(64, 96)], init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=8e-3, decouple_md=True, momentum_align=True)),
+        dict(orthogonalize=False, shapes=[(64,), (40,)], init=("normal", 0.1), dtype="f32",
+             opts=dict(lr=1e-3, momentum_align=True)),
+    ]),
     # Row-sparse gradients on (R)AdamW parameters (thorn.py:1667-1698): duplicate rows, a 1-D
     # embedding, a step whose sparse gradient has no rows, Magma on sparse rows.
     "sparse_small": dict(steps=4, grad_std=1e-3, groups=[

@@ -14,7 +14,7 @@ def load_golden(path: str) -> dict:
 
 
 def run_oracle(name: str, steps: int | None = None, state_dtype: str | None = None, cpu_quirks: bool = False,
-               seeds: list | None = None):
+               seeds: list | None = None, sharded: bool = False):
     """Step the CPU oracle on a case; returns (oracle, snapshots{tag: (params, states)}).
 
     ``cpu_quirks`` models the reference's eager CPU path (used to pin the oracle
@@ -38,7 +38,7 @@ def run_oracle(name: str, steps: int | None = None, state_dtype: str | None = No
         d["params"] = [t.float().numpy() for t in ps]
         groups.append(d)
     seed_fn = C.magma_seed if seeds is None else iter(list(seeds)).__next__
-    orc = OracleTHORN(groups, seed_fn=seed_fn)
+    orc = OracleTHORN(groups, seed_fn=seed_fn, sharded=sharded)
     n = case["steps"] if steps is None else steps
     snaps = {}
     for s in range(n):

@@ -32,6 +32,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", required=True)
     ap.add_argument("--out", required=True)
+    ap.add_argument("--pipeline-exchange", action="store_true")
     args = ap.parse_args()
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local_rank)
@@ -47,6 +48,7 @@ def main():
     params = C.build_params(case)
     tp = [[torch.nn.Parameter(distribute_tensor(t.cuda(), mesh, [Shard(0)])) for t in ps] for ps in params]
     opt = THORN(C.group_dicts(case, tp))
+    opt.pipeline_exchange = args.pipeline_exchange
     out = {}
     for s in range(case["steps"]):
         for ps, gs in zip(tp, C.build_grads(case, s)):

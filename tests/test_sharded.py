@@ -197,10 +197,11 @@ def test_shard_rows_follow_torch_chunk():
             assert sum(got) == rows and shard_rows(rows, world)[0][0] == 0
 
 
-def _run_workers(n, name, tmp_path):
+def _run_workers(n, name, tmp_path, extra=()):
     out = str(tmp_path / f"{name}_{n}.npz")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nproc-per-node", str(n), "--master-addr", "127.0.0.1",
-           "--master-port", str(_free_port()), os.path.join(HERE, "sharded_worker.py"), "--case", name, "--out", out]
+           "--master-port", str(_free_port()), os.path.join(HERE, "sharded_worker.py"), "--case", name, "--out", out,
+           *extra]
     r = subprocess.run(["timeout", "-k", "30", "600"] + cmd, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     with np.load(out) as z:
