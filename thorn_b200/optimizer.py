@@ -825,8 +825,18 @@ class THORN(Optimizer):
                 return
         arena = _Arena()
         items = self._items(params, cfg, arena, ortho=False)
-        # Magma on the raw gradient, before direction recovery (thorn.py:1702)
-        self._magma(items, cfg, recovered=False)
+        # Magma on the raw gradient, before direction recovery (thorn.py:1702); a sharded
+        # parameter scores its whole tensor (sums all-reduced over its shard group)
+        plain, by_group = [], {}
+        for p, it in zip(params, items):
+            if isinstance(p, DTensor) and not all(isinstance(pl, Replicate) for pl in p.placements):
+                from .sharded import shard_group
+                by_group.setdefault(shard_group(p, self.rank)[1], []).append(it)
+            else:
+                plain.append(it)
+        self._magma(plain, cfg, recovered=False)
+        for grp, its in by_group.items():
+            self._magma(its, cfg, recovered=False, group=grp)
         if md:
             for it in items:
                 ax = cfg.norm_axis_(it.p)
