@@ -124,10 +124,9 @@ class Exchange:
         for w in self.works:
             w.wait()
         for buf, dsts in self.unpack:
-            off = 0
-            for t in dsts:
-                t.reshape(-1).view(torch.uint8).copy_(buf[off:off + t.nbytes])
-                off += t.nbytes
+            # one multi-tensor copy for all slabs of a message
+            views = [t.reshape(-1).view(torch.uint8) for t in dsts]
+            torch._foreach_copy_(views, list(buf.split([v.numel() for v in views])))
         self.works, self.unpack = [], []
 
 
@@ -156,6 +155,8 @@ def exchange(sends: list[Slab], recvs: list[Slab], ranks: list[int], group, wait
         if out:
             ops.append(dist.P2POp(dist.isend, _bytes_of(out), ranks[to], group))
         if inc:
+            if not all(t.is_contiguous() for t in inc):
+                raise ValueError("receive slabs must be contiguous")
             buf = _span(inc)  # received in place when the destinations are back to back
             if buf is None:
                 buf = torch.empty(sum(t.nbytes for t in inc), dtype=torch.uint8, device=inc[0].device)
