@@ -213,3 +213,21 @@ def test_sparse_row_gather_and_scatter():
     assert torch.equal(st["variance"][[2, 7]], torch.full((2, 3), 2.0))
     assert torch.equal(e.detach()[[2, 7]], before[[2, 7]] + 3.0)
     assert torch.equal(e.detach()[[0, 1, 3, 4, 5, 6, 8, 9]], before[[0, 1, 3, 4, 5, 6, 8, 9]])
+
+
+def test_custom_ops_registered_with_fake_impls():
+    """torch.ops.thorn_b200.sym_addmm / polar_decomp exist and trace on meta tensors
+    (shape and dtype from their fake implementations, no device work)."""
+    import thorn_b200  # noqa: F401
+
+    A = torch.empty(3, 64, 32, device="meta", dtype=torch.float16)
+    B = torch.empty(3, 32, 64, device="meta", dtype=torch.float16)
+    C = torch.empty(64, 64, device="meta", dtype=torch.float16)
+    out = torch.ops.thorn_b200.sym_addmm(A, B, C, 1.0, 0.5)
+    assert out.shape == (3, 64, 64) and out.dtype == torch.float16 and out.device.type == "meta"
+    X = torch.empty(2, 5, 96, 40, device="meta", dtype=torch.bfloat16)
+    U = torch.ops.thorn_b200.polar_decomp(X, [1.0, 0.0, 0.0], [])
+    assert U.shape == X.shape and U.dtype == torch.bfloat16
+    with pytest.raises(RuntimeError, match="CUDA"):
+        torch.ops.thorn_b200.sym_addmm(torch.zeros(64, 32, dtype=torch.float16),
+                                       torch.zeros(32, 64, dtype=torch.float16), None, 1.0, 0.0)

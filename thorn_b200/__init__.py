@@ -3,6 +3,7 @@
 ``from thorn_b200 import THORN`` is a drop-in for ``from thorn import THORN``
 (pykeio/THORN v3.1.1).
 """
+from . import ops  # noqa: F401  (registers torch.ops.thorn_b200.*)
 from .host_stepper import PinnedStepper  # noqa: F401
 from .optimizer import THORN, THORNGroup, THORNNonOrthoGroup, THORNOrthoGroup  # noqa: F401
 

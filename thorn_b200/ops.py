@@ -1,0 +1,126 @@
+"""PyTorch custom operators over the C ABI.
+
+* ``torch.ops.thorn_b200.sym_addmm(A, B, C, alpha, beta)``: the contract of the
+  reference's operator seam ``thorn::sym_addmm`` (thorn.py:298-368), i.e.
+  ``beta * C + alpha * (A @ B)`` for products known to be symmetric, computed on
+  the lower-triangle tiles of the tcgen05 GEMM and mirrored.
+* ``torch.ops.thorn_b200.polar_decomp(X, coeffs, restarts)``: the Newton-Schulz
+  polar factor of a stack of matrices (thorn.py:626-662): Frobenius-normalised in
+  fp32, iterated on fp16 operands, returned in X's dtype.
+
+Both have fake (meta) implementations, so they trace under ``torch.compile`` and
+``torch.export`` as opaque nodes.  They run on CUDA devices only; there is no CPU
+path.
+"""
+from __future__ import annotations
+
+from math import prod
+from typing import List, Optional
+
+import torch
+
+from . import _native as N
+
+_HALF = (torch.float16, torch.bfloat16)
+
+
+def _err_flag(dev: torch.device) -> torch.Tensor:
+    flags = _err_flag.cache
+    t = flags.get(dev)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=dev)
+        flags[dev] = t
+    return t
+
+
+_err_flag.cache = {}
+
+
+def _check_cuda(*ts):
+    for t in ts:
+        if t is not None and t.device.type != "cuda":
+            raise RuntimeError(f"thorn_b200 operators run on CUDA devices only; got a tensor on {t.device}")
+
+
+@torch.library.custom_op("thorn_b200::sym_addmm", mutates_args=())
+def sym_addmm(A: torch.Tensor, B: torch.Tensor, C: Optional[torch.Tensor], alpha: float,
+              beta: float) -> torch.Tensor:
+    """``beta * C + alpha * (A @ B)`` with ``A @ B`` and ``C`` symmetric.
+
+    A: (..., M, K), B: (..., K, M), C: (..., M, M), (M, M) or None; fp16 or bf16,
+    M and K multiples of 8.  Returns (..., M, M), exactly symmetric.
+    """
+    _check_cuda(A, B, C)
+    if A.dtype not in _HALF or B.dtype != A.dtype or (C is not None and C.dtype != A.dtype):
+        raise TypeError("sym_addmm takes float16 or bfloat16 operands of one dtype")
+    if A.ndim < 2 or B.ndim != A.ndim:
+        raise ValueError("A and B must have the same number (>= 2) of dimensions")
+    *batch, M, K = A.shape
+    if tuple(B.shape) != (*batch, K, M):
+        raise ValueError(f"B must be {(*batch, K, M)}, got {tuple(B.shape)}")
+    if C is not None and not (tuple(C.shape) == (M, M) or tuple(C.shape) == (*batch, M, M)):
+        raise ValueError(f"C must be {(*batch, M, M)} or {(M, M)}, got {tuple(C.shape)}")
+    if M % 8 or K % 8:
+        raise ValueError("sym_addmm needs M and K to be multiples of 8 (16-byte TMA rows)")
+    nn = prod(batch) if batch else 1
+    a = A.reshape(nn, M, K).contiguous()
+    b = B.reshape(nn, K, M).contiguous()
+    c_batched = C is not None and C.ndim > 2
+    c = None if C is None else (C.reshape(nn, M, M) if c_batched else C).contiguous()
+    out = torch.empty((nn, M, M), dtype=A.dtype, device=A.device)
+    if nn and M:
+        lib = N.load()
+        with torch.cuda.device(A.device):
+            N.check(lib.thorn_sym_addmm(a.data_ptr(), b.data_ptr(), None if c is None else c.data_ptr(),
+                                        out.data_ptr(), nn, M, K, 1 if c_batched else 0, float(alpha), float(beta),
+                                        N.dtype_code(A.dtype), _err_flag(A.device).data_ptr(),
+                                        N.stream_of(A.device)), "sym_addmm")
+    return out.reshape(*batch, M, M)
+
+
+@sym_addmm.register_fake
+def _sym_addmm_fake(A, B, C, alpha, beta):
+    *batch, M, _ = A.shape
+    return A.new_empty((*batch, M, M))
+
+
+@torch.library.custom_op("thorn_b200::polar_decomp", mutates_args=())
+def polar_decomp(X: torch.Tensor, coeffs: List[float], restarts: List[int]) -> torch.Tensor:
+    """Polar factor of every matrix of X (..., R, C) by Newton-Schulz.
+
+    ``coeffs``: the flat (a, b, c) triples of the iterations (3 x iters floats);
+    ``restarts``: Gram-NS restart positions.  X is normalised to unit Frobenius
+    norm in fp32, iterated on fp16 operands with fp32 accumulation, and the result
+    is returned in X's dtype.
+    """
+    _check_cuda(X)
+    if X.ndim < 2:
+        raise ValueError("polar_decomp takes (..., R, C) stacks of matrices")
+    if len(coeffs) % 3:
+        raise ValueError("coeffs must hold whole (a, b, c) triples")
+    *batch, R, C = X.shape
+    nb = prod(batch) if batch else 1
+    out = torch.empty((nb, R, C), dtype=torch.float16, device=X.device)
+    if nb and R and C:
+        lib = N.load()
+        dev = X.device
+        ld = int(lib.thorn_ns_ld(C))
+        x = X.reshape(nb, R, C).to(torch.float32)
+        x = x / (x.norm(dim=(-2, -1), keepdim=True) + 1e-8)
+        xin = torch.zeros((nb, R, ld), dtype=torch.float16, device=dev)
+        xin[:, :, :C] = x.to(torch.float16)
+        wsb = int(lib.thorn_ns_workspace_bytes(nb, R, C))
+        ws = torch.empty(max(256, wsb), dtype=torch.uint8, device=dev)
+        iters = len(coeffs) // 3
+        cc = (N.ctypes.c_double * max(1, len(coeffs)))(*coeffs)
+        rr = (N.ctypes.c_int32 * max(1, len(restarts)))(*restarts)
+        with torch.cuda.device(dev):
+            N.check(lib.thorn_ns_batched(xin.data_ptr(), out.data_ptr(), ws.data_ptr(), wsb, nb, R, C, N.F16, cc,
+                                         iters, rr, len(restarts), _err_flag(dev).data_ptr(), N.stream_of(dev)),
+                    "polar_decomp")
+    return out.reshape(*batch, R, C).to(X.dtype)
+
+
+@polar_decomp.register_fake
+def _polar_decomp_fake(X, coeffs, restarts):
+    return torch.empty_like(X)
