@@ -302,6 +302,7 @@ def gpu_arm(args, rank, world, local_rank):
         sampler.start()
         time.sleep(0.3)
     opt.profile_ns = []
+    opt.profile_momentum = []
     launches0 = _native.launch_count()
     barrier()
     torch.cuda.synchronize()
@@ -321,6 +322,14 @@ def gpu_arm(args, rank, world, local_rank):
     progress(rank, "timed steps done")
     prof = opt.profile_ns
     opt.profile_ns = None
+    prof_m = opt.profile_momentum
+    opt.profile_momentum = None
+    mom_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b, _ in prof_m) / args.steps)
+    mom_bytes = sum(nb for _, _, nb in prof_m) / args.steps
+    if world > 1:
+        t = torch.tensor([mom_bytes], device=dev, dtype=torch.float64)
+        dist.all_reduce(t)
+        mom_bytes = float(t[0])
     # host cost of one step on an idle GPU (nothing blocks on a full launch queue)
     feed()
     torch.cuda.synchronize()
@@ -469,6 +478,13 @@ def gpu_arm(args, rank, world, local_rank):
                                     f"burst {peak_burst} per GPU",
                      "ns_ms_per_step": round(ns_launch_ms, 3),
                      "ns_dense_tflop_per_step": round(ns_dense_all / 1e12, 2)},
+        "roofline_elementwise": {
+            "bound": "hbm", "kernel": "ortho_pre_kernel + pre_reduce_kernel (momentum pass)",
+            "achieved": round(mom_bytes / (mom_ms * 1e-3) / 1e9, 1) if mom_ms > 0 else None,
+            "peak": round(hbm * world, 1), "unit": "GB/s",
+            "frac": round(mom_bytes / (mom_ms * 1e-3) / 1e9 / (hbm * world), 3) if mom_ms > 0 else None,
+            "bytes": "g read + m read/write + p read/write (decouple_md), compulsory",
+            "ms_per_step": round(mom_ms, 3), "gb_per_step": round(mom_bytes / 1e9, 2)},
         "cpu_baseline": cpu,
         "e2e": e2e,
         "host_ms_per_step": round(host_ms, 2),

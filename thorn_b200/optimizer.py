@@ -260,6 +260,9 @@ class THORN(Optimizer):
     # when a list: each Newton-Schulz call appends (start event, end event, dense-equivalent
     # FLOPs, executed FLOPs, (batch, rows, cols)); events are recorded on the launching stream
     profile_ns: Optional[list] = None
+    # when a list: each momentum pass of an orthogonalized group appends (start event, end
+    # event, algorithmic bytes: g read, m read + write, p read + write with decouple_md)
+    profile_momentum: Optional[list] = None
     # sharded path: exchange row slabs in waves of NS batches so that transfers overlap
     # the owners' Newton-Schulz work (False: every slab moves before any NS starts)
     pipeline_exchange: bool = False
@@ -473,6 +476,32 @@ class THORN(Optimizer):
                     self._ortho_local(ps, cfg)
                 else:
                     self._adam_local(ps, cfg)
+
+    @staticmethod
+    def _profile_start(log):
+        if log is None:
+            return None
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        return ev
+
+    @staticmethod
+    def _profile_end(log, ev0, nbytes):
+        if log is not None:
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev1.record()
+            log.append((ev0, ev1, nbytes))
+
+    @staticmethod
+    def _momentum_bytes(items, md: bool) -> int:
+        """Compulsory bytes of the momentum pass: g read, m read and written, p read and
+        written when directions are recovered (decouple_md)."""
+        tot = 0
+        for it in items:
+            n = it.B * it.R * it.C
+            tot += n * (it.g.element_size() + 2 * _local(it.state["moment"]).element_size()
+                        + (2 * it.p.element_size() if md else 0))
+        return tot
 
     def _scratch(self, dev, sizes):
         """Pointers to disjoint regions of a per-device scratch buffer (zeroed once).
@@ -691,11 +720,13 @@ class THORN(Optimizer):
                                  1 if (md and not it.split) else 0,
                                  arena.ptr(it.rgs) if md else None, arena.ptr(it.cgs) if md else None, sp)
             by_dt.setdefault((it.pdt, it.sdt), []).append(t)
+        ev = self._profile_start(self.profile_momentum)
         for (pdt, sdt), ts in by_dt.items():
             udt = pdt if pdt == sdt else torch.float32
             N.check(lib.thorn_ortho_pre_multi(N.array(N.OrthoPreTensor, ts), len(ts), N.dtype_code(pdt),
                                               N.dtype_code(sdt), N.dtype_code(udt), b1, 1 if md else 0, write_grad,
                                               stream), "ortho_pre_multi")
+        self._profile_end(self.profile_momentum, ev, self._momentum_bytes(items, md))
         if md:
             self._md_gains(items, cfg, arena, stream)
 

@@ -321,11 +321,13 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
             arena.ptr(it.normsq), it.B, it.R, it.C, arena.ptr(it.rs) if md else None,
             arena.ptr(it.cs) if md else None, 1 if (md and not it.split) else 0,
             arena.ptr(it.rgs) if md else None, arena.ptr(it.cgs) if md else None, sp))
+    ev = opt._profile_start(opt.profile_momentum)
     for (pdt, sdt), ts in by_dt.items():
         udt = pdt if pdt == sdt else torch.float32
         N.check(lib.thorn_ortho_pre_multi(N.array(N.OrthoPreTensor, ts), len(ts), N.dtype_code(pdt),
                                           N.dtype_code(sdt), N.dtype_code(udt), b1, 1 if md else 0, write_grad,
                                           stream), "ortho_pre_multi")
+    opt._profile_end(opt.profile_momentum, ev, opt._momentum_bytes(items, md))
     dist.all_reduce(arena.region("red1"), group=group)
     if md:
         opt._md_gains(items, cfg, arena, stream)
