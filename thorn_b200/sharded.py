@@ -264,7 +264,6 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
     b1 = float(cfg.betas[0])
     ns_dt = opt.ns_dtype
     ns_code = N.dtype_code(ns_dt)
-    esz = torch.empty((), dtype=ns_dt).element_size()
     rows_g = [int(p.shape[0]) for p in mats]  # global rows
     parts = [shard_rows(r, world) for r in rows_g]  # (first row, count) of every shard
     for it in items:
