@@ -123,3 +123,17 @@ def test_argument_validation_without_gpu(lib):
     assert lib.thorn_ortho_pre_multi(pre, 1, 0, 0, 0, 0.9, 0, 0, None) == 1
     mp = N.array(N.MdPrepTensor, [N.MdPrepTensor(None, None, None, 4)])
     assert lib.thorn_md_prep_multi(mp, 1, 0, None) == 1
+
+
+@pytest.mark.parametrize("name,default", [("thorn_set_gemm_pair", 1), ("thorn_set_gemm_staged_epilogue", 1),
+                                          ("thorn_set_elementwise_async", 0), ("thorn_set_gemm_pdl", 0),
+                                          ("thorn_set_gemm_l2_hints", 0)])
+def test_kernel_switches(lib, name, default):
+    """Each switch returns its previous setting; the defaults are the measured kernels."""
+    fn = getattr(lib, name)
+    prev = fn(default)
+    assert prev == default
+    assert fn(1 - default) == default
+    assert fn(default) == 1 - default
+    assert fn(7 if default else 0) == default  # any nonzero value means on
+    fn(default)
