@@ -164,6 +164,20 @@ def _ns_gpu_t(u: torch.Tensor, ns_dtype=torch.float16, iters=5):
     return out, co, rs
 
 
+@pytest.mark.parametrize("shape", [(1, 4096, 4096), (1, 14336, 4096)])
+def test_ns_full_size_matches_oracle(shape):
+    """One Llama-3-8B q/o (4096x4096) and one gate/up (14336x4096, tall: Gram NS on the
+    original orientation, transposed final product) matrix against the CPU oracle at full
+    size (the oracle needs ~10-35 s of host time for these)."""
+    torch.manual_seed(8)
+    u = sum(torch.randn(shape) * (0.9 ** k) for k in range(4)) * 1e-3
+    got, co, rs = _ns_gpu(u.cuda())
+    O.NS_DTYPE = "f16"
+    want = O.polar_decomp_2d(u[0].numpy(), co, rs, "f32")
+    err = C.rel_fro(got[0], want)
+    assert err <= 2e-2, err
+
+
 @pytest.mark.parametrize("shape,kind", [((1, 14336, 4096), "rand"), ((1, 4096, 14336), "rand"),
                                         ((2, 4096, 4096), "near_id"), ((4, 1024, 4096), "rand")])
 def test_ns_full_size_singular_values(shape, kind):
