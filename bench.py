@@ -259,6 +259,7 @@ def gpu_arm(args, rank, world, local_rank):
         {"orthogonalize": False, "params": adamw, "lr": ADAM_LR, "state_dtype": torch.float32},
     ])
     opt.pipeline_exchange = bool(args.pipeline_exchange)
+    opt.exchange = args.exchange
     apply_switches(args)
 
     def local(t):
@@ -608,6 +609,8 @@ def main():
                     help="NS GEMMs with programmatic dependent launch (thorn_set_gemm_pdl)")
     ap.add_argument("--gemm-l2-hints", action="store_true",
                     help="L2 cache policies on the 2-CTA NS GEMM's loads and stores (thorn_set_gemm_l2_hints)")
+    ap.add_argument("--exchange", default="rounds", choices=["rounds", "all_to_all"],
+                    help="N > 1: slab exchange as pairwise P2P rounds or one all_to_all_single")
     ap.add_argument("--pipeline-exchange", action="store_true",
                     help="N > 1: exchange row slabs in waves that overlap the owners' Newton-Schulz work")
     ap.add_argument("--e2e-mode", default="pipelined", choices=["serial", "pipelined"],

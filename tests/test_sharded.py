@@ -19,7 +19,8 @@ import torch.multiprocessing as mp
 
 import cases as C
 import parity as P
-from thorn_b200.sharded import assign_owners, exchange, ns_flops, plan_gather, plan_scatter, shard_rows
+from thorn_b200.sharded import assign_owners, ns_flops, plan_gather, plan_scatter, shard_rows
+from thorn_b200.sharded import exchange as _exchange
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 
@@ -47,11 +48,13 @@ def test_assign_owners_balanced_and_deterministic():
     assert assign_owners([7], 4) == [0]
 
 
-def _exchange_worker(rank, world, port, result):
+def _exchange_worker(rank, world, port, result, impl="rounds"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
+        from thorn_b200.sharded import exchange_all_to_all
+        exchange = _exchange if impl == "rounds" else exchange_all_to_all
         ranks = list(range(world))
         # even and uneven Shard(0) splits (torch.chunk sizes: the last shard is shorter)
         shapes = [(24, 3), (13, 5), (36, 2), (25, 7), (49, 4), (12, 3)]
@@ -107,13 +110,14 @@ def _exchange_worker(rank, world, port, result):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3, 4])
-def test_slab_exchange_gloo(world):
-    """Gather and scatter plans through the shifted pairwise rounds, odd world sizes included."""
+@pytest.mark.parametrize("world,impl", [(2, "rounds"), (3, "rounds"), (4, "rounds"), (3, "all_to_all")])
+def test_slab_exchange_gloo(world, impl):
+    """Gather and scatter plans through the shifted pairwise rounds (odd world sizes
+    included) and through the all_to_all_single alternative."""
     ctx = mp.get_context("spawn")
     mgr = ctx.Manager()
     result = mgr.dict()
-    mp.start_processes(_exchange_worker, args=(world, _free_port(), result), nprocs=world, join=True,
+    mp.start_processes(_exchange_worker, args=(world, _free_port(), result, impl), nprocs=world, join=True,
                        start_method="spawn")
     assert dict(result) == {r: True for r in range(world)}
 

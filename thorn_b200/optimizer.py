@@ -266,6 +266,9 @@ class THORN(Optimizer):
     # sharded path: exchange row slabs in waves of NS batches so that transfers overlap
     # the owners' Newton-Schulz work (False: every slab moves before any NS starts)
     pipeline_exchange: bool = False
+    # sharded path: "rounds" (world - 1 pairwise point-to-point rounds) or "all_to_all"
+    # (one all_to_all_single collective per exchange)
+    exchange: str = "rounds"
 
     def __init__(self, params, *, backend=torch.cuda, **conf):
         self._update_rate = 1

@@ -169,6 +169,44 @@ def exchange(sends: list[Slab], recvs: list[Slab], ranks: list[int], group, wait
     return ex
 
 
+def exchange_all_to_all(sends: list[Slab], recvs: list[Slab], ranks: list[int], group,
+                        wait: bool = True) -> Exchange:
+    """The same exchange as one ``all_to_all_single`` collective: each peer's slabs
+    packed back to back (canonical order) in one send buffer, the received bytes
+    unpacked per source.  Every rank of the group takes part, also with nothing to
+    send; the collective is the alternative when grouped point-to-point calls are
+    not wanted (``THORN.exchange = "all_to_all"``)."""
+    world = len(ranks)
+    if sends or recvs:
+        dev = (sends[0] if sends else recvs[0]).tensor.device
+    else:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    out_parts, in_parts = [[] for _ in range(world)], [[] for _ in range(world)]
+    for s_ in sends:
+        if s_.tensor.numel():
+            out_parts[s_.peer].append(s_.tensor)
+    for r in recvs:
+        if r.tensor.numel():
+            if not r.tensor.is_contiguous():
+                raise ValueError("receive slabs must be contiguous")
+            in_parts[r.peer].append(r.tensor)
+    out_sizes = [sum(t.nbytes for t in ts) for ts in out_parts]
+    in_sizes = [sum(t.nbytes for t in ts) for ts in in_parts]
+    flat = [t.reshape(-1).view(torch.uint8) for ts in out_parts for t in ts]
+    send_buf = torch.cat(flat) if flat else torch.empty(0, dtype=torch.uint8, device=dev)
+    recv_buf = torch.empty(sum(in_sizes), dtype=torch.uint8, device=dev)
+    ex = Exchange()
+    ex.works.append(dist.all_to_all_single(recv_buf, send_buf, in_sizes, out_sizes, group=group, async_op=True))
+    off = 0
+    for peer in range(world):
+        if in_sizes[peer]:
+            ex.unpack.append((recv_buf[off:off + in_sizes[peer]], in_parts[peer]))
+        off += in_sizes[peer]
+    if wait:
+        ex.wait()
+    return ex
+
+
 def plan_gather(owners: list[int], me: int, world: int, my_rows, owner_rows, subset=None):
     """Messages that bring every matrix's row slabs to its owner.
 
@@ -368,12 +406,13 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
         N.check(lib.thorn_ns_cast_multi(N.array(N.NsCastTensor, ts), len(ts), N.dtype_code(pdt), N.dtype_code(sdt),
                                         N.dtype_code(udt), ns_code, b1, stream), "ns_cast_multi")
 
+    xchg = exchange_all_to_all if getattr(opt, "exchange", "rounds") == "all_to_all" else exchange
     # 3. slabs to owners: every wave's exchange is queued now (the NCCL stream runs them
     # in order); each NS batch waits only for its own wave
     gathers = []
     for js in wave_js:
         sends, recvs = plan_gather(owners, me, world, lambda j: send_rows[j], owner_rows, subset=js)
-        gathers.append(exchange(sends, recvs, ranks, group, wait=False))
+        gathers.append(xchg(sends, recvs, ranks, group, wait=False))
 
     # 5. (buffers) result rows (+ row factors) come back to every shard
     u_loc, f_loc = {}, {}
@@ -431,7 +470,7 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
                         "pnn_stats")
                 factors[ci] = arena.get(rsh).view(nb, R)
         sends, recvs = plan_scatter(owners, me, world, owner_parts, my_parts, subset=js_w)
-        scatters.append(exchange(sends, recvs, ranks, group, wait=False))
+        scatters.append(xchg(sends, recvs, ranks, group, wait=False))
     for ex in scatters:
         ex.wait()
     del X, send_buf, send_rows
