@@ -65,10 +65,11 @@ THORN_API int thorn_set_gemm_pair(int enable);
  * strides that are multiples of 8.  Returns the previous setting.  Both settings
  * give bit-identical results. */
 THORN_API int thorn_set_gemm_staged_epilogue(int enable);
-/* Momentum pass of thorn_ortho_pre_multi: nonzero streams each thread's rows into
- * shared memory four rows ahead with cp.async (bytes in flight without registers);
- * zero (default) loads them into registers.  Returns the previous setting.  Both
- * settings give bit-identical results. */
+/* Streaming passes of thorn_ortho_pre_multi (momentum), thorn_ortho_post_multi
+ * (apply) and thorn_md_finalize_multi: nonzero streams each thread's rows into
+ * shared memory four rows ahead with cp.async (bytes in flight without
+ * registers); zero (default) loads them into registers.  Returns the previous
+ * setting.  Both settings give bit-identical results. */
 THORN_API int thorn_set_elementwise_async(int enable);
 /* NS GEMM launches: nonzero uses programmatic dependent launch, so each GEMM's
  * set-up (barriers, TMEM, descriptor prefetch) overlaps the previous kernel's

@@ -677,8 +677,17 @@ struct PostArgs {
 };
 
 template <class U, class P>
+struct PostUnits {
+  static constexpr int u = 8 * (int)sizeof(U) / 16;
+  static constexpr int p = 8 * (int)sizeof(P) / 16;
+  static constexpr int all = u + p;
+  static constexpr int bytes = kPreStages * all * kThreads * 16;
+};
+
+template <class U, class P, bool ASYNC = false>
 __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_constant__ PostArgs a) {
   __shared__ float red[32];
+  extern __shared__ uint4 post_stage[];  // ASYNC only: [kPreStages][PostUnits::all][kThreads]
   const int ti = find_tensor(a.pk, blockIdx.x);
   const thorn_ortho_post_tensor& e = a.pk.t[ti];
   const bool vec = a.pk.vec[ti];
@@ -690,6 +699,27 @@ __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_const
   if (e.mat_stats != nullptr) {
     gscale = sqrtf(e.mat_stats[2 * t.b]) / fmaxf(sqrtf(e.mat_stats[2 * t.b + 1]), a.eps);
   }
+  using UN = PostUnits<U, P>;
+  const bool staged = ASYNC && vec && nc == 8;
+  // ASYNC: this thread's U and p chunks of its i-th row into stage i % kPreStages (one group per call)
+  auto issue = [&](int i) {
+    if constexpr (ASYNC) {
+      const int64_t r = t.r0 + warp + 8 * i;
+      if (staged && i < kTR / 8 && r < e.rows) {
+        const int64_t off = (t.b * e.rows + r) * e.cols + c;
+        uint4* st = post_stage + (size_t)(i % kPreStages) * UN::all * kThreads + threadIdx.x;
+        const char* us = reinterpret_cast<const char*>((const U*)e.U + off);
+        const char* ps = reinterpret_cast<const char*>((const P*)e.p + off);
+#pragma unroll
+        for (int q = 0; q < UN::u; ++q) cp_async16(st + q * kThreads, us + 16 * q);
+#pragma unroll
+        for (int q = 0; q < UN::p; ++q) cp_async16(st + (UN::u + q) * kThreads, ps + 16 * q);
+      }
+      cp_async_commit();
+    }
+  };
+#pragma unroll
+  for (int i = 0; i < kPreAhead; ++i) issue(i);
   float sq = 0.f;
   for (int rr = warp; rr < kTR; rr += 8) {
     const int64_t r = t.r0 + rr;
@@ -698,8 +728,19 @@ __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_const
     float scale = 1.f;
     if (e.row_scale != nullptr) scale = e.row_scale[t.b * e.rows + r] * gscale;
     float uv[8], pv[8];
-    load_n((const U*)e.U + off, uv, nc, vec);
-    load_n((const P*)e.p + off, pv, nc, vec);
+    if constexpr (ASYNC) {
+      const int i = rr >> 3;
+      issue(i + kPreAhead);
+      cp_async_wait<kPreAhead>();
+    }
+    if (staged) {
+      const uint4* st = post_stage + (size_t)((rr >> 3) % kPreStages) * UN::all * kThreads + threadIdx.x;
+      load8_units<U>(st, kThreads, uv);
+      load8_units<P>(st + UN::u * kThreads, kThreads, pv);
+    } else {
+      load_n((const U*)e.U + off, uv, nc, vec);
+      load_n((const P*)e.p + off, pv, nc, vec);
+    }
     if (e.round_u) rnd8<P>(uv);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
@@ -714,6 +755,7 @@ __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_const
       if (k < nc) sq += pv[k] * pv[k];
     store_n((P*)e.p + off, pv, nc, vec);
   }
+  if constexpr (ASYNC) cp_async_wait<0>();  // no copy into shared memory outlives the block
   if (e.p_normsq != nullptr) tile_sum_to(e.p_normsq, e.scratch, t, e.batch, e.rows, e.cols, sq, red);
 }
 
@@ -752,8 +794,9 @@ struct FinalArgs {
   Pack<thorn_md_final_tensor> pk;
 };
 
-template <class P>
+template <class P, bool ASYNC = false>
 __global__ void __launch_bounds__(kThreads) md_finalize_kernel(const __grid_constant__ FinalArgs a) {
+  extern __shared__ uint4 fin_stage[];  // ASYNC only: [kPreStages][p units][kThreads]
   const int ti = find_tensor(a.pk, blockIdx.x);
   const thorn_md_final_tensor& e = a.pk.t[ti];
   const bool vec = a.pk.vec[ti];
@@ -772,12 +815,33 @@ __global__ void __launch_bounds__(kThreads) md_finalize_kernel(const __grid_cons
   const bool split = !e.scalar_gain;
   float csp[8];
   if (split) load8f(e.col_sp + t.b * e.cols + c, csp, nc, vec);
+  constexpr int kPU = 8 * (int)sizeof(P) / 16;
+  const bool staged = ASYNC && vec && nc == 8;
+  auto issue = [&](int i) {
+    if constexpr (ASYNC) {
+      const int64_t r = t.r0 + warp + 8 * i;
+      if (staged && i < kTR / 8 && r < e.rows) {
+        const char* ps = reinterpret_cast<const char*>((const P*)e.p + (t.b * e.rows + r) * e.cols + c);
+        uint4* st = fin_stage + (size_t)(i % kPreStages) * kPU * kThreads + threadIdx.x;
+#pragma unroll
+        for (int q = 0; q < kPU; ++q) cp_async16(st + q * kThreads, ps + 16 * q);
+      }
+      cp_async_commit();
+    }
+  };
+#pragma unroll
+  for (int i = 0; i < kPreAhead; ++i) issue(i);
   for (int rr = warp; rr < kTR; rr += 8) {
     const int64_t r = t.r0 + rr;
     if (r >= e.rows) break;
     const int64_t off = (t.b * e.rows + r) * e.cols + c;
     float pv[8];
-    load_n((const P*)e.p + off, pv, nc, vec);
+    if constexpr (ASYNC) {
+      issue((rr >> 3) + kPreAhead);
+      cp_async_wait<kPreAhead>();
+    }
+    if (staged) load8_units<P>(fin_stage + (size_t)((rr >> 3) % kPreStages) * kPU * kThreads + threadIdx.x, kThreads, pv);
+    else load_n((const P*)e.p + off, pv, nc, vec);
     const float rsp = split ? e.row_sp[t.b * e.rows + r] : e.row_sp[0];
     if (renorm) {
 #pragma unroll
@@ -794,6 +858,7 @@ __global__ void __launch_bounds__(kThreads) md_finalize_kernel(const __grid_cons
     }
     store_n((P*)e.p + off, pv, nc, vec);
   }
+  if constexpr (ASYNC) cp_async_wait<0>();  // no copy into shared memory outlives the block
 }
 
 struct SumsqArgs {
@@ -1060,7 +1125,18 @@ extern "C" int thorn_ortho_post_multi(const thorn_ortho_post_tensor* ts, int n, 
       a.pk = pk;
       a.wd = weight_decay;
       a.eps = eps;
-      ortho_post_kernel<U, P><<<(unsigned)nb, kThreads, 0, st>>>(a);
+      if (g_async_pre.load() != 0) {
+        constexpr int smem = PostUnits<U, P>::bytes;
+        static std::once_flag once[64];
+        int dev = 0;
+        cudaGetDevice(&dev);
+        std::call_once(once[dev & 63], []() {
+          cudaFuncSetAttribute(ortho_post_kernel<U, P, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        });
+        ortho_post_kernel<U, P, true><<<(unsigned)nb, kThreads, smem, st>>>(a);
+      } else {
+        ortho_post_kernel<U, P><<<(unsigned)nb, kThreads, 0, st>>>(a);
+      }
     });
   });
   return d ? d : rc;
@@ -1123,7 +1199,18 @@ extern "C" int thorn_md_finalize_multi(const thorn_md_final_tensor* ts, int n, i
     rc = launch_packed(ts, n, blocks, vec, [&](const Pack<thorn_md_final_tensor>& pk, int64_t nb) {
       FinalArgs a;
       a.pk = pk;
-      md_finalize_kernel<P><<<(unsigned)nb, kThreads, 0, st>>>(a);
+      if (g_async_pre.load() != 0) {
+        constexpr int smem = kPreStages * (8 * (int)sizeof(P) / 16) * kThreads * 16;
+        static std::once_flag once[64];
+        int dev = 0;
+        cudaGetDevice(&dev);
+        std::call_once(once[dev & 63], []() {
+          cudaFuncSetAttribute(md_finalize_kernel<P, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        });
+        md_finalize_kernel<P, true><<<(unsigned)nb, kThreads, smem, st>>>(a);
+      } else {
+        md_finalize_kernel<P><<<(unsigned)nb, kThreads, 0, st>>>(a);
+      }
     });
   });
   return d ? d : rc;
