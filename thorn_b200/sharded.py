@@ -12,14 +12,22 @@ and scatters fp32 results back.  Here, per step:
 2. every rank normalises its rows by the global norm and casts them to the NS
    operand type, writing straight into the owner's NS input buffer when it is
    the owner, else into a send slab;
-3. one NCCL point-to-point exchange (world - 1 shifted pairwise rounds) moves
-   all slabs to their owners (half the bytes of the reference's fp32 gather);
+3. one NCCL point-to-point exchange (world - 1 shifted pairwise rounds, one
+   packed message per direction per round) moves all slabs to their owners
+   (half the bytes of the reference's fp32 gather);
 4. owners run batched Newton-Schulz (+ per-neuron-norm statistics with the
    row scale folded into one factor per row);
 5. one exchange of the same form returns the 16-bit result rows and the fp32
    row factors;
 6. every rank applies the update to its own rows (and, with decouple_md,
    all-reduces ||p||^2 for the renorm).
+
+Shards follow DTensor's ``torch.chunk`` split, so rows need not divide evenly
+(a split that leaves a shard empty is rejected).  With ``pipeline_exchange``
+steps 3-5 run in waves of NS batches so transfers overlap the owners' NS; with
+``exchange = "all_to_all"`` each exchange is one ``all_to_all_single``.  Magma
+masking all-reduces its three sums over the shard group first and leaves a
+masked matrix out of the step.
 
 Owners are chosen by longest-processing-time over the reference's NS FLOP
 estimate (thorn.py:1001-1007), deterministically on every rank.  Parameters of
