@@ -242,3 +242,39 @@ def test_sharded_step_matches_oracle(world, name, tmp_path):
                     if not e <= tol_k:
                         bad[(tag, gi, pi, k)] = e
     assert not bad, {k: f"{v:.3e}" for k, v in sorted(bad.items())[:10]}
+
+
+def _hsdp_worker(rank, world, port, result):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from torch.distributed.device_mesh import init_device_mesh
+        from torch.distributed.tensor import Replicate, Shard, distribute_tensor
+
+        from thorn_b200.sharded import shard_group
+        mesh = init_device_mesh("cpu", (2, 2), mesh_dim_names=("replicate", "shard"))
+        full = torch.arange(9 * 4, dtype=torch.float32).reshape(9, 4)
+        p = distribute_tensor(full, mesh, [Replicate(), Shard(0)])
+        ranks, group = shard_group(p, rank)
+        # the shard group is this rank's row of the mesh; an uneven split (5 + 4 rows)
+        parts = shard_rows(9, len(ranks))
+        me = ranks.index(rank)
+        local = p.to_local()
+        ok = ranks == [r for r in mesh.mesh.tolist() if rank in r][0]
+        ok &= local.shape[0] == parts[me][1] and torch.equal(local, full[parts[me][0]:parts[me][0] + parts[me][1]])
+        # a collective on the shard group reaches exactly the row's ranks
+        t = torch.tensor([float(rank)])
+        dist.all_reduce(t, group=group)
+        ok &= float(t) == float(sum(ranks))
+        result[rank] = bool(ok)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_hsdp_shard_groups_gloo():
+    """(Replicate, Shard(0)) meshes: each replica row is a shard group of its own (thorn.py:1015-1019)."""
+    ctx = mp.get_context("spawn")
+    result = ctx.Manager().dict()
+    mp.start_processes(_hsdp_worker, args=(4, _free_port(), result), nprocs=4, join=True, start_method="spawn")
+    assert dict(result) == {r: True for r in range(4)}
