@@ -231,3 +231,60 @@ def test_custom_ops_registered_with_fake_impls():
     with pytest.raises(RuntimeError, match="CUDA"):
         torch.ops.thorn_b200.sym_addmm(torch.zeros(64, 32, dtype=torch.float16),
                                        torch.zeros(32, 64, dtype=torch.float16), None, 1.0, 0.0)
+
+
+def test_pinned_stepper_data_flow_with_fake_streams(monkeypatch):
+    """Every line of PinnedStepper on CPU tensors, with CUDA streams and events replaced by
+    recording fakes: each step sees that step's host gradients, and after synchronize the
+    host parameter buffers hold the parameters of the last step."""
+    import contextlib
+
+    import thorn_b200.host_stepper as HS
+
+    log = []
+
+    class FakeEvent:
+        def record(self, stream=None):
+            log.append(("record", id(self)))
+
+    class FakeStream:
+        def wait_event(self, ev):
+            log.append(("wait", id(ev)))
+
+        def wait_stream(self, s):
+            pass
+
+        def synchronize(self):
+            log.append(("sync",))
+
+    compute = FakeStream()
+    monkeypatch.setattr(HS.torch.cuda, "Stream", lambda dev=None: FakeStream())
+    monkeypatch.setattr(HS.torch.cuda, "Event", lambda *a, **k: FakeEvent())
+    monkeypatch.setattr(HS.torch.cuda, "current_stream", lambda dev=None: compute)
+    monkeypatch.setattr(HS.torch.cuda, "stream", lambda s: contextlib.nullcontext())
+    monkeypatch.setattr(torch.Tensor, "is_pinned", lambda self: True)
+
+    params = [nn.Parameter(torch.zeros(3, 2)), nn.Parameter(torch.zeros(5))]
+
+    class AddGrad:  # stands in for THORN: p -= grad, grad consumed
+        def __init__(self):
+            self.seen = []
+
+        def step(self):
+            self.seen.append([p.grad.clone() for p in params])
+            for p in params:
+                p.data -= p.grad
+                p.grad = None
+
+    opt = AddGrad()
+    hg = [torch.zeros(3, 2), torch.zeros(5)]
+    hp = [torch.zeros(3, 2), torch.zeros(5)]
+    st = HS.PinnedStepper(opt, params, hg, hp)
+    for k in range(4):
+        for h in hg:
+            h.fill_(k + 1.0)
+        st.step()
+    st.synchronize()
+    assert [float(g[0].flatten()[0]) for g in opt.seen] == [1.0, 2.0, 3.0, 4.0]
+    assert torch.equal(hp[0], torch.full((3, 2), -10.0)) and torch.equal(hp[1], torch.full((5,), -10.0))
+    assert ("sync",) in log and any(e[0] == "wait" for e in log)
