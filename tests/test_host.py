@@ -288,3 +288,52 @@ def test_pinned_stepper_data_flow_with_fake_streams(monkeypatch):
     assert [float(g[0].flatten()[0]) for g in opt.seen] == [1.0, 2.0, 3.0, 4.0]
     assert torch.equal(hp[0], torch.full((3, 2), -10.0)) and torch.equal(hp[1], torch.full((5,), -10.0))
     assert ("sync",) in log and any(e[0] == "wait" for e in log)
+
+
+class _StubLib:
+    """Entry points of the C ABI that succeed without doing anything (host-logic tests only)."""
+
+    def thorn_ns_ld(self, n):
+        return (n + 7) // 8 * 8
+
+    def __getattr__(self, name):
+        if name.endswith("_bytes"):
+            return lambda *a: 256
+        return lambda *a: 0
+
+
+@pytest.mark.parametrize("magma", [False, True])
+def test_local_paths_run_through_stub_library(monkeypatch, magma):
+    """The Python control flow of the single-device paths (orthogonalized with and without MD,
+    (R)AdamW dense and row-sparse, Magma on and off) runs end to end against a stub library:
+    every launch record gets built and every entry point is called with an int status."""
+    from thorn_b200 import _native as N
+
+    monkeypatch.setattr(N, "load", lambda build_if_missing=False: _StubLib())
+    monkeypatch.setattr(N, "stream_of", lambda dev: 0)
+    torch.manual_seed(0)
+    w = nn.Parameter(torch.randn(24, 16) * 0.02)
+    t = nn.Parameter(torch.randn(32, 16) * 0.02)
+    v = nn.Parameter(torch.randn(16))
+    e = nn.Parameter(torch.randn(10, 4))
+    opt = THORN([{"orthogonalize": True, "params": [w], "lr": 1e-3, "momentum_align": magma},
+                 {"orthogonalize": True, "params": [t], "lr": 1e-3, "decouple_md": True, "momentum_align": magma},
+                 {"orthogonalize": False, "params": [v, e], "lr": 1e-3, "momentum_align": magma}])
+    for step in range(3):
+        for p in (w, t, v):
+            p.grad = torch.randn_like(p) * 1e-3
+        e.grad = torch.sparse_coo_tensor(torch.tensor([[1, 4, 4]]), torch.randn(3, 4), (10, 4))
+        for gi, grp in enumerate(opt.param_groups):
+            cfg = GroupConfig.from_kwargs(**grp)
+            ps = [p for p in grp["params"] if p.grad is not None]
+            for p in ps:
+                if "step" not in opt.state[p]:
+                    opt._init_state(p, opt.state[p], cfg, grp)
+            if cfg.orthogonalize:
+                opt._ortho_local(ps, cfg)
+            else:
+                opt._adam_local(ps, cfg)
+    for p in (w, t, v, e):
+        assert opt.state[p]["step"] == 4 and p.grad is None
+        if magma:
+            assert "random_state" in opt.state[p] and opt.state[p]["s"].ndim == 0
