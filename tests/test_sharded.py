@@ -278,3 +278,72 @@ def test_hsdp_shard_groups_gloo():
     result = ctx.Manager().dict()
     mp.start_processes(_hsdp_worker, args=(4, _free_port(), result), nprocs=4, join=True, start_method="spawn")
     assert dict(result) == {r: True for r in range(4)}
+
+
+class _StubLib:
+    def thorn_ns_ld(self, n):
+        return (n + 7) // 8 * 8
+
+    def __getattr__(self, name):
+        if name.endswith("_bytes"):
+            return lambda *a: 256
+        return lambda *a: 0
+
+
+def _sharded_flow_worker(rank, world, port, result, exchange_impl, pipeline):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from torch.distributed.device_mesh import init_device_mesh
+        from torch.distributed.tensor import Shard, distribute_tensor
+
+        from thorn_b200 import THORN, _native as N
+        from thorn_b200 import sharded as S
+        from thorn_b200.optimizer import GroupConfig, _Arena, _local
+
+        N.load = lambda build_if_missing=False: _StubLib()
+        N.stream_of = lambda dev: 0
+        mesh = init_device_mesh("cpu", (world,))
+        torch.manual_seed(0)
+        shapes = [(24, 16), (13, 8), (40, 24), (33, 16), (12, 32)]
+        ps = [torch.nn.Parameter(distribute_tensor(torch.randn(s) * 0.02, mesh, [Shard(0)])) for s in shapes]
+        opt = THORN([{"orthogonalize": True, "params": ps, "lr": 1e-3, "decouple_md": True,
+                      "momentum_align": True}])
+        opt.exchange, opt.pipeline_exchange, opt.polar_decomp_batch_size = exchange_impl, pipeline, 300
+        cfg = GroupConfig.from_kwargs(**opt.param_groups[0])
+        ranks, group = S.shard_group(ps[0], rank)
+        for step in range(2):
+            for p, s in zip(ps, shapes):
+                p.grad = distribute_tensor(torch.randn(s) * 1e-3, mesh, [Shard(0)])
+            for p in ps:
+                if "step" not in opt.state[p]:
+                    opt._init_state(p, opt.state[p], cfg, opt.param_groups[0])
+            from thorn_b200.optimizer import _Item
+            recs = []
+            for p in ps:
+                it = _Item()
+                it.g, it.state, it.split, it.apply = _local(p.grad), opt.state[p], True, True
+                recs.append(it)
+            opt._magma(recs, cfg, recovered=True, group=group)
+            S._step_matrices(opt, ps, cfg, ranks, group, world, ranks.index(rank), torch.device("cpu"), _Arena,
+                             _local, [it.scale for it in recs])
+        # every rank drew or received the same generator state for each matrix
+        states = [int(opt.state[p]["random_state"]) for p in ps]
+        box = [None] * world
+        dist.all_gather_object(box, states)
+        result[rank] = all(b == states for b in box) and all(opt.state[p]["step"] == 3 for p in ps)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,impl,pipeline", [(2, "rounds", False), (3, "rounds", True), (3, "all_to_all", True)])
+def test_sharded_host_flow_gloo(world, impl, pipeline):
+    """The sharded step's host flow on gloo with a stub C ABI: owner planning, uneven
+    splits, real slab exchanges (pairwise rounds or all-to-all, one wave or pipelined
+    waves), Magma statistics all-reduced over the shard group with a shared seed."""
+    ctx = mp.get_context("spawn")
+    result = ctx.Manager().dict()
+    mp.start_processes(_sharded_flow_worker, args=(world, _free_port(), result, impl, pipeline), nprocs=world,
+                       join=True, start_method="spawn")
+    assert dict(result) == {r: True for r in range(world)}
