@@ -311,6 +311,15 @@ def test_local_paths_run_through_stub_library(monkeypatch, magma):
 
     monkeypatch.setattr(N, "load", lambda build_if_missing=False: _StubLib())
     monkeypatch.setattr(N, "stream_of", lambda dev: 0)
+
+    class _Ev:  # the profiling hooks' events
+        def __init__(self, **kw):
+            pass
+
+        def record(self, *a):
+            pass
+
+    monkeypatch.setattr(torch.cuda, "Event", _Ev)
     torch.manual_seed(0)
     w = nn.Parameter(torch.randn(24, 16) * 0.02)
     t = nn.Parameter(torch.randn(32, 16) * 0.02)
@@ -319,6 +328,7 @@ def test_local_paths_run_through_stub_library(monkeypatch, magma):
     opt = THORN([{"orthogonalize": True, "params": [w], "lr": 1e-3, "momentum_align": magma},
                  {"orthogonalize": True, "params": [t], "lr": 1e-3, "decouple_md": True, "momentum_align": magma},
                  {"orthogonalize": False, "params": [v, e], "lr": 1e-3, "momentum_align": magma}])
+    opt.profile_momentum = []
     for step in range(3):
         for p in (w, t, v):
             p.grad = torch.randn_like(p) * 1e-3
@@ -333,6 +343,9 @@ def test_local_paths_run_through_stub_library(monkeypatch, magma):
                 opt._ortho_local(ps, cfg)
             else:
                 opt._adam_local(ps, cfg)
+    # momentum-pass profile: one record per orthogonalized group and step, compulsory bytes
+    # g + 2 m (+ 2 p under MD), all fp32 here
+    assert [nb for _, _, nb in opt.profile_momentum] == [24 * 16 * 12, 32 * 16 * 20] * 3
     for p in (w, t, v, e):
         assert opt.state[p]["step"] == 4 and p.grad is None
         if magma:
