@@ -121,6 +121,37 @@ def test_step_matches_oracle(name):
     print(name, {k: f"{v:.2e}" for k, v in sorted(worst.items())})
 
 
+def _magma_seeds(name, gpu):
+    """The Magma seeds the GPU run drew, in initialisation order: each parameter's
+    generator state after step 1 stepped back once (every Magma parameter of
+    these cases runs the generator once in step 1)."""
+    from oracle.thorn_oracle import MASK64, W1_C
+
+    seeds = []
+    _, states = gpu["step1"]
+    for gi, grp in enumerate(C.CASES[name]["groups"]):
+        if grp["opts"].get("momentum_align"):
+            for st in states[gi]:
+                seeds.append((int(st["random_state"]) - W1_C) & MASK64)
+    return seeds
+
+
+@pytest.mark.parametrize("name", ["magma_small", "sparse_small"])
+def test_magma_and_sparse_rows_match_oracle(name):
+    """Magma masking (both group kinds, with and without MD) and row-sparse (R)AdamW
+    gradients (duplicate rows, 1-D rows, an empty gradient) against the oracle, which
+    is pinned to the reference's own runs of these cases; the oracle replays the GPU
+    run's Magma seeds."""
+    _, gpu = run_gpu(name)
+    _, orc = P.run_oracle(name, seeds=_magma_seeds(name, gpu))
+    init = [[t.float().numpy() for t in g] for g in C.build_params(C.CASES[name])]
+    bad, worst = compare(name, gpu, orc, init)
+    assert not bad, {k: f"{v:.3e}" for k, v in sorted(bad.items())[:10]}
+    print(name, {k: f"{v:.2e}" for k, v in sorted(worst.items())})
+
+
+
+
 def test_bf16_params_with_fp32_state():
     _, gpu = run_gpu("bf16_small", state_dtype="f32")
     _, orc = P.run_oracle("bf16_small", state_dtype="f32")
