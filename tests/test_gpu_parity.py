@@ -499,3 +499,25 @@ def test_full_size_state_updates():
         assert torch.equal(opt.state[w]["moment"], m_w)
         assert C.rel_fro(opt.state[e]["moment"].cpu().numpy(), m_e.cpu().numpy()) <= 1e-6
         assert C.rel_fro(opt.state[e]["variance"].cpu().numpy(), v_e.cpu().numpy()) <= 1e-6
+
+
+def test_custom_ops_match_c_abi():
+    """torch.ops.thorn_b200.sym_addmm (the thorn::sym_addmm contract, thorn.py:298-368) against
+    an fp32 product, and torch.ops.thorn_b200.polar_decomp against the C ABI it wraps."""
+    import thorn_b200  # noqa: F401  (registers the operators)
+    from thorn_b200.coeffs import gram_ns_restarts, optimal_composition
+
+    torch.manual_seed(4)
+    A = (torch.randn(3, 256, 128, device="cuda") / 16).half()
+    Cs = torch.randn(256, 256, device="cuda").half()
+    Cs = (Cs + Cs.T) / 2
+    out = torch.ops.thorn_b200.sym_addmm(A, A.transpose(1, 2), Cs, 0.5, -1.0)
+    want = 0.5 * (A.float() @ A.float().transpose(1, 2)) - Cs.float()
+    assert (out.float() - want).abs().max() <= 2e-2 * want.abs().max()
+    assert torch.equal(out, out.transpose(1, 2))
+    u = torch.randn(2, 384, 128, device="cuda") * 1e-3
+    co = optimal_composition(1e-3, 5, 0.03, 0.02)
+    rs = gram_ns_restarts(*co)
+    got = torch.ops.thorn_b200.polar_decomp(u, [x for t in co for x in t], list(rs))
+    ref, _, _ = _ns_gpu_t(u)
+    assert got.dtype == u.dtype and torch.equal(got, ref.float())
