@@ -212,15 +212,8 @@ def _run_workers(n, name, tmp_path, extra=()):
         return {k: z[k] for k in z.files}
 
 
-@pytest.mark.gpu
-@pytest.mark.parametrize("world", [1, 2])
-@pytest.mark.parametrize("name", ["tiny", "md_shard", "shard_uneven"])
-def test_sharded_step_matches_oracle(world, name, tmp_path):
-    if torch.cuda.device_count() < world:
-        pytest.skip(f"needs {world} GPUs")
-    got = _run_workers(world, name, tmp_path)
-    _, orc = P.run_oracle(name)
-    init = [[t.float().numpy() for t in g] for g in C.build_params(C.CASES[name])]
+def _sharded_compare(got, orc, name, init):
+    """Per (tag, group, param, key) errors above tolerance of a sharded run against the oracle."""
     bad = {}
     for tag, (params, states) in orc.items():
         for gi, ps in enumerate(params):
@@ -232,8 +225,8 @@ def test_sharded_step_matches_oracle(world, name, tmp_path):
                 if not e <= tol:
                     bad[(tag, gi, pi, "param")] = e
                 for k, v in states[gi][pi].items():
-                    if k == "step":
-                        assert int(got[f"{tag}/g{gi}/p{pi}/{k}"]) == v
+                    if k in ("step", "random_state"):  # integers: exact
+                        assert int(got[f"{tag}/g{gi}/p{pi}/{k}"]) == int(v), (tag, gi, pi, k)
                         continue
                     ref = np.asarray(v, dtype=np.float32)
                     mine = got[f"{tag}/g{gi}/p{pi}/{k}"].reshape(ref.shape)
@@ -241,6 +234,33 @@ def test_sharded_step_matches_oracle(world, name, tmp_path):
                     e = C.rel_fro(mine, ref)
                     if not e <= tol_k:
                         bad[(tag, gi, pi, k)] = e
+    return bad
+
+
+PIPE = ("--pipeline-exchange",)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [1, 2])
+@pytest.mark.parametrize("name,extra", [("tiny", ()), ("md_shard", ()), ("shard_uneven", ()),
+                                        ("shard_uneven", PIPE), ("md_shard", PIPE),
+                                        ("magma_shard", ()), ("magma_shard", PIPE)])
+def test_sharded_step_matches_oracle(world, name, extra, tmp_path):
+    """The Shard(0) path (rounds or waves of the exchange, Magma masking whole matrices)
+    against the oracle's sharded semantics; the oracle replays the run's Magma seeds."""
+    from oracle.thorn_oracle import MASK64, W1_C
+
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    got = _run_workers(world, name, tmp_path, extra)
+    seeds = []
+    for gi, grp in enumerate(C.CASES[name]["groups"]):
+        if grp["opts"].get("momentum_align"):
+            for pi in range(len(grp["shapes"])):
+                seeds.append((int(got[f"step1/g{gi}/p{pi}/random_state"]) - W1_C) & MASK64)
+    _, orc = P.run_oracle(name, seeds=seeds or None, sharded=True)
+    init = [[t.float().numpy() for t in g] for g in C.build_params(C.CASES[name])]
+    bad = _sharded_compare(got, orc, name, init)
     assert not bad, {k: f"{v:.3e}" for k, v in sorted(bad.items())[:10]}
 
 
