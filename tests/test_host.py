@@ -350,3 +350,29 @@ def test_local_paths_run_through_stub_library(monkeypatch, magma):
         assert opt.state[p]["step"] == 4 and p.grad is None
         if magma:
             assert "random_state" in opt.state[p] and opt.state[p]["s"].ndim == 0
+
+
+@pytest.mark.parametrize("name", ["tiny_small", "md_small", "bf16_small", "conv_small", "variants_small", "vad",
+                                  "tiny", "magma_small", "sparse_small", "shard_uneven", "magma_shard"])
+def test_state_keys_and_shapes_match_reference_goldens(name, golden_dir):
+    """Checkpoint compatibility: the state THORN initialises for every parameter of a case has
+    exactly the keys, and the shapes, of the reference's own state after its first step (as the
+    golden fixtures recorded it, thorn.py:1591-1633)."""
+    import cases as C
+
+    gold = P.load_golden(os.path.join(golden_dir, f"{name}.npz"))
+    case = C.CASES[name]
+    params = [[nn.Parameter(t.clone()) for t in ps] for ps in C.build_params(case)]
+    opt = THORN(C.group_dicts(case, params))
+    for gi, (grp, ps, gs) in enumerate(zip(opt.param_groups, params, C.build_grads(case, 0))):
+        cfg = GroupConfig.from_kwargs(**grp)
+        for pi, (p, g) in enumerate(zip(ps, gs)):
+            p.grad = g
+            opt._init_state(p, opt.state[p], cfg, grp)
+            base = f"step1/g{gi}/p{pi}/"
+            want = {k[len(base):].split("/")[0] for k in gold if k.startswith(base)} - {"param"}
+            st = opt.state[p]
+            assert set(st) == want, (gi, pi, sorted(set(st) ^ want))
+            for k, v in st.items():
+                if isinstance(v, torch.Tensor):
+                    assert tuple(v.shape) == tuple(gold[f"{base}{k}/shape"]), (gi, pi, k)
