@@ -114,6 +114,17 @@ CASES = {
         dict(orthogonalize=False, shapes=[(48, 16)], init=("normal", 0.5), dtype="f32",
              opts=dict(lr=1e-3, decouple_md=True, momentum_align=True)),
     ]),
+    # Edge inputs: all-zero gradients on tall matrices (zero Frobenius norm, so the NS input is
+    # 0 / (0 + 1e-8), and per-neuron norm of a zero update; zero AdamW moments), a one-row
+    # matrix, a tall matrix with an odd column count, MD on a matrix whose gradient is zero.
+    "edge_small": dict(steps=3, grad_std=1e-3, groups=[
+        dict(orthogonalize=True, shapes=[(96, 64), (1, 64), (130, 37), (40, 40)], init=("normal", 0.02),
+             dtype="f32", opts=dict(lr=2e-3, weight_decay=0.1), zero=[0]),
+        dict(orthogonalize=True, shapes=[(72, 24), (80, 48)], init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=8e-3, decouple_md=True), zero=[1]),
+        dict(orthogonalize=False, shapes=[(64,), (33,)], init=("normal", 0.5), dtype="f32",
+             opts=dict(lr=1e-3, weight_decay=0.1), zero=[0]),
+    ]),
     # Magma on the FSDP2 path (world 1 and 2): orthogonalized matrices, even and uneven splits,
     # with and without MD, next to a Magma (R)AdamW vector group.
     "magma_shard": dict(steps=6, grad_std=1e-3, groups=[
@@ -159,7 +170,8 @@ def build_grads(case: dict, s: int):
     Parameters listed in a group's ``sparse`` map get a torch sparse COO
     gradient with one sparse dimension: ``nnz`` row indices drawn with
     replacement (so rows repeat) and one value row each; ``sparse_empty`` lists
-    steps at which such a gradient has no rows at all."""
+    steps at which such a gradient has no rows at all.  Parameters listed in
+    ``zero`` get an all-zero gradient at every step."""
     torch.manual_seed(1000 + s)
     out = []
     for grp in case["groups"]:
@@ -167,7 +179,9 @@ def build_grads(case: dict, s: int):
         sparse, empty = grp.get("sparse", {}), grp.get("sparse_empty", {})
         gs = []
         for pi, shp in enumerate(grp["shapes"]):
-            if pi in sparse:
+            if pi in grp.get("zero", ()):
+                gs.append(torch.zeros(shp, dtype=dt))
+            elif pi in sparse:
                 nnz = 0 if s in empty.get(pi, ()) else sparse[pi]
                 idx = torch.randint(0, shp[0], (nnz,))
                 vals = (torch.randn((nnz, *shp[1:])) * case["grad_std"]).to(dt)

@@ -108,7 +108,7 @@ def compare(name, gpu, orc, init):
     return bad, worst
 
 
-CASES = ["tiny_small", "md_small", "bf16_small", "conv_small", "variants_small", "vad", "tiny"]
+CASES = ["tiny_small", "md_small", "bf16_small", "conv_small", "variants_small", "edge_small", "vad", "tiny"]
 
 
 @pytest.mark.parametrize("name", CASES)
