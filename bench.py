@@ -388,6 +388,7 @@ def gpu_arm(args, rank, world, local_rank):
             torch.cuda.empty_cache()
     if not args.no_e2e and args.e2e_mode == "pipelined" and e2e_note is None:
         for _ in range(2):
+            stepper.wait_host_grads()
             stepper.step()
         stepper.synchronize()
         barrier()
@@ -397,6 +398,9 @@ def gpu_arm(args, rank, world, local_rank):
         t0.record()
         stepper.h2d.wait_stream(torch.cuda.current_stream())  # no copy starts before t0
         for _ in range(args.steps):
+            # the documented loop: the host may rewrite its gradient buffers only after
+            # the previous step's copy has read them (the buffers stay as they are here)
+            stepper.wait_host_grads()
             stepper.step()
         stepper.wait_on()
         t1.record()

@@ -247,6 +247,9 @@ def test_pinned_stepper_data_flow_with_fake_streams(monkeypatch):
         def record(self, stream=None):
             log.append(("record", id(self)))
 
+        def synchronize(self):
+            log.append(("event_sync", id(self)))
+
     class FakeStream:
         def wait_event(self, ev):
             log.append(("wait", id(ev)))
@@ -281,11 +284,14 @@ def test_pinned_stepper_data_flow_with_fake_streams(monkeypatch):
     hp = [torch.zeros(3, 2), torch.zeros(5)]
     st = HS.PinnedStepper(opt, params, hg, hp)
     for k in range(4):
+        st.wait_host_grads()  # the previous step's gradient copy has read the host buffers
         for h in hg:
             h.fill_(k + 1.0)
         st.step()
     st.synchronize()
     assert [float(g[0].flatten()[0]) for g in opt.seen] == [1.0, 2.0, 3.0, 4.0]
+    # wait_host_grads blocks on the event of the slot the last step loaded (none before step 1)
+    assert [e[1] for e in log if e[0] == "event_sync"] == [id(st.loaded[0]), id(st.loaded[1]), id(st.loaded[0])]
     assert torch.equal(hp[0], torch.full((3, 2), -10.0)) and torch.equal(hp[1], torch.full((5,), -10.0))
     assert ("sync",) in log and any(e[0] == "wait" for e in log)
 

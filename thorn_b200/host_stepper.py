@@ -12,11 +12,13 @@ with the optimizer's own work on two copy streams:
 * after step k the updated parameters are snapshotted device -> device (HBM speed)
   and the snapshot is copied device -> host while step k + 1 runs.
 
-Every dependency is a CUDA event; the host blocks only in :meth:`synchronize`.  Host
-buffers must be pinned (``torch.empty(..., pin_memory=True)``) and hold the local
-shard of every parameter (its ``to_local()`` for a DTensor).  The host gradients of a
-step must be written before :meth:`step` is called for it, and the host parameter
-buffers hold the values of step k once a later :meth:`synchronize` returns.
+Every dependency is a CUDA event; the host blocks only in :meth:`wait_host_grads` and
+:meth:`synchronize`.  Host buffers must be pinned (``torch.empty(..., pin_memory=True)``)
+and hold the local shard of every parameter (its ``to_local()`` for a DTensor).  The
+host gradients of a step must be written before :meth:`step` is called for it, and not
+rewritten until :meth:`wait_host_grads` has returned: the copy that :meth:`step`
+enqueues reads them asynchronously.  The host parameter buffers hold the values of
+step k once a later :meth:`synchronize` returns.
 """
 from __future__ import annotations
 
@@ -87,6 +89,13 @@ class PinnedStepper:
             drained.record(self.d2h)
         self.drained = drained
         self.k += 1
+
+    def wait_host_grads(self):
+        """Block until the host gradients handed to the last :meth:`step` have been
+        copied to the device, so the caller may write the next step's gradients.  The
+        GPU keeps computing meanwhile."""
+        if self.k:
+            self.loaded[(self.k - 1) & 1].synchronize()
 
     def wait_on(self, stream=None):
         """Make ``stream`` (default: the current one) wait until every enqueued
