@@ -195,7 +195,9 @@ def build_params(torch, dev, rank, world, mesh, layers=LAYERS):
             t = torch.randn(shape, device=dev, dtype=torch.bfloat16, generator=gen) * std
             return t
         from torch.distributed.tensor import DTensor, Shard
-        local = (shape[0] // world,) + tuple(shape[1:])
+
+        from thorn_b200.sharded import shard_rows
+        local = (shard_rows(shape[0], world)[rank][1],) + tuple(shape[1:])  # DTensor's torch.chunk split
         t = torch.randn(local, device=dev, dtype=torch.bfloat16, generator=gen) * std
         return DTensor.from_local(t, mesh, [Shard(0)], run_check=False, shape=shape,
                                   stride=torch.empty(shape, device="meta").stride())
