@@ -137,3 +137,45 @@ def test_kernel_switches(lib, name, default):
     assert fn(default) == 1 - default
     assert fn(7 if default else 0) == default  # any nonzero value means on
     fn(default)
+
+
+def _ctype_of(decl: str):
+    """The ctypes type that binds one C parameter or return type of the header."""
+    d = " ".join(decl.replace("const ", "").split())
+    d = re.sub(r"\s*\*\s*", "*", d)
+    base = d.split()[0] if " " in d and "*" not in d.split()[0] else d
+    if d in ("void", ""):
+        return None
+    if d.endswith("*"):
+        t = d.rstrip("*").split()[0]
+        if d == "char*":
+            return ctypes.c_char_p
+        return {"double": ctypes.POINTER(ctypes.c_double), "int32_t": ctypes.POINTER(ctypes.c_int32)}.get(
+            t, "struct" if t.startswith("thorn_") else ctypes.c_void_p)
+    return {"int": ctypes.c_int, "int64_t": ctypes.c_int64, "uint64_t": ctypes.c_uint64, "float": ctypes.c_float,
+            "double": ctypes.c_double}[base.split()[0]]
+
+
+def test_ctypes_prototypes_match_header():
+    """Every function the ctypes layer binds has, in _native._PROTOS, exactly the parameter
+    count and C types (and return type) the header declares: a mismatch would hand a kernel
+    shifted arguments."""
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    protos = {}
+    for m in re.finditer(r"THORN_API\s+([\w\s\*]+?)\b(thorn_\w+)\s*\(([^)]*)\)\s*;", text):
+        ret, name, args = m.group(1).strip(), m.group(2), m.group(3).strip()
+        params = [] if args in ("", "void") else [re.sub(r"\b\w+$", "", a.strip()).strip() for a in args.split(",")]
+        protos[name] = (ret, params)
+    for name, (res, argtypes) in N._PROTOS.items():
+        ret, params = protos[name]
+        assert len(params) == len(argtypes), (name, params, argtypes)
+        want_ret = _ctype_of(ret)
+        assert res == want_ret, (name, ret, res)
+        for i, (cdecl, got) in enumerate(zip(params, argtypes)):
+            want = _ctype_of(cdecl)
+            if want == "struct":  # an array of launch records: POINTER(<matching Structure>)
+                assert hasattr(got, "_type_") and issubclass(got._type_, ctypes.Structure), (name, i, cdecl, got)
+                cname = cdecl.replace("const", "").replace("*", "").strip()
+                assert got._type_ is STRUCTS[cname][0], (name, i, cname, got._type_)
+            else:
+                assert got == want, (name, i, cdecl, got, want)
