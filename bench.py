@@ -554,6 +554,16 @@ def ns_only(args):
         N.check(lib.thorn_ns_batched(X.data_ptr(), U.data_ptr(), ws.data_ptr(), wsb, B, R, C, N.F16, cc, 5, rr,
                                      len(rs), err.data_ptr(), st), "ns_batched")
 
+    if args.ns_library:
+        # the same recurrences with every product a dense cuBLAS GEMM (torch.bmm / baddbmm),
+        # for a library baseline on the same box: no symmetry, no fused epilogues
+        Xw = X[:, :, :C] if R <= C else X[:, :, :C].mT  # wide orientation, m = min(R, C)
+        Xw = Xw.contiguous()
+        lib_out = {}
+
+        def run():  # noqa: F811  (replaces the thorn_b200 call)
+            lib_out["U"] = ns_library(Xw, co, rs)
+
     for _ in range(args.warmup):
         run()
     torch.cuda.synchronize()
@@ -567,9 +577,46 @@ def ns_only(args):
     d1, x1 = N.gemm_flops()
     ms = e0.elapsed_time(e1) / args.steps
     dense = B * dense_ns_flops(R, C)
-    print(json.dumps({"ns_only": f"{B}x{R}x{C}", "ms": round(ms, 4), "dense_tflops": round(dense / ms / 1e9, 1),
-                      "executed_tflops": round((x1 - x0) / args.steps / ms / 1e9, 1), "err_flag": int(err.item()),
-                      "finite": bool(torch.isfinite(U).all())}), flush=True)
+    line = {"ns_only": f"{B}x{R}x{C}", "ms": round(ms, 4), "dense_tflops": round(dense / ms / 1e9, 1),
+            "executed_tflops": round((x1 - x0) / args.steps / ms / 1e9, 1), "err_flag": int(err.item()),
+            "finite": bool(torch.isfinite(U).all())}
+    if args.ns_library:
+        Ul = lib_out["U"] if R <= C else lib_out["U"].mT
+        N.check(lib.thorn_ns_batched(X.data_ptr(), U.data_ptr(), ws.data_ptr(), wsb, B, R, C, N.F16, cc, 5, rr,
+                                     len(rs), err.data_ptr(), st), "ns_batched")
+        line.update(impl="torch.bmm/baddbmm (cuBLAS), dense", executed_tflops=line["dense_tflops"],
+                    finite=bool(torch.isfinite(Ul).all()),
+                    rel_fro_vs_thorn_b200=round(float((Ul.float() - U.float()).norm() / U.float().norm()), 6))
+    print(json.dumps(line), flush=True)
+
+
+def ns_library(X, coeffs, restarts):
+    """Newton-Schulz of a batch of wide (m <= n) fp16 matrices with the recurrences of
+    thorn_ns_batched (thorn.py:626-662), every product a torch GEMM."""
+    import torch
+
+    B_, m, n = X.shape
+    if m == n:
+        for a, b, c in coeffs:
+            A = torch.bmm(X, X.mT)
+            Bm = torch.baddbmm(A, A, A, beta=b, alpha=c)
+            X = torch.baddbmm(X, Bm, X, beta=a)
+        return X
+    eye = torch.eye(m, dtype=X.dtype, device=X.device)
+    R = torch.bmm(X, X.mT)
+    Q = None
+    iters = len(coeffs)
+    for i, (a, b, c) in enumerate(coeffs):
+        rs = i in restarts
+        if rs and i != 0:
+            X = torch.bmm(Q, X)
+            R = torch.bmm(X, X.mT)
+        Z = torch.baddbmm(R, R, R, beta=b, alpha=c)
+        Q = Z + a * eye if (Q is None or rs) else torch.baddbmm(Q, Q, Z, beta=a)
+        if i < iters - 1 and (i + 1) not in restarts:
+            RZ = torch.baddbmm(R, R, Z, beta=a)
+            R = torch.baddbmm(RZ, Z, RZ, beta=a)
+    return torch.bmm(Q, X)
 
 
 def ortho_only(args):
@@ -632,6 +679,8 @@ def main():
                          "falling back to serial if it cannot run; serial: copy in, step, copy out on one stream")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ns-only", default=None, help="BxRxC: time thorn_ns_batched alone on this batch (profiling)")
+    ap.add_argument("--ns-library", action="store_true",
+                    help="with --ns-only: time the same recurrences on torch/cuBLAS GEMMs instead (library baseline)")
     ap.add_argument("--layers", type=int, default=LAYERS, help="transformer layers (profiling runs use fewer)")
     ap.add_argument("--ortho-only", default=None,
                     help="BxRxC: time steps of one decouple_md group of B bf16 RxC matrices (profiling)")
