@@ -383,3 +383,24 @@ def test_state_keys_and_shapes_match_reference_goldens(name, golden_dir):
             for k, v in st.items():
                 if isinstance(v, torch.Tensor):
                     assert tuple(v.shape) == tuple(gold[f"{base}{k}/shape"]), (gi, pi, k)
+
+
+@pytest.mark.parametrize("shape", [(2, 48, 48), (2, 40, 130)])
+def test_ns_recurrences_equal_composed_polynomial(shape):
+    """The Newton-Schulz recurrences that thorn_ns_batched runs (restated on torch GEMMs as
+    bench.py's library baseline): square quintic and Gram NS with its restart, in float64,
+    equal the composed Polar-Express polynomial applied to the singular values
+    (thorn.py:626-662)."""
+    from bench import ns_library
+
+    co = optimal_composition(1e-3, 5, 0.03, 0.02)
+    rs = gram_ns_restarts(*co)
+    torch.manual_seed(1)
+    X = torch.randn(*shape, dtype=torch.float64)
+    X = X / X.norm(dim=(-2, -1), keepdim=True)
+    u, s, vh = torch.linalg.svd(X, full_matrices=False)
+    for a, b, c in co:
+        s = a * s + b * s ** 3 + c * s ** 5
+    want = u @ torch.diag_embed(s) @ vh
+    got = ns_library(X, co, rs)
+    assert float((got - want).norm() / want.norm()) < 1e-12
