@@ -367,3 +367,61 @@ def test_sharded_host_flow_gloo(world, impl, pipeline):
     mp.start_processes(_sharded_flow_worker, args=(world, _free_port(), result, impl, pipeline), nprocs=world,
                        join=True, start_method="spawn")
     assert dict(result) == {r: True for r in range(world)}
+
+
+def _rank_loss_worker(rank, world, port, result):
+    import datetime
+    import time
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    from torch.distributed.device_mesh import init_device_mesh
+    from torch.distributed.tensor import Shard, distribute_tensor
+
+    from thorn_b200 import THORN, _native as N
+    from thorn_b200 import sharded as S
+    from thorn_b200.optimizer import GroupConfig, _Arena, _local
+
+    N.load = lambda build_if_missing=False: _StubLib()
+    N.stream_of = lambda dev: 0
+    mesh = init_device_mesh("cpu", (world,))
+    torch.manual_seed(0)
+    shapes = [(24, 16), (13, 8), (40, 24)]
+    ps = [torch.nn.Parameter(distribute_tensor(torch.randn(s) * 0.02, mesh, [Shard(0)])) for s in shapes]
+    opt = THORN([{"orthogonalize": True, "params": ps, "lr": 1e-3}])
+    cfg = GroupConfig.from_kwargs(**opt.param_groups[0])
+    ranks, group = S.shard_group(ps[0], rank)
+
+    def step():
+        for p, s in zip(ps, shapes):
+            p.grad = distribute_tensor(torch.randn(s) * 1e-3, mesh, [Shard(0)])
+            if "step" not in opt.state[p]:
+                opt._init_state(p, opt.state[p], cfg, opt.param_groups[0])
+        S._step_matrices(opt, ps, cfg, ranks, group, world, ranks.index(rank), torch.device("cpu"), _Arena, _local,
+                         [1.0] * len(ps))
+
+    step()
+    if rank == world - 1:  # leaves between steps, with nothing in flight
+        result[rank] = "left"
+        os._exit(0)
+    t0 = time.time()
+    try:
+        step()
+        result[rank] = "no error"
+    except Exception as exc:  # the lost peer surfaces as an error, not a hang
+        result[rank] = (type(exc).__name__, round(time.time() - t0, 1))
+    os._exit(0)
+
+
+def test_lost_rank_fails_the_next_step_gloo():
+    """Failure detection on the host: a rank that leaves between steps makes the remaining
+    rank's next sharded step raise (its first collective on the shard group fails) within the
+    process group's timeout, instead of waiting for good."""
+    ctx = mp.get_context("spawn")
+    result = ctx.Manager().dict()
+    mp.start_processes(_rank_loss_worker, args=(2, _free_port(), result), nprocs=2, join=True,
+                       start_method="spawn")
+    assert result[1] == "left"
+    assert isinstance(result[0], tuple), result[0]
+    assert result[0][1] < 30, result[0]
