@@ -110,7 +110,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
       if (abort && *abort) return false;
       if (global_ns() - t0 > kTimeoutNs) {
         if (err) atomicExch(err, 1);
-        *abort = 1;
+        if (abort) *abort = 1;
         return false;
       }
     }
