@@ -99,6 +99,17 @@ __device__ __forceinline__ uint64_t global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+// Abort path only: TMA loads and MMAs that this CTA issued before its roles gave
+// up may still be in flight.  They complete within microseconds, so every thread
+// lets 1 ms of global time pass before the CTA's final synchronisation, TMEM
+// release and exit.
+constexpr uint64_t kSettleNs = 1000ull * 1000;
+__device__ __forceinline__ void abort_settle(volatile int* abort) {
+  if (!*abort) return;
+  const uint64_t t0 = global_ns();
+  while (global_ns() - t0 < kSettleNs) {
+  }
+}
 // Bounded wait on the phase with parity `parity`.  Returns false on timeout or
 // when another role of this CTA has already aborted.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int* err) {
@@ -433,6 +444,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) ns_gemm_kernel(const __grid_cons
     }
   }
 
+  abort_settle(abort_flag);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -913,6 +925,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
     }
   }
 
+  abort_settle(abort_flag);
   tc_fence_before();
   __syncwarp();
   cluster_sync_all();  // no CTA leaves while its peer may still signal it
