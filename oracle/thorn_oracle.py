@@ -36,18 +36,29 @@ DTYPES = ("f32", "bf16", "f16")
 EPS = {"f32": float(np.finfo(np.float32).eps), "bf16": 0.0078125, "f16": float(np.finfo(np.float16).eps)}
 
 
+_CHUNK = 1 << 18  # elements per block of the rounding loops (working set stays in cache)
+
+
 def to_bf16(x) -> np.ndarray:
     """Round float32 values to bfloat16 (round-to-nearest-even); returns float32.
 
     uint32 arithmetic: only NaN bit patterns can wrap, and those are restored.
+    Large arrays are rounded in cache-sized blocks with reused temporaries.
     """
     x = np.ascontiguousarray(np.asarray(x, dtype=F32))
-    b = x.view(np.uint32)
-    r = (b >> 16) & np.uint32(1)
-    r += np.uint32(0x7FFF)
-    r += b
-    r &= np.uint32(0xFFFF0000)
-    out = r.view(F32)
+    b = x.reshape(-1).view(np.uint32)
+    out = np.empty_like(x)
+    o = out.reshape(-1).view(np.uint32)
+    r = np.empty(min(b.size, _CHUNK), dtype=np.uint32)
+    for i in range(0, b.size, _CHUNK):
+        bb = b[i:i + _CHUNK]
+        rr = r[:bb.size]
+        np.right_shift(bb, 16, out=rr)
+        rr &= np.uint32(1)
+        rr += np.uint32(0x7FFF)
+        rr += bb
+        rr &= np.uint32(0xFFFF0000)
+        o[i:i + _CHUNK] = rr
     nan = np.isnan(x)
     if nan.any():
         out[nan] = np.nan
@@ -412,6 +423,28 @@ def adam_update(p, g, m, v, step, beta1, beta2, lr, wd, eps, dt, degenerate=Fals
     return p, m, v
 
 
+_BLOCK = 1 << 18  # elements per block of a large tensor's AdamW update
+
+
+def adam_update_blocked(p, g, m, v, *args, **kw):
+    """:func:`adam_update` over 256 Ki-element blocks of the flattened tensors: every
+    operation of the update is elementwise, so the result is the same, without the
+    tensor-sized temporaries (a 151936 x 1024 embedding otherwise allocates dozens)."""
+    n = g.size
+    if n <= _BLOCK:
+        return adam_update(p, g, m, v, *args, **kw)
+    shape = g.shape
+    flat = [None if t is None else np.ascontiguousarray(t).reshape(-1) for t in (p, g, m, v)]
+    outs = [None if p is None else np.empty(n, F32), np.empty(n, F32), np.empty(n, F32)]
+    for i in range(0, n, _BLOCK):
+        sl = slice(i, i + _BLOCK)
+        res = adam_update(*[None if t is None else t[sl] for t in flat], *args, **kw)
+        for o, r in zip(outs, res):
+            if o is not None:
+                o[sl] = r
+    return tuple(None if o is None else o.reshape(shape) for o in outs)
+
+
 # ---------------------------------------------------------------------------
 # Group config (thorn.py:535-612)
 # ---------------------------------------------------------------------------
@@ -712,9 +745,9 @@ class OracleTHORN:
             if grp.decouple_md:
                 p, g, p_g, gains = recover_direction(p, g, st, dt)
             apply = scale != 0.0 and (step + 1) % self.update_rate == 0
-            newp, m, v = adam_update(p if apply else None, g, st["moment"], st["variance"], step, b1, b2,
-                                     grp.lr * rect * scale, grp.weight_decay, grp.eps, dt,
-                                     degenerate=(rect == 0.0), sdt=grp.state_dtype)
+            newp, m, v = adam_update_blocked(p if apply else None, g, st["moment"], st["variance"], step, b1,
+                                             b2, grp.lr * rect * scale, grp.weight_decay, grp.eps, dt,
+                                             degenerate=(rect == 0.0), sdt=grp.state_dtype)
             st["moment"], st["variance"] = m, v
             if apply:
                 p = rnd(newp, dt)

@@ -6,6 +6,7 @@ grads in param order), so fixtures only need to hold outputs.
 """
 from __future__ import annotations
 
+import functools
 import math
 
 import numpy as np
@@ -125,6 +126,20 @@ CASES = {
         dict(orthogonalize=False, shapes=[(64,), (33,)], init=("normal", 0.5), dtype="f32",
              opts=dict(lr=1e-3, weight_decay=0.1), zero=[0]),
     ]),
+    # One decoder layer of BASELINE config 3 (Qwen3-style, hidden 1024) at full size, with its
+    # tied 151936 x 1024 embedding: bf16 params and state in the param dtype (the reference's
+    # own layout), q/k RMSNorm weights of 128 and layer norms of 1024 without weight decay.
+    # The orthogonalized lr makes each step's update ~10 bf16 ulps of the parameter, so that
+    # rounding flips do not dominate the compared update.
+    "qwen_layer": dict(steps=2, grad_std=1e-4, groups=[
+        dict(orthogonalize=True, shapes=[(2048, 1024), (1024, 1024), (1024, 1024), (1024, 2048), (3072, 1024),
+                                         (3072, 1024), (1024, 3072)], init=("normal", 0.02), dtype="bf16",
+             opts=dict(lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1)),
+        dict(orthogonalize=False, shapes=[(151936, 1024)], init=("normal", 0.02), dtype="bf16",
+             opts=dict(lr=1e-3, betas=(0.9, 0.95), weight_decay=0.1)),
+        dict(orthogonalize=False, shapes=[(1024,), (1024,), (128,), (128,), (1024,)], init=("const", 1.0),
+             dtype="bf16", opts=dict(lr=1e-3, betas=(0.9, 0.95), weight_decay=0.0)),
+    ]),
     # Magma on the FSDP2 path (world 1 and 2): orthogonalized matrices, even and uneven splits,
     # with and without MD, next to a Magma (R)AdamW vector group.
     "magma_shard": dict(steps=6, grad_std=1e-3, groups=[
@@ -205,15 +220,46 @@ def group_dicts(case: dict, params):
     return gs
 
 
+@functools.lru_cache(maxsize=16)
 def probe_vector(n: int) -> np.ndarray:
-    """Deterministic projection vector for checksums (no RNG involved)."""
+    """Deterministic projection vector for checksums (no RNG involved); cached and
+    read-only, since a large tensor's checksums ask for the same length many times."""
     i = np.arange(n, dtype=np.float64)
-    return np.cos(0.37 * i + 0.11)
+    v = np.cos(0.37 * i + 0.11)
+    v.setflags(write=False)
+    return v
+
+
+_SUM_BLOCK = 1 << 20
+
+
+@functools.lru_cache(maxsize=16)
+def probe_norm_sq(n: int) -> float:
+    """Squared norm of ``probe_vector(n)``."""
+    v = probe_vector(n)
+    return float(sum(float((v[i:i + _SUM_BLOCK] ** 2).sum()) for i in range(0, n, _SUM_BLOCK)))
 
 
 def checksum(a: np.ndarray) -> np.ndarray:
-    x = np.asarray(a, dtype=np.float64).reshape(-1)
-    return np.array([x.sum(), (x * x).sum(), (x * probe_vector(x.size)).sum()], dtype=np.float64)
+    """(sum, sum of squares, projection on ``probe_vector``) in float64, accumulated over
+    blocks so that a large tensor needs no tensor-sized float64 temporaries."""
+    flat = np.asarray(a).reshape(-1)
+    pv = probe_vector(flat.size)
+    out = np.zeros(3, dtype=np.float64)
+    for i in range(0, flat.size, _SUM_BLOCK):
+        x = flat[i:i + _SUM_BLOCK].astype(np.float64)
+        out += (x.sum(), (x * x).sum(), (x * pv[i:i + _SUM_BLOCK]).sum())
+    return out
+
+
+def sq_dist(a: np.ndarray, b: np.ndarray) -> float:
+    """Sum of (a - b)^2 in float64, over blocks."""
+    fa, fb = np.asarray(a).reshape(-1), np.asarray(b).reshape(-1)
+    s = 0.0
+    for i in range(0, fa.size, _SUM_BLOCK):
+        d = fa[i:i + _SUM_BLOCK].astype(np.float64) - fb[i:i + _SUM_BLOCK].astype(np.float64)
+        s += float((d * d).sum())
+    return s
 
 
 def rel_fro(a, b) -> float:

@@ -69,21 +69,25 @@ def compare_tensor(mine: np.ndarray, gold: dict, key: str, base: np.ndarray | No
     Returns the worst of: relative Frobenius error over the stored values
     (full array or head), and the checksum bound |d proj| / (||d|| ||r||).
     """
-    mine = np.asarray(mine, dtype=np.float64)
-    b = np.zeros_like(mine) if base is None else np.asarray(base, dtype=np.float64)
+    mine = np.asarray(mine)
+    b = np.zeros(mine.shape, dtype=np.float32) if base is None else np.asarray(base)
     if key + "/full" in gold:
+        mine, b = mine.astype(np.float64), b.astype(np.float64)
         ref = gold[key + "/full"].astype(np.float64).reshape(mine.shape)
         return C.rel_fro(mine - b, ref - b)
+    # large tensors: the head in full, the rest through checksums (float64, accumulated
+    # over blocks; no tensor-sized temporaries)
     head = gold[key + "/head"].astype(np.float64)
     n = head.size
-    e1 = C.rel_fro((mine - b).reshape(-1)[:n], head - b.reshape(-1)[:n])
+    mh = mine.reshape(-1)[:n].astype(np.float64)
+    bh = b.reshape(-1)[:n].astype(np.float64)
+    e1 = C.rel_fro(mh - bh, head - bh)
     cs_ref = gold[key + "/sum"]
     cs_mine = C.checksum(mine)
     cs_base = C.checksum(b)
-    d = (mine - b).reshape(-1)
-    scale = math.sqrt(float((d * d).sum())) * math.sqrt(float((C.probe_vector(d.size) ** 2).sum()))
+    scale = math.sqrt(C.sq_dist(mine, b)) * math.sqrt(C.probe_norm_sq(mine.size))
     e2 = abs((cs_mine[2] - cs_base[2]) - (cs_ref[2] - cs_base[2])) / max(scale, 1e-30)
-    sq_scale = max(float((mine * mine).sum()), 1e-30)
+    sq_scale = max(float(cs_mine[1]), 1e-30)
     e3 = abs(cs_mine[1] - cs_ref[1]) / sq_scale if base is None else 0.0
     return max(e1, e2, e3)
 

@@ -483,6 +483,20 @@ def test_edge_inputs_match_oracle():
         assert all(np.isfinite(p).all() for g in gpu[tag][0] for p in g)
 
 
+def test_qwen_layer_matches_oracle():
+    """One decoder layer of the Qwen3-style configuration at full size (q 2048x1024, k/v
+    1024x1024, o 1024x2048, gate/up 3072x1024, down 1024x3072) with its 151936x1024 tied
+    embedding and RMSNorm weights, bf16 params and state, two steps against the oracle (whose
+    first step is pinned to the reference's goldens at these shapes)."""
+    name = "qwen_layer"
+    _, gpu = run_gpu(name)
+    _, orc = P.run_oracle(name)
+    init = [[t.float().numpy() for t in g] for g in C.build_params(C.CASES[name])]
+    bad, worst = compare(name, gpu, orc, init)
+    assert not bad, {k: f"{v:.3e}" for k, v in sorted(bad.items())[:10]}
+    print(name, {k: f"{v:.2e}" for k, v in sorted(worst.items())})
+
+
 def _magma_seeds(name, gpu):
     """The Magma seeds the GPU run drew, in initialisation order: each parameter's
     generator state after step 1 stepped back once (every Magma parameter of

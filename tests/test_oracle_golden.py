@@ -23,6 +23,7 @@ import parity as P
 from oracle import thorn_oracle as O
 
 ORTHO_TOL = {"f32": 1e-2, "bf16": 4e-2}
+PIN_STEPS = {"qwen_layer": 1}
 VEC_TOL = 1e-4
 GAIN_TOL = 1e-3
 
@@ -47,7 +48,9 @@ def test_oracle_matches_reference_goldens(name, golden_dir):
                    for g in C.build_grads(C.CASES[name], 0) for t in g])
     np.testing.assert_allclose(g0, gold["input/grad0_sum"], rtol=1e-12, atol=1e-12)
 
-    _, snaps = P.run_oracle(name, cpu_quirks=True)
+    # full-size layer: its first step is pinned here (the later steps' logic is pinned by the
+    # small cases; the GPU test runs both steps against the oracle)
+    _, snaps = P.run_oracle(name, steps=PIN_STEPS.get(name), cpu_quirks=True)
     init = [[t.float().numpy() for t in g] for g in params]
     errs = P.compare_run(name, gold, snaps, init)
     bad = {k: e for k, e in errs.items() if not e <= _group_tol(name, k[1], k[3])}
