@@ -5,7 +5,8 @@
 
 For N > 1 launch one process per GPU with torch.distributed.run; parameters
 are then DTensors sharded Shard(0) over the ranks (FSDP2 layout) and the
-orthogonalized group takes the sharded path.
+orthogonalized group takes the sharded path.  ``--model llama70b`` runs
+BASELINE configs[4] instead (80 layers, hidden 8192, moonlight scaling; 8 GPUs).
 
 Workload: 32 layers, hidden 4096; per layer q/o
 4096x4096, k/v 1024x4096, gate/up 14336x4096, down 4096x14336 in the
@@ -47,7 +48,21 @@ LAYERS, HIDDEN, KV, FFN, VOCAB = 32, 4096, 1024, 14336, 128256
 LAYER_SHAPES = [(HIDDEN, HIDDEN), (KV, HIDDEN), (KV, HIDDEN), (HIDDEN, HIDDEN), (FFN, HIDDEN), (FFN, HIDDEN),
                 (HIDDEN, FFN)]
 ORTHO_LR, ADAM_LR = 8e-3, 8e-3
+MD = True  # decouple_md on the orthogonalized group
 METRIC = "THORN.step ms, Llama-3-8B shapes"
+WORKLOAD = "llama3-8b-fsdp2 (BASELINE configs[3])"
+
+
+def use_llama70b():
+    """80 layers, hidden 8192, gate/up 28672; scaling_mode moonlight
+    without decouple_md.  Fits 8 GPUs (about 72 GB of params, grads and state per rank)."""
+    global LAYERS, HIDDEN, KV, FFN, LAYER_SHAPES, ORTHO_LR, ADAM_LR, MD, METRIC, WORKLOAD
+    LAYERS, HIDDEN, KV, FFN = 80, 8192, 1024, 28672
+    LAYER_SHAPES = [(HIDDEN, HIDDEN), (KV, HIDDEN), (KV, HIDDEN), (HIDDEN, HIDDEN), (FFN, HIDDEN), (FFN, HIDDEN),
+                    (HIDDEN, FFN)]
+    ORTHO_LR, ADAM_LR, MD = 1e-3, 1e-3, False
+    METRIC = "THORN.step ms, Llama-3-70B shapes"
+    WORKLOAD = "llama3-70b-fsdp2 (BASELINE configs[4])"
 # DRAM bytes (read + write) of one ns_gemm2_kernel launch from the ncu capture in
 # profiles/ns_gemm_2x4096.md: X X^T on two 4096x4096 matrices (K = 4096), whose
 # compulsory traffic is 67 MB read + 67 MB written.
@@ -55,7 +70,8 @@ NS_GEMM_TRAFFIC = 100.1e6
 NS_GEMM_TRAFFIC_CASE = "one X X^T launch on 2 x 4096x4096 (K=4096); compulsory 67 MB read + 67 MB write"
 
 
-def shapes(layers=LAYERS):
+def shapes(layers=None):
+    layers = LAYERS if layers is None else layers
     ortho = [s for _ in range(layers) for s in LAYER_SHAPES]
     adamw = [(VOCAB, HIDDEN), (VOCAB, HIDDEN)] + [(HIDDEN,)] * (2 * layers + 1)
     return ortho, adamw
@@ -150,7 +166,7 @@ def cpu_oracle_sample(warm_only: bool = False):
         orc.step([grads])
         return time.perf_counter() - t0
 
-    og = {"orthogonalize": True, "lr": ortho_lr, "decouple_md": True, "dtype": "bf16", "state_dtype": "f32"}
+    og = {"orthogonalize": True, "lr": ortho_lr, "decouple_md": MD, "dtype": "bf16", "state_dtype": "f32"}
     ag = {"orthogonalize": False, "lr": adam_lr, "dtype": "bf16", "state_dtype": "f32"}
     if warm_only:
         timed(og, [(KV, HIDDEN)])
@@ -165,13 +181,18 @@ def cpu_oracle_sample(warm_only: bool = False):
     total = (LAYERS * (2 * t_sq + 2 * t_kv + 3 * t_ffn) + 2 * (VOCAB / emb_rows) * t_emb
              + (2 * LAYERS + 1) * t_norm)
     sample = (f"one {HIDDEN}x{HIDDEN}, one {KV}x{HIDDEN} and one {FFN}x{HIDDEN} orthogonalized matrix "
-              f"(decouple_md), a {emb_rows}x{HIDDEN} embedding slice and one norm vector; "
-              f"sum scaled to 32 layers + 2 x {VOCAB}-row embeddings + 65 norms (extrapolated)")
+              f"({'decouple_md' if MD else 'moonlight'}), a {emb_rows}x{HIDDEN} embedding slice and one norm "
+              f"vector; sum scaled to {LAYERS} layers + 2 x {VOCAB}-row embeddings + {2 * LAYERS + 1} norms "
+              "(extrapolated)")
     return total * 1e3, sample, (t_sq + t_kv + t_ffn + t_emb + t_norm)
 
 
 def reference_arm(args, rank):
     if rank != 0:
+        return
+    if args.model != "llama8b":
+        print(json.dumps({"impl": "reference", "unavailable": "the CPU sample covers the llama8b set only (one "
+                          "28672x8192 Newton-Schulz takes hours on the host cores)"}), flush=True)
         return
     cores = os.cpu_count() or 1
     vals = []
@@ -185,15 +206,15 @@ def reference_arm(args, rank):
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "ms", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v, 3), "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "llama3-8b-fsdp2 (BASELINE configs[3])", "sample": "bounded, extrapolated"},
+            "config": {"workload": WORKLOAD, "sample": "bounded, extrapolated"},
             "cpu_baseline": {"value": round(v, 3), "unit": "ms", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": round(v, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
 # ------------------------------------------------------------- GPU arm
-def build_params(torch, dev, rank, world, mesh, layers=LAYERS):
-    """Llama-8B-shaped params (bf16 ~N(0, 0.02)) and grads (bf16 ~N(0, 1e-4)) on `dev`."""
+def build_params(torch, dev, rank, world, mesh, layers=None):
+    """Llama-shaped params (bf16 ~N(0, 0.02)) and grads (bf16 ~N(0, 1e-4)) on `dev`."""
     ortho_s, adam_s = shapes(layers)
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
@@ -265,7 +286,7 @@ def gpu_arm(args, rank, world, local_rank):
     params = ortho + adamw
     grads = g_ortho + g_adam
     opt = THORN([
-        {"orthogonalize": True, "params": ortho, "lr": ORTHO_LR, "decouple_md": True, "state_dtype": torch.float32},
+        {"orthogonalize": True, "params": ortho, "lr": ORTHO_LR, "decouple_md": MD, "state_dtype": torch.float32},
         {"orthogonalize": False, "params": adamw, "lr": ADAM_LR, "state_dtype": torch.float32},
     ])
     opt.pipeline_exchange = bool(args.pipeline_exchange)
@@ -475,11 +496,11 @@ def gpu_arm(args, rank, world, local_rank):
         "metric": METRIC, "value": round(ms, 3), "unit": "ms", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False,
         "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": "llama3-8b-fsdp2 (BASELINE configs[3])" + (" sharded Shard(0)" if world > 1 else "")
+        "config": {"workload": WORKLOAD + (" sharded Shard(0)" if world > 1 else "")
                    + ("" if args.layers == LAYERS else f" REDUCED to {args.layers} layers (profiling only)"),
                    "ortho_matrices": len(ortho_s), "adamw_tensors": len(adam_s),
                    "params": sum(math.prod(s) for s in ortho_s + adam_s), "param_dtype": "bf16",
-                   "state_dtype": "f32", "ns_dtype": "f16", "decouple_md": True, "lr": ORTHO_LR,
+                   "state_dtype": "f32", "ns_dtype": "f16", "decouple_md": MD, "lr": ORTHO_LR,
                    "parallelism": f"fsdp{world}" if world > 1 else "single",
                    "l2": "no flush: every step reads params, grads and state (~70 GB) >> 126 MB L2"},
         "roofline": {"bound": "tensor", "kernel": "ns_gemm2_kernel (Newton-Schulz phase)",
@@ -498,7 +519,8 @@ def gpu_arm(args, rank, world, local_rank):
             "achieved": round(mom_bytes / (mom_ms * 1e-3) / 1e9, 1) if mom_ms > 0 else None,
             "peak": round(hbm * world, 1), "unit": "GB/s",
             "frac": round(mom_bytes / (mom_ms * 1e-3) / 1e9 / (hbm * world), 3) if mom_ms > 0 else None,
-            "bytes": "g read + m read/write + p read/write (decouple_md), compulsory",
+            "bytes": ("g read + m read/write + p read/write (decouple_md), compulsory" if MD
+                      else "g read + m read/write, compulsory"),
             "ms_per_step": round(mom_ms, 3), "gb_per_step": round(mom_bytes / 1e9, 2)},
         "cpu_baseline": cpu,
         "e2e": e2e,
@@ -681,10 +703,16 @@ def main():
     ap.add_argument("--ns-only", default=None, help="BxRxC: time thorn_ns_batched alone on this batch (profiling)")
     ap.add_argument("--ns-library", action="store_true",
                     help="with --ns-only: time the same recurrences on torch/cuBLAS GEMMs instead (library baseline)")
-    ap.add_argument("--layers", type=int, default=LAYERS, help="transformer layers (profiling runs use fewer)")
+    ap.add_argument("--layers", type=int, default=None, help="transformer layers (profiling runs use fewer)")
+    ap.add_argument("--model", default="llama8b", choices=["llama8b", "llama70b"],
+                    help="parameter set: llama8b (BASELINE configs[3], the headline) or llama70b (configs[4], 8 GPUs)")
     ap.add_argument("--ortho-only", default=None,
                     help="BxRxC: time steps of one decouple_md group of B bf16 RxC matrices (profiling)")
     args = ap.parse_args()
+    if args.model == "llama70b":
+        use_llama70b()
+    if args.layers is None:
+        args.layers = LAYERS
     if args.ns_only:
         ns_only(args)
         return
