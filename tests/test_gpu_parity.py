@@ -420,9 +420,10 @@ def test_ns_full_size_matches_oracle(shape):
 
 
 @pytest.mark.parametrize("shape,kind", [((1, 14336, 4096), "rand"), ((1, 4096, 14336), "rand"),
-                                        ((2, 4096, 4096), "near_id"), ((4, 1024, 4096), "rand")])
+                                        ((2, 4096, 4096), "near_id"), ((4, 1024, 4096), "rand"),
+                                        ((1, 28672, 8192), "rand"), ((1, 8192, 8192), "near_id")])
 def test_ns_full_size_singular_values(shape, kind):
-    """At the Llama-3-8B shapes (too large for the CPU oracle), a size-independent property:
+    """At the Llama-3-8B and 70B shapes (too large for the CPU oracle), a size-independent property:
     every singular value of the NS output lies in the band the Polar-Express composition
     maps [1e-3, 1] into (the oracle gives [0.848, 1.153] at smaller sizes), while the
     Frobenius-normalised inputs have singular values near 1/sqrt(min dim) ~ 0.016."""
