@@ -252,19 +252,22 @@ def checksum(a: np.ndarray) -> np.ndarray:
     return out
 
 
-def sq_dist(a: np.ndarray, b: np.ndarray) -> float:
-    """Sum of (a - b)^2 in float64, over blocks."""
-    fa, fb = np.asarray(a).reshape(-1), np.asarray(b).reshape(-1)
+def sq_dist(a: np.ndarray, b) -> float:
+    """Sum of (a - b)^2 (of a^2 when b is None) in float64, over blocks."""
+    fa = np.asarray(a).reshape(-1)
+    fb = None if b is None else np.asarray(b).reshape(-1)
     s = 0.0
     for i in range(0, fa.size, _SUM_BLOCK):
-        d = fa[i:i + _SUM_BLOCK].astype(np.float64) - fb[i:i + _SUM_BLOCK].astype(np.float64)
+        d = fa[i:i + _SUM_BLOCK].astype(np.float64)
+        if fb is not None:
+            d -= fb[i:i + _SUM_BLOCK]
         s += float((d * d).sum())
     return s
 
 
 def rel_fro(a, b) -> float:
-    a = np.asarray(a, dtype=np.float64)
-    b = np.asarray(b, dtype=np.float64)
-    den = math.sqrt(float((b * b).sum()))
-    num = math.sqrt(float(((a - b) ** 2).sum()))
+    """||a - b|| / ||b|| in float64 (||a - b|| when b is zero), accumulated over blocks."""
+    a, b = np.broadcast_arrays(np.asarray(a), np.asarray(b))
+    den = math.sqrt(sq_dist(b, None))
+    num = math.sqrt(sq_dist(a, b))
     return num / den if den > 0 else num
