@@ -698,8 +698,10 @@ class OracleTHORN:
                 p, g, p_g, gains = recover_direction(p, g, st, dt)
             # Magma on the recovered gradient and the moment before this step (thorn.py:1392)
             scale = magma_scale(g, st["moment"], st, dt, sharded=self.sharded) if grp.momentum_align else 1.0
-            if self.sharded and scale == 0.0:
-                continue  # thorn.py:1485-1490: the masked matrix is left as it is
+            if self.sharded and (scale == 0.0 or (st["step"] + 1) % self.update_rate != 0):
+                # thorn.py:1485-1490: a masked matrix, or one whose step is not due, is left out
+                # of the step entirely (no momentum update, no step count: thorn.py:1564)
+                continue
             # momentum (thorn.py:1376-1381): m = m*b1 + g ; u = g + b1*m
             m = rnd(st["moment"] * b1, sdt)
             m = rnd(m + g, sdt)

@@ -150,6 +150,26 @@ CASES = {
         dict(orthogonalize=False, shapes=[(64,), (40,)], init=("normal", 0.1), dtype="f32",
              opts=dict(lr=1e-3, momentum_align=True)),
     ]),
+    # update_rate 2 on one device (what setup_gradient_release(update_rate=2) sets): the moments
+    # and the step count advance every step, the parameters every second step (thorn.py:1395,
+    # 1681, 1707).
+    "rate_small": dict(steps=4, grad_std=1e-3, update_rate=2, groups=[
+        dict(orthogonalize=True, shapes=[(64, 64), (96, 64)], init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=2e-3, weight_decay=0.1)),
+        dict(orthogonalize=True, shapes=[(64, 96)], init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=8e-3, decouple_md=True)),
+        dict(orthogonalize=False, shapes=[(64,), (40, 24)], init=("normal", 0.1), dtype="f32",
+             opts=dict(lr=1e-3, weight_decay=0.1)),
+    ]),
+    # The reference's own FSDP2 path (its goldens come from 2 gloo ranks, make_sharded_golden.py):
+    # even splits, no decouple_md (which the reference cannot run sharded on this torch).
+    # update_rate 2 (what setup_gradient_release(update_rate=2) sets): the sharded reference
+    # leaves a matrix whose step is not due out of the step entirely, step count included
+    # (thorn.py:1485-1490, 1564), so after its first update no later step is ever due.
+    "rate_shard": dict(steps=4, grad_std=1e-3, update_rate=2, groups=[
+        dict(orthogonalize=True, shapes=[(64, 64), (96, 64), (64, 160)], init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=2e-3, weight_decay=0.1)),
+    ]),
     # Row-sparse gradients on (R)AdamW parameters (thorn.py:1667-1698): duplicate rows, a 1-D
     # embedding, a step whose sparse gradient has no rows, Magma on sparse rows.
     "sparse_small": dict(steps=4, grad_std=1e-3, groups=[

@@ -55,6 +55,7 @@ def run_case(THORN, name: str) -> dict:
     params = C.build_params(case)
     torch_params = [[torch.nn.Parameter(t.clone()) for t in ps] for ps in params]
     opt = THORN(C.group_dicts(case, torch_params))
+    opt._update_rate = case.get("update_rate", 1)  # what setup_gradient_release(update_rate=...) sets
     out = {}
     lim = LIMITS.get(name, (FULL_LIMIT, SLICE))
     g0 = C.build_grads(case, 0)

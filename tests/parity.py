@@ -39,6 +39,7 @@ def run_oracle(name: str, steps: int | None = None, state_dtype: str | None = No
         groups.append(d)
     seed_fn = C.magma_seed if seeds is None else iter(list(seeds)).__next__
     orc = OracleTHORN(groups, seed_fn=seed_fn, sharded=sharded)
+    orc.update_rate = case.get("update_rate", 1)
     n = case["steps"] if steps is None else steps
     snaps = {}
     for s in range(n):

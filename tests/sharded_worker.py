@@ -48,6 +48,7 @@ def main():
     params = C.build_params(case)
     tp = [[torch.nn.Parameter(distribute_tensor(t.cuda(), mesh, [Shard(0)])) for t in ps] for ps in params]
     opt = THORN(C.group_dicts(case, tp))
+    opt._update_rate = case.get("update_rate", 1)  # what setup_gradient_release(update_rate=...) sets
     opt.pipeline_exchange = args.pipeline_exchange
     out = {}
     for s in range(case["steps"]):

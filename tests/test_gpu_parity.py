@@ -49,6 +49,7 @@ def run_gpu(name, state_dtype=None, ns_dtype=None, steps=None):
         for g in groups:
             g["state_dtype"] = C.TORCH_DTYPES[state_dtype]
     opt = THORN(groups)
+    opt._update_rate = case.get("update_rate", 1)  # what setup_gradient_release(update_rate=...) sets
     if ns_dtype is not None:
         opt.ns_dtype = ns_dtype
     n = case["steps"] if steps is None else steps
@@ -496,6 +497,18 @@ def test_qwen_layer_matches_oracle():
     bad, worst = compare(name, gpu, orc, init)
     assert not bad, {k: f"{v:.3e}" for k, v in sorted(bad.items())[:10]}
     print(name, {k: f"{v:.2e}" for k, v in sorted(worst.items())})
+
+
+def test_update_rate_matches_oracle():
+    """update_rate 2 on one device (thorn.py:1395, 1681, 1707): moments and step counts advance
+    every step, parameters (orthogonalized, MD and AdamW) every second step; against the
+    oracle, which is pinned to the reference's goldens for this case."""
+    name = "rate_small"
+    _, gpu = run_gpu(name)
+    _, orc = P.run_oracle(name)
+    init = [[t.float().numpy() for t in g] for g in C.build_params(C.CASES[name])]
+    bad, _ = compare(name, gpu, orc, init)
+    assert not bad, {k: f"{v:.3e}" for k, v in sorted(bad.items())[:10]}
 
 
 def _magma_seeds(name, gpu):

@@ -244,7 +244,7 @@ PIPE = ("--pipeline-exchange",)
 @pytest.mark.parametrize("world", [1, 2])
 @pytest.mark.parametrize("name,extra", [("tiny", ()), ("md_shard", ()), ("shard_uneven", ()),
                                         ("shard_uneven", PIPE), ("md_shard", PIPE),
-                                        ("magma_shard", ()), ("magma_shard", PIPE)])
+                                        ("magma_shard", ()), ("magma_shard", PIPE), ("rate_shard", ())])
 def test_sharded_step_matches_oracle(world, name, extra, tmp_path):
     """The Shard(0) path (rounds or waves of the exchange, Magma masking whole matrices)
     against the oracle's sharded semantics; the oracle replays the run's Magma seeds."""
@@ -425,3 +425,64 @@ def test_lost_rank_fails_the_next_step_gloo():
     assert result[1] == "left"
     assert isinstance(result[0], tuple), result[0]
     assert result[0][1] < 30, result[0]
+
+
+def _due_worker(rank, world, port, result):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from torch.distributed.device_mesh import init_device_mesh
+        from torch.distributed.tensor import Shard, distribute_tensor
+
+        from thorn_b200 import THORN
+        from thorn_b200 import sharded as S
+        from thorn_b200.optimizer import GroupConfig
+
+        mesh = init_device_mesh("cpu", (world,))
+        torch.manual_seed(0)
+        shapes = [(8, 4), (6, 4), (10, 4), (4, 4)]
+        ps = [torch.nn.Parameter(distribute_tensor(torch.randn(s), mesh, [Shard(0)])) for s in shapes]
+        opt = THORN([{"orthogonalize": True, "params": ps, "lr": 1e-3, "momentum_align": True}])
+        opt._update_rate = 2
+        cfg = GroupConfig.from_kwargs(**opt.param_groups[0])
+        ranks, group = S.shard_group(ps[0], rank)
+        log = []
+        for step in range(3):
+            for p, s in zip(ps, shapes):
+                p.grad = distribute_tensor(torch.randn(s), mesh, [Shard(0)])
+                if "step" not in opt.state[p]:
+                    opt._init_state(p, opt.state[p], cfg, opt.param_groups[0])
+                opt.state[p]["moment"] = opt.state[p]["moment"] + 0.1  # a nonzero moment for Magma
+            due, scales = S.due_matrices(opt, list(ps), cfg, group)
+            sel = [any(d is p for d in due) for p in ps]
+            assert all((p.grad is None) != s for p, s in zip(ps, sel))
+            assert len(scales) == len(due) and all(sc > 0 for sc in scales)
+            for p in due:  # what the step's finish does for an updated matrix
+                opt.state[p]["step"] += 1
+                p.grad = None
+            log.append(sel)
+        box = [None] * world
+        dist.all_gather_object(box, log)
+        steps = [opt.state[p]["step"] for p in ps]
+        # every rank selects the same matrices; step 1 is due for every unmasked matrix, and a
+        # matrix that updated (step 2) is never due again under update_rate 2
+        result[rank] = (all(b == log for b in box), log, steps)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_due_matrices_gloo():
+    """The sharded step's selection of the matrices it updates (Magma on, update_rate 2), on
+    gloo ranks: the same on every rank, a masked or not-due matrix left out with its gradient
+    dropped and its step count kept (thorn.py:1485-1490, 1564)."""
+    ctx = mp.get_context("spawn")
+    result = ctx.Manager().dict()
+    mp.start_processes(_due_worker, args=(2, _free_port(), result), nprocs=2, join=True, start_method="spawn")
+    same, log, steps = result[0]
+    assert same and result[1][0]
+    for j in range(4):
+        col = [sel[j] for sel in log]
+        assert sum(col) <= 1  # updates at most once
+        assert steps[j] == 1 + sum(col)
+    assert any(any(sel) for sel in log)

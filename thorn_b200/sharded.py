@@ -26,8 +26,8 @@ Shards follow DTensor's ``torch.chunk`` split, so rows need not divide evenly
 (a split that leaves a shard empty is rejected).  With ``pipeline_exchange``
 steps 3-5 run in waves of NS batches so transfers overlap the owners' NS; with
 ``exchange = "all_to_all"`` each exchange is one ``all_to_all_single``.  Magma
-masking all-reduces its three sums over the shard group first and leaves a
-masked matrix out of the step.
+masking all-reduces its three sums over the shard group first; a masked matrix,
+or one whose step is not due under ``update_rate``, is left out of the step.
 
 Owners are chosen by longest-processing-time over the reference's NS FLOP
 estimate (thorn.py:1001-1007), deterministically on every rank.  Parameters of
@@ -274,30 +274,39 @@ def sharded_ortho_step(opt, params, cfg) -> None:
             opt._ortho_local(batched, cfg)
     if not mats:
         return
+    dev = _local(mats[0]).device
+    with torch.cuda.device(dev):
+        mats, scales = due_matrices(opt, mats, cfg, group)
+        if mats:
+            _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, _Arena, _local, scales)
+
+
+def due_matrices(opt, mats, cfg, group):
+    """The sharded matrices this step updates, and their Magma LR scales.
+
+    Magma scores every matrix first, its three sums all-reduced over the shard group
+    (thorn.py:1483-1490).  A masked matrix, or one whose step is not due under
+    ``update_rate``, is then left out of the step entirely: its gradient is dropped, its
+    momentum and step count stay (thorn.py:1485-1490, 1564).  So with update_rate > 1 a
+    sharded matrix updates once and is never due again; the reference's sharded path
+    behaves so, and it is kept for drop-in parity."""
+    from .optimizer import _Item, _local
+
     scales = [1.0] * len(mats)
     if cfg.momentum_align:
-        # Magma on the shards: the three sums are all-reduced over the shard group
-        # (thorn.py:1483-1490).  A masked matrix is left out of this step entirely:
-        # no momentum update and no step count, as in the reference's sharded path.
-        from .optimizer import _Item
         recs = []
         for p in mats:
             it = _Item()
             it.g, it.state = _local(p.grad), opt.state[p]
             it.split, it.apply = "row_gain" in it.state, True
             recs.append(it)
-        with torch.cuda.device(_local(mats[0]).device):
-            opt._magma(recs, cfg, recovered=True, group=group)
-        for p, it in zip(mats, recs):
-            if not it.apply:
-                p.grad = None
-        scales = [it.scale for it in recs if it.apply]
-        mats = [p for p, it in zip(mats, recs) if it.apply]
-        if not mats:
-            return
-    dev = _local(mats[0]).device
-    with torch.cuda.device(dev):
-        _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, _Arena, _local, scales)
+        opt._magma(recs, cfg, recovered=True, group=group)
+        scales = [it.scale for it in recs]
+    due = [sc != 0.0 and (opt.state[p]["step"] + 1) % opt._update_rate == 0 for p, sc in zip(mats, scales)]
+    for p, d in zip(mats, due):
+        if not d:
+            p.grad = None
+    return [p for p, d in zip(mats, due) if d], [sc for sc, d in zip(scales, due) if d]
 
 
 def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, scales):
@@ -315,8 +324,6 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
     for it in items:
         if it.C % 8:
             raise NotImplementedError("sharded NS needs a column count that is a multiple of 8")
-        if not it.apply:
-            raise NotImplementedError("update_rate > 1 is not implemented for sharded parameters")
     owners = assign_owners([ns_flops(rows_g[j], it.C, cfg.iters) for j, it in enumerate(items)], world)
 
     def owner_chunks(r):
