@@ -479,16 +479,20 @@ class Group:
         """thorn.py:704-707."""
         return self.betas[1] > 0 and (shape[-2] > shape[-1] or self.force_per_neuron_norm)
 
+    def norm_axes(self, p):
+        """thorn.py:594-595: the group's norm_axis, else the last two dims (the last of a vector)."""
+        if self.norm_axis is not None:
+            ax = self.norm_axis
+            return tuple(ax) if isinstance(ax, (tuple, list)) else (ax,)
+        return (-2, -1) if p.ndim > 1 else (-1,)
+
     def target_norm_(self, p, dt):
         """thorn.py:597-612 for the string modes (callables are not modelled)."""
         tn = self.target_norm
         if tn is None:
             tn = "max" if self.orthogonalize else "init"
         if tn == "init":
-            if p.ndim > 1:
-                val = np.sqrt(np.sum(p.astype(np.float64) ** 2, axis=(-2, -1), keepdims=True))
-            else:
-                val = np.sqrt(np.sum(p.astype(np.float64) ** 2, axis=-1, keepdims=True))
+            val = np.sqrt(np.sum(p.astype(np.float64) ** 2, axis=self.norm_axes(p), keepdims=True))
             return rnd(val, dt)
         if tn == "min":
             return rnd(F32(min(p.shape[-2], p.shape[-1]) ** 0.5), dt)
@@ -543,10 +547,6 @@ def magma_scale(g, m, st, dt: str, tau: float = 2.0, p: float = 0.9, sharded: bo
     if out % 2 != 0:
         return 0.0
     return float(st["s"])
-
-
-def norm_axes(p):
-    return (-2, -1) if p.ndim > 1 else (-1,)
 
 
 # ---------------------------------------------------------------------------
@@ -754,7 +754,7 @@ class OracleTHORN:
             if apply:
                 p = rnd(newp, dt)
                 if grp.decouple_md:
-                    p = renorm(p, st["target_norm"], norm_axes(p), dt)
+                    p = renorm(p, st["target_norm"], grp.norm_axes(p), dt)  # thorn.py:1717
                     update_magnitudes(p_g, gains, st, grp, dt)
             if grp.decouple_md:
                 p = reassemble_md(p, st, dt)

@@ -150,6 +150,15 @@ CASES = {
         dict(orthogonalize=False, shapes=[(64,), (40,)], init=("normal", 0.1), dtype="f32",
              opts=dict(lr=1e-3, momentum_align=True)),
     ]),
+    # decouple_md with norm_axis=-1 (thorn.py:594-595, 605, 1717): the (R)AdamW group's "init"
+    # target norms and renorm run per row (per last-dim slice, also of a 3-D tensor); the
+    # orthogonalized group renorms whole matrices whatever norm_axis says (thorn.py:1417).
+    "md_axis_small": dict(steps=3, grad_std=1e-3, groups=[
+        dict(orthogonalize=True, shapes=[(64, 64), (96, 64)], init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=8e-3, decouple_md=True, norm_axis=-1)),
+        dict(orthogonalize=False, shapes=[(48, 16), (32, 8), (4, 6, 8), (64,)], init=("normal", 0.5),
+             dtype="f32", opts=dict(lr=1e-3, decouple_md=True, norm_axis=-1, weight_decay=0.05)),
+    ]),
     # update_rate 2 on one device (what setup_gradient_release(update_rate=2) sets): the moments
     # and the step count advance every step, the parameters every second step (thorn.py:1395,
     # 1681, 1707).

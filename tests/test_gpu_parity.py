@@ -511,6 +511,18 @@ def test_update_rate_matches_oracle():
     assert not bad, {k: f"{v:.3e}" for k, v in sorted(bad.items())[:10]}
 
 
+def test_md_norm_axis_matches_oracle():
+    """decouple_md with norm_axis=-1: the (R)AdamW renorm per row (2-D and 3-D tensors, a
+    vector), the orthogonalized renorm per matrix; against the oracle, which is pinned to the
+    reference's goldens for this case."""
+    name = "md_axis_small"
+    _, gpu = run_gpu(name)
+    _, orc = P.run_oracle(name)
+    init = [[t.float().numpy() for t in g] for g in C.build_params(C.CASES[name])]
+    bad, _ = compare(name, gpu, orc, init)
+    assert not bad, {k: f"{v:.3e}" for k, v in sorted(bad.items())[:10]}
+
+
 def _magma_seeds(name, gpu):
     """The Magma seeds the GPU run drew, in initialisation order: each parameter's
     generator state after step 1 stepped back once (every Magma parameter of

@@ -201,6 +201,33 @@ def _mat_view(shape) -> tuple[int, int, int]:
     return 1, 1, 1
 
 
+def _row_norm_axis(cfg, p) -> bool:
+    """Whether the (R)AdamW decouple_md renorm of ``p`` runs per last-dim slice.
+
+    norm_axis (thorn.py:594-595) defaults to the last two dims of a matrix (one norm per
+    matrix of the batch) and to the last dim of a vector; a norm_axis naming only the last
+    dim of a tensor of rank >= 2 renorms every row (thorn.py:605, 1717).  Other axes are not
+    implemented here and raise."""
+    ax = cfg.norm_axis_(p)
+    axes = tuple(ax) if isinstance(ax, (tuple, list)) else (ax,)
+    nd = max(p.ndim, 1)
+    axes = tuple(sorted(a % nd for a in axes))
+    if p.ndim <= 1:
+        if axes == (0,):
+            return False
+    elif axes == (nd - 2, nd - 1):
+        return False
+    elif axes == (nd - 1,):
+        return True
+    raise NotImplementedError(f"decouple_md with norm_axis={ax!r} on a {p.ndim}-D parameter is not implemented by "
+                              "thorn_b200 (the last dim, or the default, is)")
+
+
+def _renorm_view(it) -> tuple[int, int, int]:
+    """(batch, rows, cols) over which the renorm's norms are taken: per matrix, or per row."""
+    return (it.B * it.R, 1, it.C) if getattr(it, "row_norm", False) else (it.B, it.R, it.C)
+
+
 class _Arena:
     """Carves fp32 scratch views out of a few buffers ("regions").
 
@@ -246,7 +273,7 @@ class _Arena:
 class _Item:
     __slots__ = ("p", "g", "state", "B", "R", "C", "apply", "pdt", "sdt", "normsq", "rs", "cs", "sig_r", "sig_c",
                  "rgs", "cgs", "rs_new", "cs_new", "pnorm", "scalar", "ggrad_r", "ggrad_c", "split", "scale",
-                 "m_rows", "v_rows")
+                 "m_rows", "v_rows", "row_norm")
 
 
 class THORN(Optimizer):
@@ -297,6 +324,7 @@ class THORN(Optimizer):
         self._err = {}
         self._scratch_bufs = {}
         self._targets = {}
+        self._ones_cache = {}
         if isinstance(params, nn.Module) and conf.get("gradient_release", False):
             self.setup_gradient_release(params)
 
@@ -569,7 +597,9 @@ class THORN(Optimizer):
                     it.cgs = arena.alloc(nc, red1)
                 else:
                     it.cs = it.sig_c = it.cs_new = it.cgs = None
-                it.pnorm = arena.alloc(it.B, red2)
+                # per-slice norms when norm_axis names the last dim of a matrix ((R)AdamW renorm)
+                it.row_norm = not ortho and _row_norm_axis(cfg, it.p)
+                it.pnorm = arena.alloc(it.B * it.R if it.row_norm else it.B, red2)
             items.append(it)
         return items
 
@@ -652,20 +682,39 @@ class THORN(Optimizer):
         lib = N.load()
         by_dt: dict = {}
         keep = []
+        rows_first: dict = {}  # per-row renorms, launched before the gains are applied
         for it in items:
             st = it.state
             normsq = arena.ptr(it.pnorm) if (it.apply and renorm_of(it)) else None
             tgt = self._target_f32(st)
             keep.append(tgt)
             stride = 0 if tgt.numel() == 1 else 1
-            if stride and tgt.numel() != it.B:
-                raise NotImplementedError("target_norm must be a scalar or one value per matrix")
+            vb, vr, vc = _renorm_view(it)
+            if stride and tgt.numel() != vb:
+                raise NotImplementedError("target_norm must be a scalar or one value per renormed slice")
+            if getattr(it, "row_norm", False) and normsq is not None:
+                # p *= target / (||row|| + 1e-8) on the (B*R, 1, C) view, gains of one, then the
+                # gains on the natural view: the same roundings as one fused pass
+                ones = self._ones(it.p.device)
+                rows_first.setdefault(N.dtype_code(it.pdt), []).append(N.MdFinalTensor(
+                    it.p.data_ptr(), normsq, tgt.data_ptr(), stride, ones.data_ptr(), None, 1, vb, vr, vc))
+                normsq = None
             t = N.MdFinalTensor(it.p.data_ptr(), normsq, tgt.data_ptr(), stride, arena.ptr(it.rs_new),
                                 arena.ptr(it.cs_new), 0 if it.split else 1, it.B, it.R, it.C)
             by_dt.setdefault(N.dtype_code(it.pdt), []).append(t)
+        for pc, ts in rows_first.items():
+            N.check(lib.thorn_md_finalize_multi(N.array(N.MdFinalTensor, ts), len(ts), pc, stream), "md_finalize")
         for pc, ts in by_dt.items():
             N.check(lib.thorn_md_finalize_multi(N.array(N.MdFinalTensor, ts), len(ts), pc, stream), "md_finalize")
         return keep
+
+    def _ones(self, dev):
+        """A device float 1.0 (the unit gain of a renorm-only pass)."""
+        t = self._ones_cache.get(dev)
+        if t is None:
+            t = torch.ones(1, dtype=torch.float32, device=dev)
+            self._ones_cache[dev] = t
+        return t
 
     def _finish(self, params, cfg):
         for p in params:
@@ -873,9 +922,7 @@ class THORN(Optimizer):
             self._magma(its, cfg, recovered=False, group=grp)
         if md:
             for it in items:
-                ax = cfg.norm_axis_(it.p)
-                if ax not in ((-2, -1), -1) or (ax == -1 and it.p.ndim > 1):
-                    raise NotImplementedError("decouple_md with a custom norm_axis is not implemented by thorn_b200")
+                _row_norm_axis(cfg, it.p)  # raises for a norm_axis other than the default or the last dim
         arena.materialize(dev)
         b1, b2 = cfg.betas
         if md:
@@ -910,9 +957,9 @@ class THORN(Optimizer):
             self._md_gains(items, cfg, arena, stream)
             app = [it for it in items if it.apply]
             if app:
-                scr = self._scratch(dev, [lib.thorn_sumsq_scratch_bytes(it.B, it.R, it.C) for it in app])
+                scr = self._scratch(dev, [lib.thorn_sumsq_scratch_bytes(*_renorm_view(it)) for it in app])
                 for pdt in {it.pdt for it in app}:
-                    ts = [N.SumsqTensor(it.p.data_ptr(), arena.ptr(it.pnorm), it.B, it.R, it.C, sp)
+                    ts = [N.SumsqTensor(it.p.data_ptr(), arena.ptr(it.pnorm), *_renorm_view(it), sp)
                           for it, sp in zip(app, scr) if it.pdt == pdt]
                     N.check(lib.thorn_sumsq_multi(N.array(N.SumsqTensor, ts), len(ts), N.dtype_code(pdt), stream),
                             "sumsq_multi")
