@@ -159,6 +159,13 @@ CASES = {
         dict(orthogonalize=False, shapes=[(48, 16), (32, 8), (4, 6, 8), (64,)], init=("normal", 0.5),
              dtype="f32", opts=dict(lr=1e-3, decouple_md=True, norm_axis=-1, weight_decay=0.05)),
     ]),
+    # Column counts that are not multiples of 8 on the FSDP2 path: the NS input rows travel with
+    # the padded leading dimension of the NS kernels (world 1 and 2, uneven splits included).
+    "shard_odd_cols": dict(steps=3, grad_std=1e-3, groups=[
+        dict(orthogonalize=True, shapes=[(66, 37), (40, 20), (97, 64), (30, 90)], init=("normal", 0.02),
+             dtype="f32", opts=dict(lr=2e-3, weight_decay=0.1)),
+        dict(orthogonalize=False, shapes=[(21,)], init=("normal", 0.5), dtype="f32", opts=dict(lr=1e-3)),
+    ]),
     # update_rate 2 on one device (what setup_gradient_release(update_rate=2) sets): the moments
     # and the step count advance every step, the parameters every second step (thorn.py:1395,
     # 1681, 1707).

@@ -244,7 +244,8 @@ PIPE = ("--pipeline-exchange",)
 @pytest.mark.parametrize("world", [1, 2])
 @pytest.mark.parametrize("name,extra", [("tiny", ()), ("md_shard", ()), ("shard_uneven", ()),
                                         ("shard_uneven", PIPE), ("md_shard", PIPE),
-                                        ("magma_shard", ()), ("magma_shard", PIPE), ("rate_shard", ())])
+                                        ("magma_shard", ()), ("magma_shard", PIPE), ("rate_shard", ()),
+                                        ("shard_odd_cols", ()), ("shard_odd_cols", PIPE)])
 def test_sharded_step_matches_oracle(world, name, extra, tmp_path):
     """The Shard(0) path (rounds or waves of the exchange, Magma masking whole matrices)
     against the oracle's sharded semantics; the oracle replays the run's Magma seeds."""
@@ -326,7 +327,7 @@ def _sharded_flow_worker(rank, world, port, result, exchange_impl, pipeline):
         N.stream_of = lambda dev: 0
         mesh = init_device_mesh("cpu", (world,))
         torch.manual_seed(0)
-        shapes = [(24, 16), (13, 8), (40, 24), (33, 16), (12, 32)]
+        shapes = [(24, 16), (13, 8), (40, 24), (33, 16), (12, 32), (17, 13)]
         ps = [torch.nn.Parameter(distribute_tensor(torch.randn(s) * 0.02, mesh, [Shard(0)])) for s in shapes]
         opt = THORN([{"orthogonalize": True, "params": ps, "lr": 1e-3, "decouple_md": True,
                       "momentum_align": True}])

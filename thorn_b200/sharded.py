@@ -321,9 +321,9 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
     ns_code = N.dtype_code(ns_dt)
     rows_g = [int(p.shape[0]) for p in mats]  # global rows
     parts = [shard_rows(r, world) for r in rows_g]  # (first row, count) of every shard
-    for it in items:
-        if it.C % 8:
-            raise NotImplementedError("sharded NS needs a column count that is a multiple of 8")
+    # NS input rows (owner buffers and send slabs) use the padded leading dimension the
+    # NS kernels need (16-byte TMA rows); results come back unpadded
+    ld = [int(lib.thorn_ns_ld(it.C)) for it in items]
     owners = assign_owners([ns_flops(rows_g[j], it.C, cfg.iters) for j, it in enumerate(items)], world)
 
     def owner_chunks(r):
@@ -389,20 +389,20 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
     U = {}
     slot = {}  # j -> (chunk index, position in chunk)
     for ci, (R, C, pdt, sdt, js) in enumerate(chunks):
-        X[ci] = torch.empty((len(js), R, C), dtype=ns_dt, device=dev)
+        X[ci] = torch.empty((len(js), R, ld[js[0]]), dtype=ns_dt, device=dev)
         U[ci] = torch.empty((len(js), R, C), dtype=ns_dt, device=dev)
         for k, j in enumerate(js):
             slot[j] = (ci, k)
     # send slabs grouped by owner (matrix index ascending within an owner): each
     # round's message to one owner is then one contiguous range of this buffer
     send_rows = {}
-    n_send = sum(it.R * it.C for j, it in enumerate(items) if owners[j] != me)
+    n_send = sum(it.R * ld[j] for j, it in enumerate(items) if owners[j] != me)
     send_buf = torch.empty(max(1, n_send), dtype=ns_dt, device=dev)
     off = 0
     for j in sorted((j for j in range(len(items)) if owners[j] != me), key=lambda j: (owners[j], j)):
         it = items[j]
-        send_rows[j] = send_buf[off:off + it.R * it.C].view(it.R, it.C)
-        off += it.R * it.C
+        send_rows[j] = send_buf[off:off + it.R * ld[j]].view(it.R, ld[j])
+        off += it.R * ld[j]
 
     def owner_rows(j, s):
         ci, k = slot[j]
