@@ -646,6 +646,7 @@ class OracleTHORN:
             if g.orthogonalize:
                 assert all(p.ndim >= 2 for p in g.params)
             g.state = [dict() for _ in g.params]
+            g.grad_after = {}  # none_grad=False: the gradient each parameter keeps after the step
             self.groups.append(g)
         self.update_rate = 1
 
@@ -723,6 +724,8 @@ class OracleTHORN:
                 p = reassemble_md(p, st, dt)
             grp.params[i] = p
             st["step"] += 1
+            if not grp.none_grad:
+                grp.grad_after[i] = g  # what p.grad holds after the step (MD: the recovered gradient)
 
     # -- AdamW group (thorn.py:1659-1727) ------------------------------------
     def _adam_step(self, grp: Group, idx, gl):
@@ -760,6 +763,8 @@ class OracleTHORN:
                 p = reassemble_md(p, st, dt)
             grp.params[i] = p
             st["step"] += 1
+            if not grp.none_grad:
+                grp.grad_after[i] = g
 
 
 class SparseRows:

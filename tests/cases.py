@@ -166,6 +166,18 @@ CASES = {
              dtype="f32", opts=dict(lr=2e-3, weight_decay=0.1)),
         dict(orthogonalize=False, shapes=[(21,)], init=("normal", 0.5), dtype="f32", opts=dict(lr=1e-3)),
     ]),
+    # MD options: scalar gains on matrices (split_gain=False), gain_lr and gain_betas, "min" and
+    # "max" target norms, and none_grad=False, which leaves the gradient in p.grad (under MD the
+    # direction-recovered one, thorn.py:890-908).
+    "md_options_small": dict(steps=3, grad_std=1e-3, groups=[
+        dict(orthogonalize=True, shapes=[(64, 64), (96, 64)], init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=8e-3, decouple_md=True, split_gain=False, gain_lr=3e-3, gain_betas=(0.8, 0.99),
+                       target_norm="min", none_grad=False)),
+        dict(orthogonalize=True, shapes=[(64, 96)], init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=2e-3, none_grad=False)),
+        dict(orthogonalize=False, shapes=[(48, 16), (20, 12)], init=("normal", 0.5), dtype="f32",
+             opts=dict(lr=1e-3, decouple_md=True, split_gain=False, target_norm="max", none_grad=False)),
+    ]),
     # update_rate 2 on one device (what setup_gradient_release(update_rate=2) sets): the moments
     # and the step count advance every step, the parameters every second step (thorn.py:1395,
     # 1681, 1707).

@@ -73,6 +73,8 @@ def run_case(THORN, name: str) -> dict:
                 for pi, p in enumerate(ps):
                     base = f"{tag}/g{gi}/p{pi}"
                     _store(out, base + "/param", p.data, lim)
+                    if p.grad is not None:  # groups with none_grad=False keep it (MD: recovered)
+                        _store(out, base + "/grad_after", p.grad, lim)
                     for k, v in opt.state[p].items():
                         if isinstance(v, torch.Tensor):
                             _store(out, f"{base}/{k}", v, lim)

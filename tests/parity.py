@@ -49,8 +49,9 @@ def run_oracle(name: str, steps: int | None = None, state_dtype: str | None = No
             tag = "step1" if s == 0 else "final"
             snaps[tag] = (
                 [[p.copy() for p in g.params] for g in orc.groups],
-                [[{k: (np.array(v, copy=True) if isinstance(v, np.ndarray) else v) for k, v in st.items()}
-                  for st in g.state] for g in orc.groups],
+                [[{**{k: (np.array(v, copy=True) if isinstance(v, np.ndarray) else v) for k, v in st.items()},
+                   **({"grad_after": np.array(g.grad_after[i], copy=True)} if i in g.grad_after else {})}
+                  for i, st in enumerate(g.state)] for g in orc.groups],
             )
     return orc, snaps
 

@@ -63,13 +63,15 @@ def run_gpu(name, state_dtype=None, ns_dtype=None, steps=None):
         if s == 0 or s == n - 1:
             tag = "step1" if s == 0 else "final"
             snaps[tag] = ([[_np(p) for p in ps] for ps in tp],
-                          [[{k: (_np(v) if isinstance(v, torch.Tensor) else v) for k, v in opt.state[p].items()}
+                          [[{**{k: (_np(v) if isinstance(v, torch.Tensor) else v) for k, v in opt.state[p].items()},
+                             **({"grad_after": _np(p.grad)} if p.grad is not None else {})}
                             for p in ps] for ps in tp])
     torch.cuda.synchronize()
     assert not opt.device_error()
-    for ps in tp:
+    for grp, ps in zip(case["groups"], tp):
         for p in ps:
-            assert p.grad is None  # none_grad default
+            # none_grad (default True) drops the gradient; otherwise it stays (MD: recovered)
+            assert (p.grad is None) == grp["opts"].get("none_grad", True)
     return opt, snaps
 
 
@@ -521,6 +523,20 @@ def test_md_norm_axis_matches_oracle():
     init = [[t.float().numpy() for t in g] for g in C.build_params(C.CASES[name])]
     bad, _ = compare(name, gpu, orc, init)
     assert not bad, {k: f"{v:.3e}" for k, v in sorted(bad.items())[:10]}
+
+
+def test_md_options_match_oracle():
+    """MD with scalar gains on matrices (split_gain=False), gain_lr / gain_betas, "min" and
+    "max" target norms, and none_grad=False: the gradient each parameter keeps (the
+    direction-recovered one under MD) is compared too; against the oracle, pinned to the
+    reference's goldens for this case."""
+    name = "md_options_small"
+    _, gpu = run_gpu(name)
+    _, orc = P.run_oracle(name)
+    init = [[t.float().numpy() for t in g] for g in C.build_params(C.CASES[name])]
+    bad, worst = compare(name, gpu, orc, init)
+    assert not bad, {k: f"{v:.3e}" for k, v in sorted(bad.items())[:10]}
+    assert any(k[2] == "grad_after" for k in worst)
 
 
 def _magma_seeds(name, gpu):
