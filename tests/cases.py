@@ -178,6 +178,14 @@ CASES = {
         dict(orthogonalize=False, shapes=[(48, 16), (20, 12)], init=("normal", 0.5), dtype="f32",
              opts=dict(lr=1e-3, decouple_md=True, split_gain=False, target_norm="max", none_grad=False)),
     ]),
+    # MD on conv kernels (batches of matrices: row and column gains per batch entry) with the
+    # "init" target norm on an orthogonalized group (one target per matrix of the batch).
+    "md_conv_small": dict(steps=3, grad_std=1e-3, groups=[
+        dict(orthogonalize=True, shapes=[(8, 4, 3), (16, 8, 5), (4, 6, 6)], init=("normal", 0.05), dtype="f32",
+             opts=dict(lr=4e-3, decouple_md=True, target_norm="init")),
+        dict(orthogonalize=True, shapes=[(6, 8, 8)], init=("normal", 0.05), dtype="f32",
+             opts=dict(lr=4e-3, decouple_md=True)),
+    ]),
     # update_rate 2 on one device (what setup_gradient_release(update_rate=2) sets): the moments
     # and the step count advance every step, the parameters every second step (thorn.py:1395,
     # 1681, 1707).

@@ -539,6 +539,18 @@ def test_md_options_match_oracle():
     assert any(k[2] == "grad_after" for k in worst)
 
 
+def test_md_conv_kernels_match_oracle():
+    """decouple_md on 3-D conv kernels (batches of matrices with per-entry row and column gains)
+    and the "init" target norm on an orthogonalized group; against the oracle, pinned to the
+    reference's goldens for this case."""
+    name = "md_conv_small"
+    _, gpu = run_gpu(name)
+    _, orc = P.run_oracle(name)
+    init = [[t.float().numpy() for t in g] for g in C.build_params(C.CASES[name])]
+    bad, _ = compare(name, gpu, orc, init)
+    assert not bad, {k: f"{v:.3e}" for k, v in sorted(bad.items())[:10]}
+
+
 def _magma_seeds(name, gpu):
     """The Magma seeds the GPU run drew, in initialisation order: each parameter's
     generator state after step 1 stepped back once (every Magma parameter of
