@@ -6,7 +6,8 @@
   the lower-triangle tiles of the tcgen05 GEMM and mirrored.
 * ``torch.ops.thorn_b200.polar_decomp(X, coeffs, restarts)``: the Newton-Schulz
   polar factor of a stack of matrices (thorn.py:626-662): Frobenius-normalised in
-  fp32, iterated on fp16 operands, returned in X's dtype.
+  fp32 and cast to fp16 by the library's NS-input pass, iterated on fp16 operands,
+  returned in X's dtype.
 
 Both have fake (meta) implementations, so they trace under ``torch.compile`` and
 ``torch.export`` as opaque nodes.  They run on CUDA devices only; there is no CPU
@@ -104,20 +105,28 @@ def polar_decomp(X: torch.Tensor, coeffs: List[float], restarts: List[int]) -> t
     if nb and R and C:
         lib = N.load()
         dev = X.device
-        ld = int(lib.thorn_ns_ld(C))
-        x = X.reshape(nb, R, C).to(torch.float32)
-        x = x / (x.norm(dim=(-2, -1), keepdim=True) + 1e-8)
-        xin = torch.zeros((nb, R, ld), dtype=torch.float16, device=dev)
-        xin[:, :, :C] = x.to(torch.float16)
-        wsb = int(lib.thorn_ns_workspace_bytes(nb, R, C))
-        ws = torch.empty(max(256, wsb), dtype=torch.uint8, device=dev)
-        iters = len(coeffs) // 3
-        cc = (N.ctypes.c_double * max(1, len(coeffs)))(*coeffs)
-        rr = (N.ctypes.c_int32 * max(1, len(restarts)))(*restarts)
+        code = N.dtype_code(X.dtype)
+        x = X.reshape(nb, R, C).contiguous()
+        st = N.stream_of(dev)
         with torch.cuda.device(dev):
+            # ||x||^2 per matrix (fixed-order sums), then x / (||x|| + 1e-8) cast to fp16 rows of
+            # the padded leading dimension: the NS-input pass with u = x (beta1 = 0)
+            normsq = torch.empty(nb, dtype=torch.float32, device=dev)
+            scr = torch.zeros(max(16, int(lib.thorn_sumsq_scratch_bytes(nb, R, C))), dtype=torch.uint8, device=dev)
+            N.check(lib.thorn_sumsq_multi(N.array(N.SumsqTensor, [N.SumsqTensor(
+                x.data_ptr(), normsq.data_ptr(), nb, R, C, scr.data_ptr())]), 1, code, st), "polar_decomp norms")
+            xin = torch.empty((nb, R, int(lib.thorn_ns_ld(C))), dtype=torch.float16, device=dev)
+            N.check(lib.thorn_ns_cast_multi(N.array(N.NsCastTensor, [N.NsCastTensor(
+                x.data_ptr(), x.data_ptr(), normsq.data_ptr(), xin.data_ptr(), nb, R, C, None, None, 0, 0)]), 1,
+                code, code, code, N.F16, 0.0, st), "polar_decomp input")
+            wsb = int(lib.thorn_ns_workspace_bytes(nb, R, C))
+            ws = torch.empty(max(256, wsb), dtype=torch.uint8, device=dev)
+            iters = len(coeffs) // 3
+            cc = (N.ctypes.c_double * max(1, len(coeffs)))(*coeffs)
+            rr = (N.ctypes.c_int32 * max(1, len(restarts)))(*restarts)
             N.check(lib.thorn_ns_batched(xin.data_ptr(), out.data_ptr(), ws.data_ptr(), wsb, nb, R, C, N.F16, cc,
-                                         iters, rr, len(restarts), _err_flag(dev).data_ptr(), N.stream_of(dev)),
-                    "polar_decomp")
+                                         iters, rr, len(restarts), _err_flag(dev).data_ptr(), st), "polar_decomp")
+        # the fp16 result converted to X's dtype (a dtype conversion, as in thorn.py:662)
     return out.reshape(*batch, R, C).to(X.dtype)
 
 
