@@ -21,7 +21,6 @@ by running the reference itself (``tests/golden/make_golden.py``).
 """
 from __future__ import annotations
 
-import math
 from itertools import combinations
 
 import numpy as np

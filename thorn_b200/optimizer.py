@@ -23,7 +23,6 @@ Extensions (all optional, off by default):
 from __future__ import annotations
 
 import ctypes
-import math
 from dataclasses import MISSING, dataclass, field, fields
 from functools import partial
 from math import prod
@@ -34,7 +33,6 @@ import torch.distributed as dist
 import torch.nn as nn
 import torch.nn.functional as F
 from torch.distributed.tensor import DTensor, Replicate
-from torch.nn import Parameter
 from torch.optim import Optimizer
 
 from . import _native as N
