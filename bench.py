@@ -679,6 +679,82 @@ def ortho_only(args):
                       "finite": bool(all(torch.isfinite(p).all() for p in ps))}), flush=True)
 
 
+def small_config_groups(name):
+    """(groups, param dtype, state dtype, grad std) of BASELINE configs[0]-[2]: lists of
+    (orthogonalize, shapes, init std or None for ones, group options)."""
+    if name == "tiny":  # configs[0]
+        return [(True, [(512, 512)] * 4 + [(1024, 512)] * 2 + [(512, 1024)] * 2, 0.02,
+                 dict(lr=1e-3, weight_decay=0.1, scaling_mode="moonlight")),
+                (False, [(512,)] * 8, None, dict(lr=1e-3, weight_decay=0.0, scaling_mode="moonlight"))], \
+            "f32", "f32", 1e-3
+    if name == "vad":  # configs[1]: 24 Conv1d kernels flattened to out x (in*k), 4 + 2 Linear weights
+        convs = [[(64, 32, 3), (64, 64, 3), (128, 64, 5), (128, 128, 3)][i % 4] for i in range(24)]
+        mats = [(o, i * k) for o, i, k in convs] + [(128, 128)] * 4 + [(2, 128)] * 2
+        vecs = [(o,) for o, _, _ in convs for _ in range(3)] + [(128,)] * 4 + [(2,)] * 2
+        return [(True, mats, 0.05, dict(lr=1e-3, weight_decay=0.1)),
+                (False, vecs, 0.05, dict(lr=1e-3, weight_decay=0.0))], "f32", "f32", 1e-3
+    if name == "qwen300m":  # configs[2]: 20 layers, hidden 1024, tied embedding
+        layer = [(2048, 1024), (1024, 1024), (1024, 1024), (1024, 2048), (3072, 1024), (3072, 1024), (1024, 3072)]
+        norms = [(1024,), (1024,), (128,), (128,)] * 20 + [(1024,)]
+        return [(True, layer * 20, 0.02, dict(lr=1e-3, weight_decay=0.1)),
+                (False, [(151936, 1024)], 0.02, dict(lr=1e-3, weight_decay=0.1)),
+                (False, norms, None, dict(lr=1e-3, weight_decay=0.0))], "bf16", "f32", 1e-4
+    raise ValueError(name)
+
+
+def small_config(args):
+    """Time THORN steps on BASELINE configs[0]-[2] (one GPU): device time per step, the NS phase
+    and the host time to enqueue a step (these configs are launch- and host-bound)."""
+    import torch
+
+    from thorn_b200 import THORN
+
+    groups, pdt, sdt, gstd = small_config_groups(args.model)
+    dtypes = {"f32": torch.float32, "bf16": torch.bfloat16}
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    apply_switches(args)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    params, grads, tg = [], [], []
+    for ortho, shapes_, std, opts in groups:
+        ps = [torch.nn.Parameter(torch.ones(s, device=dev, dtype=dtypes[pdt]) if std is None else
+                                 torch.randn(s, device=dev, dtype=dtypes[pdt], generator=gen) * std) for s in shapes_]
+        grads += [torch.randn(s, device=dev, dtype=dtypes[pdt], generator=gen) * gstd for s in shapes_]
+        params += ps
+        tg.append({"orthogonalize": ortho, "params": ps, "state_dtype": dtypes[sdt], **opts})
+    opt = THORN(tg)
+    opt.profile_ns = []
+
+    def step():
+        for p, g in zip(params, grads):
+            p.grad = g
+        opt.step()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    opt.profile_ns = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    h0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    prof, opt.profile_ns = opt.profile_ns, None
+    ns_ms = sum(a.elapsed_time(b) for a, b, *_ in prof) / args.steps
+    ns_dense = sum(d for _, _, d, _, _ in prof) / args.steps
+    print(json.dumps({"model": args.model, "ms_per_step": round(ms, 4), "host_ms_per_step": round(host_ms, 3),
+                      "ns_ms_per_step": round(ns_ms, 4),
+                      "ns_dense_tflops": round(ns_dense / (ns_ms * 1e-3) / 1e12, 1) if ns_ms > 0 else None,
+                      "params": sum(p.numel() for p in params), "param_dtype": pdt, "state_dtype": sdt,
+                      "err_flag": int(opt.device_error()),
+                      "finite": bool(all(torch.isfinite(p).all() for p in params))}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -704,11 +780,15 @@ def main():
     ap.add_argument("--ns-library", action="store_true",
                     help="with --ns-only: time the same recurrences on torch/cuBLAS GEMMs instead (library baseline)")
     ap.add_argument("--layers", type=int, default=None, help="transformer layers (profiling runs use fewer)")
-    ap.add_argument("--model", default="llama8b", choices=["llama8b", "llama70b"],
-                    help="parameter set: llama8b (BASELINE configs[3], the headline) or llama70b (configs[4], 8 GPUs)")
+    ap.add_argument("--model", default="llama8b", choices=["llama8b", "llama70b", "tiny", "vad", "qwen300m"],
+                    help="parameter set: llama8b (BASELINE configs[3], the headline), llama70b (configs[4], 8 "
+                         "GPUs), or tiny / vad / qwen300m (configs[0]-[2], one GPU, step timing only)")
     ap.add_argument("--ortho-only", default=None,
                     help="BxRxC: time steps of one decouple_md group of B bf16 RxC matrices (profiling)")
     args = ap.parse_args()
+    if args.model in ("tiny", "vad", "qwen300m"):
+        small_config(args)
+        return
     if args.model == "llama70b":
         use_llama70b()
     if args.layers is None:
