@@ -46,6 +46,12 @@ def test_assign_owners_balanced_and_deterministic():
     assert owners == assign_owners(flops, 8)
     assert assign_owners([5, 3, 3, 1], 2) == [0, 1, 1, 0]
     assert assign_owners([7], 4) == [0]
+    # a rotating start: one matrix per call goes round the ranks; a balanced set stays balanced
+    assert [assign_owners([7], 4, start)[0] for start in range(6)] == [0, 1, 2, 3, 0, 1]
+    for start in range(8):
+        rot = assign_owners(flops, 8, start)
+        load = [sum(f for f, o in zip(flops, rot) if o == r) for r in range(8)]
+        assert max(load) == min(load)
 
 
 def _exchange_worker(rank, world, port, result, impl="rounds"):

@@ -71,18 +71,20 @@ def ns_flops(rows: int, cols: int, iters: int) -> int:
     return iters * ((m ** 3) * 2 + (m ** 2 * n) * 4 + m * n * 2 + m ** 2 * 3)
 
 
-def assign_owners(flops: list[int], world: int) -> list[int]:
+def assign_owners(flops: list[int], world: int, start: int = 0) -> list[int]:
     """Longest-processing-time assignment: heaviest matrix first, to the least-loaded rank.
 
-    Ties go to the lower matrix index and the lower rank, so every rank computes
-    the same assignment.  (The reference deals sorted matrices round-robin,
-    thorn.py:1348-1372; both balance the Llama sets exactly.)
+    Ties go to the lower matrix index and to the first rank counting from ``start``, so
+    every rank computes the same assignment.  (The reference deals sorted matrices
+    round-robin, thorn.py:1348-1372; both balance the Llama sets exactly.)  ``start``
+    rotates from call to call: steps of one matrix at a time (gradient release) then
+    spread their Newton-Schulz work over the ranks instead of all landing on rank 0.
     """
     order = sorted(range(len(flops)), key=lambda j: (-flops[j], j))
     load = [0] * world
     owner = [0] * len(flops)
     for j in order:
-        r = min(range(world), key=lambda k: (load[k], k))
+        r = min(range(world), key=lambda k: (load[k], (k - start) % world))
         owner[j] = r
         load[r] += flops[j]
     return owner
@@ -324,7 +326,9 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
     # NS input rows (owner buffers and send slabs) use the padded leading dimension the
     # NS kernels need (16-byte TMA rows); results come back unpadded
     ld = [int(lib.thorn_ns_ld(it.C)) for it in items]
-    owners = assign_owners([ns_flops(rows_g[j], it.C, cfg.iters) for j, it in enumerate(items)], world)
+    start = getattr(opt, "_owner_start", 0) % world
+    owners = assign_owners([ns_flops(rows_g[j], it.C, cfg.iters) for j, it in enumerate(items)], world, start)
+    opt._owner_start = start + len(items)  # the same on every rank: every rank steps the same matrices
 
     def owner_chunks(r):
         """NS batches of owner r: its matrices by (global shape, dtypes), in batches of at
