@@ -186,6 +186,14 @@ CASES = {
         dict(orthogonalize=True, shapes=[(6, 8, 8)], init=("normal", 0.05), dtype="f32",
              opts=dict(lr=4e-3, decouple_md=True)),
     ]),
+    # Matrices with fewer rows than ranks on the FSDP2 path: at world 2 the one-row matrices leave
+    # the second shard empty (with and without MD).
+    "shard_tiny_rows": dict(steps=3, grad_std=1e-3, groups=[
+        dict(orthogonalize=True, shapes=[(1, 64), (3, 32), (66, 37)], init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=2e-3, weight_decay=0.1)),
+        dict(orthogonalize=True, shapes=[(1, 48), (5, 40)], init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=8e-3, decouple_md=True)),
+    ]),
     # update_rate 2 on one device (what setup_gradient_release(update_rate=2) sets): the moments
     # and the step count advance every step, the parameters every second step (thorn.py:1395,
     # 1681, 1707).

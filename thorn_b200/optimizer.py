@@ -249,9 +249,10 @@ class _Arena:
     def zeros(self, n):
         return self.alloc(n, "z")
 
-    def materialize(self, device):
+    def materialize(self, device, zero=()):
+        """Allocate the regions; "z" and the regions named in ``zero`` start at zero."""
         for reg, n in self.sizes.items():
-            make = torch.zeros if reg == "z" else torch.empty
+            make = torch.zeros if (reg == "z" or reg in zero) else torch.empty
             self.bufs[reg] = make(max(4, n), dtype=torch.float32, device=device)
 
     def region(self, name):

@@ -22,8 +22,8 @@ and scatters fp32 results back.  Here, per step:
 6. every rank applies the update to its own rows (and, with decouple_md,
    all-reduces ||p||^2 for the renorm).
 
-Shards follow DTensor's ``torch.chunk`` split, so rows need not divide evenly
-(a split that leaves a shard empty is rejected).  With ``pipeline_exchange``
+Shards follow DTensor's ``torch.chunk`` split, so rows need not divide evenly,
+and a matrix with fewer rows than ranks leaves some shards empty.  With ``pipeline_exchange``
 steps 3-5 run in waves of NS batches so transfers overlap the owners' NS; with
 ``exchange = "all_to_all"`` each exchange is one ``all_to_all_single``.  Magma
 masking all-reduces its three sums over the shard group first; a masked matrix,
@@ -259,9 +259,6 @@ def sharded_ortho_step(opt, params, cfg) -> None:
     for p in params:
         if p.ndim == 2:
             parts = shard_rows(p.shape[0], world)
-            if any(n == 0 for _, n in parts):
-                raise NotImplementedError(f"Shard(0) split with an empty shard: {p.shape[0]} rows over {world} "
-                                          "ranks")
             if _local(p).shape[0] != parts[me][1]:
                 raise ValueError(f"local shard of {_local(p).shape[0]} rows does not follow the Shard(0) split of "
                                  f"{p.shape[0]} rows over {world} ranks")
@@ -363,7 +360,9 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
     for ci, (R, C, pdt, sdt, js) in enumerate(chunks):
         if cfg.needs_pnn(R, C):
             pnn_h[ci] = (arena.empty(len(js) * R), arena.empty(2 * len(js)))
-    arena.materialize(dev)
+    # a rank whose shard of a matrix has no rows (fewer rows than ranks) launches no block for
+    # it, so that matrix's entries of the all-reduced sums start at zero
+    arena.materialize(dev, zero=("red1", "red2") if any(it.R == 0 for it in items) else ())
 
     # 1. momentum pass on local rows, then one all-reduce of the partial sums
     if md:
