@@ -8,9 +8,13 @@ param=None)`` (thorn.py:1738-1753), ``setup_gradient_release``
 optimizer-state layout (thorn.py:1591-1634), so ``state_dict`` /
 ``load_state_dict`` round-trip between the two.
 
-Every numeric operation of the step is a kernel of ``libthorn_b200.so`` called
-through its C ABI; host code only plans launches and allocates scratch from
-the torch caching allocator.  Parameters must live on a CUDA device; there is
+Every pass over parameters, gradients and state (momentum, Newton-Schulz,
+per-neuron norm, weight decay and apply, (R)AdamW, magnitude-direction
+decoupling) is a kernel of ``libthorn_b200.so`` called through its C ABI.  Host
+code plans launches and allocates scratch from the torch caching allocator.  Two
+optional features use torch ops on the device the way the reference does: Magma's
+three sums and score (thorn.py:806-836) and the row gather/scatter of sparse
+gradients (thorn.py:1669-1698).  Parameters must live on a CUDA device; there is
 no CPU path.
 
 Extensions (all optional, off by default):
