@@ -486,10 +486,14 @@ class Group:
         return (-2, -1) if p.ndim > 1 else (-1,)
 
     def target_norm_(self, p, dt):
-        """thorn.py:597-612 for the string modes (callables are not modelled)."""
+        """thorn.py:597-612.  A callable target gets the parameter as a float32 numpy array
+        (the reference passes the torch tensor); its float or array result is rounded to
+        the parameter dtype, like the reference's ``torch.full`` / ``.to(dtype)``."""
         tn = self.target_norm
         if tn is None:
             tn = "max" if self.orthogonalize else "init"
+        if callable(tn):
+            return rnd(np.asarray(tn(p), dtype=F32), dt)
         if tn == "init":
             val = np.sqrt(np.sum(p.astype(np.float64) ** 2, axis=self.norm_axes(p), keepdims=True))
             return rnd(val, dt)

@@ -15,6 +15,12 @@ import torch
 TORCH_DTYPES = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
 
 
+def _fro(p) -> float:
+    """Frobenius norm of a torch tensor or a numpy array, as a Python float (float64 sum)."""
+    a = p.detach().double().cpu().numpy() if isinstance(p, torch.Tensor) else np.asarray(p, dtype=np.float64)
+    return float(np.sqrt((a * a).sum()))
+
+
 def _conv_flat(shape):
     o, i, k = shape
     return (o, i * k)
@@ -193,6 +199,14 @@ CASES = {
              opts=dict(lr=2e-3, weight_decay=0.1)),
         dict(orthogonalize=True, shapes=[(1, 48), (5, 40)], init=("normal", 0.02), dtype="f32",
              opts=dict(lr=8e-3, decouple_md=True)),
+    ]),
+    # A callable target norm (thorn.py:601-602) on both group kinds with decouple_md: half the
+    # initial Frobenius norm, as a Python float.
+    "md_target_fn_small": dict(steps=3, grad_std=1e-3, groups=[
+        dict(orthogonalize=True, shapes=[(64, 48), (32, 96)], init=("normal", 0.02), dtype="f32",
+             opts=dict(lr=8e-3, decouple_md=True, target_norm=lambda p: 0.5 * _fro(p))),
+        dict(orthogonalize=False, shapes=[(40, 12)], init=("normal", 0.5), dtype="f32",
+             opts=dict(lr=1e-3, decouple_md=True, target_norm=lambda p: 0.5 * _fro(p))),
     ]),
     # update_rate 2 on one device (what setup_gradient_release(update_rate=2) sets): the moments
     # and the step count advance every step, the parameters every second step (thorn.py:1395,

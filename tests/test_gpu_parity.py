@@ -539,11 +539,11 @@ def test_md_options_match_oracle():
     assert any(k[2] == "grad_after" for k in worst)
 
 
-def test_md_conv_kernels_match_oracle():
+@pytest.mark.parametrize("name", ["md_conv_small", "md_target_fn_small"])
+def test_md_conv_kernels_and_target_fn_match_oracle(name):
     """decouple_md on 3-D conv kernels (batches of matrices with per-entry row and column gains)
-    and the "init" target norm on an orthogonalized group; against the oracle, pinned to the
-    reference's goldens for this case."""
-    name = "md_conv_small"
+    and the "init" target norm on an orthogonalized group; a callable target norm on both group
+    kinds; against the oracle, pinned to the reference's goldens for these cases."""
     _, gpu = run_gpu(name)
     _, orc = P.run_oracle(name)
     init = [[t.float().numpy() for t in g] for g in C.build_params(C.CASES[name])]

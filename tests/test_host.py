@@ -361,7 +361,7 @@ def test_local_paths_run_through_stub_library(monkeypatch, magma):
 @pytest.mark.parametrize("name", ["tiny_small", "md_small", "bf16_small", "conv_small", "variants_small", "vad",
                                   "tiny", "edge_small", "magma_small", "sparse_small", "shard_uneven",
                                   "magma_shard", "md_axis_small", "rate_small", "md_options_small",
-                                  "md_conv_small"])
+                                  "md_conv_small", "md_target_fn_small"])
 def test_state_keys_and_shapes_match_reference_goldens(name, golden_dir):
     """Checkpoint compatibility: the state THORN initialises for every parameter of a case has
     exactly the keys, and the shapes, of the reference's own state after its first step (as the
