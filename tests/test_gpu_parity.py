@@ -596,6 +596,13 @@ def test_custom_ops_match_c_abi():
     want = 0.5 * (A.float() @ A.float().transpose(1, 2)) - Cs.float()
     assert (out.float() - want).abs().max() <= 2e-2 * want.abs().max()
     assert torch.equal(out, out.transpose(1, 2))
+    # M and K that are not multiples of 8 (zero-padded inside the operator)
+    A2 = (torch.randn(2, 37, 20, device="cuda") / 8).half()
+    C2 = torch.randn(2, 37, 37, device="cuda").half()
+    C2 = (C2 + C2.transpose(1, 2)) / 2
+    out2 = torch.ops.thorn_b200.sym_addmm(A2, A2.transpose(1, 2), C2, 1.0, 0.5)
+    want2 = A2.float() @ A2.float().transpose(1, 2) + 0.5 * C2.float()
+    assert out2.shape == (2, 37, 37) and (out2.float() - want2).abs().max() <= 2e-2 * want2.abs().max()
     co = optimal_composition(1e-3, 5, 0.03, 0.02)
     rs = gram_ns_restarts(*co)
     for shape in [(2, 384, 128), (1, 100, 37)]:

@@ -19,6 +19,7 @@ from math import prod
 from typing import List, Optional
 
 import torch
+import torch.nn.functional as F
 
 from . import _native as N
 
@@ -48,8 +49,8 @@ def sym_addmm(A: torch.Tensor, B: torch.Tensor, C: Optional[torch.Tensor], alpha
               beta: float) -> torch.Tensor:
     """``beta * C + alpha * (A @ B)`` with ``A @ B`` and ``C`` symmetric.
 
-    A: (..., M, K), B: (..., K, M), C: (..., M, M), (M, M) or None; fp16 or bf16,
-    M and K multiples of 8.  Returns (..., M, M), exactly symmetric.
+    A: (..., M, K), B: (..., K, M), C: (..., M, M), (M, M) or None; fp16 or bf16.
+    Returns (..., M, M), exactly symmetric.
     """
     _check_cuda(A, B, C)
     if A.dtype not in _HALF or B.dtype != A.dtype or (C is not None and C.dtype != A.dtype):
@@ -61,21 +62,29 @@ def sym_addmm(A: torch.Tensor, B: torch.Tensor, C: Optional[torch.Tensor], alpha
         raise ValueError(f"B must be {(*batch, K, M)}, got {tuple(B.shape)}")
     if C is not None and not (tuple(C.shape) == (M, M) or tuple(C.shape) == (*batch, M, M)):
         raise ValueError(f"C must be {(*batch, M, M)} or {(M, M)}, got {tuple(C.shape)}")
-    if M % 8 or K % 8:
-        raise ValueError("sym_addmm needs M and K to be multiples of 8 (16-byte TMA rows)")
     nn = prod(batch) if batch else 1
     a = A.reshape(nn, M, K).contiguous()
     b = B.reshape(nn, K, M).contiguous()
     c_batched = C is not None and C.ndim > 2
     c = None if C is None else (C.reshape(nn, M, M) if c_batched else C).contiguous()
-    out = torch.empty((nn, M, M), dtype=A.dtype, device=A.device)
+    # the kernel's TMA rows need M and K in multiples of 8: zero rows and columns are
+    # appended (zeros along K add nothing to A @ B; the extra output rows and columns
+    # are dropped), which the reference's Triton kernel does not need
+    Mp, Kp = -(-M // 8) * 8, -(-K // 8) * 8
+    if (Mp, Kp) != (M, K):
+        a = F.pad(a, (0, Kp - K, 0, Mp - M))
+        b = F.pad(b, (0, Mp - M, 0, Kp - K))
+        c = None if c is None else F.pad(c, (0, Mp - M, 0, Mp - M))
+    out = torch.empty((nn, Mp, Mp), dtype=A.dtype, device=A.device)
     if nn and M:
         lib = N.load()
         with torch.cuda.device(A.device):
             N.check(lib.thorn_sym_addmm(a.data_ptr(), b.data_ptr(), None if c is None else c.data_ptr(),
-                                        out.data_ptr(), nn, M, K, 1 if c_batched else 0, float(alpha), float(beta),
-                                        N.dtype_code(A.dtype), _err_flag(A.device).data_ptr(),
+                                        out.data_ptr(), nn, Mp, Kp, 1 if c_batched else 0, float(alpha),
+                                        float(beta), N.dtype_code(A.dtype), _err_flag(A.device).data_ptr(),
                                         N.stream_of(A.device)), "sym_addmm")
+    if Mp != M:
+        out = out[:, :M, :M].contiguous()
     return out.reshape(*batch, M, M)
 
 
