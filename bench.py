@@ -65,9 +65,9 @@ def use_llama70b():
     WORKLOAD = "llama3-70b-fsdp2 (BASELINE configs[4])"
 
 
-# DRAM bytes (read + write) of one ns_gemm2_kernel launch from the ncu capture in
-# profiles/ns_gemm_2x4096.md: X X^T on two 4096x4096 matrices (K = 4096), whose
-# compulsory traffic is 67 MB read + 67 MB written.
+# DRAM bytes (read + write) of one ns_gemm2_kernel launch from an ncu capture of
+# X X^T on two 4096x4096 matrices (K = 4096), whose compulsory traffic is 67 MB
+# read + 67 MB written.
 NS_GEMM_TRAFFIC = 100.1e6
 NS_GEMM_TRAFFIC_CASE = "one X X^T launch on 2 x 4096x4096 (K=4096); compulsory 67 MB read + 67 MB write"
 
