@@ -33,6 +33,7 @@ def main():
     ap.add_argument("--case", required=True)
     ap.add_argument("--out", required=True)
     ap.add_argument("--pipeline-exchange", action="store_true")
+    ap.add_argument("--exchange", default="rounds", choices=["rounds", "all_to_all"])
     args = ap.parse_args()
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local_rank)
@@ -50,6 +51,7 @@ def main():
     opt = THORN(C.group_dicts(case, tp))
     opt._update_rate = case.get("update_rate", 1)  # what setup_gradient_release(update_rate=...) sets
     opt.pipeline_exchange = args.pipeline_exchange
+    opt.exchange = args.exchange
     out = {}
     for s in range(case["steps"]):
         for ps, gs in zip(tp, C.build_grads(case, s)):

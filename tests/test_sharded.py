@@ -244,6 +244,7 @@ def _sharded_compare(got, orc, name, init):
 
 
 PIPE = ("--pipeline-exchange",)
+A2A = ("--exchange", "all_to_all")
 
 
 @pytest.mark.gpu
@@ -252,7 +253,7 @@ PIPE = ("--pipeline-exchange",)
                                         ("shard_uneven", PIPE), ("md_shard", PIPE),
                                         ("magma_shard", ()), ("magma_shard", PIPE), ("rate_shard", ()),
                                         ("shard_odd_cols", ()), ("shard_odd_cols", PIPE),
-                                        ("shard_tiny_rows", ())])
+                                        ("shard_tiny_rows", ()), ("shard_uneven", A2A), ("md_shard", A2A + PIPE)])
 def test_sharded_step_matches_oracle(world, name, extra, tmp_path):
     """The Shard(0) path (rounds or waves of the exchange, Magma masking whole matrices)
     against the oracle's sharded semantics; the oracle replays the run's Magma seeds."""
