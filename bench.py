@@ -271,6 +271,58 @@ def stall_watchdog(rank, limit_s):
     threading.Thread(target=run, daemon=True).start()
 
 
+def result_line(args, world, ms, ns_launch_ms, ns_dense_all, ns_exec_all, mom_ms, mom_bytes, cpu, e2e, host_ms,
+                host_enqueue_ms, launches, clocks) -> dict:
+    """The JSON line of a GPU run (rank 0) from its measurements: device time per step, the
+    NS phase (ms per step, dense-equivalent and executed FLOPs of all ranks), the momentum
+    pass (ms and compulsory bytes per step), the CPU baseline, the end-to-end figure, host
+    times, launch count and clock record."""
+    hbm, peak_burst, peak_sus, peak_src = load_peaks()
+    peak_job = peak_sus * world  # whole-job peak: the NS work is spread over all ranks
+    achieved = ns_dense_all / (ns_launch_ms * 1e-3) / 1e12 if ns_launch_ms > 0 else None
+    achieved_exec = ns_exec_all / (ns_launch_ms * 1e-3) / 1e12 if ns_launch_ms > 0 else None
+    ortho_s, adam_s = shapes(args.layers)
+    line = {
+        "metric": METRIC, "value": round(ms, 3), "unit": "ms", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": WORKLOAD + (" sharded Shard(0)" if world > 1 else "")
+                   + ("" if args.layers == LAYERS else f" REDUCED to {args.layers} layers (profiling only)"),
+                   "ortho_matrices": len(ortho_s), "adamw_tensors": len(adam_s),
+                   "params": sum(math.prod(s) for s in ortho_s + adam_s), "param_dtype": "bf16",
+                   "state_dtype": "f32", "ns_dtype": "f16", "decouple_md": MD, "lr": ORTHO_LR,
+                   "parallelism": f"fsdp{world}" if world > 1 else "single",
+                   "l2": "no flush: every step reads params, grads and state (~70 GB) >> 126 MB L2"},
+        "roofline": {"bound": "tensor", "kernel": "ns_gemm2_kernel (Newton-Schulz phase)",
+                     "achieved": round(achieved, 1) if achieved else None, "peak": round(peak_job, 1),
+                     "unit": "TFLOP/s", "frac": round(achieved / peak_job, 3) if achieved else None,
+                     "traffic": NS_GEMM_TRAFFIC,
+                     "traffic_case": NS_GEMM_TRAFFIC_CASE,
+                     "flops": "dense-equivalent (2MNK per reference GEMM)",
+                     "achieved_executed": round(achieved_exec, 1) if achieved_exec else None,
+                     "peak_source": f"{peak_src} sustained bf16 (MEASURED_PEAKS.json) x {world} GPU(s); "
+                                    f"burst {peak_burst} per GPU",
+                     "ns_ms_per_step": round(ns_launch_ms, 3),
+                     "ns_dense_tflop_per_step": round(ns_dense_all / 1e12, 2)},
+        "roofline_elementwise": {
+            "bound": "hbm", "kernel": "ortho_pre_kernel + pre_reduce_kernel (momentum pass)",
+            "achieved": round(mom_bytes / (mom_ms * 1e-3) / 1e9, 1) if mom_ms > 0 else None,
+            "peak": round(hbm * world, 1), "unit": "GB/s",
+            "frac": round(mom_bytes / (mom_ms * 1e-3) / 1e9 / (hbm * world), 3) if mom_ms > 0 else None,
+            "bytes": ("g read + m read/write + p read/write (decouple_md), compulsory" if MD
+                      else "g read + m read/write, compulsory"),
+            "ms_per_step": round(mom_ms, 3), "gb_per_step": round(mom_bytes / 1e9, 2)},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "host_ms_per_step": round(host_ms, 2),
+        "host_enqueue_ms_idle_gpu": round(host_enqueue_ms, 2),
+        "gpu_launches": int(launches),
+        "gpu_launches_per_step": round(launches / args.steps, 1),
+        "clocks": clocks,
+    }
+    return line
+
+
 def gpu_arm(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -492,54 +544,13 @@ def gpu_arm(args, rank, world, local_rank):
 
     if rank != 0:
         return
-    hbm, peak_burst, peak_sus, peak_src = load_peaks()
-    peak_job = peak_sus * world  # whole-job peak: the NS work is spread over all ranks
-    achieved = ns_dense_all / (ns_launch_ms * 1e-3) / 1e12 if ns_launch_ms > 0 else None
-    achieved_exec = ns_exec_all / (ns_launch_ms * 1e-3) / 1e12 if ns_launch_ms > 0 else None
     cpu = None
     if not args.no_cpu_baseline and world == 1:
         v, sample, secs = cpu_oracle_sample()
         cpu = {"value": round(v, 3), "unit": "ms", "cores": os.cpu_count() or 1, "kind": "port", "sample": sample,
                "sample_cpu_seconds": round(secs, 2)}
-    ortho_s, adam_s = shapes(args.layers)
-    line = {
-        "metric": METRIC, "value": round(ms, 3), "unit": "ms", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": WORKLOAD + (" sharded Shard(0)" if world > 1 else "")
-                   + ("" if args.layers == LAYERS else f" REDUCED to {args.layers} layers (profiling only)"),
-                   "ortho_matrices": len(ortho_s), "adamw_tensors": len(adam_s),
-                   "params": sum(math.prod(s) for s in ortho_s + adam_s), "param_dtype": "bf16",
-                   "state_dtype": "f32", "ns_dtype": "f16", "decouple_md": MD, "lr": ORTHO_LR,
-                   "parallelism": f"fsdp{world}" if world > 1 else "single",
-                   "l2": "no flush: every step reads params, grads and state (~70 GB) >> 126 MB L2"},
-        "roofline": {"bound": "tensor", "kernel": "ns_gemm2_kernel (Newton-Schulz phase)",
-                     "achieved": round(achieved, 1) if achieved else None, "peak": round(peak_job, 1),
-                     "unit": "TFLOP/s", "frac": round(achieved / peak_job, 3) if achieved else None,
-                     "traffic": NS_GEMM_TRAFFIC,
-                     "traffic_case": NS_GEMM_TRAFFIC_CASE,
-                     "flops": "dense-equivalent (2MNK per reference GEMM)",
-                     "achieved_executed": round(achieved_exec, 1) if achieved_exec else None,
-                     "peak_source": f"{peak_src} sustained bf16 (MEASURED_PEAKS.json) x {world} GPU(s); "
-                                    f"burst {peak_burst} per GPU",
-                     "ns_ms_per_step": round(ns_launch_ms, 3),
-                     "ns_dense_tflop_per_step": round(ns_dense_all / 1e12, 2)},
-        "roofline_elementwise": {
-            "bound": "hbm", "kernel": "ortho_pre_kernel + pre_reduce_kernel (momentum pass)",
-            "achieved": round(mom_bytes / (mom_ms * 1e-3) / 1e9, 1) if mom_ms > 0 else None,
-            "peak": round(hbm * world, 1), "unit": "GB/s",
-            "frac": round(mom_bytes / (mom_ms * 1e-3) / 1e9 / (hbm * world), 3) if mom_ms > 0 else None,
-            "bytes": ("g read + m read/write + p read/write (decouple_md), compulsory" if MD
-                      else "g read + m read/write, compulsory"),
-            "ms_per_step": round(mom_ms, 3), "gb_per_step": round(mom_bytes / 1e9, 2)},
-        "cpu_baseline": cpu,
-        "e2e": e2e,
-        "host_ms_per_step": round(host_ms, 2),
-        "host_enqueue_ms_idle_gpu": round(host_enqueue_ms, 2),
-        "gpu_launches": int(launches),
-        "gpu_launches_per_step": round(launches / args.steps, 1),
-        "clocks": clocks,
-    }
+    line = result_line(args, world, ms, ns_launch_ms, ns_dense_all, ns_exec_all, mom_ms, mom_bytes, cpu, e2e,
+                       host_ms, host_enqueue_ms, launches, clocks)
     print(json.dumps(line), flush=True)
 
 

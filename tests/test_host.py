@@ -405,3 +405,37 @@ def test_ns_recurrences_equal_composed_polynomial(shape):
     want = u @ torch.diag_embed(s) @ vh
     got = ns_library(X, co, rs)
     assert float((got - want).norm() / want.norm()) < 1e-12
+
+
+def test_bench_line_carries_the_contract_keys():
+    """bench.py's JSON line (built by ``result_line`` from a run's measurements): every key the
+    bench contract asks for, the whole-job roofline arithmetic, and the end-to-end object."""
+    import argparse
+    import json
+
+    import bench
+
+    args = argparse.Namespace(steps=5, warmup=3, layers=bench.LAYERS)
+    e2e = {"value": 400.0, "unit": "ms", "h2d_bytes_per_step": 16 << 30, "d2h_bytes_per_step": 16 << 30,
+           "mode": "pipelined"}
+    cpu = {"value": 1.4e6, "unit": "ms", "cores": 16, "kind": "port", "sample": "s"}
+    clocks = {"sm_mhz": 1400.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"]}
+    line = bench.result_line(args, 2, 200.0, 150.0, 505.5e12, 321.5e12, 10.0, 49e9, cpu, e2e, 9.0, 18.0, 3485,
+                             clocks)
+    json.dumps(line)  # serialisable
+    for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+              "vs_baseline", "dtype", "data", "config", "roofline", "cpu_baseline", "e2e", "gpu_launches", "clocks"):
+        assert k in line, k
+    assert line["higher_is_better"] is False and line["n_gpus"] == 2 and line["value"] == 200.0
+    assert "workload" in line["config"] and "model" not in line["config"]
+    r = line["roofline"]
+    for k in ("bound", "achieved", "peak", "unit", "frac", "traffic"):
+        assert k in r, k
+    _, _, peak_sus, _ = bench.load_peaks()
+    assert r["peak"] == pytest.approx(2 * peak_sus, abs=0.1)  # whole-job peak at 2 GPUs
+    assert r["achieved"] == pytest.approx(505.5e12 / 0.150 / 1e12, rel=1e-3)
+    assert r["frac"] == pytest.approx(r["achieved"] / r["peak"], abs=1e-3)
+    el = line["roofline_elementwise"]
+    assert el["achieved"] == pytest.approx(49e9 / 0.010 / 1e9, rel=1e-3)
+    assert set(line["e2e"]) >= {"value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step"}
+    assert line["gpu_launches"] == 3485 and line["cpu_baseline"]["kind"] == "port"
