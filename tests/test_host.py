@@ -439,3 +439,22 @@ def test_bench_line_carries_the_contract_keys():
     assert el["achieved"] == pytest.approx(49e9 / 0.010 / 1e9, rel=1e-3)
     assert set(line["e2e"]) >= {"value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step"}
     assert line["gpu_launches"] == 3485 and line["cpu_baseline"]["kind"] == "port"
+
+
+def test_bench_reference_arm_line(monkeypatch, capsys):
+    """bench.py --impl reference: rank 0 prints one line with impl, cpu_baseline and an e2e of
+    the line's own value with no host-device bytes; other ranks print nothing."""
+    import argparse
+    import json
+
+    import bench
+
+    monkeypatch.setattr(bench, "cpu_oracle_sample", lambda warm_only=False: None if warm_only else (1234.5, "s", 2.0))
+    args = argparse.Namespace(steps=2, warmup=1, gpus=1, model="llama8b")
+    bench.reference_arm(args, 1)
+    assert capsys.readouterr().out == ""
+    bench.reference_arm(args, 0)
+    line = json.loads(capsys.readouterr().out.strip())
+    assert line["impl"] == "reference" and line["value"] == 1234.5 and line["higher_is_better"] is False
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["value"] == 1234.5
+    assert line["e2e"] == {"value": 1234.5, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
