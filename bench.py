@@ -389,6 +389,7 @@ def gpu_arm(args, rank, world, local_rank):
         time.sleep(0.3)
     opt.profile_ns = []
     opt.profile_momentum = []
+    opt.profile_stages = [] if world > 1 else None
     launches0 = _native.launch_count()
     barrier()
     torch.cuda.synchronize()
@@ -410,6 +411,8 @@ def gpu_arm(args, rank, world, local_rank):
     opt.profile_ns = None
     prof_m = opt.profile_momentum
     opt.profile_momentum = None
+    stages = stage_times(torch, dist, dev, opt.profile_stages, args.steps) if world > 1 else None
+    opt.profile_stages = None
     mom_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b, _ in prof_m) / args.steps)
     mom_bytes = sum(nb for _, _, nb in prof_m) / args.steps
     if world > 1:
@@ -551,7 +554,29 @@ def gpu_arm(args, rank, world, local_rank):
                "sample_cpu_seconds": round(secs, 2)}
     line = result_line(args, world, ms, ns_launch_ms, ns_dense_all, ns_exec_all, mom_ms, mom_bytes, cpu, e2e,
                        host_ms, host_enqueue_ms, launches, clocks)
+    if stages:
+        line["sharded_stages_ms"] = stages
     print(json.dumps(line), flush=True)
+
+
+def stage_times(torch, dist, dev, logs, steps):
+    """Per-stage device time of the sharded step (ms per step, max over ranks): each entry of
+    ``logs`` is one sharded step's list of (stage, event) marks on the launching stream."""
+    slots = 8  # every rank all-reduces the same fixed-size tensor, whatever it recorded
+    names = [n for n, _ in logs[0][1:]][:slots] if logs else []
+    tot = [0.0] * slots
+    ok = 1.0 if names else 0.0
+    for marks in logs or []:
+        if [n for n, _ in marks[1:]][:slots] != names:
+            ok = 0.0
+            break
+        for i in range(1, min(len(marks), slots + 1)):
+            tot[i - 1] += marks[i - 1][1].elapsed_time(marks[i][1])
+    t = torch.tensor([x / steps for x in tot] + [-ok], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)  # the last slot: -1 only if every rank recorded alike
+    if t[-1].item() != -1.0:
+        return None
+    return {n: round(float(v), 3) for n, v in zip(names, t[:len(names)].tolist())}
 
 
 def apply_switches(args):

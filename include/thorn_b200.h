@@ -81,6 +81,17 @@ THORN_API int thorn_set_gemm_pdl(int enable);
  * and output bulk stores an evict_first policy; zero (default) uses none.
  * Returns the previous setting.  Both settings give bit-identical results. */
 THORN_API int thorn_set_gemm_l2_hints(int enable);
+/* Limit, in nanoseconds of GPU global time, of every bounded wait inside the NS
+ * GEMMs (default 10 s; 0 restores the default).  A wait that runs out sets the
+ * call's err_flag, stops the CTA's other roles and frees its tensor memory, so
+ * the kernel returns and the context stays usable.  Returns the previous limit. */
+THORN_API uint64_t thorn_set_wait_limit_ns(uint64_t limit_ns);
+/* Failure test of the bounded waits: nonzero makes the NS GEMMs' TMA producers
+ * issue no loads, so no copy or MMA is ever in flight and the MMA warp's wait
+ * for its first operand stage runs out after the wait limit.  Results are
+ * undefined while set; zero (default) is the normal path.  Returns the previous
+ * setting.  For tests of the error path only. */
+THORN_API int thorn_set_gemm_test_stall(int enable);
 
 /* --------------------------------------------------------------------------
  * (R)Adam(-atan2)W over many tensors in one launch per dtype pair.
@@ -210,9 +221,12 @@ THORN_API int thorn_ns_batched(const void* x, void* out, void* workspace, int64_
  * THORN_ERR_TOO_LARGE (e.g. one 2896x2896 or 1024x8192 matrix fits).
  * The first call on a device looks up the array's device address (once per
  * device, with that device current); make that first call before any CUDA
- * stream capture.  All calls on a device share the one array and nothing in it
- * needs to start at zero, so calls that overlap on the GPU (two streams, two
- * host threads) race on it and must be serialised by the caller. */
+ * stream capture.  The address is cached for the life of the process: after
+ * cudaDeviceReset (or any other teardown of the device's primary context) it
+ * is stale, so do not use this entry point on that device again.  All calls on
+ * a device share the one array and nothing in it needs to start at zero, so
+ * calls that overlap on the GPU (two streams, two host threads) race on it and
+ * must be serialised by the caller. */
 #define THORN_NS_STATIC_WORKSPACE_BYTES (64ll * 1024 * 1024)
 THORN_API int thorn_ns_batched_static(const void* x, void* out, int64_t batch, int64_t rows, int64_t cols,
                                       int ns_dtype, const double* coeffs, int iters, const int32_t* restarts,
@@ -222,7 +236,10 @@ THORN_API int thorn_ns_batched_static(const void* x, void* out, int64_t batch, i
  * contract (thorn.py:298-363).  A [batch, M, K], B [batch, K, M],
  * C [batch, M, M] (c_batched) or [M, M] or NULL, O [batch, M, M]; all with
  * leading dimensions a multiple of 8 elements.  Only tiles on or below the
- * diagonal are computed; the upper triangle is the mirror of the lower. */
+ * diagonal are computed.  O is split into 128 x 128 blocks: diagonal blocks
+ * hold the computed values, each block below the diagonal is mirrored into
+ * the block above it (the reference's Triton kernel likewise keeps its
+ * diagonal tiles as computed and mirrors the others). */
 THORN_API int thorn_sym_addmm(const void* A, const void* B, const void* C, void* O, int64_t batch, int64_t M,
                     int64_t K, int c_batched, float alpha, float beta, int dtype, int* err_flag,
                     void* stream);

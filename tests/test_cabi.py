@@ -116,6 +116,12 @@ def test_argument_validation_without_gpu(lib):
     assert lib.thorn_ns_batched(None, None, None, 0, 1, 8, 8, 2, co, 1, rs, 0, None, None) == 1
     assert lib.thorn_ns_batched(None, None, None, 0, 0, 8, 8, 2, co, 1, rs, 0, None, None) == 0
     assert lib.thorn_ns_batched(1024, 2048, 4096, 1 << 30, 1, 8, 8, 0, co, 1, rs, 0, None, None) == 1  # f32 NS
+    # sizes whose workspace does not fit in int64 are rejected, not wrapped to a small or negative size
+    big = (1 << 31) - 1
+    assert lib.thorn_ns_workspace_bytes(big, big, big) == -1
+    assert lib.thorn_ns_workspace_bytes(1, 1 << 62, 3) == -1
+    assert lib.thorn_ns_batched(1024, 2048, 4096, 1 << 62, big, big, big, 2, co, 1, rs, 0, None, None) == 1
+    assert lib.thorn_ns_batched_static(1024, 2048, big, big, big, 2, co, 1, rs, 0, None, None) == 5  # too large
     # symmetric GEMM needs 8-element leading dimensions
     assert lib.thorn_sym_addmm(16, 16, None, 16, 1, 12, 16, 0, 1.0, 0.0, 2, None, None) == 2
     pre = N.array(N.OrthoPreTensor, [N.OrthoPreTensor(None, None, None, None, 1, 4, 4, None, None, 0, None, None,
@@ -127,7 +133,7 @@ def test_argument_validation_without_gpu(lib):
 
 @pytest.mark.parametrize("name,default", [("thorn_set_gemm_pair", 1), ("thorn_set_gemm_staged_epilogue", 1),
                                           ("thorn_set_elementwise_async", 0), ("thorn_set_gemm_pdl", 0),
-                                          ("thorn_set_gemm_l2_hints", 0)])
+                                          ("thorn_set_gemm_l2_hints", 0), ("thorn_set_gemm_test_stall", 0)])
 def test_kernel_switches(lib, name, default):
     """Each switch returns its previous setting; the defaults are the measured kernels."""
     fn = getattr(lib, name)
@@ -137,6 +143,15 @@ def test_kernel_switches(lib, name, default):
     assert fn(default) == 1 - default
     assert fn(7 if default else 0) == default  # any nonzero value means on
     fn(default)
+
+
+def test_wait_limit_setter(lib):
+    """The GEMM wait limit: returns the previous value; 0 restores the 10 s default."""
+    default = 10 * 10 ** 9
+    assert lib.thorn_set_wait_limit_ns(0) == default
+    assert lib.thorn_set_wait_limit_ns(20 * 10 ** 6) == default
+    assert lib.thorn_set_wait_limit_ns(0) == 20 * 10 ** 6
+    assert lib.thorn_set_wait_limit_ns(0) == default
 
 
 def _ctype_of(decl: str):

@@ -133,6 +133,20 @@ def test_bf16_params_with_fp32_state():
 
 
 # ---------------------------------------------------------------- NS / GEMM
+def assert_block_symmetric(o: torch.Tensor, blk: int = 128):
+    """A symmetric GEMM output (thorn::sym_addmm contract): outside the diagonal 128-blocks the
+    output is an exact mirror image; inside them every element is stored as computed (as the
+    reference's Triton kernel stores its diagonal tiles), which for a Gram product A A^T with a
+    symmetric C is symmetric up to one rounding."""
+    m = o.shape[-1]
+    idx = torch.arange(m, device=o.device) // blk
+    off = idx[:, None] != idx[None, :]
+    ot = o.transpose(-2, -1)
+    assert torch.equal(o[..., off], ot[..., off])
+    gap = (o.float() - ot.float()).abs().max().item()
+    assert gap <= 1e-3 * o.float().abs().max().item(), gap
+
+
 def _ns_gpu(u: torch.Tensor, ns_dtype=torch.float16, iters=5):
     """Polar factor of each matrix of u (B, R, C) via thorn_ns_batched (as numpy on the host)."""
     out, co, rs = _ns_gpu_t(u, ns_dtype, iters)
@@ -169,7 +183,7 @@ def _ns_gpu_t(u: torch.Tensor, ns_dtype=torch.float16, iters=5):
 
 @pytest.mark.parametrize("shape", [(1, 64, 64), (3, 128, 64), (2, 64, 128), (1, 512, 512), (1, 1024, 512),
                                    (1, 512, 1024), (4, 96, 32), (2, 2, 128), (6, 128, 384), (1, 300, 200),
-                                   (1, 1024, 4096), (1, 2048, 2048)])
+                                   (1, 1024, 4096), (1, 2048, 2048), (1, 66, 64), (2, 64, 66), (1, 260, 256)])
 def test_ns_matches_oracle(shape):
     torch.manual_seed(7)
     u = sum(torch.randn(shape) * (0.9 ** k) for k in range(4)) * 1e-3
@@ -177,6 +191,25 @@ def test_ns_matches_oracle(shape):
     O.NS_DTYPE = "f16"
     want = np.stack([O.polar_decomp_2d(x, co, rs, "f32") for x in u.numpy()])
     err = C.rel_fro(got, want)
+    assert err <= 2e-2, err
+
+
+@pytest.mark.parametrize("transpose", [False, True])
+def test_ns_ill_conditioned_near_square(transpose):
+    """The 66 x 64 momentum of the shard_uneven case: its normalised smallest singular value
+    (9.6e-4) is below the Polar-Express lower bound (1e-3), so Newton-Schulz amplifies every
+    rounding difference in that direction, and a product stored with a different rounding
+    (e.g. a mirrored instead of computed element) moves the result by ~2e-2.  Both orientations
+    (Gram NS on the tall input read transposed, and on the wide input) against the oracle."""
+    case = C.CASES["shard_uneven"]
+    g = C.build_grads(case, 0)[0][0].float()
+    u = (g + 0.9 * g)[None]  # step 1: m = g, u = g + beta1 m
+    if transpose:
+        u = u.mT.contiguous()
+    got, co, rs = _ns_gpu(u.cuda())
+    O.NS_DTYPE = "f16"
+    want = O.polar_decomp_2d(u[0].numpy(), co, rs, "f32")
+    err = C.rel_fro(got[0], want)
     assert err <= 2e-2, err
 
 
@@ -222,7 +255,7 @@ def test_sym_addmm_against_torch(M, K, batch, c_mode):
     if Cm is not None:
         ref = ref + beta * Cm.float()
     got = O_.float()
-    assert torch.equal(got, got.mT)  # exactly symmetric by construction
+    assert_block_symmetric(O_)
     tol = 2e-3 * ref.abs().max().item() + 1e-3
     assert (got - ref).abs().max().item() <= tol
 
@@ -403,6 +436,6 @@ def test_staged_epilogue_sym_addmm(batch, m, k, c_batched):
         lib.thorn_set_gemm_staged_epilogue(prev)
     assert int(err.item()) == 0
     assert torch.equal(staged, plain)
-    assert torch.equal(staged, staged.transpose(1, 2))
+    assert_block_symmetric(staged)
     want = 0.75 * (a.float() @ bt.float()) - 0.5 * c.float().expand(batch, m, m)
     assert (staged.float() - want).abs().max().item() <= 2e-2 * want.abs().max().item()

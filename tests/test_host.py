@@ -231,6 +231,12 @@ def test_custom_ops_registered_with_fake_impls():
     with pytest.raises(RuntimeError, match="CUDA"):
         torch.ops.thorn_b200.sym_addmm(torch.zeros(64, 32, dtype=torch.float16),
                                        torch.zeros(32, 64, dtype=torch.float16), None, 1.0, 0.0)
+    # the reference's own operator name (thorn.py:298) is registered too, with the same schema
+    out = torch.ops.thorn.sym_addmm(A, B, None, 1.0, 0.0)
+    assert out.shape == (3, 64, 64) and out.device.type == "meta"
+    with pytest.raises(RuntimeError, match="CUDA"):
+        torch.ops.thorn.sym_addmm(torch.zeros(64, 32, dtype=torch.float16),
+                                  torch.zeros(32, 64, dtype=torch.float16), None, 1.0, 0.0)
 
 
 def test_pinned_stepper_data_flow_with_fake_streams(monkeypatch):

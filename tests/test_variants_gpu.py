@@ -3,6 +3,8 @@ norm_axis, MD options, conv kernels, callable target norms), Magma and row-spars
 and the torch custom operators; each against the CPU oracle or a property that holds at any
 size.  Tolerances as in test_gpu_parity.py.  (Collected after test_sharded.py, before the
 allocation-free test.)"""
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -10,7 +12,7 @@ import torch
 import cases as C
 import parity as P
 from oracle import thorn_oracle as O
-from test_gpu_parity import _ns_gpu, _ns_gpu_t, compare, run_gpu
+from test_gpu_parity import _ns_gpu, _ns_gpu_t, assert_block_symmetric, compare, run_gpu
 
 pytestmark = pytest.mark.gpu
 
@@ -202,7 +204,9 @@ def test_custom_ops_match_c_abi():
     out = torch.ops.thorn_b200.sym_addmm(A, A.transpose(1, 2), Cs, 0.5, -1.0)
     want = 0.5 * (A.float() @ A.float().transpose(1, 2)) - Cs.float()
     assert (out.float() - want).abs().max() <= 2e-2 * want.abs().max()
-    assert torch.equal(out, out.transpose(1, 2))
+    assert_block_symmetric(out)
+    # the reference's operator name reaches the same kernel (bit for bit)
+    assert torch.equal(torch.ops.thorn.sym_addmm(A, A.transpose(1, 2), Cs, 0.5, -1.0), out)
     # M and K that are not multiples of 8 (zero-padded inside the operator)
     A2 = (torch.randn(2, 37, 20, device="cuda") / 8).half()
     C2 = torch.randn(2, 37, 37, device="cuda").half()
@@ -219,3 +223,52 @@ def test_custom_ops_match_c_abi():
         ref, _, _ = _ns_gpu_t(u)
         assert got.dtype == u.dtype and got.shape == u.shape
         assert C.rel_fro(got.cpu().numpy(), ref.float().cpu().numpy()) <= 1e-2
+
+
+@pytest.mark.parametrize("shape", [(2, 96, 64), (1, 256, 512)])
+def test_bounded_wait_runs_out_and_device_recovers(shape):
+    """The failure path of the NS GEMMs' bounded waits, made to run without any fault.
+
+    With the test stall switch on, the GEMMs' TMA producers issue no loads, so nothing is
+    ever in flight and the MMA warp's wait for its first operand stage runs out after the
+    (shortened) wait limit.  The call must return, the error flag must be set (also through
+    THORN.device_error()), and the next normal call on the same device must be correct.
+    (96x64 runs the single-CTA GEMM, 256x512 the 2-CTA cluster GEMM.)"""
+    import time
+
+    from thorn_b200 import THORN
+    from thorn_b200 import _native as N
+
+    lib = N.load()
+    torch.manual_seed(31)
+    u = torch.randn(shape, device="cuda") * 1e-3
+    prev_limit = lib.thorn_set_wait_limit_ns(20 * 10 ** 6)
+    prev_stall = lib.thorn_set_gemm_test_stall(1)
+    try:
+        ldc = int(lib.thorn_ns_ld(shape[2]))
+        X = torch.zeros((shape[0], shape[1], ldc), dtype=torch.float16, device="cuda")
+        out = torch.empty(shape, dtype=torch.float16, device="cuda")
+        wsb = int(lib.thorn_ns_workspace_bytes(*shape))
+        ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        co, rr = (ctypes.c_double * 3)(1.0, 0.0, 0.0), (ctypes.c_int32 * 1)(0)
+        t0 = time.perf_counter()
+        N.check(lib.thorn_ns_batched(X.data_ptr(), out.data_ptr(), ws.data_ptr(), wsb, *shape, N.F16, co, 1, rr, 0,
+                                     err.data_ptr(), N.stream_of(torch.device("cuda"))), "ns_batched")
+        torch.cuda.synchronize()
+        assert time.perf_counter() - t0 < 30.0
+        assert int(err.item()) == 1
+        # the optimizer sees it too: one step of a small orthogonalized group
+        p = torch.nn.Parameter(torch.randn(shape[1], shape[2], device="cuda") * 0.02)
+        opt = THORN([{"params": [p], "orthogonalize": True, "lr": 1e-3}])
+        p.grad = torch.randn_like(p) * 1e-3
+        opt.step()
+        assert opt.device_error()
+    finally:
+        lib.thorn_set_gemm_test_stall(prev_stall)
+        lib.thorn_set_wait_limit_ns(prev_limit)
+    # the context is usable: the same NS now matches the oracle
+    got, co5, rs5 = _ns_gpu(u)
+    O.NS_DTYPE = "f16"
+    want = np.stack([O.polar_decomp_2d(x, co5, rs5, "f32") for x in u.cpu().numpy()])
+    assert C.rel_fro(got, want) <= 2e-2

@@ -5,11 +5,16 @@
 //   D2 = D + diag2 * I                         (optional second output)
 // A is K-major ([M, K] row-major) or MN-major ([K, M], the Gram product of a
 // tall input kept in its original orientation).  B is either K-major ([N, K],
-// used for X X^T and for products with a symmetric right operand) or MN-major
-// ([K, N], used for Q @ X and B @ X).  With `sym`, only 128x BN tiles that
-// touch the lower triangle are computed; each lower element is stored at
-// (r, c) and mirrored to (c, r), so the output is exactly symmetric.  With
-// `trans_out`, D is stored transposed (the tall-matrix final product).
+// used for X X^T) or MN-major ([K, N], used for every other product).  With
+// `sym` the output is known to be symmetric up to rounding, and only tiles that
+// touch the lower triangle are computed.  The output is split into 128 x 128
+// blocks: a block on the diagonal is stored exactly as computed, a block below
+// it is stored and mirrored into the block above, so off-diagonal blocks are
+// exactly symmetric.  (The reference's Triton kernel, thorn.py:53-139, does the
+// same with its autotuned BLOCK_SIZE_M: diagonal tiles as computed, the other
+// triangle mirrored.  For a matrix of at most 128 rows the output is the plain
+// product.)  With `trans_out`, D is stored transposed (the tall-matrix final
+// product).
 //
 // Roles per CTA (192 threads, one CTA per SM):
 //   warp 0      TMA producer: fills a ring of shared-memory stages
@@ -37,6 +42,7 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 x 16-bit = one 128-byte swizzle row
 constexpr int kThreadsG = 192;
+// Default limit of every mbarrier wait (thorn_set_wait_limit_ns changes it).
 constexpr uint64_t kTimeoutNs = 10ull * 1000 * 1000 * 1000;
 
 template <int BN>
@@ -66,6 +72,8 @@ struct Params {
   int sym, trans_out, c_vec, d_vec, tma_epi, c_bcast, l2hint;
   int tiles_m, tiles_n, tiles_per_mat, total_tiles, num_kb;
   int* err;
+  uint64_t wait_limit_ns;  // limit of every mbarrier wait before the CTA gives up
+  int test_stall;          // failure test: producers issue no loads, so the MMA warp's wait runs out
 };
 
 // ---------------------------------------------------------------------------
@@ -110,16 +118,17 @@ __device__ __forceinline__ void abort_settle(volatile int* abort) {
   while (global_ns() - t0 < kSettleNs) {
   }
 }
-// Bounded wait on the phase with parity `parity`.  Returns false on timeout or
-// when another role of this CTA has already aborted.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int* err) {
+// Bounded wait on the phase with parity `parity`.  Returns false after `limit_ns`
+// or when another role of this CTA has already aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int* err,
+                                          uint64_t limit_ns) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try(bar, parity)) return true;
     if ((it & 255u) == 0) {
       if (abort && *abort) return false;
-      if (global_ns() - t0 > kTimeoutNs) {
+      if (global_ns() - t0 > limit_ns) {
         if (err) atomicExch(err, 1);
         if (abort) *abort = 1;
         return false;
@@ -227,10 +236,12 @@ __device__ __forceinline__ void decode_tile(const Params& p, int t, int& b, int&
 
 // Epilogue of one 32-column chunk of a thread's accumulator row: alpha/beta/C,
 // one rounding, optional second output D + diag2 I, and plain, transposed or
-// mirrored (symmetric) stores with bounds checks.
+// mirrored (symmetric) stores with bounds checks.  The 32 columns of a chunk and
+// the 32 rows of a warp each lie in one 128-block; with `sym` the caller passes
+// only chunks whose block is not right of the rows' block.
 template <class T>
 __device__ __forceinline__ void epilogue_chunk(const Params& p, float* v, int row, bool row_ok, int col0,
-                                               int warp_row_max, T* D, T* D2, const T* Cb) {
+                                               T* D, T* D2, const T* Cb) {
   const bool full = row_ok && col0 + 32 <= p.N;
   if (Cb != nullptr) {
     float cv[32];
@@ -266,8 +277,7 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, float* v, int ro
         if (row_ok && col0 + j < p.N) O[(int64_t)(col0 + j) * ld + row] = from_f<T>(w[j]);
       continue;
     }
-    const bool lower_full = !p.sym || row >= col0 + 31;
-    if (full && p.d_vec && lower_full) {
+    if (full && p.d_vec) {
       T* dst = O + (int64_t)row * ld + col0;
       store_n(dst, w, 8, true);
       store_n(dst + 8, w + 8, 8, true);
@@ -276,13 +286,13 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, float* v, int ro
     } else if (row_ok) {
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        if (col0 + j < p.N && (!p.sym || row >= col0 + j)) O[(int64_t)row * ld + col0 + j] = from_f<T>(w[j]);
+        if (col0 + j < p.N) O[(int64_t)row * ld + col0 + j] = from_f<T>(w[j]);
     }
-    if (p.sym && warp_row_max > col0) {
-      // mirror strictly-lower elements: lanes hold consecutive rows -> coalesced
+    if (p.sym && (col0 >> 7) < (row >> 7)) {
+      // a chunk of an off-diagonal block: mirror it; lanes hold consecutive rows -> coalesced
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        if (row_ok && col0 + j < p.N && row > col0 + j) O[(int64_t)(col0 + j) * ld + row] = from_f<T>(w[j]);
+        if (row_ok && col0 + j < p.N) O[(int64_t)(col0 + j) * ld + row] = from_f<T>(w[j]);
     }
   }
 }
@@ -338,14 +348,14 @@ __global__ void __launch_bounds__(kThreadsG, 1) ns_gemm_kernel(const __grid_cons
 
   if (warp == 0) {
     // ------------------------------ producer ------------------------------
-    if (lane == 0) {
+    if (lane == 0 && !p.test_stall) {
       int stage = 0;
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < p.total_tiles && !*abort_flag; t += gridDim.x) {
         int b, tm, tn;
         decode_tile<BN>(p, t, b, tm, tn);
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.err)) break;
+          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.err, p.wait_limit_ns)) break;
           const uint32_t fb = smem_u32(&full[stage]);
           mbar_expect_tx(fb, C_::kStageBytes);
           if (!A_MN) {
@@ -381,12 +391,12 @@ __global__ void __launch_bounds__(kThreadsG, 1) ns_gemm_kernel(const __grid_cons
       for (int t = blockIdx.x; t < p.total_tiles && !*abort_flag; t += gridDim.x, ++it) {
         const int acc = it & 1;
         const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
-        if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag, p.err)) break;
+        if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag, p.err, p.wait_limit_ns)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         bool ok = true;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, p.err)) {
+          if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, p.err, p.wait_limit_ns)) {
             ok = false;
             break;
           }
@@ -420,13 +430,13 @@ __global__ void __launch_bounds__(kThreadsG, 1) ns_gemm_kernel(const __grid_cons
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
       const int acc = it & 1;
       const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
-      if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag, p.err)) break;
+      if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag, p.err, p.wait_limit_ns)) break;
       tc_fence_after();
       int b, tm, tn;
       decode_tile<BN>(p, t, b, tm, tn);
       const int row = tm * BM + rloc;
       const bool row_ok = row < p.M;
-      const int warp_row_max = tm * BM + q * 32 + 31;
+      const int row_blk = (tm * BM + q * 32) >> 7;  // the 128-block of this warp's rows
       T* D = Dp + (int64_t)b * p.d_bs;
       T* D2 = D2p ? D2p + (int64_t)b * p.d2_bs : nullptr;
       const T* Cb = Cp ? Cp + (int64_t)b * p.c_bs : nullptr;
@@ -434,10 +444,10 @@ __global__ void __launch_bounds__(kThreadsG, 1) ns_gemm_kernel(const __grid_cons
       for (int ch = 0; ch < BN / 32; ++ch) {
         const int col0 = tn * BN + ch * 32;
         if (col0 >= p.N) break;
-        if (p.sym && warp_row_max < col0) continue;  // whole warp above the diagonal
+        if (p.sym && (col0 >> 7) > row_blk) continue;  // a block above the diagonal: the mirror writes it
         float v[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + ch * 32), v);
-        epilogue_chunk(p, v, row, row_ok, col0, warp_row_max, D, D2, Cb);
+        epilogue_chunk(p, v, row, row_ok, col0, D, D2, Cb);
       }
       tc_fence_before();
       mbar_arrive(smem_u32(&tempty[acc]));
@@ -586,7 +596,7 @@ __device__ __forceinline__ int warp_blocks(const Params& p, int t, int row_base,
   const int row0 = tm * BM2 + row_base;
   if (row0 >= p.M) return 0;
   int nv = min(8, (p.N - tn * 256 + 31) >> 5);
-  if (p.sym) nv = min(nv, ((row0 + 31 - tn * 256) >> 5) + 1);  // blocks on or below the diagonal
+  if (p.sym) nv = min(nv, (((row0 | 127) - tn * 256) >> 5) + 1);  // blocks up to the end of the rows' 128-block
   return max(nv, 0);
 }
 
@@ -662,7 +672,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
 
   if (warp == 0) {
     // ------------------------------ producer (both CTAs) -------------------
-    if (lane == 0) {
+    if (lane == 0 && !p.test_stall) {
       int stage = 0;
       uint32_t phase = 0;
       const int row_off = (int)rank * 128;
@@ -675,7 +685,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
         int b, tm, tn;
         decode_tile2(p, t, b, tm, tn);
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.err)) break;
+          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.err, p.wait_limit_ns)) break;
           const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
           if (leader) mbar_expect_tx(smem_u32(&full[stage]), 4 * kHalfBytes);
           const uint32_t a_dst = smem_u32(sA + stage * kHalfBytes);
@@ -709,12 +719,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
       for (int t = cid; t < p.total_tiles && !*abort_flag; t += nclusters, ++it) {
         const int acc = it & 1;
         const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
-        if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag, p.err)) break;
+        if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag, p.err, p.wait_limit_ns)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * 256);
         bool ok = true;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, p.err)) {
+          if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, p.err, p.wait_limit_ns)) {
             ok = false;
             break;
           }
@@ -788,7 +798,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
       const int acc = it & 1;
       const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
       // warp-uniform outcome: the .sync.aligned TMEM loads and __syncwarp below need all lanes
-      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag, p.err))) break;
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag, p.err, p.wait_limit_ns)))
+        break;
       tc_fence_after();
       int b, tm, tn;
       const int nv = warp_blocks(p, t, row_base, b, tm, tn);
@@ -813,7 +825,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
           mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
         }
         if (has_c) {
-          if (!__all_sync(0xffffffffu, mbar_wait(cb0 + 8 * k, (uint32_t)(n >> 1) & 1u, abort_flag, p.err))) {
+          if (!__all_sync(0xffffffffu,
+                          mbar_wait(cb0 + 8 * k, (uint32_t)(n >> 1) & 1u, abort_flag, p.err, p.wait_limit_ns))) {
             aborted = true;
             break;
           }
@@ -831,8 +844,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
           if (lane == 0) bulk_wait_read<1>();  // stores of block n - 2 no longer read buffer k
         }
         __syncwarp();
-        const bool diag = row0 == col0;
-        const bool mirror = p.sym && row0 > col0;
+        const bool diag = row0 == col0;                             // holds the matrix diagonal (D2 patch)
+        const bool mirror = p.sym && (row0 >> 7) > (col0 >> 7);  // an off-diagonal 128-block
         if (!p.trans_out) {
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -842,13 +855,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
             for (int i = 0; i < 8; ++i) h[i] = from_f<T>(v[8 * c + i]);
             *reinterpret_cast<uint4*>(gM + sw64_off(lane, 8 * c)) = r;
           }
-        }
-        if (p.sym && diag) {
-          // upper half of a diagonal block: element (j, lane) = lower element (lane, j)
-          __syncwarp();
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (j < lane) *reinterpret_cast<T*>(gM + sw64_off(j, lane)) = from_f<T>(v[j]);
         }
         if (mirror || p.trans_out) {
 #pragma unroll
@@ -889,7 +895,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
     }
     if (lane == 0) bulk_wait_all<0>();
     // a C block still in flight (abort path) must land before the CTA exits
-    if (c_inflight) mbar_wait(cb0 + 8 * c_buf, c_par, nullptr, p.err);
+    if (c_inflight) mbar_wait(cb0 + 8 * c_buf, c_par, nullptr, p.err, p.wait_limit_ns);
   } else {
     // ------------------------------ epilogue (both CTAs) -------------------
     const int q = warp & 3;
@@ -901,13 +907,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
     for (int t = cid; t < p.total_tiles; t += nclusters, ++it) {
       const int acc = it & 1;
       const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
-      if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag, p.err)) break;
+      if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag, p.err, p.wait_limit_ns)) break;
       tc_fence_after();
       int b, tm, tn;
       decode_tile2(p, t, b, tm, tn);
       const int row = tm * BM2 + rloc;
       const bool row_ok = row < p.M;
-      const int warp_row_max = tm * BM2 + (int)rank * 128 + q * 32 + 31;
+      const int row_blk = (tm * BM2 + (int)rank * 128 + q * 32) >> 7;  // the 128-block of this warp's rows
       T* D = Dp + (int64_t)b * p.d_bs;
       T* D2 = D2p ? D2p + (int64_t)b * p.d2_bs : nullptr;
       const T* Cb = Cp ? Cp + (int64_t)b * p.c_bs : nullptr;
@@ -915,10 +921,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
       for (int ch = 0; ch < 256 / 32; ++ch) {
         const int col0 = tn * 256 + ch * 32;
         if (col0 >= p.N) break;
-        if (p.sym && warp_row_max < col0) continue;
+        if (p.sym && (col0 >> 7) > row_blk) continue;  // a block above the diagonal: the mirror writes it
         float v[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 256 + ch * 32), v);
-        epilogue_chunk(p, v, row, row_ok, col0, warp_row_max, D, D2, Cb);
+        epilogue_chunk(p, v, row, row_ok, col0, D, D2, Cb);
       }
       tc_fence_before();
       mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
@@ -1020,6 +1026,9 @@ static std::atomic<uint64_t> g_flops_dense{0}, g_flops_exec{0};
 static std::atomic<int> g_gemm_pdl{0};
 // L2 cache policies on the 2-CTA kernel's operand loads and output stores (1) or none (0, default).
 static std::atomic<int> g_l2_hints{0};
+// Limit of every mbarrier wait in the NS GEMMs, and the failure-test switch (producers issue no loads).
+static std::atomic<uint64_t> g_wait_limit_ns{gemm::kTimeoutNs};
+static std::atomic<int> g_test_stall{0};
 
 template <int BN, bool AMN, bool BMN, class T>
 static int launch_gemm(gemm::Params& prm, int grid, cudaStream_t st) {
@@ -1100,8 +1109,8 @@ static int launch_gemm2(gemm::Params& prm, int64_t total, int sms, cudaStream_t 
 
 template <class T>
 static int launch_any2(const GemmOp& op, gemm::Params& prm, int64_t total, int sms, cudaStream_t st) {
-  if (op.a_mn && !op.b_mn) return THORN_ERR_ARG;
-  if (op.a_mn) return launch_gemm2<true, true, T>(prm, total, sms, st);
+  if (op.a_mn) return op.b_mn ? launch_gemm2<true, true, T>(prm, total, sms, st)
+                              : launch_gemm2<true, false, T>(prm, total, sms, st);
   if (op.b_mn) return launch_gemm2<false, true, T>(prm, total, sms, st);
   return launch_gemm2<false, false, T>(prm, total, sms, st);
 }
@@ -1111,14 +1120,15 @@ static std::atomic<int> g_staged_epilogue{1};
 
 template <class T>
 static int launch_any(const GemmOp& op, int BN, gemm::Params& prm, int grid, cudaStream_t st) {
-  // instantiated operand layouts: (A K, B K), (A K, B MN), (A MN, B MN)
-  if (op.a_mn && !op.b_mn) return THORN_ERR_ARG;
+  // every operand layout: A and B each K-major or MN-major
   if (BN == 256) {
-    if (op.a_mn) return launch_gemm<256, true, true, T>(prm, grid, st);
+    if (op.a_mn) return op.b_mn ? launch_gemm<256, true, true, T>(prm, grid, st)
+                                : launch_gemm<256, true, false, T>(prm, grid, st);
     if (op.b_mn) return launch_gemm<256, false, true, T>(prm, grid, st);
     return launch_gemm<256, false, false, T>(prm, grid, st);
   }
-  if (op.a_mn) return launch_gemm<128, true, true, T>(prm, grid, st);
+  if (op.a_mn) return op.b_mn ? launch_gemm<128, true, true, T>(prm, grid, st)
+                              : launch_gemm<128, true, false, T>(prm, grid, st);
   if (op.b_mn) return launch_gemm<128, false, true, T>(prm, grid, st);
   return launch_gemm<128, false, false, T>(prm, grid, st);
 }
@@ -1204,6 +1214,8 @@ int run_gemm(const GemmOp& op, int dtype, int* err, cudaStream_t st) {
   prm.total_tiles = (int)total;
   prm.num_kb = (op.K + BK - 1) / BK;
   prm.err = err;
+  prm.wait_limit_ns = g_wait_limit_ns.load();
+  prm.test_stall = g_test_stall.load();
   const int grid = (int)min64(total, (int64_t)di.sms);
   const double dense = 2.0 * op.M * (double)op.N * op.K * op.batch;
   const double exec = 2.0 * BMt * (double)BN * (prm.num_kb * (double)BK) * total;
@@ -1230,17 +1242,35 @@ struct NsLayout {
   int64_t xs, ms;  // bytes of one [batch, m, ldn] / [batch, m, ldm] buffer (256-aligned)
   int64_t total;
 };
+// Buffer sizes of one NS call.  Every product is overflow-checked: a size that
+// does not fit in int64 leaves total = -1 (the callers reject it).
 NsLayout ns_layout(int64_t batch, int64_t rows, int64_t cols) {
   NsLayout L;
   L.m = std::min(rows, cols);
   L.n = std::max(rows, cols);
+  L.gram = L.m != L.n;
+  L.ldm = L.ldn = L.xs = L.ms = 0;
+  L.total = -1;
+  if (L.n > (INT64_MAX >> 4)) return L;  // the padded leading dimensions would overflow
   L.ldm = thorn_ns_ld(L.m);
   L.ldn = thorn_ns_ld(L.n);
-  L.gram = L.m != L.n;
-  auto al = [](int64_t x) { return (x + 255) / 256 * 256; };
-  L.xs = al(batch * L.m * L.ldn * 2);
-  L.ms = al(batch * L.m * L.ldm * 2);
-  L.total = L.gram ? (2 * L.xs + 5 * L.ms) : (4 * L.ms);
+  auto bytes = [&](int64_t ld, int64_t* out) {
+    int64_t v = 0;
+    if (__builtin_mul_overflow(batch, L.m, &v) || __builtin_mul_overflow(v, ld, &v) ||
+        __builtin_mul_overflow(v, (int64_t)2, &v) || v > INT64_MAX - 255)
+      return false;
+    *out = (v + 255) / 256 * 256;
+    return true;
+  };
+  if (!bytes(L.ldn, &L.xs) || !bytes(L.ldm, &L.ms)) return L;
+  int64_t a = 0, b = 0;
+  if (L.gram) {
+    if (__builtin_mul_overflow(L.xs, (int64_t)2, &a) || __builtin_mul_overflow(L.ms, (int64_t)5, &b) ||
+        __builtin_add_overflow(a, b, &L.total))
+      L.total = -1;
+  } else if (__builtin_mul_overflow(L.ms, (int64_t)4, &L.total)) {
+    L.total = -1;
+  }
   return L;
 }
 }  // namespace
@@ -1259,7 +1289,7 @@ extern "C" int thorn_ns_batched(const void* x, void* out, void* workspace, int64
   if (ns_dtype != THORN_F16 && ns_dtype != THORN_BF16) return THORN_ERR_ARG;
   if (batch > INT32_MAX || rows > INT32_MAX || cols > INT32_MAX) return THORN_ERR_ARG;
   const NsLayout L = ns_layout(batch, rows, cols);
-  if (workspace_bytes < L.total) return THORN_ERR_ARG;
+  if (L.total < 0 || workspace_bytes < L.total) return THORN_ERR_ARG;
   if (!aligned16(x) || !aligned16(workspace)) return THORN_ERR_ALIGN;
   cudaStream_t st = (cudaStream_t)stream;
   const bool tall = rows > cols;
@@ -1272,12 +1302,14 @@ extern "C" int thorn_ns_batched(const void* x, void* out, void* workspace, int64
   };
   uint8_t* ws = (uint8_t*)workspace;
   int rc = THORN_OK;
-  // product of two m x m matrices (second operand symmetric or K-major)
+  // product A @ Bm of two m x m matrices.  Bm is read MN-major: the symmetric
+  // outputs are exactly symmetric only off their diagonal 128-blocks, so Bm and
+  // Bm^T may differ there and the product must be the reference's A @ Bm.
   auto mm = [&](const void* A, const void* Bm, const void* C, void* D, void* D2, float alpha, float beta,
                 float diag2) {
     GemmOp op;
     op.A = A; op.a_ld = ldm; op.a_bs = m * ldm;
-    op.B = Bm; op.b_ld = ldm; op.b_bs = m * ldm; op.b_mn = false;
+    op.B = Bm; op.b_ld = ldm; op.b_bs = m * ldm; op.b_mn = true;
     op.C = C; op.c_ld = ldm; op.c_bs = m * ldm;
     op.D = D; op.d_ld = ldm; op.d_bs = m * ldm;
     op.D2 = D2; op.d2_ld = ldm; op.d2_bs = m * ldm;
@@ -1295,11 +1327,13 @@ extern "C" int thorn_ns_batched(const void* x, void* out, void* workspace, int64
     op.sym = true;
     return run_gemm(op, ns_dtype, err_flag, st);
   };
-  // Q @ X with X [m, N] (MN-major second operand), optional C = X
+  // Q @ X with X [m, N] (MN-major second operand), optional C = X.  With q_t
+  // the first operand is Q^T (Q read MN-major): the tall final product
+  // X^T @ Q = (Q^T @ X)^T of thorn.py:653, stored transposed.
   auto qx = [&](const void* Q, const void* X, int64_t ldx, int N, const void* C, float beta, void* D, int64_t d_ld,
-                int64_t d_bs, bool trans) {
+                int64_t d_bs, bool trans, bool q_t) {
     GemmOp op;
-    op.A = Q; op.a_ld = ldm; op.a_bs = m * ldm;
+    op.A = Q; op.a_ld = ldm; op.a_bs = m * ldm; op.a_mn = q_t;
     op.B = X; op.b_ld = ldx; op.b_bs = m * ldx; op.b_mn = true;
     op.C = C; op.c_ld = ldx; op.c_bs = m * ldx;
     op.D = D; op.d_ld = d_ld; op.d_bs = d_bs;
@@ -1319,9 +1353,9 @@ extern "C" int thorn_ns_batched(const void* x, void* out, void* workspace, int64
     op.sym = true;
     return run_gemm(op, ns_dtype, err_flag, st);
   };
-  auto qx_tall = [&](const void* Q, const void* U, void* D, int64_t d_ld, int64_t d_bs, bool trans) {
+  auto qx_tall = [&](const void* Q, const void* U, void* D, int64_t d_ld, int64_t d_bs, bool trans, bool q_t) {
     GemmOp op;
-    op.A = Q; op.a_ld = ldm; op.a_bs = m * ldm;
+    op.A = Q; op.a_ld = ldm; op.a_bs = m * ldm; op.a_mn = q_t;
     op.B = U; op.b_ld = ldm; op.b_bs = n * ldm; op.b_mn = false;
     op.D = D; op.d_ld = d_ld; op.d_bs = d_bs;
     op.M = m; op.N = n; op.K = m; op.batch = B;
@@ -1349,8 +1383,8 @@ extern "C" int thorn_ns_batched(const void* x, void* out, void* workspace, int64
       const float a = (float)coeffs[3 * i], b = (float)coeffs[3 * i + 1], c = (float)coeffs[3 * i + 2];
       const bool rs = in_restarts(i);
       if (rs && i != 0) {
-        if (x_is_input_tall) NS_TRY(qx_tall(Qb[qi], X, Xb[xi], ldn, m * ldn, false));
-        else NS_TRY(qx(Qb[qi], X, ldn, n, nullptr, 0.f, Xb[xi], ldn, m * ldn, false));
+        if (x_is_input_tall) NS_TRY(qx_tall(Qb[qi], X, Xb[xi], ldn, m * ldn, false, false));
+        else NS_TRY(qx(Qb[qi], X, ldn, n, nullptr, 0.f, Xb[xi], ldn, m * ldn, false, false));
         X = Xb[xi];
         x_is_input_tall = false;
         xi ^= 1;
@@ -1369,9 +1403,10 @@ extern "C" int thorn_ns_batched(const void* x, void* out, void* workspace, int64
       }
     }
     if (iters == 0) return THORN_ERR_ARG;
-    // out = Q @ X ; stored transposed for tall inputs (X.mT @ Q)
-    if (x_is_input_tall) NS_TRY(qx_tall(Qb[qi], X, out, (int64_t)m, (int64_t)m * n, true));
-    else NS_TRY(qx(Qb[qi], X, ldn, n, nullptr, 0.f, out, tall ? (int64_t)m : (int64_t)n, (int64_t)m * n, tall));
+    // out = Q @ X; for tall inputs X^T @ Q (thorn.py:653) = (Q^T @ X)^T, stored transposed
+    if (x_is_input_tall) NS_TRY(qx_tall(Qb[qi], X, out, (int64_t)m, (int64_t)m * n, true, true));
+    else
+      NS_TRY(qx(Qb[qi], X, ldn, n, nullptr, 0.f, out, tall ? (int64_t)m : (int64_t)n, (int64_t)m * n, tall, tall));
   } else {
     void* Xb[2] = {ws, ws + L.ms};
     void* A = ws + 2 * L.ms;
@@ -1385,7 +1420,8 @@ extern "C" int thorn_ns_batched(const void* x, void* out, void* workspace, int64
       NS_TRY(mm(A, A, A, Bm, nullptr, c, b, 0.f));         // B = c A A + b A
       const bool last = i == iters - 1;
       void* D = last ? out : Xb[xi];
-      NS_TRY(qx(Bm, X, ldm, m, X, a, D, last ? (int64_t)m : ldm, last ? (int64_t)m * m : m * ldm, false));  // X = a X + B X
+      NS_TRY(qx(Bm, X, ldm, m, X, a, D, last ? (int64_t)m : ldm, last ? (int64_t)m * m : m * ldm, false,
+                false));  // X = a X + B X
       X = D;
       xi ^= 1;
     }
@@ -1419,6 +1455,13 @@ extern "C" int thorn_set_gemm_staged_epilogue(int enable) { return g_staged_epil
 extern "C" int thorn_set_gemm_pdl(int enable) { return g_gemm_pdl.exchange(enable ? 1 : 0); }
 
 extern "C" int thorn_set_gemm_l2_hints(int enable) { return g_l2_hints.exchange(enable ? 1 : 0); }
+
+extern "C" uint64_t thorn_set_wait_limit_ns(uint64_t limit_ns) {
+  if (limit_ns == 0) limit_ns = gemm::kTimeoutNs;
+  return g_wait_limit_ns.exchange(limit_ns);
+}
+
+extern "C" int thorn_set_gemm_test_stall(int enable) { return g_test_stall.exchange(enable ? 1 : 0); }
 
 // Dense-equivalent and executed tensor-core FLOPs issued so far (for roofline reports).
 extern "C" void thorn_gemm_flops(double* dense, double* executed) {
@@ -1470,8 +1513,8 @@ extern "C" int thorn_ns_batched_static(const void* x, void* out, int64_t batch, 
                                        int n_restarts, int* err_flag, void* stream) {
   if (batch < 0 || rows < 0 || cols < 0) return THORN_ERR_ARG;
   if (batch == 0 || rows == 0 || cols == 0) return THORN_OK;
-  if (thorn_ns_workspace_bytes(batch, rows, cols) > (int64_t)THORN_NS_STATIC_WORKSPACE_BYTES)
-    return THORN_ERR_TOO_LARGE;
+  const int64_t need = thorn_ns_workspace_bytes(batch, rows, cols);
+  if (need < 0 || need > (int64_t)THORN_NS_STATIC_WORKSPACE_BYTES) return THORN_ERR_TOO_LARGE;
   void* ws = nullptr;
   const int rc = static_workspace(&ws);
   if (rc) return rc;

@@ -3,7 +3,11 @@
 * ``torch.ops.thorn_b200.sym_addmm(A, B, C, alpha, beta)``: the contract of the
   reference's operator seam ``thorn::sym_addmm`` (thorn.py:298-368), i.e.
   ``beta * C + alpha * (A @ B)`` for products known to be symmetric, computed on
-  the lower-triangle tiles of the tcgen05 GEMM and mirrored.
+  the lower-triangle tiles of the tcgen05 GEMM and mirrored.  The same kernel is
+  also registered under the reference's own name, ``torch.ops.thorn.sym_addmm``,
+  unless the reference's module registered that name first (then its operator
+  stays in place; importing the reference after this package would fail on the
+  duplicate name, so code that imports both imports ``thorn`` first).
 * ``torch.ops.thorn_b200.polar_decomp(X, coeffs, restarts)``: the Newton-Schulz
   polar factor of a stack of matrices (thorn.py:626-662): Frobenius-normalised in
   fp32 and cast to fp16 by the library's NS-input pass, iterated on fp16 operands,
@@ -44,9 +48,8 @@ def _check_cuda(*ts):
             raise RuntimeError(f"thorn_b200 operators run on CUDA devices only; got a tensor on {t.device}")
 
 
-@torch.library.custom_op("thorn_b200::sym_addmm", mutates_args=())
-def sym_addmm(A: torch.Tensor, B: torch.Tensor, C: Optional[torch.Tensor], alpha: float,
-              beta: float) -> torch.Tensor:
+def _sym_addmm_cuda(A: torch.Tensor, B: torch.Tensor, C: Optional[torch.Tensor], alpha: float,
+                    beta: float) -> torch.Tensor:
     """``beta * C + alpha * (A @ B)`` with ``A @ B`` and ``C`` symmetric.
 
     A: (..., M, K), B: (..., K, M), C: (..., M, M), (M, M) or None; fp16 or bf16.
@@ -88,10 +91,30 @@ def sym_addmm(A: torch.Tensor, B: torch.Tensor, C: Optional[torch.Tensor], alpha
     return out.reshape(*batch, M, M)
 
 
-@sym_addmm.register_fake
 def _sym_addmm_fake(A, B, C, alpha, beta):
     *batch, M, _ = A.shape
     return A.new_empty((*batch, M, M))
+
+
+sym_addmm = torch.library.custom_op("thorn_b200::sym_addmm", _sym_addmm_cuda, mutates_args=())
+sym_addmm.register_fake(_sym_addmm_fake)
+
+
+def _reference_op_registered() -> bool:
+    """True when ``thorn::sym_addmm`` exists already (the reference's module was imported)."""
+    try:
+        torch.ops.thorn.sym_addmm
+    except (AttributeError, RuntimeError):
+        return False
+    return True
+
+
+# the reference's operator name (thorn.py:298): code written against the reference that calls
+# torch.ops.thorn.sym_addmm reaches the same tcgen05 kernel
+reference_sym_addmm = None
+if not _reference_op_registered():
+    reference_sym_addmm = torch.library.custom_op("thorn::sym_addmm", _sym_addmm_cuda, mutates_args=())
+    reference_sym_addmm.register_fake(_sym_addmm_fake)
 
 
 @torch.library.custom_op("thorn_b200::polar_decomp", mutates_args=())

@@ -293,6 +293,10 @@ class THORN(Optimizer):
     # when a list: each momentum pass of an orthogonalized group appends (start event, end
     # event, algorithmic bytes: g read, m read + write, p read + write with decouple_md)
     profile_momentum: Optional[list] = None
+    # when a list: each sharded step appends a list of (stage name, event) pairs recorded on
+    # the launching stream at the end of each stage (the first is the step's start); with
+    # pipeline_exchange the exchange and NS stages overlap and are timed as one
+    profile_stages: Optional[list] = None
     # sharded path: exchange row slabs in waves of NS batches so that transfers overlap
     # the owners' Newton-Schulz work (False: every slab moves before any NS starts)
     pipeline_exchange: bool = False

@@ -308,9 +308,28 @@ def due_matrices(opt, mats, cfg, group):
     return [p for p, d in zip(mats, due) if d], [sc for sc, d in zip(scales, due) if d]
 
 
+def _stage_marks(opt):
+    """A function that records a named CUDA event on the current stream into this step's
+    stage list when ``opt.profile_stages`` is a list, else does nothing."""
+    log = getattr(opt, "profile_stages", None)
+    if log is None:
+        return lambda name: None
+    marks = []
+    log.append(marks)
+
+    def mark(name):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        marks.append((name, ev))
+
+    return mark
+
+
 def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, scales):
     lib = N.load()
     stream = N.stream_of(dev)
+    mark = _stage_marks(opt)
+    mark("start")
     err = opt._err_flag(dev)
     md = cfg.decouple_md
     arena = Arena()
@@ -383,7 +402,9 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
                                           N.dtype_code(sdt), N.dtype_code(udt), b1, 1 if md else 0, write_grad,
                                           stream), "ortho_pre_multi")
     opt._profile_end(opt.profile_momentum, ev, opt._momentum_bytes(items, md))
+    mark("momentum")
     dist.all_reduce(arena.region("red1"), group=group)
+    mark("all_reduce")
     if md:
         opt._md_gains(items, cfg, arena, stream)
 
@@ -423,6 +444,7 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
         udt = pdt if pdt == sdt else torch.float32
         N.check(lib.thorn_ns_cast_multi(N.array(N.NsCastTensor, ts), len(ts), N.dtype_code(pdt), N.dtype_code(sdt),
                                         N.dtype_code(udt), ns_code, b1, stream), "ns_cast_multi")
+    mark("gains_and_cast" if md else "cast")
 
     xchg = exchange_all_to_all if getattr(opt, "exchange", "rounds") == "all_to_all" else exchange
     # 3. slabs to owners: every wave's exchange is queued now (the NCCL stream runs them
@@ -460,6 +482,8 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
     scatters = []
     for w, js_w in enumerate(wave_js):
         gathers[w].wait()  # the current stream waits; the host does not
+        if n_waves == 1:
+            mark("exchange_out")
         for ci, (R, C, pdt, sdt, js) in enumerate(chunks):
             if wave_of[js[0]] != w:
                 continue
@@ -487,10 +511,13 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
                 N.check(lib.thorn_pnn_stats_multi(N.array(N.PnnTensor, [pt]), 1, ns_code, N.F32, stream),
                         "pnn_stats")
                 factors[ci] = arena.get(rsh).view(nb, R)
+        if n_waves == 1:
+            mark("newton_schulz")
         sends, recvs = plan_scatter(owners, me, world, owner_parts, my_parts, subset=js_w)
         scatters.append(xchg(sends, recvs, ranks, group, wait=False))
     for ex in scatters:
         ex.wait()
+    mark("exchange_back" if n_waves == 1 else "exchange_and_newton_schulz")
     del X, send_buf, send_rows
 
     # 6. apply on local rows
@@ -511,9 +538,11 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
     for pdt, ts in posts.items():
         N.check(lib.thorn_ortho_post_multi(N.array(N.OrthoPostTensor, ts), len(ts), ns_code, N.dtype_code(pdt),
                                            float(cfg.weight_decay), stream), "ortho_post_multi")
+    mark("apply")
     if md:
         dist.all_reduce(arena.region("red2"), group=group)
         opt._md_prep(items, arena, new=True, stream=stream)
         opt._md_finalize(items, arena, lambda it: True, stream)
+        mark("md_renorm")
     del U, u_loc, f_loc
     opt._finish(mats, cfg)
