@@ -189,6 +189,31 @@ def cpu_oracle_sample(warm_only: bool = False):
     return total * 1e3, sample, (t_sq + t_kv + t_ffn + t_emb + t_norm)
 
 
+def port_calibration():
+    """The reference's own CPU step time over the port's on the same sample, measured where the
+    reference can be imported (oracle/time_reference.py; committed under profiles/), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "cpu_reference_vs_port.json")) as f:
+            cal = json.load(f)
+        return float(cal["reference_over_port"]), f"{cal.get('threads')} threads of {cal.get('cpu', '?')}"
+    except (OSError, ValueError, KeyError):
+        return None
+
+
+def cpu_baseline_entry(v, sample, cores, extra=None) -> dict:
+    """The cpu_baseline object: the port's extrapolated step, with the reference-equivalent
+    figure when the port has been timed against the reference itself."""
+    d = {"value": round(v, 3), "unit": "ms", "cores": cores, "kind": "port", "sample": sample}
+    cal = port_calibration()
+    if cal is not None:
+        d["reference_over_port"] = cal[0]
+        d["reference_equivalent_ms"] = round(v * cal[0], 3)
+        d["calibration"] = (f"the reference's thorn.THORN.step / the port's step on the same sample, timed on "
+                            f"{cal[1]} (profiles/cpu_reference_vs_port.md)")
+    d.update(extra or {})
+    return d
+
+
 def reference_arm(args, rank):
     if rank != 0:
         return
@@ -208,8 +233,8 @@ def reference_arm(args, rank):
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "ms", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v, 3), "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "sample": "bounded, extrapolated"},
-            "cpu_baseline": {"value": round(v, 3), "unit": "ms", "cores": cores, "kind": "port", "sample": sample},
+            "config": bench_config(args, int(os.environ.get("WORLD_SIZE", "1"))),
+            "cpu_baseline": cpu_baseline_entry(v, sample, cores),
             "e2e": {"value": round(v, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -271,6 +296,19 @@ def stall_watchdog(rank, limit_s):
     threading.Thread(target=run, daemon=True).start()
 
 
+def bench_config(args, world) -> dict:
+    """The workload description of the line, the same on both arms."""
+    layers = getattr(args, "layers", None) or LAYERS
+    ortho_s, adam_s = shapes(layers)
+    return {"workload": WORKLOAD + (" sharded Shard(0)" if world > 1 else "")
+            + ("" if layers == LAYERS else f" REDUCED to {layers} layers (profiling only)"),
+            "ortho_matrices": len(ortho_s), "adamw_tensors": len(adam_s),
+            "params": sum(math.prod(s) for s in ortho_s + adam_s), "param_dtype": "bf16",
+            "state_dtype": "f32", "ns_dtype": "f16", "decouple_md": MD, "lr": ORTHO_LR,
+            "parallelism": f"fsdp{world}" if world > 1 else "single",
+            "l2": "no flush: every step reads params, grads and state (~70 GB) >> 126 MB L2"}
+
+
 def result_line(args, world, ms, ns_launch_ms, ns_dense_all, ns_exec_all, mom_ms, mom_bytes, cpu, e2e, host_ms,
                 host_enqueue_ms, launches, clocks) -> dict:
     """The JSON line of a GPU run (rank 0) from its measurements: device time per step, the
@@ -281,18 +319,11 @@ def result_line(args, world, ms, ns_launch_ms, ns_dense_all, ns_exec_all, mom_ms
     peak_job = peak_sus * world  # whole-job peak: the NS work is spread over all ranks
     achieved = ns_dense_all / (ns_launch_ms * 1e-3) / 1e12 if ns_launch_ms > 0 else None
     achieved_exec = ns_exec_all / (ns_launch_ms * 1e-3) / 1e12 if ns_launch_ms > 0 else None
-    ortho_s, adam_s = shapes(args.layers)
     line = {
         "metric": METRIC, "value": round(ms, 3), "unit": "ms", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False,
         "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": WORKLOAD + (" sharded Shard(0)" if world > 1 else "")
-                   + ("" if args.layers == LAYERS else f" REDUCED to {args.layers} layers (profiling only)"),
-                   "ortho_matrices": len(ortho_s), "adamw_tensors": len(adam_s),
-                   "params": sum(math.prod(s) for s in ortho_s + adam_s), "param_dtype": "bf16",
-                   "state_dtype": "f32", "ns_dtype": "f16", "decouple_md": MD, "lr": ORTHO_LR,
-                   "parallelism": f"fsdp{world}" if world > 1 else "single",
-                   "l2": "no flush: every step reads params, grads and state (~70 GB) >> 126 MB L2"},
+        "config": bench_config(args, world),
         "roofline": {"bound": "tensor", "kernel": "ns_gemm2_kernel (Newton-Schulz phase)",
                      "achieved": round(achieved, 1) if achieved else None, "peak": round(peak_job, 1),
                      "unit": "TFLOP/s", "frac": round(achieved / peak_job, 3) if achieved else None,
@@ -550,8 +581,7 @@ def gpu_arm(args, rank, world, local_rank):
     cpu = None
     if not args.no_cpu_baseline and world == 1:
         v, sample, secs = cpu_oracle_sample()
-        cpu = {"value": round(v, 3), "unit": "ms", "cores": os.cpu_count() or 1, "kind": "port", "sample": sample,
-               "sample_cpu_seconds": round(secs, 2)}
+        cpu = cpu_baseline_entry(v, sample, os.cpu_count() or 1, {"sample_cpu_seconds": round(secs, 2)})
     line = result_line(args, world, ms, ns_launch_ms, ns_dense_all, ns_exec_all, mom_ms, mom_bytes, cpu, e2e,
                        host_ms, host_enqueue_ms, launches, clocks)
     if stages:

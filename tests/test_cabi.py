@@ -96,8 +96,10 @@ def test_host_only_entry_points(lib):
     assert lib.thorn_ns_workspace_bytes(3, 512, 512) == 4 * 3 * 512 * 512 * 2
     assert lib.thorn_ns_workspace_bytes(2, 96, 32) == lib.thorn_ns_workspace_bytes(2, 32, 96)
     assert lib.thorn_ns_workspace_bytes(0, 8, 8) == 0
-    # scratch: counters + one partial per 64x256 tile (+ md row/col partials)
-    assert lib.thorn_sumsq_scratch_bytes(1, 64, 256) == (4 + 1) * 4
+    # scratch: counters + one partial per 64x256 tile (+ md row/col partials); the renorm sums
+    # of squares keep fp64 partials
+    assert lib.thorn_sumsq_scratch_bytes(1, 64, 256) == 4 * 4 + 1 * 8
+    assert lib.thorn_sumsq_scratch_bytes(5, 130, 300) == 8 * 4 + 5 * 3 * 2 * 8
     assert lib.thorn_ortho_pre_scratch_bytes(2, 128, 512, 0) > 0
     assert lib.thorn_ortho_pre_scratch_bytes(2, 128, 512, 1) > lib.thorn_ortho_pre_scratch_bytes(2, 128, 512, 0)
     assert lib.thorn_pnn_scratch_bytes(3, 100) == (4 + 2 * 300) * 4

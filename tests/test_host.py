@@ -464,3 +464,6 @@ def test_bench_reference_arm_line(monkeypatch, capsys):
     assert line["impl"] == "reference" and line["value"] == 1234.5 and line["higher_is_better"] is False
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["value"] == 1234.5
     assert line["e2e"] == {"value": 1234.5, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    # the same workload description as the GPU arm's line
+    args.layers = None
+    assert line["config"] == bench.bench_config(args, 1)

@@ -135,6 +135,24 @@ __device__ __forceinline__ float block_sum(float x, float* red /* >= 32 floats *
   return t;
 }
 
+__device__ __forceinline__ double warp_sum_d(double x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+// Block-wide fp64 sum; every thread gets the result.  blockDim.x multiple of 32, <= 1024.
+__device__ __forceinline__ double block_sum_d(double x, double* red /* >= 32 doubles */) {
+  x = warp_sum_d(x);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = x;
+  __syncthreads();
+  double t = (l < nw) ? red[l] : 0.0;
+  t = warp_sum_d(t);
+  return t;
+}
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------

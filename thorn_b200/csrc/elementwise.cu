@@ -219,28 +219,43 @@ __host__ __device__ inline PreLayout pre_layout(int64_t B, int64_t R, int64_t C,
   return L;
 }
 
-// Scratch of a per-sub-matrix sum over 2-D tiles (post / sumsq).
+// Scratch of a per-sub-matrix sum over 2-D tiles (post / sumsq): B counters,
+// padded to 16 bytes, then B x tiles fp64 partials.
 __host__ __device__ inline int64_t tiles_per_mat(int64_t R, int64_t C) {
   return ((R + kTR - 1) / kTR) * ((C + kTC - 1) / kTC);
 }
-__host__ __device__ inline int64_t sq_pf(int64_t B) { return (B + 3) / 4 * 4; }  // float offset of partials
+__host__ __device__ inline int64_t sq_pf(int64_t B) { return (B + 3) / 4 * 4; }  // 4-byte words of counters
 __host__ __device__ inline int64_t sq_bytes(int64_t B, int64_t R, int64_t C) {
-  return (sq_pf(B) + B * tiles_per_mat(R, C)) * 4;
+  return sq_pf(B) * 4 + B * tiles_per_mat(R, C) * 8;
 }
 
-// Partials of one value per 2-D tile, then the last tile block of each
-// sub-matrix writes the fixed-order sum (used by post and sumsq).
+// Fixed-order fp64 block sum of n partials (each zeroed after it is read).
+__device__ __forceinline__ double ordered_sum_d(double* x, int64_t n, double* red) {
+  double s = 0.0;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    s += __ldcg(x + i);
+    x[i] = 0.0;
+  }
+  return block_sum_d(s, red);
+}
+
+// Sum of squares of a sub-matrix (the decouple_md renorm, thorn.py:1414-1416,
+// 1716-1717): per-tile fp64 partials, then the last tile block of each
+// sub-matrix writes the fixed-order fp64 sum rounded once to fp32.  The
+// reference sums in fp32; fp64 keeps the sum within one rounding of the exact
+// value, which the renorm's scale factor (and with it the whole parameter)
+// carries straight into the update.
 __device__ __forceinline__ void tile_sum_to(float* out, void* scratch, const Tile& t, int64_t B, int64_t R,
-                                            int64_t C, float v, float* red) {
+                                            int64_t C, double v, double* red) {
   unsigned* cnt = (unsigned*)scratch;
-  float* part = (float*)scratch + sq_pf(B);
+  double* part = reinterpret_cast<double*>((char*)scratch + sq_pf(B) * 4);
   const int64_t tpm = tiles_per_mat(R, C);
   const int64_t lt = (t.r0 / kTR) * ((C + kTC - 1) / kTC) + t.c0 / kTC;
-  const float tot = block_sum(v, red);
+  const double tot = block_sum_d(v, red);
   if (threadIdx.x == 0) part[t.b * tpm + lt] = tot;
   if (last_block(cnt + t.b, (unsigned)tpm)) {
-    const float s = ordered_sum(part + t.b * tpm, tpm, red);
-    if (threadIdx.x == 0) out[t.b] = s;
+    const double s = ordered_sum_d(part + t.b * tpm, tpm, red);
+    if (threadIdx.x == 0) out[t.b] = (float)s;
   }
 }
 
@@ -686,7 +701,7 @@ struct PostUnits {
 
 template <class U, class P, bool ASYNC = false>
 __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_constant__ PostArgs a) {
-  __shared__ float red[32];
+  __shared__ double red[32];
   extern __shared__ uint4 post_stage[];  // ASYNC only: [kPreStages][PostUnits::all][kThreads]
   const int ti = find_tensor(a.pk, blockIdx.x);
   const thorn_ortho_post_tensor& e = a.pk.t[ti];
@@ -720,7 +735,7 @@ __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_const
   };
 #pragma unroll
   for (int i = 0; i < kPreAhead; ++i) issue(i);
-  float sq = 0.f;
+  double sq = 0.0;
   for (int rr = warp; rr < kTR; rr += 8) {
     const int64_t r = t.r0 + rr;
     if (r >= e.rows || nc == 0) break;
@@ -750,9 +765,11 @@ __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_const
       pv[k] = pv[k] - e.lr * u;
     }
     rnd8<P>(pv);
+    if (e.p_normsq != nullptr) {
 #pragma unroll
-    for (int k = 0; k < 8; ++k)
-      if (k < nc) sq += pv[k] * pv[k];
+      for (int k = 0; k < 8; ++k)
+        if (k < nc) sq = fma((double)pv[k], (double)pv[k], sq);
+    }
     store_n((P*)e.p + off, pv, nc, vec);
   }
   if constexpr (ASYNC) cp_async_wait<0>();  // no copy into shared memory outlives the block
@@ -867,7 +884,7 @@ struct SumsqArgs {
 
 template <class T>
 __global__ void __launch_bounds__(kThreads) sumsq_kernel(const __grid_constant__ SumsqArgs a) {
-  __shared__ float red[32];
+  __shared__ double red[32];
   const int ti = find_tensor(a.pk, blockIdx.x);
   const thorn_sumsq_tensor& e = a.pk.t[ti];
   const bool vec = a.pk.vec[ti];
@@ -875,7 +892,7 @@ __global__ void __launch_bounds__(kThreads) sumsq_kernel(const __grid_constant__
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t c = t.c0 + lane * 8;
   const int nc = (int)max64(0, min64(8, e.cols - c));
-  float sq = 0.f;
+  double sq = 0.0;
   for (int rr = warp; rr < kTR; rr += 8) {
     const int64_t r = t.r0 + rr;
     if (r >= e.rows || nc == 0) break;
@@ -883,7 +900,7 @@ __global__ void __launch_bounds__(kThreads) sumsq_kernel(const __grid_constant__
     load_n((const T*)e.x + (t.b * e.rows + r) * e.cols + c, v, nc, vec);
 #pragma unroll
     for (int k = 0; k < 8; ++k)
-      if (k < nc) sq += v[k] * v[k];
+      if (k < nc) sq = fma((double)v[k], (double)v[k], sq);
   }
   tile_sum_to(e.out, e.scratch, t, e.batch, e.rows, e.cols, sq, red);
 }
