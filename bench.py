@@ -376,6 +376,8 @@ def gpu_arm(args, rank, world, local_rank):
     ])
     opt.pipeline_exchange = bool(args.pipeline_exchange)
     opt.exchange = args.exchange
+    if args.ns_batch_elems:
+        opt.polar_decomp_batch_size = int(args.ns_batch_elems)
     apply_switches(args)
 
     def local(t):
@@ -614,8 +616,6 @@ def apply_switches(args):
     from thorn_b200 import _native
 
     lib = _native.load()
-    if args.elementwise_async:
-        lib.thorn_set_elementwise_async(1)
     if args.gemm_pdl:
         lib.thorn_set_gemm_pdl(1)
     if args.gemm_l2_hints:
@@ -838,8 +838,6 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="thorn_b200", choices=["thorn_b200", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--elementwise-async", action="store_true",
-                    help="momentum pass with cp.async row staging (thorn_set_elementwise_async)")
     ap.add_argument("--gemm-pdl", action="store_true",
                     help="NS GEMMs with programmatic dependent launch (thorn_set_gemm_pdl)")
     ap.add_argument("--gemm-l2-hints", action="store_true",
@@ -852,6 +850,8 @@ def main():
                     help="pipelined (default): thorn_b200.PinnedStepper overlaps both copies with the steps, "
                          "falling back to serial if it cannot run; serial: copy in, step, copy out on one stream")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ns-batch-elems", type=int, default=None,
+                    help="THORN.polar_decomp_batch_size: elements per Newton-Schulz batch (default: the optimizer's)")
     ap.add_argument("--ns-only", default=None, help="BxRxC: time thorn_ns_batched alone on this batch (profiling)")
     ap.add_argument("--ns-library", action="store_true",
                     help="with --ns-only: time the same recurrences on torch/cuBLAS GEMMs instead (library baseline)")

@@ -65,12 +65,6 @@ THORN_API int thorn_set_gemm_pair(int enable);
  * strides that are multiples of 8.  Returns the previous setting.  Both settings
  * give bit-identical results. */
 THORN_API int thorn_set_gemm_staged_epilogue(int enable);
-/* Streaming passes of thorn_ortho_pre_multi (momentum), thorn_ortho_post_multi
- * (apply) and thorn_md_finalize_multi: nonzero streams each thread's rows into
- * shared memory four rows ahead with cp.async (bytes in flight without
- * registers); zero (default) loads them into registers.  Returns the previous
- * setting.  Both settings give bit-identical results. */
-THORN_API int thorn_set_elementwise_async(int enable);
 /* NS GEMM launches: nonzero uses programmatic dependent launch, so each GEMM's
  * set-up (barriers, TMEM, descriptor prefetch) overlaps the previous kernel's
  * tail and its CTAs wait for that kernel to finish before touching global
@@ -87,11 +81,17 @@ THORN_API int thorn_set_gemm_l2_hints(int enable);
  * the kernel returns and the context stays usable.  Returns the previous limit. */
 THORN_API uint64_t thorn_set_wait_limit_ns(uint64_t limit_ns);
 /* Failure test of the bounded waits: nonzero makes the NS GEMMs' TMA producers
- * issue no loads, so no copy or MMA is ever in flight and the MMA warp's wait
- * for its first operand stage runs out after the wait limit.  Results are
- * undefined while set; zero (default) is the normal path.  Returns the previous
- * setting.  For tests of the error path only. */
+ * issue no loads (and the small-matrix NS kernel issue no MMA), so no copy or
+ * MMA is ever in flight and the first wait for one runs out after the wait
+ * limit.  Results are undefined while set; zero (default) is the normal path.
+ * Returns the previous setting.  For tests of the error path only. */
 THORN_API int thorn_set_gemm_test_stall(int enable);
+/* Newton-Schulz of matrices whose smaller dimension is at most 128 and larger
+ * at most 512: nonzero (default) runs the whole iteration of a batch in one
+ * launch, one CTA per matrix with every operand resident in shared memory;
+ * zero runs the same products as separate GEMM launches.  Returns the previous
+ * setting. */
+THORN_API int thorn_set_ns_small(int enable);
 
 /* --------------------------------------------------------------------------
  * (R)Adam(-atan2)W over many tensors in one launch per dtype pair.

@@ -134,8 +134,9 @@ def test_argument_validation_without_gpu(lib):
 
 
 @pytest.mark.parametrize("name,default", [("thorn_set_gemm_pair", 1), ("thorn_set_gemm_staged_epilogue", 1),
-                                          ("thorn_set_elementwise_async", 0), ("thorn_set_gemm_pdl", 0),
-                                          ("thorn_set_gemm_l2_hints", 0), ("thorn_set_gemm_test_stall", 0)])
+                                          ("thorn_set_gemm_pdl", 0),
+                                          ("thorn_set_gemm_l2_hints", 0), ("thorn_set_gemm_test_stall", 0),
+                                          ("thorn_set_ns_small", 1)])
 def test_kernel_switches(lib, name, default):
     """Each switch returns its previous setting; the defaults are the measured kernels."""
     fn = getattr(lib, name)
@@ -145,6 +146,27 @@ def test_kernel_switches(lib, name, default):
     assert fn(default) == 1 - default
     assert fn(7 if default else 0) == default  # any nonzero value means on
     fn(default)
+
+
+def test_empty_shards_accepted_without_device_work(lib):
+    """A Shard(0) shard with no rows (a matrix with fewer rows than ranks) arrives with null
+    data pointers; every entry point accepts it and launches nothing, with and without
+    decouple_md (so no GPU is needed here)."""
+    pre = N.array(N.OrthoPreTensor, [N.OrthoPreTensor(None, None, None, None, 1, 0, 48, None, None, 0, None, None,
+                                                       None)])
+    for md in (0, 1):
+        assert lib.thorn_ortho_pre_multi(pre, 1, 0, 0, 0, 0.9, md, 0, None) == 0
+    cast = N.array(N.NsCastTensor, [N.NsCastTensor(None, None, None, None, 1, 0, 48, None, None, 0, 1)])
+    assert lib.thorn_ns_cast_multi(cast, 1, 0, 0, 0, 2, 0.9, None) == 0
+    post = N.array(N.OrthoPostTensor, [N.OrthoPostTensor(None, None, None, None, None, 1, 0, 48, 1e-3, None, 0)])
+    assert lib.thorn_ortho_post_multi(post, 1, 2, 0, 0.1, None) == 0
+    fin = N.array(N.MdFinalTensor, [N.MdFinalTensor(None, None, None, 0, None, None, 0, 1, 0, 48)])
+    assert lib.thorn_md_finalize_multi(fin, 1, 0, None) == 0
+    pnn = N.array(N.PnnTensor, [N.PnnTensor(None, None, None, 1, 0, 48, None, 1)])
+    assert lib.thorn_pnn_stats_multi(pnn, 1, 2, 0, None) == 0
+    # a non-empty tensor with the same null pointers is still rejected
+    fin_bad = N.array(N.MdFinalTensor, [N.MdFinalTensor(None, None, None, 0, None, None, 0, 1, 2, 48)])
+    assert lib.thorn_md_finalize_multi(fin_bad, 1, 0, None) == 1
 
 
 def test_wait_limit_setter(lib):

@@ -194,6 +194,37 @@ def test_ns_matches_oracle(shape):
     assert err <= 2e-2, err
 
 
+@pytest.mark.parametrize("ns_dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(6, 64, 96), (6, 128, 384), (4, 128, 128), (2, 2, 128), (3, 96, 64),
+                                   (2, 100, 37), (1, 1, 64), (1, 512, 128), (2, 128, 512), (2, 40, 40)])
+def test_ns_small_kernel_matches_gemm_sequence(shape, ns_dtype):
+    """Matrices with min dim <= 128 and max dim <= 512 run the whole Newton-Schulz iteration in
+    one launch (one CTA per matrix, operands resident in shared memory).  Against the same
+    recurrences issued as separate GEMM launches on the same input: the same products, operand
+    orders and roundings, so the two agree to accumulation order at most; and one launch."""
+    from thorn_b200 import _native as N
+
+    lib = N.load()
+    torch.manual_seed(11)
+    u = torch.randn(shape, device="cuda") * 1e-3
+    prev = lib.thorn_set_ns_small(1)
+    try:
+        n0 = N.launch_count()
+        small, co, rs = _ns_gpu_t(u, ns_dtype)
+        assert N.launch_count() - n0 == 1
+        lib.thorn_set_ns_small(0)
+        n0 = N.launch_count()
+        gemms, _, _ = _ns_gpu_t(u, ns_dtype)
+        assert N.launch_count() - n0 > 1
+    finally:
+        lib.thorn_set_ns_small(prev)
+    a, b = small.float().cpu().numpy(), gemms.float().cpu().numpy()
+    assert np.isfinite(a).all()
+    rel = C.rel_fro(a, b)
+    print(shape, ns_dtype, "bitwise equal" if np.array_equal(a, b) else f"rel {rel:.2e}")
+    assert rel <= 1e-3, rel
+
+
 @pytest.mark.parametrize("transpose", [False, True])
 def test_ns_ill_conditioned_near_square(transpose):
     """The 66 x 64 momentum of the shard_uneven case: its normalised smallest singular value

@@ -225,15 +225,16 @@ def test_custom_ops_match_c_abi():
         assert C.rel_fro(got.cpu().numpy(), ref.float().cpu().numpy()) <= 1e-2
 
 
-@pytest.mark.parametrize("shape", [(2, 96, 64), (1, 256, 512)])
-def test_bounded_wait_runs_out_and_device_recovers(shape):
-    """The failure path of the NS GEMMs' bounded waits, made to run without any fault.
+@pytest.mark.parametrize("shape,small", [((2, 96, 64), True), ((2, 96, 64), False), ((1, 256, 512), False)])
+def test_bounded_wait_runs_out_and_device_recovers(shape, small):
+    """The failure path of the NS kernels' bounded waits, made to run without any fault.
 
-    With the test stall switch on, the GEMMs' TMA producers issue no loads, so nothing is
-    ever in flight and the MMA warp's wait for its first operand stage runs out after the
-    (shortened) wait limit.  The call must return, the error flag must be set (also through
-    THORN.device_error()), and the next normal call on the same device must be correct.
-    (96x64 runs the single-CTA GEMM, 256x512 the 2-CTA cluster GEMM.)"""
+    With the test stall switch on, the GEMMs' TMA producers issue no loads (the small-matrix
+    kernel issues no MMA), so nothing is ever in flight and the first wait for one runs out
+    after the (shortened) wait limit.  The call must return, the error flag must be set (also
+    through THORN.device_error()), and the next normal call on the same device must be
+    correct.  (96x64 runs the one-launch small-matrix kernel, or with it switched off the
+    single-CTA GEMM; 256x512 the 2-CTA cluster GEMM.)"""
     import time
 
     from thorn_b200 import THORN
@@ -242,6 +243,7 @@ def test_bounded_wait_runs_out_and_device_recovers(shape):
     lib = N.load()
     torch.manual_seed(31)
     u = torch.randn(shape, device="cuda") * 1e-3
+    prev_small = lib.thorn_set_ns_small(1 if small else 0)
     prev_limit = lib.thorn_set_wait_limit_ns(20 * 10 ** 6)
     prev_stall = lib.thorn_set_gemm_test_stall(1)
     try:
@@ -267,6 +269,7 @@ def test_bounded_wait_runs_out_and_device_recovers(shape):
     finally:
         lib.thorn_set_gemm_test_stall(prev_stall)
         lib.thorn_set_wait_limit_ns(prev_limit)
+        lib.thorn_set_ns_small(prev_small)
     # the context is usable: the same NS now matches the oracle
     got, co5, rs5 = _ns_gpu(u)
     O.NS_DTYPE = "f16"

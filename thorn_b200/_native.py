@@ -78,11 +78,11 @@ _PROTOS = {
     "thorn_gemm_flops": (None, [POINTER(c_double), POINTER(c_double)]),
     "thorn_set_gemm_pair": (c_int, [c_int]),
     "thorn_set_gemm_staged_epilogue": (c_int, [c_int]),
-    "thorn_set_elementwise_async": (c_int, [c_int]),
     "thorn_set_gemm_pdl": (c_int, [c_int]),
     "thorn_set_gemm_l2_hints": (c_int, [c_int]),
     "thorn_set_wait_limit_ns": (c_uint64, [c_uint64]),
     "thorn_set_gemm_test_stall": (c_int, [c_int]),
+    "thorn_set_ns_small": (c_int, [c_int]),
     "thorn_adamw_multi": (c_int, [POINTER(AdamTensor), c_int, c_int, c_int, c_double, c_double, c_float, c_float,
                                   c_void_p]),
     "thorn_ortho_pre_scratch_bytes": (c_int64, [c_int64, c_int64, c_int64, c_int]),

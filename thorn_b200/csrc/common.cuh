@@ -82,6 +82,20 @@ __device__ __forceinline__ void rnd8(float* v) {
   }
 }
 
+// Packed 16-bit products.  The fp32 product of two bf16 (or two fp16) values is
+// exact, so one packed multiply with round-to-nearest-even gives, per element,
+// exactly the fp32 product rounded once to T: an fp32 multiply and a rounding
+// to T in one instruction for two elements.
+template <class T> struct Pair2;
+template <> struct Pair2<__nv_bfloat16> { using V = __nv_bfloat162; };
+template <> struct Pair2<__half> { using V = __half2; };
+template <class T>
+__device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
+  using V = typename Pair2<T>::V;
+  const V r = __hmul2(*reinterpret_cast<const V*>(&a), *reinterpret_cast<const V*>(&b));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+
 template <class H> struct Vec8Half {
   static __device__ __forceinline__ void load(const H* p, float* v) {
     const uint4 r = *reinterpret_cast<const uint4*>(p);

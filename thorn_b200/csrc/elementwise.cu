@@ -10,6 +10,7 @@
 #include <mutex>
 #include <math.h>
 #include <type_traits>
+#include <vector>
 
 #include "common.cuh"
 
@@ -288,53 +289,14 @@ struct PreArgs {
   int write_grad;
 };
 
-// Async-copy staging of the momentum pass (ASYNC = true): each thread streams
-// its rows' g, m (and p) chunks into shared memory kPreAhead rows ahead with
-// cp.async, so the bytes in flight do not occupy registers.  Per stage and
-// thread the chunks are 16-byte units laid out [unit][thread]: a warp's unit
-// accesses are 512 contiguous bytes, free of bank conflicts.
-constexpr int kPreAhead = 4;
-constexpr int kPreStages = kPreAhead + 1;
-template <class P, class S>
-struct PreUnits {
-  static constexpr int g = 8 * (int)sizeof(P) / 16;  // units of g (and of p)
-  static constexpr int m = 8 * (int)sizeof(S) / 16;
-  static constexpr int all = 2 * g + m;
-  static constexpr int bytes = kPreStages * all * kThreads * 16;
-};
-
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
-               "l"(gmem_src)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-// 8 values of type T from 16-byte units at u[0] (and u[stride] for 4-byte T)
-template <class T>
-__device__ __forceinline__ void load8_units(const uint4* u, int stride, float* v) {
-  if constexpr (sizeof(T) == 4) {
-    const uint4 a = u[0], b = u[stride];
-    v[0] = __uint_as_float(a.x); v[1] = __uint_as_float(a.y); v[2] = __uint_as_float(a.z); v[3] = __uint_as_float(a.w);
-    v[4] = __uint_as_float(b.x); v[5] = __uint_as_float(b.y); v[6] = __uint_as_float(b.z); v[7] = __uint_as_float(b.w);
-  } else {
-    const uint4 a = u[0];
-    unpack2(a.x, v[0], v[1], (T*)nullptr);
-    unpack2(a.y, v[2], v[3], (T*)nullptr);
-    unpack2(a.z, v[4], v[5], (T*)nullptr);
-    unpack2(a.w, v[6], v[7], (T*)nullptr);
-  }
-}
-
-template <class P, class S, class U, bool MD, bool ASYNC = false>
+// PACKED: every tensor of the launch is a 16-bit parameter with decouple_md and
+// rows of whole 16-byte chunks (the host sorts tensors into such launches), so
+// the direction recovery runs as packed products only.
+template <class P, class S, class U, bool MD, bool PACKED = false>
 __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_constant__ PreArgs a) {
   __shared__ float red[32];
   __shared__ float colacc[MD ? 8 : 1][MD ? kTC : 1];
-  extern __shared__ uint4 pre_stage[];  // ASYNC only: [kPreStages][PreUnits::all][kThreads]
+  constexpr bool kHalfP = !std::is_same<P, float>::value;
   const int ti = find_tensor(a.pk, blockIdx.x);
   const thorn_ortho_pre_tensor& e = a.pk.t[ti];
   const bool vec = a.pk.vec[ti];
@@ -355,100 +317,111 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
   for (int k = 0; k < 8; ++k) csum[k] = 0.f;
   float csp[8];
   if (MD && !scalar_gain) load8f(e.col_sp + t.b * e.cols + c, csp, nc, vec);
-  float rsum_scalar = 0.f;
-  using UN = PreUnits<P, S>;
-  const bool staged = ASYNC && vec && nc == 8;  // this thread's chunks are whole, aligned units
-  // ASYNC: copy this thread's chunks of its i-th row (row warp + 8 i of the tile) into stage i % kPreStages;
-  // every call commits one group (possibly empty), so group counts stay uniform
-  auto issue = [&](int i) {
-    if constexpr (ASYNC) {
-      const int64_t r = t.r0 + warp + 8 * i;
-      if (staged && i < kTR / 8 && r < e.rows) {
-        const int64_t off = (t.b * e.rows + r) * e.cols + c;
-        uint4* st = pre_stage + (size_t)(i % kPreStages) * UN::all * kThreads + threadIdx.x;
-        const char* gs = reinterpret_cast<const char*>((const P*)e.g + off);
+  // 16-bit parameters in whole 16-byte chunks: the direction recovery as packed
+  // products (mul2), which round exactly like the fp32 products + roundings of
+  // the general path below
+  static_assert(!PACKED || (MD && kHalfP), "the packed kernel serves 16-bit parameters with decouple_md");
+  const bool packed = PACKED && nc == 8;
+  uint32_t cs2[4] = {0u, 0u, 0u, 0u};
+  if constexpr (PACKED) {
+    if (packed && !scalar_gain) {
 #pragma unroll
-        for (int u = 0; u < UN::g; ++u) cp_async16(st + u * kThreads, gs + 16 * u);
-        if (momentum) {
-          const char* ms = reinterpret_cast<const char*>((const S*)e.m + off);
-#pragma unroll
-          for (int u = 0; u < UN::m; ++u) cp_async16(st + (UN::g + u) * kThreads, ms + 16 * u);
-        }
-        if (MD) {
-          const char* ps = reinterpret_cast<const char*>((const P*)e.p + off);
-#pragma unroll
-          for (int u = 0; u < UN::g; ++u) cp_async16(st + (UN::g + UN::m + u) * kThreads, ps + 16 * u);
-        }
-      }
-      cp_async_commit();
+      for (int q = 0; q < 4; ++q) cs2[q] = pack2(csp[2 * q], csp[2 * q + 1], (P*)nullptr);
     }
-  };
-#pragma unroll
-  for (int i = 0; i < kPreAhead; ++i) issue(i);
+  }
+  float rsum_scalar = 0.f;
   for (int rr = warp; rr < kTR; rr += 8) {
     const int64_t r = t.r0 + rr;
     if (r >= e.rows) break;
     float rs = 0.f;
-    const uint4* st = nullptr;
-    if constexpr (ASYNC) {
-      const int i = rr >> 3;
-      issue(i + kPreAhead);
-      cp_async_wait<kPreAhead>();  // row i's group has landed
-      st = pre_stage + (size_t)(i % kPreStages) * UN::all * kThreads + threadIdx.x;
-    }
     if (nc > 0) {
       const int64_t off = (t.b * e.rows + r) * e.cols + c;
       float gv[8], mv[8];
-      if (staged) load8_units<P>(st, kThreads, gv);
-      else load_n((const P*)e.g + off, gv, nc, vec);
-      if (momentum) {
-        if (staged) load8_units<S>(st + UN::g * kThreads, kThreads, mv);
-        else load_n((const S*)e.m + off, mv, nc, vec);
-      }
-      if (MD) {
-        // every step below rounds 8 values to the param dtype at once (packed
-        // conversions); lanes k >= nc hold padding and are neither summed nor stored
-        float pv[8], gain[8], pg[8];
-        if (staged) load8_units<P>(st + (UN::g + UN::m) * kThreads, kThreads, pv);
-        else load_n((const P*)e.p + off, pv, nc, vec);
-        const float rsp = scalar_gain ? e.row_sp[0] : e.row_sp[t.b * e.rows + r];
+      if (momentum) load_n((const S*)e.m + off, mv, nc, vec);
+      if constexpr (PACKED) {
+        if (packed) {
+          const uint4 g4 = *reinterpret_cast<const uint4*>((const P*)e.g + off);
+          const uint4 p4 = *reinterpret_cast<const uint4*>((const P*)e.p + off);
+          const float rsp = scalar_gain ? e.row_sp[0] : e.row_sp[t.b * e.rows + r];
+          const uint32_t rs2 = pack2(rsp, rsp, (P*)nullptr);
+          const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w}, pw[4] = {p4.x, p4.y, p4.z, p4.w};
+          uint32_t pvo[4], geo[4];
+          float part = 0.f;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) gain[k] = scalar_gain ? rsp : __fmul_rn(rsp, csp[k]);
-        if (!scalar_gain) rnd8<P>(gain);
-        // fast division (<= 2 fp32 ulp) before the rounding to the param dtype
-#pragma unroll
-        for (int k = 0; k < 8; ++k) pv[k] = __fdividef(pv[k], gain[k]);
-        rnd8<P>(pv);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) pg[k] = __fmul_rn(pv[k], gv[k]);
-        rnd8<P>(pg);
-        float part = 0.f;
-        if (scalar_gain) {
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-            if (k < nc) part = __fadd_rn(part, pg[k]);
-        } else {
-          float pc[8], pr[8];
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            pc[k] = __fmul_rn(pg[k], csp[k]);
-            pr[k] = __fmul_rn(pg[k], rsp);
-          }
-          rnd8<P>(pc);
-          rnd8<P>(pr);
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-            if (k < nc) {
-              part = __fadd_rn(part, pc[k]);
-              csum[k] = __fadd_rn(csum[k], pr[k]);
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t gain2 = scalar_gain ? rs2 : mul2<P>(rs2, cs2[q]);  // gain = rs cs
+            float p0, p1, d0, d1;
+            unpack2(pw[q], p0, p1, (P*)nullptr);
+            unpack2(gain2, d0, d1, (P*)nullptr);
+            // fast division (<= 2 fp32 ulp) before the rounding to the param dtype
+            pvo[q] = pack2(__fdividef(p0, d0), __fdividef(p1, d1), (P*)nullptr);  // p /= gain
+            const uint32_t pg2 = mul2<P>(pvo[q], gw[q]);                           // p_g = p g
+            if (scalar_gain) {
+              float a0, a1;
+              unpack2(pg2, a0, a1, (P*)nullptr);
+              part = __fadd_rn(__fadd_rn(part, a0), a1);
+            } else {
+              float c0, c1, r0, r1;
+              unpack2(mul2<P>(pg2, cs2[q]), c0, c1, (P*)nullptr);  // p_g * col gain (row-gain gradient)
+              unpack2(mul2<P>(pg2, rs2), r0, r1, (P*)nullptr);     // p_g * row gain (column-gain gradient)
+              part = __fadd_rn(__fadd_rn(part, c0), c1);
+              csum[2 * q] = __fadd_rn(csum[2 * q], r0);
+              csum[2 * q + 1] = __fadd_rn(csum[2 * q + 1], r1);
             }
+            geo[q] = mul2<P>(gw[q], gain2);  // g *= gain
+            unpack2(geo[q], gv[2 * q], gv[2 * q + 1], (P*)nullptr);
+          }
+          rs = part;
+          *reinterpret_cast<uint4*>((P*)e.p + off) = make_uint4(pvo[0], pvo[1], pvo[2], pvo[3]);
+          if (a.write_grad) *reinterpret_cast<uint4*>((P*)e.g + off) = make_uint4(geo[0], geo[1], geo[2], geo[3]);
         }
+      }
+      if constexpr (!PACKED) {
+        load_n((const P*)e.g + off, gv, nc, vec);
+        if (MD) {
+          // every step below rounds 8 values to the param dtype at once (packed
+          // conversions); lanes k >= nc hold padding and are neither summed nor stored
+          float pv[8], gain[8], pg[8];
+          load_n((const P*)e.p + off, pv, nc, vec);
+          const float rsp = scalar_gain ? e.row_sp[0] : e.row_sp[t.b * e.rows + r];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) gv[k] = __fmul_rn(gv[k], gain[k]);
-        rnd8<P>(gv);
-        rs = part;
-        store_n((P*)e.p + off, pv, nc, vec);
-        if (a.write_grad) store_n((P*)e.g + off, gv, nc, vec);
+          for (int k = 0; k < 8; ++k) gain[k] = scalar_gain ? rsp : __fmul_rn(rsp, csp[k]);
+          if (!scalar_gain) rnd8<P>(gain);
+          // fast division (<= 2 fp32 ulp) before the rounding to the param dtype
+#pragma unroll
+          for (int k = 0; k < 8; ++k) pv[k] = __fdividef(pv[k], gain[k]);
+          rnd8<P>(pv);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) pg[k] = __fmul_rn(pv[k], gv[k]);
+          rnd8<P>(pg);
+          float part = 0.f;
+          if (scalar_gain) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+              if (k < nc) part = __fadd_rn(part, pg[k]);
+          } else {
+            float pc[8], pr[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              pc[k] = __fmul_rn(pg[k], csp[k]);
+              pr[k] = __fmul_rn(pg[k], rsp);
+            }
+            rnd8<P>(pc);
+            rnd8<P>(pr);
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+              if (k < nc) {
+                part = __fadd_rn(part, pc[k]);
+                csum[k] = __fadd_rn(csum[k], pr[k]);
+              }
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k) gv[k] = __fmul_rn(gv[k], gain[k]);
+          rnd8<P>(gv);
+          rs = part;
+          store_n((P*)e.p + off, pv, nc, vec);
+          if (a.write_grad) store_n((P*)e.g + off, gv, nc, vec);
+        }
       }
       if (momentum) {
         float u[8];
@@ -472,7 +445,6 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
       else if (lane == 0) sf[L.pr + (t.b * L.tc + ct) * e.rows + r] = rs;
     }
   }
-  if constexpr (ASYNC) cp_async_wait<0>();  // no copy into shared memory outlives the block
   const int64_t gt = (t.b * L.tr + rt) * L.tc + ct;  // tile index within the tensor
   if (momentum) {
     const float tot = block_sum(sq, red);
@@ -692,17 +664,8 @@ struct PostArgs {
 };
 
 template <class U, class P>
-struct PostUnits {
-  static constexpr int u = 8 * (int)sizeof(U) / 16;
-  static constexpr int p = 8 * (int)sizeof(P) / 16;
-  static constexpr int all = u + p;
-  static constexpr int bytes = kPreStages * all * kThreads * 16;
-};
-
-template <class U, class P, bool ASYNC = false>
 __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_constant__ PostArgs a) {
   __shared__ double red[32];
-  extern __shared__ uint4 post_stage[];  // ASYNC only: [kPreStages][PostUnits::all][kThreads]
   const int ti = find_tensor(a.pk, blockIdx.x);
   const thorn_ortho_post_tensor& e = a.pk.t[ti];
   const bool vec = a.pk.vec[ti];
@@ -714,27 +677,6 @@ __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_const
   if (e.mat_stats != nullptr) {
     gscale = sqrtf(e.mat_stats[2 * t.b]) / fmaxf(sqrtf(e.mat_stats[2 * t.b + 1]), a.eps);
   }
-  using UN = PostUnits<U, P>;
-  const bool staged = ASYNC && vec && nc == 8;
-  // ASYNC: this thread's U and p chunks of its i-th row into stage i % kPreStages (one group per call)
-  auto issue = [&](int i) {
-    if constexpr (ASYNC) {
-      const int64_t r = t.r0 + warp + 8 * i;
-      if (staged && i < kTR / 8 && r < e.rows) {
-        const int64_t off = (t.b * e.rows + r) * e.cols + c;
-        uint4* st = post_stage + (size_t)(i % kPreStages) * UN::all * kThreads + threadIdx.x;
-        const char* us = reinterpret_cast<const char*>((const U*)e.U + off);
-        const char* ps = reinterpret_cast<const char*>((const P*)e.p + off);
-#pragma unroll
-        for (int q = 0; q < UN::u; ++q) cp_async16(st + q * kThreads, us + 16 * q);
-#pragma unroll
-        for (int q = 0; q < UN::p; ++q) cp_async16(st + (UN::u + q) * kThreads, ps + 16 * q);
-      }
-      cp_async_commit();
-    }
-  };
-#pragma unroll
-  for (int i = 0; i < kPreAhead; ++i) issue(i);
   double sq = 0.0;
   for (int rr = warp; rr < kTR; rr += 8) {
     const int64_t r = t.r0 + rr;
@@ -743,19 +685,8 @@ __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_const
     float scale = 1.f;
     if (e.row_scale != nullptr) scale = e.row_scale[t.b * e.rows + r] * gscale;
     float uv[8], pv[8];
-    if constexpr (ASYNC) {
-      const int i = rr >> 3;
-      issue(i + kPreAhead);
-      cp_async_wait<kPreAhead>();
-    }
-    if (staged) {
-      const uint4* st = post_stage + (size_t)((rr >> 3) % kPreStages) * UN::all * kThreads + threadIdx.x;
-      load8_units<U>(st, kThreads, uv);
-      load8_units<P>(st + UN::u * kThreads, kThreads, pv);
-    } else {
-      load_n((const U*)e.U + off, uv, nc, vec);
-      load_n((const P*)e.p + off, pv, nc, vec);
-    }
+    load_n((const U*)e.U + off, uv, nc, vec);
+    load_n((const P*)e.p + off, pv, nc, vec);
     if (e.round_u) rnd8<P>(uv);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
@@ -766,13 +697,15 @@ __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_const
     }
     rnd8<P>(pv);
     if (e.p_normsq != nullptr) {
+      // eight squares in fp32 (each exact for a 16-bit parameter), their sum into fp64
+      float s8 = 0.f;
 #pragma unroll
       for (int k = 0; k < 8; ++k)
-        if (k < nc) sq = fma((double)pv[k], (double)pv[k], sq);
+        if (k < nc) s8 = __fmaf_rn(pv[k], pv[k], s8);
+      sq += (double)s8;
     }
     store_n((P*)e.p + off, pv, nc, vec);
   }
-  if constexpr (ASYNC) cp_async_wait<0>();  // no copy into shared memory outlives the block
   if (e.p_normsq != nullptr) tile_sum_to(e.p_normsq, e.scratch, t, e.batch, e.rows, e.cols, sq, red);
 }
 
@@ -811,9 +744,9 @@ struct FinalArgs {
   Pack<thorn_md_final_tensor> pk;
 };
 
-template <class P, bool ASYNC = false>
+template <class P>
 __global__ void __launch_bounds__(kThreads) md_finalize_kernel(const __grid_constant__ FinalArgs a) {
-  extern __shared__ uint4 fin_stage[];  // ASYNC only: [kPreStages][p units][kThreads]
+  constexpr bool kHalfP = !std::is_same<P, float>::value;
   const int ti = find_tensor(a.pk, blockIdx.x);
   const thorn_md_final_tensor& e = a.pk.t[ti];
   const bool vec = a.pk.vec[ti];
@@ -832,33 +765,41 @@ __global__ void __launch_bounds__(kThreads) md_finalize_kernel(const __grid_cons
   const bool split = !e.scalar_gain;
   float csp[8];
   if (split) load8f(e.col_sp + t.b * e.cols + c, csp, nc, vec);
-  constexpr int kPU = 8 * (int)sizeof(P) / 16;
-  const bool staged = ASYNC && vec && nc == 8;
-  auto issue = [&](int i) {
-    if constexpr (ASYNC) {
-      const int64_t r = t.r0 + warp + 8 * i;
-      if (staged && i < kTR / 8 && r < e.rows) {
-        const char* ps = reinterpret_cast<const char*>((const P*)e.p + (t.b * e.rows + r) * e.cols + c);
-        uint4* st = fin_stage + (size_t)(i % kPreStages) * kPU * kThreads + threadIdx.x;
+  if constexpr (kHalfP) {
+    if (vec && nc == 8) {
+      // every factor (renorm scale, row gain, column gain) is a value of P, so each
+      // multiply-and-round is one packed product
+      const uint32_t f2 = pack2(f, f, (P*)nullptr);
+      uint32_t cs2[4] = {0u, 0u, 0u, 0u};
+      if (split) {
 #pragma unroll
-        for (int q = 0; q < kPU; ++q) cp_async16(st + q * kThreads, ps + 16 * q);
+        for (int q = 0; q < 4; ++q) cs2[q] = pack2(csp[2 * q], csp[2 * q + 1], (P*)nullptr);
       }
-      cp_async_commit();
-    }
-  };
+      for (int rr = warp; rr < kTR; rr += 8) {
+        const int64_t r = t.r0 + rr;
+        if (r >= e.rows) break;
+        P* pp = (P*)e.p + (t.b * e.rows + r) * e.cols + c;
+        const uint4 p4 = *reinterpret_cast<const uint4*>(pp);
+        const float rsp = split ? e.row_sp[t.b * e.rows + r] : e.row_sp[0];
+        const uint32_t rs2 = pack2(rsp, rsp, (P*)nullptr);
+        uint32_t w[4] = {p4.x, p4.y, p4.z, p4.w};
 #pragma unroll
-  for (int i = 0; i < kPreAhead; ++i) issue(i);
+        for (int q = 0; q < 4; ++q) {
+          if (renorm) w[q] = mul2<P>(w[q], f2);
+          w[q] = mul2<P>(w[q], rs2);
+          if (split) w[q] = mul2<P>(w[q], cs2[q]);
+        }
+        *reinterpret_cast<uint4*>(pp) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      return;
+    }
+  }
   for (int rr = warp; rr < kTR; rr += 8) {
     const int64_t r = t.r0 + rr;
     if (r >= e.rows) break;
     const int64_t off = (t.b * e.rows + r) * e.cols + c;
     float pv[8];
-    if constexpr (ASYNC) {
-      issue((rr >> 3) + kPreAhead);
-      cp_async_wait<kPreAhead>();
-    }
-    if (staged) load8_units<P>(fin_stage + (size_t)((rr >> 3) % kPreStages) * kPU * kThreads + threadIdx.x, kThreads, pv);
-    else load_n((const P*)e.p + off, pv, nc, vec);
+    load_n((const P*)e.p + off, pv, nc, vec);
     const float rsp = split ? e.row_sp[t.b * e.rows + r] : e.row_sp[0];
     if (renorm) {
 #pragma unroll
@@ -875,7 +816,6 @@ __global__ void __launch_bounds__(kThreads) md_finalize_kernel(const __grid_cons
     }
     store_n((P*)e.p + off, pv, nc, vec);
   }
-  if constexpr (ASYNC) cp_async_wait<0>();  // no copy into shared memory outlives the block
 }
 
 struct SumsqArgs {
@@ -898,9 +838,11 @@ __global__ void __launch_bounds__(kThreads) sumsq_kernel(const __grid_constant__
     if (r >= e.rows || nc == 0) break;
     float v[8];
     load_n((const T*)e.x + (t.b * e.rows + r) * e.cols + c, v, nc, vec);
+    float s8 = 0.f;  // eight squares in fp32, their sum into fp64
 #pragma unroll
     for (int k = 0; k < 8; ++k)
-      if (k < nc) sq = fma((double)v[k], (double)v[k], sq);
+      if (k < nc) s8 = __fmaf_rn(v[k], v[k], s8);
+    sq += (double)s8;
   }
   tile_sum_to(e.out, e.scratch, t, e.batch, e.rows, e.cols, sq, red);
 }
@@ -984,11 +926,6 @@ extern "C" int thorn_adamw_multi(const thorn_adam_tensor* ts, int n, int p_dtype
   return d ? d : rc;
 }
 
-// Momentum pass with cp.async row staging (1) or register loads (0, default).
-static std::atomic<int> g_async_pre{0};
-
-extern "C" int thorn_set_elementwise_async(int enable) { return g_async_pre.exchange(enable ? 1 : 0); }
-
 extern "C" int thorn_ortho_pre_multi(const thorn_ortho_pre_tensor* ts, int n, int p_dtype, int s_dtype,
                                      int u_dtype, float beta1, int md, int write_grad, void* stream) {
   if (n < 0 || (n > 0 && ts == nullptr) || !valid_dt(p_dtype) || !valid_dt(s_dtype) || !valid_dt(u_dtype))
@@ -998,7 +935,9 @@ extern "C" int thorn_ortho_pre_multi(const thorn_ortho_pre_tensor* ts, int n, in
     if (e.batch < 0 || e.rows < 0 || e.cols < 0) return THORN_ERR_ARG;
     if (e.batch * e.rows * e.cols > 0 && (!e.g || (e.m && !e.normsq) || (!e.m && !md) || (md && !e.p) || !e.scratch))
       return THORN_ERR_ARG;
-    if (md && (!e.row_gsum || !e.row_sp || (!e.scalar_gain && (!e.col_sp || !e.col_gsum)))) return THORN_ERR_ARG;
+    if (e.batch * e.rows * e.cols > 0 && md &&
+        (!e.row_gsum || !e.row_sp || (!e.scalar_gain && (!e.col_sp || !e.col_gsum))))
+      return THORN_ERR_ARG;
   }
   PreArgs base;
   base.beta1 = beta1;
@@ -1015,28 +954,35 @@ extern "C" int thorn_ortho_pre_multi(const thorn_ortho_pre_tensor* ts, int n, in
     using S = std::remove_pointer_t<decltype(ps)>;
     int d2 = dispatch1(u_dtype, [&](auto* pu) {
       using U = std::remove_pointer_t<decltype(pu)>;
-      rc = launch_packed(ts, n, blocks, vec, [&](const Pack<thorn_ortho_pre_tensor>& pk, int64_t nb) {
-        PreArgs a = base;
-        a.pk = pk;
-        if (g_async_pre.load() != 0) {
-          constexpr int smem = PreUnits<P, S>::bytes;
-          static std::once_flag once[64][2];
-          int dev = 0;
-          cudaGetDevice(&dev);
-          std::call_once(once[dev & 63][md ? 1 : 0], [md]() {
-            if (md) cudaFuncSetAttribute(ortho_pre_kernel<P, S, U, true, true>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            else cudaFuncSetAttribute(ortho_pre_kernel<P, S, U, false, true>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-          });
-          if (md) ortho_pre_kernel<P, S, U, true, true><<<(unsigned)nb, kThreads, smem, st>>>(a);
-          else ortho_pre_kernel<P, S, U, false, true><<<(unsigned)nb, kThreads, smem, st>>>(a);
-        } else if (md) {
-          ortho_pre_kernel<P, S, U, true><<<(unsigned)nb, kThreads, 0, st>>>(a);
-        } else {
-          ortho_pre_kernel<P, S, U, false><<<(unsigned)nb, kThreads, 0, st>>>(a);
+      bool split_done = false;
+      if constexpr (!std::is_same<P, float>::value) {
+        if (md) {
+          // tensors whose rows are whole 16-byte chunks take the packed kernel, the rest the general one
+          std::vector<thorn_ortho_pre_tensor> whole, rest;
+          for (int i = 0; i < n; ++i) (vec(ts[i]) ? whole : rest).push_back(ts[i]);
+          rc = launch_packed(whole.data(), (int)whole.size(), blocks, vec,
+                             [&](const Pack<thorn_ortho_pre_tensor>& pk, int64_t nb) {
+                               PreArgs a = base;
+                               a.pk = pk;
+                               ortho_pre_kernel<P, S, U, true, true><<<(unsigned)nb, kThreads, 0, st>>>(a);
+                             });
+          if (rc == THORN_OK)
+            rc = launch_packed(rest.data(), (int)rest.size(), blocks, vec,
+                               [&](const Pack<thorn_ortho_pre_tensor>& pk, int64_t nb) {
+                                 PreArgs a = base;
+                                 a.pk = pk;
+                                 ortho_pre_kernel<P, S, U, true><<<(unsigned)nb, kThreads, 0, st>>>(a);
+                               });
+          split_done = true;
         }
-      });
+      }
+      if (!split_done)
+        rc = launch_packed(ts, n, blocks, vec, [&](const Pack<thorn_ortho_pre_tensor>& pk, int64_t nb) {
+          PreArgs a = base;
+          a.pk = pk;
+          if (md) ortho_pre_kernel<P, S, U, true><<<(unsigned)nb, kThreads, 0, st>>>(a);
+          else ortho_pre_kernel<P, S, U, false><<<(unsigned)nb, kThreads, 0, st>>>(a);
+        });
       if (rc == THORN_OK) {
         rc = launch_packed(
             ts, n,
@@ -1067,7 +1013,7 @@ extern "C" int thorn_ns_cast_multi(const thorn_ns_cast_tensor* ts, int n, int p_
     const auto& e = ts[i];
     if (e.batch < 0 || e.rows < 0 || e.cols < 0) return THORN_ERR_ARG;
     if (e.batch * e.rows * e.cols > 0 && (!e.g || !e.m || !e.x || !e.normsq)) return THORN_ERR_ARG;
-    if (e.md && (!e.row_sp || (!e.scalar_gain && !e.col_sp))) return THORN_ERR_ARG;
+    if (e.batch * e.rows * e.cols > 0 && e.md && (!e.row_sp || (!e.scalar_gain && !e.col_sp))) return THORN_ERR_ARG;
   }
   cudaStream_t st = (cudaStream_t)stream;
   int rc = THORN_OK;
@@ -1142,18 +1088,7 @@ extern "C" int thorn_ortho_post_multi(const thorn_ortho_post_tensor* ts, int n, 
       a.pk = pk;
       a.wd = weight_decay;
       a.eps = eps;
-      if (g_async_pre.load() != 0) {
-        constexpr int smem = PostUnits<U, P>::bytes;
-        static std::once_flag once[64];
-        int dev = 0;
-        cudaGetDevice(&dev);
-        std::call_once(once[dev & 63], []() {
-          cudaFuncSetAttribute(ortho_post_kernel<U, P, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        });
-        ortho_post_kernel<U, P, true><<<(unsigned)nb, kThreads, smem, st>>>(a);
-      } else {
-        ortho_post_kernel<U, P><<<(unsigned)nb, kThreads, 0, st>>>(a);
-      }
+      ortho_post_kernel<U, P><<<(unsigned)nb, kThreads, 0, st>>>(a);
     });
   });
   return d ? d : rc;
@@ -1203,7 +1138,8 @@ extern "C" int thorn_md_finalize_multi(const thorn_md_final_tensor* ts, int n, i
   if (n < 0 || (n > 0 && ts == nullptr) || !valid_dt(p_dtype)) return THORN_ERR_ARG;
   for (int i = 0; i < n; ++i) {
     const auto& e = ts[i];
-    if (e.batch * e.rows * e.cols > 0 && !e.p) return THORN_ERR_ARG;
+    if (e.batch * e.rows * e.cols == 0) continue;  // an empty shard: nothing to check or launch
+    if (!e.p) return THORN_ERR_ARG;
     if (e.normsq && !e.target) return THORN_ERR_ARG;
     if (!e.row_sp || (!e.scalar_gain && !e.col_sp)) return THORN_ERR_ARG;
   }
@@ -1216,18 +1152,7 @@ extern "C" int thorn_md_finalize_multi(const thorn_md_final_tensor* ts, int n, i
     rc = launch_packed(ts, n, blocks, vec, [&](const Pack<thorn_md_final_tensor>& pk, int64_t nb) {
       FinalArgs a;
       a.pk = pk;
-      if (g_async_pre.load() != 0) {
-        constexpr int smem = kPreStages * (8 * (int)sizeof(P) / 16) * kThreads * 16;
-        static std::once_flag once[64];
-        int dev = 0;
-        cudaGetDevice(&dev);
-        std::call_once(once[dev & 63], []() {
-          cudaFuncSetAttribute(md_finalize_kernel<P, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        });
-        md_finalize_kernel<P, true><<<(unsigned)nb, kThreads, smem, st>>>(a);
-      } else {
-        md_finalize_kernel<P><<<(unsigned)nb, kThreads, 0, st>>>(a);
-      }
+      md_finalize_kernel<P><<<(unsigned)nb, kThreads, 0, st>>>(a);
     });
   });
   return d ? d : rc;

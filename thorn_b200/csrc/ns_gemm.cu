@@ -255,11 +255,13 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, float* v, int ro
       for (int j = 0; j < 32; ++j)
         cv[j] = (row_ok && col0 + j < p.N) ? to_f(Cb[(int64_t)row * p.c_ld + col0 + j]) : 0.f;
     }
+    // alpha acc and beta C each rounded, then their sum: the roundings of torch's
+    // alpha / beta scaling, in a fixed order (no contraction into an fma)
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = p.alpha * v[j] + p.beta * cv[j];
+    for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(__fmul_rn(p.alpha, v[j]), __fmul_rn(p.beta, cv[j]));
   } else {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = p.alpha * v[j];
+    for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(p.alpha, v[j]);
   }
   // round once to the output type
 #pragma unroll
@@ -836,11 +838,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
             const uint4 r = *reinterpret_cast<const uint4*>(gM + sw64_off(lane, 8 * c));
             const T* h = reinterpret_cast<const T*>(&r);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[8 * c + i] = p.alpha * v[8 * c + i] + p.beta * to_f(h[i]);
+            for (int i = 0; i < 8; ++i)
+              v[8 * c + i] = __fadd_rn(__fmul_rn(p.alpha, v[8 * c + i]), __fmul_rn(p.beta, to_f(h[i])));
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = p.alpha * v[j];
+          for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(p.alpha, v[j]);
           if (lane == 0) bulk_wait_read<1>();  // stores of block n - 2 no longer read buffer k
         }
         __syncwarp();
@@ -1228,6 +1231,340 @@ int run_gemm(const GemmOp& op, int dtype, int* err, cudaStream_t st) {
                              : launch_any<__half>(op, BN, prm, grid, st);
 }
 
+// ---------------------------------------------------------------------------
+// Newton-Schulz of small matrices, one CTA per matrix (min dim <= 128, max dim
+// <= 512): X and every m x m iterate stay in shared memory for all iterations,
+// accumulators in TMEM, so a batch of small matrices (conv kernels, heads) is
+// one launch instead of one launch per product.  Same recurrences, operand
+// orders and roundings as the GEMM sequence of thorn_ns_batched; a matrix of at
+// most 128 rows is one 128-block, so every product is the plain product.
+//
+// Shared-memory layout of every operand: row-major, split into 64-column chunks
+// of 128 rows x 128 bytes (16 KB) in the 128-byte swizzle of the tensor maps
+// (16-byte unit u of row r stored at unit u ^ (r % 8)).  One layout serves as a
+// K-major operand (rows = M or N, K along the row) and as an MN-major one (rows
+// = K), so no operand is ever copied or transposed.  Rows and columns beyond
+// the matrix are zero.
+// ---------------------------------------------------------------------------
+namespace nss {
+
+constexpr int kThreads = 128;  // thread t owns TMEM lane t = output row t
+constexpr int kChunk = 128 * 128;  // bytes of one 64-column chunk
+constexpr int kMaxIters = 16;
+constexpr int kMaxN = 512;  // largest max(rows, cols)
+
+struct Params {
+  const void* x;  // [batch][rows][ld_in], the NS input in the matrix's own orientation
+  void* out;      // [batch][rows][cols]
+  int64_t ld_in;
+  int batch, rows, cols;
+  int m, n;  // min / max dim
+  int tall, gram;
+  int iters;
+  uint32_t restart_mask;  // bit i: Gram restart before iteration i
+  float coef[3 * kMaxIters];
+  int* err;
+  uint64_t wait_limit_ns;
+  int test_stall;  // failure test: no MMA is issued, so the first completion wait runs out
+};
+
+__host__ __device__ constexpr int round_up(int x, int a) { return (x + a - 1) / a * a; }
+
+// Shared memory of one CTA: X (n padded to 64-column chunks) + three m x m
+// buffers (two 64-column chunks each) + barrier words.
+__host__ __device__ inline int smem_bytes(int n) { return (round_up(n, 64) / 64 + 6) * kChunk + 1024 + 64; }
+
+__device__ __forceinline__ uint32_t off(int r, int c) {
+  return (uint32_t)((c >> 6) * kChunk + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) + ((c & 7) << 1));
+}
+
+// tcgen05 descriptors of one operand buffer for K step kk (16 elements)
+__device__ __forceinline__ uint64_t desc_k(uint32_t base, int kk, int row0) {  // K-major: rows = M or N
+  return gemm::sdesc(base + (kk >> 2) * kChunk + (kk & 3) * 32 + row0 * 128, 16, 1024);
+}
+__device__ __forceinline__ uint64_t desc_mn(uint32_t base, int kk, int col0) {  // MN-major: rows = K
+  return gemm::sdesc(base + (col0 >> 6) * kChunk + kk * 2048, kChunk, 1024);
+}
+
+// D[128 x N] (TMEM columns [0, N)) = A[128 x K] @ B[K x N]; issued by one thread.
+// A: K-major (A[i][k] at row i) or MN-major (A[i][k] at row k: the transpose of
+// the buffer).  B: K-major (B[k][j] at row j: the transpose of the buffer, for
+// X X^T) or MN-major (B[k][j] at row k).
+__device__ __forceinline__ void mma(uint32_t tmem, uint32_t a, bool a_mn, uint32_t b, bool b_mn, int K, int N,
+                                    bool bf16) {
+  for (int n0 = 0; n0 < N; n0 += 256) {
+    const int nn = min(256, N - n0);
+    const uint32_t idesc = gemm::idesc_f16(nn, bf16, a_mn, b_mn);
+    for (int kk = 0; kk < K / 16; ++kk) {
+      const uint64_t ad = a_mn ? desc_mn(a, kk, 0) : desc_k(a, kk, 0);
+      const uint64_t bd = b_mn ? desc_mn(b, kk, n0) : desc_k(b, kk, n0);
+      gemm::umma(tmem + (uint32_t)n0, ad, bd, idesc, kk != 0 ? 1u : 0u);
+    }
+  }
+}
+
+template <class T>
+__device__ __forceinline__ void load8(const uint8_t* buf, int r, int c, float* v) {
+  const uint4 u = *reinterpret_cast<const uint4*>(buf + off(r, c));
+  unpack2(u.x, v[0], v[1], (T*)nullptr);
+  unpack2(u.y, v[2], v[3], (T*)nullptr);
+  unpack2(u.z, v[4], v[5], (T*)nullptr);
+  unpack2(u.w, v[6], v[7], (T*)nullptr);
+}
+template <class T>
+__device__ __forceinline__ void store8(uint8_t* buf, int r, int c, const float* v) {
+  uint4 u;
+  u.x = pack2(v[0], v[1], (T*)nullptr);
+  u.y = pack2(v[2], v[3], (T*)nullptr);
+  u.z = pack2(v[4], v[5], (T*)nullptr);
+  u.w = pack2(v[6], v[7], (T*)nullptr);
+  *reinterpret_cast<uint4*>(buf + off(r, c)) = u;
+}
+
+// Epilogue of one product for this thread's row: D = alpha acc + beta C (C in
+// shared memory, may be the destination itself: each thread reads and writes
+// only its own row), one rounding; optional second output D2 = D + diag2 I.
+// Columns >= nv and rows >= mv are written as zero.  dst == nullptr: the final
+// product, stored to global memory in the caller's orientation.
+template <class T>
+__device__ __forceinline__ void epilogue(uint32_t tmem_row, int row, int N, int nv, int mv, float alpha, float beta,
+                                         const uint8_t* C, uint8_t* dst, uint8_t* dst2, float diag2, const Params& p,
+                                         T* gout) {
+  for (int c0 = 0; c0 < N; c0 += 32) {
+    float v[32];
+    gemm::tmem_ld32(tmem_row + (uint32_t)c0, v);
+    if (C != nullptr) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float cv[8];
+        load8<T>(C, row, c0 + 8 * q, cv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[8 * q + j] = __fadd_rn(__fmul_rn(alpha, v[8 * q + j]), __fmul_rn(beta, cv[j]));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(alpha, v[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = (row < mv && c0 + j < nv) ? rnd<T>(v[j]) : 0.f;
+    if (gout != nullptr) {
+      if (row < mv) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (c0 + j >= nv) break;
+          // wide: out[row][col]; tall: the result is the transpose, out[col][row]
+          if (p.tall) gout[(int64_t)(c0 + j) * p.cols + row] = from_f<T>(v[j]);
+          else gout[(int64_t)row * p.cols + c0 + j] = from_f<T>(v[j]);
+        }
+      }
+      continue;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) store8<T>(dst, row, c0 + 8 * q, v + 8 * q);
+    if (dst2 != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (row == c0 + j && row < mv) v[j] = rnd<T>(v[j] + diag2);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) store8<T>(dst2, row, c0 + 8 * q, v + 8 * q);
+    }
+  }
+}
+
+template <class T>
+__global__ void __launch_bounds__(kThreads, 1) ns_small_kernel(const __grid_constant__ Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int n_pad = round_up(p.n, 64);
+  uint8_t* X = smem;
+  uint8_t* B0 = X + (n_pad / 64) * kChunk;  // Gram: R; square: A = X X^T
+  uint8_t* B1 = B0 + 2 * kChunk;            // Gram: Z; square: B = c A A + b A
+  uint8_t* B2 = B1 + 2 * kChunk;            // Gram: Q
+  uint64_t* bar = reinterpret_cast<uint64_t*>(B2 + 2 * kChunk);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 1);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int b = blockIdx.x;
+  const bool bf16 = !std::is_same<T, __half>::value;
+  const int m = p.m, n = p.n;
+  // K extents in 16-element MMA steps; N extents in whole 64-column chunks
+  const int Km = round_up(m, 16), Nm = round_up(m, 64), Kn = round_up(n, 16), Nn = round_up(n, 64);
+  const uint32_t tcols = Nn > 256 ? 512u : (Nn > 128 ? 256u : (Nn > 64 ? 128u : 64u));
+
+  if (tid == 0) {
+    gemm::mbar_init(gemm::smem_u32(bar), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     gemm::smem_u32(tmem_holder)),
+                 "r"(tcols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  // X (wide orientation, m x n) from global memory, zero beyond the matrix
+  {
+    const T* xg = reinterpret_cast<const T*>(p.x) + (int64_t)b * p.rows * p.ld_in;
+    const int units = 128 * (n_pad / 8);  // 16-byte units of X
+    for (int u = tid; u < units; u += kThreads) {
+      const int r = u / (n_pad / 8), c = (u % (n_pad / 8)) * 8;
+      if (!p.tall && r < m && c + 8 <= n) {  // 8 whole elements of a row: one 16-byte load
+        *reinterpret_cast<uint4*>(X + off(r, c)) = *reinterpret_cast<const uint4*>(xg + (int64_t)r * p.ld_in + c);
+        continue;
+      }
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        // X[r][c + j] = x[r][c + j] (wide) or x[c + j][r] (tall)
+        const bool in = r < m && c + j < n;
+        v[j] = in ? to_f(p.tall ? xg[(int64_t)(c + j) * p.ld_in + r] : xg[(int64_t)r * p.ld_in + c + j]) : 0.f;
+      }
+      store8<T>(X, r, c, v);
+    }
+    // the m x m buffers start at zero (their padding must stay zero)
+    for (int u = tid; u < 6 * kChunk / 16; u += kThreads) reinterpret_cast<uint4*>(B0)[u] = make_uint4(0, 0, 0, 0);
+  }
+  gemm::tc_fence_before();
+  __syncthreads();
+  gemm::tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const uint32_t tmem_row = tmem + ((uint32_t)(warp * 32) << 16);
+  const uint32_t sX = gemm::smem_u32(X), s0 = gemm::smem_u32(B0), s1 = gemm::smem_u32(B1), s2 = gemm::smem_u32(B2);
+  uint32_t phase = 0;
+  bool ok = true;
+  T* gout = reinterpret_cast<T*>(p.out) + (int64_t)b * p.rows * p.cols;
+
+  // one product: operands ready in shared memory -> MMAs -> wait -> epilogue
+  auto product = [&](uint32_t a, bool a_mn, uint32_t bb, bool b_mn, int K, int N, int nv, float alpha, float beta,
+                     const uint8_t* C, uint8_t* dst, uint8_t* dst2, float diag2, T* g) {
+    if (!ok) return;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic-proxy writes -> tensor core
+    gemm::tc_fence_before();
+    __syncthreads();
+    gemm::tc_fence_after();
+    if (tid == 0 && !p.test_stall) {
+      mma(tmem, a, a_mn, bb, b_mn, K, N, bf16);
+      gemm::umma_commit(gemm::smem_u32(bar));
+    }
+    // every thread takes the same branch: the TMEM loads and barriers below need the whole CTA
+    ok = __syncthreads_and(gemm::mbar_wait(gemm::smem_u32(bar), phase, nullptr, p.err, p.wait_limit_ns) ? 1 : 0);
+    if (!ok) return;
+    phase ^= 1u;
+    gemm::tc_fence_after();
+    epilogue<T>(tmem_row, tid, N, nv, m, alpha, beta, C, dst, dst2, diag2, p, g);
+    gemm::tc_fence_before();
+  };
+
+  if (p.gram) {
+    uint8_t *R = B0, *Z = B1, *Q = B2;
+    const uint32_t sR = s0, sZ = s1, sQ = s2;
+    product(sX, false, sX, false, Kn, Nm, m, 1.f, 0.f, nullptr, R, nullptr, 0.f, nullptr);  // R = X X^T
+    for (int i = 0; i < p.iters && ok; ++i) {
+      const float a = p.coef[3 * i], bc = p.coef[3 * i + 1], c = p.coef[3 * i + 2];
+      const bool rs = (p.restart_mask >> i) & 1u;
+      if (rs && i != 0) {
+        product(sQ, false, sX, true, Km, Nn, n, 1.f, 0.f, nullptr, X, nullptr, 0.f, nullptr);  // X = Q X
+        product(sX, false, sX, false, Kn, Nm, m, 1.f, 0.f, nullptr, R, nullptr, 0.f, nullptr);  // R = X X^T
+      }
+      if (i != 0 && !rs) {
+        product(sR, false, sR, true, Km, Nm, m, c, bc, R, Z, nullptr, 0.f, nullptr);  // Z = c R R + b R
+        product(sQ, false, sZ, true, Km, Nm, m, 1.f, a, Q, Q, nullptr, 0.f, nullptr);  // Q = Q Z + a Q
+      } else {
+        product(sR, false, sR, true, Km, Nm, m, c, bc, R, Z, Q, a, nullptr);  // Z = c R R + b R; Q = Z + a I
+      }
+      if (i < p.iters - 1 && !((p.restart_mask >> (i + 1)) & 1u)) {
+        product(sR, false, sZ, true, Km, Nm, m, 1.f, a, R, R, nullptr, 0.f, nullptr);  // RZ = R Z + a R
+        product(sZ, false, sR, true, Km, Nm, m, 1.f, a, R, R, nullptr, 0.f, nullptr);  // R = Z RZ + a RZ
+      }
+    }
+    // out = Q X; a tall input gets X^T Q (thorn.py:653) = (Q^T X)^T
+    product(sQ, p.tall != 0, sX, true, Km, Nn, n, 1.f, 0.f, nullptr, nullptr, nullptr, 0.f, gout);
+  } else {
+    uint8_t *A = B0, *Bm = B1;
+    const uint32_t sA = s0, sB = s1;
+    for (int i = 0; i < p.iters && ok; ++i) {
+      const float a = p.coef[3 * i], bc = p.coef[3 * i + 1], c = p.coef[3 * i + 2];
+      const bool last = i == p.iters - 1;
+      product(sX, false, sX, false, Km, Nm, m, 1.f, 0.f, nullptr, A, nullptr, 0.f, nullptr);  // A = X X^T
+      product(sA, false, sA, true, Km, Nm, m, c, bc, A, Bm, nullptr, 0.f, nullptr);          // B = c A A + b A
+      product(sB, false, sX, true, Km, Nm, m, 1.f, a, X, last ? nullptr : X, nullptr, 0.f,
+              last ? gout : nullptr);  // X = a X + B X
+    }
+  }
+  if (!ok) {  // a wait ran out: let an MMA still in flight land before the TMEM is released
+    const uint64_t t0 = gemm::global_ns();
+    while (gemm::global_ns() - t0 < gemm::kSettleNs) {
+    }
+  }
+  gemm::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    gemm::tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols) : "memory");
+  }
+}
+
+}  // namespace nss
+
+static std::atomic<int> g_ns_small{1};
+
+// Dense-equivalent FLOPs of the reference's GEMMs for one matrix (roofline counters).
+static double dense_ns_flops(int64_t m, int64_t n, int iters, bool) {
+  const double M = (double)m, N = (double)n;
+  if (m == n) return iters * (4.0 * M * M * N + 2.0 * M * M * M);
+  return 28.0 * M * M * M + 8.0 * M * M * N;
+}
+
+// The small-matrix kernel for one thorn_ns_batched call, or THORN_ERR_UNSUPPORTED
+// when the shape or settings do not fit it (the caller then runs the GEMM sequence).
+int run_ns_small(const void* x, void* out, int64_t batch, int64_t rows, int64_t cols, int dtype,
+                 const double* coeffs, int iters, const int32_t* restarts, int n_restarts, int* err,
+                 cudaStream_t st) {
+  const int64_t m = std::min(rows, cols), n = std::max(rows, cols);
+  if (g_ns_small.load() == 0 || m > 128 || n > nss::kMaxN || iters < 1 || iters > nss::kMaxIters ||
+      batch > INT32_MAX)
+    return THORN_ERR_UNSUPPORTED;
+  gemm::DevInfo di = gemm::dev_info();
+  if (di.major != 10) return THORN_ERR_UNSUPPORTED;
+  nss::Params p;
+  memset(&p, 0, sizeof(p));
+  p.x = x;
+  p.out = out;
+  p.ld_in = thorn_ns_ld(cols);
+  p.batch = (int)batch;
+  p.rows = (int)rows;
+  p.cols = (int)cols;
+  p.m = (int)m;
+  p.n = (int)n;
+  p.tall = rows > cols;
+  p.gram = m != n;
+  p.iters = iters;
+  for (int k = 0; k < n_restarts; ++k)
+    if (restarts[k] >= 0 && restarts[k] < nss::kMaxIters) p.restart_mask |= 1u << restarts[k];
+  for (int i = 0; i < 3 * iters; ++i) p.coef[i] = (float)coeffs[i];
+  p.err = err;
+  p.wait_limit_ns = g_wait_limit_ns.load();
+  p.test_stall = g_test_stall.load();
+  const int smem = nss::smem_bytes((int)n);
+  static std::once_flag once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(once[dev & 63], []() {
+    cudaFuncSetAttribute(nss::ns_small_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         nss::smem_bytes(nss::kMaxN));
+    cudaFuncSetAttribute(nss::ns_small_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         nss::smem_bytes(nss::kMaxN));
+  });
+  if (dtype == THORN_BF16)
+    nss::ns_small_kernel<__nv_bfloat16><<<(unsigned)batch, nss::kThreads, smem, st>>>(p);
+  else
+    nss::ns_small_kernel<__half><<<(unsigned)batch, nss::kThreads, smem, st>>>(p);
+  count_launch();
+  const double d = dense_ns_flops(m, n, iters, n_restarts > 0) * (double)batch;
+  g_flops_dense.fetch_add((uint64_t)d);
+  g_flops_exec.fetch_add((uint64_t)d);
+  return check_launch();
+}
+
 }  // namespace thorn
 
 using namespace thorn;
@@ -1292,6 +1629,11 @@ extern "C" int thorn_ns_batched(const void* x, void* out, void* workspace, int64
   if (L.total < 0 || workspace_bytes < L.total) return THORN_ERR_ARG;
   if (!aligned16(x) || !aligned16(workspace)) return THORN_ERR_ALIGN;
   cudaStream_t st = (cudaStream_t)stream;
+  // small matrices: the whole iteration in one launch, operands resident in shared memory
+  if (iters > 0) {
+    const int rs = run_ns_small(x, out, batch, rows, cols, ns_dtype, coeffs, iters, restarts, n_restarts, err_flag, st);
+    if (rs != THORN_ERR_UNSUPPORTED) return rs;
+  }
   const bool tall = rows > cols;
   const int m = (int)L.m, n = (int)L.n, B = (int)batch;
   const int64_t ldm = L.ldm, ldn = L.ldn;
@@ -1462,6 +1804,8 @@ extern "C" uint64_t thorn_set_wait_limit_ns(uint64_t limit_ns) {
 }
 
 extern "C" int thorn_set_gemm_test_stall(int enable) { return g_test_stall.exchange(enable ? 1 : 0); }
+
+extern "C" int thorn_set_ns_small(int enable) { return g_ns_small.exchange(enable ? 1 : 0); }
 
 // Dense-equivalent and executed tensor-core FLOPs issued so far (for roofline reports).
 extern "C" void thorn_gemm_flops(double* dense, double* executed) {

@@ -171,6 +171,16 @@ THORNNonOrthoGroup = dict
 THORNGroup = dict
 
 
+def balanced_cap(total: int, cap: int) -> int:
+    """Batch size that splits ``total`` matrices into the fewest batches of at most ``cap``
+    with sizes as equal as possible (64 with cap 18: four batches of 16, not 18+18+18+10):
+    the last batch's GEMM waves are then as full as the others'."""
+    if total <= 0 or cap <= 0:
+        return max(1, cap)
+    k = -(-total // cap)
+    return -(-total // k)
+
+
 def _local(t):
     return t.to_local() if isinstance(t, DTensor) else t
 
@@ -751,6 +761,7 @@ class THORN(Optimizer):
         chunks = []
         for (R, C, pdt, sdt), its in buckets.items():
             cap = max(1, self.polar_decomp_batch_size // max(1, R * C)) if self.polar_decomp_batch_size > 0 else 1
+            cap = balanced_cap(sum(it.B for it in its), cap)
             cur, n = [], 0
             for it in its:
                 if cur and n + it.B > cap:

@@ -326,6 +326,8 @@ def _stage_marks(opt):
 
 
 def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, scales):
+    from .optimizer import balanced_cap
+
     lib = N.load()
     stream = N.stream_of(dev)
     mark = _stage_marks(opt)
@@ -356,6 +358,7 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
         out = []
         for (R, C, pdt, sdt), js in buckets.items():
             cap = max(1, opt.polar_decomp_batch_size // max(1, R * C)) if opt.polar_decomp_batch_size > 0 else 1
+            cap = balanced_cap(len(js), cap)
             for i in range(0, len(js), cap):
                 out.append((R, C, pdt, sdt, js[i:i + cap]))
         return out
