@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """THORN.step benchmark on the Llama-3-8B-shaped parameter set.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl thorn_b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl thorn_b200|reference|reference_gpu]
 
 For N > 1 launch one process per GPU with torch.distributed.run; parameters
 are then DTensors sharded Shard(0) over the ranks (FSDP2 layout) and the
@@ -25,9 +25,13 @@ One line of JSON on rank 0:
   (``--e2e-mode serial``: copy in, step, copy out, one after the other);
 * roofline: Newton-Schulz GEMM phase, dense-equivalent FLOPs / event time,
   against the measured sustained bf16 peak;
-* cpu_baseline: the CPU oracle's step on a bounded sample (one q, k and gate
+* cpu_baseline: the reference's own CPU step (thorn.THORN from its install
+  under baseline/_ref, made by oracle/install_reference.sh; the numpy port of
+  the oracle when it is not installed) on a bounded sample (one q, k and gate
   matrix, an embedding slice and a norm vector), extrapolated to the full set.
-``--impl reference`` times that CPU oracle alone (rank 0; other ranks exit).
+``--impl reference`` times that CPU step alone (rank 0; other ranks exit).
+``--impl reference_gpu`` times the reference's own GPU step (its Triton kernels
+and torch.compile Newton-Schulz) on cuda:0 on the same parameter set.
 """
 from __future__ import annotations
 
@@ -189,6 +193,55 @@ def cpu_oracle_sample(warm_only: bool = False):
     return total * 1e3, sample, (t_sq + t_kv + t_ffn + t_emb + t_norm)
 
 
+def cpu_reference_sample(warm_only: bool = False):
+    """The reference's own CPU step (thorn.THORN with backend=torch.cpu, its eager
+    path: thorn.py:1583-1732) on the same bounded sample as ``cpu_oracle_sample``,
+    extrapolated to one full step (ms); None when the reference is not installed
+    under baseline/_ref.  fp32 parameters: the reference keeps state in the
+    parameter dtype, so this is its fp32-state configuration."""
+    if import_reference() is None:
+        return None
+    import torch
+
+    from oracle.time_reference import time_reference
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    if warm_only:
+        time_reference("ortho", (KV, HIDDEN), 0, md=MD, lr=ORTHO_LR)
+        time_reference("adamw", (HIDDEN,), 0, lr=ADAM_LR)
+        return None
+    t_sq = time_reference("ortho", (HIDDEN, HIDDEN), 1, md=MD, lr=ORTHO_LR)
+    t_kv = time_reference("ortho", (KV, HIDDEN), 2, md=MD, lr=ORTHO_LR)
+    t_ffn = time_reference("ortho", (FFN, HIDDEN), 3, md=MD, lr=ORTHO_LR)
+    emb_rows = 4096
+    t_emb = time_reference("adamw", (emb_rows, HIDDEN), 4, lr=ADAM_LR)
+    t_norm = time_reference("adamw", (HIDDEN,), 5, lr=ADAM_LR)
+    total = (LAYERS * (2 * t_sq + 2 * t_kv + 3 * t_ffn) + 2 * (VOCAB / emb_rows) * t_emb
+             + (2 * LAYERS + 1) * t_norm)
+    sample = (f"the reference's thorn.THORN.step (CPU, fp32 params and state) on one {HIDDEN}x{HIDDEN}, one "
+              f"{KV}x{HIDDEN} and one {FFN}x{HIDDEN} orthogonalized matrix "
+              f"({'decouple_md' if MD else 'moonlight'}), a {emb_rows}x{HIDDEN} embedding slice and one norm "
+              f"vector; sum scaled to {LAYERS} layers + 2 x {VOCAB}-row embeddings + {2 * LAYERS + 1} norms "
+              "(extrapolated)")
+    return total * 1e3, sample, (t_sq + t_kv + t_ffn + t_emb + t_norm), torch.get_num_threads()
+
+
+def cpu_sample(warm_only: bool = False):
+    """One bounded CPU sample of the step: the reference's own thorn.THORN when it is
+    installed under baseline/_ref (kind "reference"), else the numpy port (kind "port").
+    Returns (ms per full step, sample description, seconds spent, threads, kind)."""
+    r = cpu_reference_sample(warm_only)
+    if warm_only:
+        if import_reference() is None:
+            cpu_oracle_sample(warm_only=True)
+        return None
+    if r is not None:
+        v, sample, secs, threads = r
+        return v, sample, secs, threads, "reference"
+    v, sample, secs = cpu_oracle_sample()
+    return v, sample, secs, os.cpu_count() or 1, "port"
+
+
 def port_calibration():
     """The reference's own CPU step time over the port's on the same sample, measured where the
     reference can be imported (oracle/time_reference.py; committed under profiles/), or None."""
@@ -200,11 +253,11 @@ def port_calibration():
         return None
 
 
-def cpu_baseline_entry(v, sample, cores, extra=None) -> dict:
-    """The cpu_baseline object: the port's extrapolated step, with the reference-equivalent
-    figure when the port has been timed against the reference itself."""
-    d = {"value": round(v, 3), "unit": "ms", "cores": cores, "kind": "port", "sample": sample}
-    cal = port_calibration()
+def cpu_baseline_entry(v, sample, cores, kind="port", extra=None) -> dict:
+    """The cpu_baseline object.  For the port, the reference-equivalent figure is added
+    when the port has been timed against the reference itself."""
+    d = {"value": round(v, 3), "unit": "ms", "cores": cores, "kind": kind, "sample": sample}
+    cal = port_calibration() if kind == "port" else None
     if cal is not None:
         d["reference_over_port"] = cal[0]
         d["reference_equivalent_ms"] = round(v * cal[0], 3)
@@ -221,21 +274,93 @@ def reference_arm(args, rank):
         print(json.dumps({"impl": "reference", "unavailable": "the CPU sample covers the llama8b set only (one "
                           "28672x8192 Newton-Schulz takes hours on the host cores)"}), flush=True)
         return
-    cores = os.cpu_count() or 1
     vals = []
-    sample = ""
+    sample, cores, kind = "", os.cpu_count() or 1, "port"
     for _ in range(args.warmup):  # warm-up steps: the sample's small pieces only
-        cpu_oracle_sample(warm_only=True)
+        cpu_sample(warm_only=True)
     for _ in range(args.steps):
-        v, sample, _ = cpu_oracle_sample()
+        v, sample, _, cores, kind = cpu_sample()
         vals.append(v)
     v = statistics.median(vals)
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "ms", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v, 3), "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": bench_config(args, int(os.environ.get("WORLD_SIZE", "1"))),
-            "cpu_baseline": cpu_baseline_entry(v, sample, cores),
+            "cpu_baseline": cpu_baseline_entry(v, sample, cores, kind),
             "e2e": {"value": round(v, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def import_reference():
+    """The reference's ``thorn`` package from its install under baseline/_ref
+    (``oracle/install_reference.sh``), or None when it is not installed."""
+    if not os.path.isfile(os.path.join(REF_DIR, "thorn", "thorn.py")):
+        return None
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    import thorn
+
+    return thorn
+
+
+def reference_gpu_arm(args, rank):
+    """The reference's own GPU step (Triton kernels and torch.compile Newton-Schulz,
+    thorn.py:53-377, 387-423, 1427-1457) on cuda:0, same parameter set and groups
+    as the GPU arm.  The reference keeps optimizer state in the parameter dtype
+    (thorn.py:1596-1599), so its state is bf16 here where this build's is fp32."""
+    if rank != 0:
+        return
+    ref = import_reference()
+    if ref is None:
+        print(json.dumps({"impl": "reference_gpu", "unavailable": "no reference install under baseline/_ref"}),
+              flush=True)
+        return
+    import torch
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    ortho, adamw, g_ortho, g_adam = build_params(torch, dev, 0, 1, None, args.layers)
+    params, grads = ortho + adamw, g_ortho + g_adam
+    opt = ref.THORN([
+        {"orthogonalize": True, "params": ortho, "lr": ORTHO_LR, "decouple_md": MD},
+        {"orthogonalize": False, "params": adamw, "lr": ADAM_LR},
+    ])
+
+    def feed():
+        for p, g in zip(params, grads):
+            p.grad = g.clone() if MD else g  # the reference scales the gradient in place under decouple_md
+
+    t0 = time.perf_counter()
+    for i in range(args.warmup):
+        feed()
+        opt.step()
+        torch.cuda.synchronize()
+        progress(rank, f"reference warm-up step {i + 1} done")
+    warm_s = time.perf_counter() - t0
+    sampler = ClockSampler(None)
+    sampler.start()
+    ms = []
+    for _ in range(args.steps):
+        feed()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        opt.step()
+        e1.record()
+        torch.cuda.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    clocks = sampler.stop()
+    v = statistics.median(ms)
+    line = {"impl": "reference_gpu", "metric": METRIC, "value": round(v, 3), "unit": "ms", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v, 3), "higher_is_better": False,
+            "dtype": "f16", "data": "synthetic", "config": bench_config(args, 1),
+            "reference": "thorn 3.1.1 from baseline/_ref, unmodified",
+            "state_dtype": "bf16 (the reference keeps state in the parameter dtype)",
+            "ms_all_steps": [round(x, 3) for x in ms], "warmup_s_incl_compile": round(warm_s, 1),
+            "clocks": clocks}
     print(json.dumps(line), flush=True)
 
 
@@ -582,8 +707,8 @@ def gpu_arm(args, rank, world, local_rank):
         return
     cpu = None
     if not args.no_cpu_baseline and world == 1:
-        v, sample, secs = cpu_oracle_sample()
-        cpu = cpu_baseline_entry(v, sample, os.cpu_count() or 1, {"sample_cpu_seconds": round(secs, 2)})
+        v, sample, secs, cores, kind = cpu_sample()
+        cpu = cpu_baseline_entry(v, sample, cores, kind, {"sample_cpu_seconds": round(secs, 2)})
     line = result_line(args, world, ms, ns_launch_ms, ns_dense_all, ns_exec_all, mom_ms, mom_bytes, cpu, e2e,
                        host_ms, host_enqueue_ms, launches, clocks)
     if stages:
@@ -836,7 +961,9 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="thorn_b200", choices=["thorn_b200", "reference"])
+    ap.add_argument("--impl", default="thorn_b200", choices=["thorn_b200", "reference", "reference_gpu"],
+                    help="reference: the reference's CPU step (rank 0); reference_gpu: the reference's own GPU "
+                         "step (Triton + torch.compile) on cuda:0, from its install under baseline/_ref")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--gemm-pdl", action="store_true",
                     help="NS GEMMs with programmatic dependent launch (thorn_set_gemm_pdl)")
@@ -880,6 +1007,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         reference_arm(args, rank)
+        return
+    if args.impl == "reference_gpu":
+        reference_gpu_arm(args, rank)
         return
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")

@@ -44,15 +44,16 @@ def _inputs(shape, seed):
             rng.standard_normal(shape, dtype=np.float32) * 1e-4)
 
 
-def time_reference(kind, shape, seed):
-    """One step of the reference's THORN on one parameter (state created by a first step)."""
+def time_reference(kind, shape, seed, md=True, lr=8e-3):
+    """One step of the reference's THORN on one parameter (state created by a first step).
+    ``md``: decouple_md on an orthogonalized parameter (else the default moonlight scaling)."""
     import torch
     from thorn import THORN
 
     p0, g0 = _inputs(shape, seed)
     p = torch.nn.Parameter(torch.from_numpy(p0.copy()))
-    group = {"orthogonalize": kind == "ortho", "params": [p], "lr": 8e-3}
-    if kind == "ortho":
+    group = {"orthogonalize": kind == "ortho", "params": [p], "lr": lr}
+    if kind == "ortho" and md:
         group["decouple_md"] = True
     opt = THORN([group], backend=torch.cpu)
     p.grad = torch.from_numpy(g0.copy())

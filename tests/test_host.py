@@ -455,10 +455,21 @@ def test_bench_reference_arm_line(monkeypatch, capsys):
 
     import bench
 
-    monkeypatch.setattr(bench, "cpu_oracle_sample", lambda warm_only=False: None if warm_only else (1234.5, "s", 2.0))
+    # the reference installed under baseline/_ref: its own CPU step is the baseline
+    monkeypatch.setattr(bench, "import_reference", lambda: object())
+    monkeypatch.setattr(bench, "cpu_reference_sample",
+                        lambda warm_only=False: None if warm_only else (1234.5, "s", 2.0, 8))
     args = argparse.Namespace(steps=2, warmup=1, gpus=1, model="llama8b")
     bench.reference_arm(args, 1)
     assert capsys.readouterr().out == ""
+    bench.reference_arm(args, 0)
+    line = json.loads(capsys.readouterr().out.strip())
+    assert line["impl"] == "reference" and line["value"] == 1234.5 and line["higher_is_better"] is False
+    assert line["cpu_baseline"]["kind"] == "reference" and line["cpu_baseline"]["cores"] == 8
+    # without the install: the numpy port
+    monkeypatch.setattr(bench, "import_reference", lambda: None)
+    monkeypatch.setattr(bench, "cpu_reference_sample", lambda warm_only=False: None)
+    monkeypatch.setattr(bench, "cpu_oracle_sample", lambda warm_only=False: None if warm_only else (1234.5, "s", 2.0))
     bench.reference_arm(args, 0)
     line = json.loads(capsys.readouterr().out.strip())
     assert line["impl"] == "reference" and line["value"] == 1234.5 and line["higher_is_better"] is False
