@@ -403,7 +403,7 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
             unpack2(geo[q], gv[2 * q], gv[2 * q + 1], (P*)nullptr);
           }
           rs = part;
-          *reinterpret_cast<uint4*>((P*)e.p + off) = make_uint4(pvo[0], pvo[1], pvo[2], pvo[3]);
+          if (!e.keep_p) *reinterpret_cast<uint4*>((P*)e.p + off) = make_uint4(pvo[0], pvo[1], pvo[2], pvo[3]);
           if (a.write_grad) *reinterpret_cast<uint4*>((P*)e.g + off) = make_uint4(geo[0], geo[1], geo[2], geo[3]);
         }
       }
@@ -450,7 +450,7 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
           for (int k = 0; k < 8; ++k) gv[k] = __fmul_rn(gv[k], gain[k]);
           rnd8<P>(gv);
           rs = part;
-          store_n((P*)e.p + off, pv, nc, vec);
+          if (!e.keep_p) store_n((P*)e.p + off, pv, nc, vec);
           if (a.write_grad) store_n((P*)e.g + off, gv, nc, vec);
         }
       }
@@ -666,6 +666,10 @@ __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_const
     gscale = sqrtf(e.mat_stats[2 * t.b]) / fmaxf(sqrtf(e.mat_stats[2 * t.b + 1]), a.eps);
   }
   double sq = 0.0;
+  const bool gdiv = e.gain_div != 0, split = gdiv && !e.scalar_gain;
+  float csp[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) csp[k] = (split && k < nc) ? e.col_sp[t.b * e.cols + c + k] : 1.f;
   for (int rr = warp; rr < kTR; rr += 8) {
     const int64_t r = t.r0 + rr;
     if (r >= e.rows || nc == 0) break;
@@ -675,6 +679,18 @@ __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_const
     float uv[8], pv[8];
     load_n((const U*)e.U + off, uv, nc, vec);
     load_n((const P*)e.p + off, pv, nc, vec);
+    if (gdiv) {
+      // the direction p / gain, rounded exactly as the momentum pass forms it
+      // (that pass left p unchanged: thorn_ortho_pre_tensor.keep_p)
+      const float rsp = split ? e.row_sp[t.b * e.rows + r] : e.row_sp[0];
+      float gain[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) gain[k] = split ? __fmul_rn(rsp, csp[k]) : rsp;
+      if (split) rnd8<P>(gain);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) pv[k] = __fdividef(pv[k], gain[k]);
+      rnd8<P>(pv);
+    }
     if (e.round_u) rnd8<P>(uv);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
@@ -1046,7 +1062,9 @@ extern "C" int thorn_ortho_post_multi(const thorn_ortho_post_tensor* ts, int n, 
                                       float weight_decay, void* stream) {
   if (n < 0 || (n > 0 && ts == nullptr) || !valid_dt(u_dtype) || !valid_dt(p_dtype)) return THORN_ERR_ARG;
   for (int i = 0; i < n; ++i)
-    if (ts[i].batch * ts[i].rows * ts[i].cols > 0 && (!ts[i].U || !ts[i].p || (ts[i].p_normsq && !ts[i].scratch)))
+    if (ts[i].batch * ts[i].rows * ts[i].cols > 0 &&
+        (!ts[i].U || !ts[i].p || (ts[i].p_normsq && !ts[i].scratch) ||
+         (ts[i].gain_div && (!ts[i].row_sp || (!ts[i].scalar_gain && !ts[i].col_sp)))))
       return THORN_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   int rc = THORN_OK;
