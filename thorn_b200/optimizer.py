@@ -542,13 +542,14 @@ class THORN(Optimizer):
 
     @staticmethod
     def _momentum_bytes(items, md: bool) -> int:
-        """Compulsory bytes of the momentum pass: g read, m read and written, p read and
-        written when directions are recovered (decouple_md)."""
+        """Bytes the momentum pass moves: g read, m read and written; with decouple_md p read,
+        and p written back only for a matrix that is not applied this step (an applied one
+        keeps p, and the apply pass forms its direction)."""
         tot = 0
         for it in items:
             n = it.B * it.R * it.C
             tot += n * (it.g.element_size() + 2 * _local(it.state["moment"]).element_size()
-                        + (2 * it.p.element_size() if md else 0))
+                        + ((1 if it.apply else 2) * it.p.element_size() if md else 0))
         return tot
 
     def _scratch(self, dev, sizes):
