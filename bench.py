@@ -461,7 +461,7 @@ def result_line(args, world, ms, ns_launch_ms, ns_dense_all, ns_exec_all, mom_ms
                      "ns_ms_per_step": round(ns_launch_ms, 3),
                      "ns_dense_tflop_per_step": round(ns_dense_all / 1e12, 2)},
         "roofline_elementwise": {
-            "bound": "hbm", "kernel": "ortho_pre_kernel (momentum pass, partial sums reduced in-kernel)",
+            "bound": "hbm", "kernel": "ortho_pre_kernel + pre_reduce_kernel (momentum pass)",
             "achieved": round(mom_bytes / (mom_ms * 1e-3) / 1e9, 1) if mom_ms > 0 else None,
             "peak": round(hbm * world, 1), "unit": "GB/s",
             "frac": round(mom_bytes / (mom_ms * 1e-3) / 1e9 / (hbm * world), 3) if mom_ms > 0 else None,
