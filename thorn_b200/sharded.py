@@ -202,8 +202,9 @@ def exchange_all_to_all(sends: list[Slab], recvs: list[Slab], ranks: list[int], 
             in_parts[r.peer].append(r.tensor)
     out_sizes = [sum(t.nbytes for t in ts) for ts in out_parts]
     in_sizes = [sum(t.nbytes for t in ts) for ts in in_parts]
-    flat = [t.reshape(-1).view(torch.uint8) for ts in out_parts for t in ts]
-    send_buf = torch.cat(flat) if flat else torch.empty(0, dtype=torch.uint8, device=dev)
+    flat = [t for ts in out_parts for t in ts]
+    # the gather's slabs are laid out by owner, so its send buffer is a view (no packing copy)
+    send_buf = _bytes_of(flat) if flat else torch.empty(0, dtype=torch.uint8, device=dev)
     recv_buf = torch.empty(sum(in_sizes), dtype=torch.uint8, device=dev)
     ex = Exchange()
     ex.works.append(dist.all_to_all_single(recv_buf, send_buf, in_sizes, out_sizes, group=group, async_op=True))
