@@ -12,9 +12,11 @@ and scatters fp32 results back.  Here, per step:
 2. every rank normalises its rows by the global norm and casts them to the NS
    operand type, writing straight into the owner's NS input buffer when it is
    the owner, else into a send slab;
-3. one NCCL point-to-point exchange (world - 1 shifted pairwise rounds, one
-   packed message per direction per round) moves all slabs to their owners
-   (half the bytes of the reference's fp32 gather);
+3. one NCCL exchange moves all slabs to their owners (half the bytes of the
+   reference's fp32 gather): by default one ``all_to_all_single`` whose send
+   buffer is the owner-ordered slabs themselves; with ``exchange = "rounds"``
+   world - 1 shifted pairwise point-to-point rounds, one packed message per
+   direction per round;
 4. owners run batched Newton-Schulz (+ per-neuron-norm statistics with the
    row scale folded into one factor per row);
 5. one exchange of the same form returns the 16-bit result rows and the fp32
@@ -24,8 +26,7 @@ and scatters fp32 results back.  Here, per step:
 
 Shards follow DTensor's ``torch.chunk`` split, so rows need not divide evenly,
 and a matrix with fewer rows than ranks leaves some shards empty.  With ``pipeline_exchange``
-steps 3-5 run in waves of NS batches so transfers overlap the owners' NS; with
-``exchange = "all_to_all"`` each exchange is one ``all_to_all_single``.  Magma
+steps 3-5 run in waves of NS batches so transfers overlap the owners' NS.  Magma
 masking all-reduces its three sums over the shard group first; a masked matrix,
 or one whose step is not due under ``update_rate``, is left out of the step.
 
@@ -184,8 +185,8 @@ def exchange_all_to_all(sends: list[Slab], recvs: list[Slab], ranks: list[int], 
     """The same exchange as one ``all_to_all_single`` collective: each peer's slabs
     packed back to back (canonical order) in one send buffer, the received bytes
     unpacked per source.  Every rank of the group takes part, also with nothing to
-    send; the collective is the alternative when grouped point-to-point calls are
-    not wanted (``THORN.exchange = "all_to_all"``)."""
+    send.  This is the default exchange (``THORN.exchange = "all_to_all"``): NCCL moves
+    all peers' messages at once, where the rounds move one peer's per call."""
     world = len(ranks)
     if sends or recvs:
         dev = (sends[0] if sends else recvs[0]).tensor.device
@@ -450,7 +451,7 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
                                         N.dtype_code(udt), ns_code, b1, stream), "ns_cast_multi")
     mark("gains_and_cast" if md else "cast")
 
-    xchg = exchange_all_to_all if getattr(opt, "exchange", "rounds") == "all_to_all" else exchange
+    xchg = exchange if getattr(opt, "exchange", "all_to_all") == "rounds" else exchange_all_to_all
     # 3. slabs to owners: every wave's exchange is queued now (the NCCL stream runs them
     # in order); each NS batch waits only for its own wave
     gathers = []
