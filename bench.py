@@ -936,12 +936,16 @@ def small_config(args):
         step()
     torch.cuda.synchronize()
     opt.profile_ns = []
+    from thorn_b200 import _native
+
+    launches0 = _native.launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     h0 = time.perf_counter()
     for _ in range(args.steps):
         step()
     host_ms = (time.perf_counter() - h0) * 1e3 / args.steps
+    launches = (_native.launch_count() - launches0) / args.steps
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
@@ -949,6 +953,7 @@ def small_config(args):
     ns_ms = sum(a.elapsed_time(b) for a, b, *_ in prof) / args.steps
     ns_dense = sum(d for _, _, d, _, _ in prof) / args.steps
     print(json.dumps({"model": args.model, "ms_per_step": round(ms, 4), "host_ms_per_step": round(host_ms, 3),
+                      "gpu_launches_per_step": launches,
                       "ns_ms_per_step": round(ns_ms, 4),
                       "ns_dense_tflops": round(ns_dense / (ns_ms * 1e-3) / 1e12, 1) if ns_ms > 0 else None,
                       "params": sum(p.numel() for p in params), "param_dtype": pdt, "state_dtype": sdt,
