@@ -465,8 +465,8 @@ def result_line(args, world, ms, ns_launch_ms, ns_dense_all, ns_exec_all, mom_ms
             "achieved": round(mom_bytes / (mom_ms * 1e-3) / 1e9, 1) if mom_ms > 0 else None,
             "peak": round(hbm * world, 1), "unit": "GB/s",
             "frac": round(mom_bytes / (mom_ms * 1e-3) / 1e9 / (hbm * world), 3) if mom_ms > 0 else None,
-            "bytes": ("g read + m read/write + p read (decouple_md; p is written by the apply pass), "
-                      "compulsory" if MD else "g read + m read/write, compulsory"),
+            "bytes": ("g read + m read/write + p read/write (decouple_md), compulsory" if MD
+                      else "g read + m read/write, compulsory"),
             "ms_per_step": round(mom_ms, 3), "gb_per_step": round(mom_bytes / 1e9, 2)},
         "cpu_baseline": cpu,
         "e2e": e2e,

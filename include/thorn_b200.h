@@ -158,8 +158,6 @@ typedef struct {
   const float* row_sp;  /* md: softplus(row_gain) rounded to p dtype, [batch*rows] (scalar gain: [1]) */
   const float* col_sp;  /* md: softplus(col_gain) rounded to p dtype, [batch*cols] (scalar gain: unused) */
   int32_t scalar_gain;  /* md: nonzero when the gain is one scalar, row_sp[0] */
-  int32_t keep_p;       /* md: nonzero leaves p as it is (the direction p / gain is not stored); the
-                           apply pass then forms it from the same gains (thorn_ortho_post_tensor.gain_div) */
   float* row_gsum;      /* md out: [batch*rows] (scalar gain: [1]) */
   float* col_gsum;      /* md out: [batch*cols] (unused for a scalar gain) */
   void* scratch;        /* thorn_ortho_pre_scratch_bytes(batch, rows, cols, md) bytes (see above) */
@@ -289,11 +287,6 @@ typedef struct {
   void* scratch;           /* with p_normsq: thorn_sumsq_scratch_bytes(batch, rows, cols) bytes */
   int32_t round_u;         /* nonzero: round U to the param dtype first (thorn.py:1404);
                               zero: use it as is (the sharded path's fp32 u, thorn.py:1079-1081, 1143) */
-  int32_t gain_div;        /* decouple_md with keep_p in the momentum pass: p holds the undivided parameter,
-                              and the update applies to round_p(p / round_p(row_sp col_sp)) (thorn.py:904) */
-  int32_t scalar_gain;     /* with gain_div: the gain is the scalar row_sp[0] */
-  const float* row_sp;     /* with gain_div: the momentum pass's gains, as in thorn_ortho_pre_tensor */
-  const float* col_sp;
 } thorn_ortho_post_tensor;
 
 THORN_API int thorn_ortho_post_multi(const thorn_ortho_post_tensor* tensors, int n, int u_dtype, int p_dtype,

@@ -126,8 +126,8 @@ def test_argument_validation_without_gpu(lib):
     assert lib.thorn_ns_batched_static(1024, 2048, big, big, big, 2, co, 1, rs, 0, None, None) == 5  # too large
     # symmetric GEMM needs 8-element leading dimensions
     assert lib.thorn_sym_addmm(16, 16, None, 16, 1, 12, 16, 0, 1.0, 0.0, 2, None, None) == 2
-    pre = N.array(N.OrthoPreTensor, [N.OrthoPreTensor(None, None, None, None, 1, 4, 4, None, None, 0, 0, None,
-                                                       None, None)])
+    pre = N.array(N.OrthoPreTensor, [N.OrthoPreTensor(None, None, None, None, 1, 4, 4, None, None, 0, None, None,
+                                                       None)])
     assert lib.thorn_ortho_pre_multi(pre, 1, 0, 0, 0, 0.9, 0, 0, None) == 1
     mp = N.array(N.MdPrepTensor, [N.MdPrepTensor(None, None, None, 4)])
     assert lib.thorn_md_prep_multi(mp, 1, 0, None) == 1
@@ -152,8 +152,8 @@ def test_empty_shards_accepted_without_device_work(lib):
     """A Shard(0) shard with no rows (a matrix with fewer rows than ranks) arrives with null
     data pointers; every entry point accepts it and launches nothing, with and without
     decouple_md (so no GPU is needed here)."""
-    pre = N.array(N.OrthoPreTensor, [N.OrthoPreTensor(None, None, None, None, 1, 0, 48, None, None, 0, 0, None,
-                                                       None, None)])
+    pre = N.array(N.OrthoPreTensor, [N.OrthoPreTensor(None, None, None, None, 1, 0, 48, None, None, 0, None, None,
+                                                       None)])
     for md in (0, 1):
         assert lib.thorn_ortho_pre_multi(pre, 1, 0, 0, 0, 0.9, md, 0, None) == 0
     cast = N.array(N.NsCastTensor, [N.NsCastTensor(None, None, None, None, 1, 0, 48, None, None, 0, 1)])

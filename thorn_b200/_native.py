@@ -29,7 +29,7 @@ class AdamTensor(Structure):
 class OrthoPreTensor(Structure):
     _fields_ = [("p", c_void_p), ("g", c_void_p), ("m", c_void_p), ("normsq", c_void_p),
                 ("batch", c_int64), ("rows", c_int64), ("cols", c_int64),
-                ("row_sp", c_void_p), ("col_sp", c_void_p), ("scalar_gain", c_int32), ("keep_p", c_int32),
+                ("row_sp", c_void_p), ("col_sp", c_void_p), ("scalar_gain", c_int32),
                 ("row_gsum", c_void_p), ("col_gsum", c_void_p), ("scratch", c_void_p)]
 
 
@@ -47,8 +47,7 @@ class PnnTensor(Structure):
 class OrthoPostTensor(Structure):
     _fields_ = [("U", c_void_p), ("p", c_void_p), ("row_scale", c_void_p), ("mat_stats", c_void_p),
                 ("p_normsq", c_void_p), ("batch", c_int64), ("rows", c_int64), ("cols", c_int64), ("lr", c_float),
-                ("scratch", c_void_p), ("round_u", c_int32), ("gain_div", c_int32), ("scalar_gain", c_int32),
-                ("row_sp", c_void_p), ("col_sp", c_void_p)]
+                ("scratch", c_void_p), ("round_u", c_int32)]
 
 
 class SumsqTensor(Structure):

@@ -334,7 +334,7 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
     const int64_t r = t.r0 + rr;
     if (r >= e.rows) break;
     {  // this warp's row two iterations ahead, prefetched into L2: each thread keeps more
-       // DRAM requests in flight than its registers hold (17.2 vs 17.7 ms per Llama-3-8B step)
+       // DRAM requests in flight than its registers hold (0.5 ms less per Llama-3-8B step)
       const int64_t rp = r + 16;
       if (rr + 16 < kTR && rp < e.rows && nc > 0) {
         const int64_t offp = (t.b * e.rows + rp) * e.cols + c;
@@ -384,7 +384,7 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
             unpack2(geo[q], gv[2 * q], gv[2 * q + 1], (P*)nullptr);
           }
           rs = part;
-          if (!e.keep_p) *reinterpret_cast<uint4*>((P*)e.p + off) = make_uint4(pvo[0], pvo[1], pvo[2], pvo[3]);
+          *reinterpret_cast<uint4*>((P*)e.p + off) = make_uint4(pvo[0], pvo[1], pvo[2], pvo[3]);
           if (a.write_grad) *reinterpret_cast<uint4*>((P*)e.g + off) = make_uint4(geo[0], geo[1], geo[2], geo[3]);
         }
       }
@@ -431,7 +431,7 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
           for (int k = 0; k < 8; ++k) gv[k] = __fmul_rn(gv[k], gain[k]);
           rnd8<P>(gv);
           rs = part;
-          if (!e.keep_p) store_n((P*)e.p + off, pv, nc, vec);
+          store_n((P*)e.p + off, pv, nc, vec);
           if (a.write_grad) store_n((P*)e.g + off, gv, nc, vec);
         }
       }
@@ -689,10 +689,6 @@ __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_const
     gscale = sqrtf(e.mat_stats[2 * t.b]) / fmaxf(sqrtf(e.mat_stats[2 * t.b + 1]), a.eps);
   }
   double sq = 0.0;
-  const bool gdiv = e.gain_div != 0, split = gdiv && !e.scalar_gain;
-  float csp[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) csp[k] = (split && k < nc) ? e.col_sp[t.b * e.cols + c + k] : 1.f;
   for (int rr = warp; rr < kTR; rr += 8) {
     const int64_t r = t.r0 + rr;
     if (r >= e.rows || nc == 0) break;
@@ -702,16 +698,6 @@ __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_const
     float uv[8], pv[8];
     load_n((const U*)e.U + off, uv, nc, vec);
     load_n((const P*)e.p + off, pv, nc, vec);
-    if (gdiv) {
-      const float rsp = split ? e.row_sp[t.b * e.rows + r] : e.row_sp[0];
-      float gain[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) gain[k] = split ? __fmul_rn(rsp, csp[k]) : rsp;
-      if (split) rnd8<P>(gain);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) pv[k] = __fdividef(pv[k], gain[k]);
-      rnd8<P>(pv);
-    }
     if (e.round_u) rnd8<P>(uv);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {

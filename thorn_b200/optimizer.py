@@ -545,14 +545,13 @@ class THORN(Optimizer):
 
     @staticmethod
     def _momentum_bytes(items, md: bool) -> int:
-        """Bytes the momentum pass moves: g read, m read and written; with decouple_md p read,
-        and p written back only for a matrix that is not applied this step (an applied one
-        keeps p, and the apply pass forms its direction)."""
+        """Compulsory bytes of the momentum pass: g read, m read and written, p read and
+        written when directions are recovered (decouple_md)."""
         tot = 0
         for it in items:
             n = it.B * it.R * it.C
             tot += n * (it.g.element_size() + 2 * _local(it.state["moment"]).element_size()
-                        + ((1 if it.apply else 2) * it.p.element_size() if md else 0))
+                        + (2 * it.p.element_size() if md else 0))
         return tot
 
     def _scratch(self, dev, sizes):
@@ -791,7 +790,7 @@ class THORN(Optimizer):
             t = N.OrthoPreTensor(it.p.data_ptr() if md else None, it.g.data_ptr(), _local(it.state["moment"]).data_ptr(),
                                  arena.ptr(it.normsq), it.B, it.R, it.C,
                                  arena.ptr(it.rs) if md else None, arena.ptr(it.cs) if md else None,
-                                 1 if (md and not it.split) else 0, 1 if (md and it.apply) else 0,
+                                 1 if (md and not it.split) else 0,
                                  arena.ptr(it.rgs) if md else None, arena.ptr(it.cgs) if md else None, sp)
             by_dt.setdefault((it.pdt, it.sdt), []).append(t)
         ev = self._profile_start(self.profile_momentum)
@@ -854,9 +853,7 @@ class THORN(Optimizer):
                     U.data_ptr() + off * R * C * usz, it.p.data_ptr(),
                     None if row_scale is None else row_scale.data_ptr() + off * R * 4,
                     None if mat_stats is None else mat_stats.data_ptr() + off * 2 * 4,
-                    arena.ptr(it.pnorm) if md else None, it.B, it.R, it.C, lr_eff * it.scale, sp if md else None, 1,
-                    1 if md else 0, 1 if (md and not it.split) else 0, arena.ptr(it.rs) if md else None,
-                    arena.ptr(it.cs) if md else None))
+                    arena.ptr(it.pnorm) if md else None, it.B, it.R, it.C, lr_eff * it.scale, sp if md else None, 1))
                 off += it.B
             N.check(lib.thorn_ortho_post_multi(N.array(N.OrthoPostTensor, posts), len(posts), ns_code,
                                                N.dtype_code(pdt), float(cfg.weight_decay), stream), "ortho_post_multi")
@@ -955,7 +952,7 @@ class THORN(Optimizer):
             scr = self._scratch(dev, [lib.thorn_ortho_pre_scratch_bytes(it.B, it.R, it.C, 1) for it in items])
             for it, sp in zip(items, scr):
                 t = N.OrthoPreTensor(it.p.data_ptr(), it.g.data_ptr(), None, None, it.B, it.R, it.C,
-                                     arena.ptr(it.rs), arena.ptr(it.cs), 0 if it.split else 1, 0,
+                                     arena.ptr(it.rs), arena.ptr(it.cs), 0 if it.split else 1,
                                      arena.ptr(it.rgs), arena.ptr(it.cgs), sp)
                 by_dt.setdefault((it.pdt, it.sdt), []).append(t)
             for (pdt, sdt), ts in by_dt.items():

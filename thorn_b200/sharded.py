@@ -398,7 +398,7 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
         by_dt.setdefault((it.pdt, it.sdt), []).append(N.OrthoPreTensor(
             it.p.data_ptr() if md else None, it.g.data_ptr(), _local(it.state["moment"]).data_ptr(),
             arena.ptr(it.normsq), it.B, it.R, it.C, arena.ptr(it.rs) if md else None,
-            arena.ptr(it.cs) if md else None, 1 if (md and not it.split) else 0, 1 if (md and it.apply) else 0,
+            arena.ptr(it.cs) if md else None, 1 if (md and not it.split) else 0,
             arena.ptr(it.rgs) if md else None, arena.ptr(it.cgs) if md else None, sp))
     ev = opt._profile_start(opt.profile_momentum)
     for (pdt, sdt), ts in by_dt.items():
@@ -539,9 +539,7 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
         lr_eff = float(cfg.lr) * cfg.lr_scale(rows_g[j], it.C) * scales[j]
         posts.setdefault(it.pdt, []).append(N.OrthoPostTensor(
             uj.data_ptr(), it.p.data_ptr(), None if fj is None else fj.data_ptr(), None,
-            arena.ptr(it.pnorm) if md else None, it.B, it.R, it.C, lr_eff, sp if md else None, 0,
-            1 if (md and it.apply) else 0, 1 if (md and not it.split) else 0, arena.ptr(it.rs) if md else None,
-            arena.ptr(it.cs) if md else None))
+            arena.ptr(it.pnorm) if md else None, it.B, it.R, it.C, lr_eff, sp if md else None, 0))
     for pdt, ts in posts.items():
         N.check(lib.thorn_ortho_post_multi(N.array(N.OrthoPostTensor, ts), len(ts), ns_code, N.dtype_code(pdt),
                                            float(cfg.weight_decay), stream), "ortho_post_multi")
