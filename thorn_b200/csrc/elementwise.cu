@@ -574,8 +574,8 @@ __global__ void __launch_bounds__(kThreads) ns_cast_kernel(const __grid_constant
   const int64_t ld = ns_ld(e.cols);
   const P* G = (const P*)e.g;
   const S* M = (const S*)e.m;
-  // multiply by the reciprocal of (||u|| + 1e-8): <= 1 fp32 ulp from the
-  // reference's division, before the rounding to the 16-bit NS type
+  // u / (||u|| + 1e-8) as an IEEE division, like the reference (thorn.py:633),
+  // then one rounding to the 16-bit NS type
   const bool md = e.md != 0;
   const bool split = md && !e.scalar_gain;
   float csp[8];
