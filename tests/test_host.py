@@ -478,3 +478,29 @@ def test_bench_reference_arm_line(monkeypatch, capsys):
     # the same workload description as the GPU arm's line
     args.layers = None
     assert line["config"] == bench.bench_config(args, 1)
+
+
+def test_bench_reference_gpu_arm_unavailable_without_install(monkeypatch, capsys):
+    """bench.py --impl reference_gpu without the reference installed under baseline/_ref:
+    rank 0 prints one line that says so and nothing runs; other ranks print nothing."""
+    import argparse
+    import json
+
+    import bench
+
+    monkeypatch.setattr(bench, "import_reference", lambda: None)
+    args = argparse.Namespace(steps=2, warmup=1, gpus=1, model="llama8b", layers=None)
+    bench.reference_gpu_arm(args, 1)
+    assert capsys.readouterr().out == ""
+    bench.reference_gpu_arm(args, 0)
+    line = json.loads(capsys.readouterr().out.strip())
+    assert line["impl"] == "reference_gpu" and "unavailable" in line
+
+
+def test_sharded_exchange_defaults_to_all_to_all():
+    """The sharded path's exchange default is one all_to_all_single per exchange (the
+    faster form on 8 GPUs); the pairwise rounds stay selectable."""
+    from thorn_b200 import THORN
+
+    assert THORN.exchange == "all_to_all"
+    assert THORN.pipeline_exchange is False
