@@ -87,10 +87,11 @@ static int launch_packed(const E* ts, int n, Blocks blocks_of, Vec vec_of, Launc
 
 static inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
-// Bring the 128-byte line holding p into L2 ahead of its load.  The row loops
-// below issue it for the row two iterations ahead (16 rows further down the
+// Bring the 128-byte line holding p into L2 ahead of its load.  The momentum
+// pass issues it for the row two iterations ahead (16 rows further down the
 // tile): each thread then has more DRAM requests in flight than its registers
-// hold.  One lane per 128-byte line issues it.
+// hold (0.5 ms less per Llama-3-8B step).  One lane per 128-byte line issues it.
+// The same prefetch in the NS input, apply and finalize passes measured no gain.
 __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
@@ -341,7 +342,7 @@ __global__ void __launch_bounds__(kThreads) ortho_pre_kernel(const __grid_consta
   for (int rr = warp; rr < kTR; rr += 8) {
     const int64_t r = t.r0 + rr;
     if (r >= e.rows) break;
-    if (rr + 16 < kTR && r + 16 < e.rows && nc > 0) {  // two rows ahead (0.5 ms less per Llama-3-8B step)
+    if (rr + 16 < kTR && r + 16 < e.rows && nc > 0) {  // this warp's row two iterations ahead
       const int64_t offp = (t.b * e.rows + r + 16) * e.cols + c;
       if (momentum && (lane & (16 / sizeof(S) - 1)) == 0) prefetch_l2((const S*)e.m + offp);
       if ((lane & (16 / sizeof(P) - 1)) == 0) {
@@ -588,11 +589,6 @@ __global__ void __launch_bounds__(kThreads) ns_cast_kernel(const __grid_constant
     const int64_t r = t.r0 + rr;
     if (r >= e.rows) break;
     const int64_t off = (t.b * e.rows + r) * e.cols + c;
-    if (rr + 16 < kTR && r + 16 < e.rows) {
-      const int64_t offp = off + 16 * e.cols;
-      if ((lane & (16 / sizeof(S) - 1)) == 0) prefetch_l2(M + offp);
-      if ((lane & (16 / sizeof(P) - 1)) == 0) prefetch_l2(G + offp);
-    }
     float gv[8], mv[8], v[8];
     load_n(G + off, gv, nc, vec);
     load_n(M + off, mv, nc, vec);
@@ -702,11 +698,6 @@ __global__ void __launch_bounds__(kThreads) ortho_post_kernel(const __grid_const
     const int64_t r = t.r0 + rr;
     if (r >= e.rows || nc == 0) break;
     const int64_t off = (t.b * e.rows + r) * e.cols + c;
-    if (rr + 16 < kTR && r + 16 < e.rows) {
-      const int64_t offp = off + 16 * e.cols;
-      if ((lane & (16 / sizeof(U) - 1)) == 0) prefetch_l2((const U*)e.U + offp);
-      if ((lane & (16 / sizeof(P) - 1)) == 0) prefetch_l2((const P*)e.p + offp);
-    }
     float scale = 1.f;
     if (e.row_scale != nullptr) scale = e.row_scale[t.b * e.rows + r] * gscale;
     float uv[8], pv[8];
@@ -804,7 +795,6 @@ __global__ void __launch_bounds__(kThreads) md_finalize_kernel(const __grid_cons
         const int64_t r = t.r0 + rr;
         if (r >= e.rows) break;
         P* pp = (P*)e.p + (t.b * e.rows + r) * e.cols + c;
-        if (rr + 16 < kTR && r + 16 < e.rows && (lane & 7) == 0) prefetch_l2(pp + 16 * e.cols);
         const uint4 p4 = *reinterpret_cast<const uint4*>(pp);
         const float rsp = split ? e.row_sp[t.b * e.rows + r] : e.row_sp[0];
         const uint32_t rs2 = pack2(rsp, rsp, (P*)nullptr);
