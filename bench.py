@@ -974,8 +974,9 @@ def main():
                     help="NS GEMMs with programmatic dependent launch (thorn_set_gemm_pdl)")
     ap.add_argument("--gemm-l2-hints", action="store_true",
                     help="L2 cache policies on the 2-CTA NS GEMM's loads and stores (thorn_set_gemm_l2_hints)")
-    ap.add_argument("--exchange", default="all_to_all", choices=["rounds", "all_to_all"],
-                    help="N > 1: slab exchange as one all_to_all_single (default) or pairwise P2P rounds")
+    ap.add_argument("--exchange", default="all_to_all", choices=["rounds", "all_to_all", "peer"],
+                    help="N > 1: slab exchange as one all_to_all_single (default), pairwise P2P rounds, or "
+                         "peer: stores into the owners' IPC-mapped arenas and copy-engine peer copies")
     ap.add_argument("--pipeline-exchange", action="store_true",
                     help="N > 1: exchange row slabs in waves that overlap the owners' Newton-Schulz work")
     ap.add_argument("--e2e-mode", default="pipelined", choices=["serial", "pipelined"],

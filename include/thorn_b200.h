@@ -343,6 +343,35 @@ typedef struct {
 THORN_API int64_t thorn_sumsq_scratch_bytes(int64_t batch, int64_t rows, int64_t cols);
 THORN_API int thorn_sumsq_multi(const thorn_sumsq_tensor* tensors, int n, int dtype, void* stream);
 
+/* --------------------------------------------------------------------------
+ * Peer-memory exchange of the FSDP2 Shard(0) path (THORN.exchange = "peer").
+ * Replaces the reference's per-matrix dist.gather / dist.scatter of fp32 rows
+ * (_DistributedTHORNState.gather / scatter, thorn.py:1023-1122) for ranks of one
+ * node: every rank exports one device arena by CUDA IPC and maps its peers'.
+ * The NS input pass (thorn_ns_cast_multi) then stores each rank's rows straight
+ * into the owner's arena, and result rows return with thorn_copy_async (copy
+ * engines; no SMs).  Ordering: after its stores or copies a rank calls
+ * thorn_peer_signal on its slot in every destination's arena; a receiver calls
+ * thorn_peer_wait on its own slots.  Slot values must grow from step to step.
+ * A wait that exceeds limit_ns sets *err_flag to 3 and returns.
+ *   thorn_peer_alloc     cudaMalloc + zero fill (the flag slots start at 0)
+ *   thorn_ipc_handle     THORN_IPC_HANDLE_BYTES bytes that another process opens
+ *   thorn_ipc_open       map a peer's arena into the current device's context
+ *   thorn_copy_async     cudaMemcpyAsync (cudaMemcpyDefault) on `stream`
+ *   thorn_peer_signal    slots[i] <- value (release, system scope), i < n <= 64
+ *   thorn_peer_wait      wait until slots[0..n) >= value (acquire, system scope)
+ * ------------------------------------------------------------------------ */
+#define THORN_IPC_HANDLE_BYTES 64
+THORN_API int thorn_peer_alloc(int64_t bytes, void** out);
+THORN_API int thorn_peer_free(void* p);
+THORN_API int thorn_ipc_handle(const void* p, void* handle);
+THORN_API int thorn_ipc_open(const void* handle, void** out);
+THORN_API int thorn_ipc_close(void* p);
+THORN_API int thorn_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
+THORN_API int thorn_peer_signal(uint64_t* const* slots, int n, uint64_t value, void* stream);
+THORN_API int thorn_peer_wait(const uint64_t* slots, int n, uint64_t value, uint64_t limit_ns, int* err_flag,
+                              void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -33,7 +33,7 @@ def main():
     ap.add_argument("--case", required=True)
     ap.add_argument("--out", required=True)
     ap.add_argument("--pipeline-exchange", action="store_true")
-    ap.add_argument("--exchange", default="rounds", choices=["rounds", "all_to_all"])
+    ap.add_argument("--exchange", default="rounds", choices=["rounds", "all_to_all", "peer"])
     args = ap.parse_args()
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local_rank)

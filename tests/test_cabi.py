@@ -180,11 +180,13 @@ def test_wait_limit_setter(lib):
 
 def _ctype_of(decl: str):
     """The ctypes type that binds one C parameter or return type of the header."""
-    d = " ".join(decl.replace("const ", "").split())
+    d = " ".join(re.sub(r"\bconst\b", " ", decl).split())
     d = re.sub(r"\s*\*\s*", "*", d)
     base = d.split()[0] if " " in d and "*" not in d.split()[0] else d
     if d in ("void", ""):
         return None
+    if d.endswith("**"):  # an out-parameter or an array of device pointers
+        return ctypes.POINTER(ctypes.c_void_p)
     if d.endswith("*"):
         t = d.rstrip("*").split()[0]
         if d == "char*":
@@ -218,3 +220,20 @@ def test_ctypes_prototypes_match_header():
                 assert got._type_ is STRUCTS[cname][0], (name, i, cname, got._type_)
             else:
                 assert got == want, (name, i, cdecl, got, want)
+
+
+def test_peer_exchange_entry_points_validate_without_gpu(lib):
+    """The peer-exchange entry points reject bad arguments before touching a device."""
+    vp = ctypes.c_void_p()
+    assert lib.thorn_peer_alloc(0, ctypes.byref(vp)) == 1
+    assert lib.thorn_ipc_handle(None, None) == 1
+    assert lib.thorn_ipc_open(None, ctypes.byref(vp)) == 1
+    assert lib.thorn_copy_async(None, None, -1, None) == 1
+    assert lib.thorn_copy_async(None, None, 0, None) == 0  # nothing to copy
+    slots = (ctypes.c_void_p * 65)()
+    assert lib.thorn_peer_signal(slots, 65, 1, None) == 1  # at most 64 peers
+    assert lib.thorn_peer_signal(slots, 1, 1, None) == 1  # a null slot
+    slots[0] = 12  # not 8-byte aligned
+    assert lib.thorn_peer_signal(slots, 1, 1, None) == 1
+    assert lib.thorn_peer_wait(12, 1, 1, 1000, None, None) == 1
+    assert lib.thorn_peer_wait(None, 0, 1, 1000, None, None) == 0  # no slots: no launch

@@ -245,6 +245,7 @@ def _sharded_compare(got, orc, name, init):
 
 PIPE = ("--pipeline-exchange",)
 A2A = ("--exchange", "all_to_all")
+PEER = ("--exchange", "peer")
 
 
 @pytest.mark.gpu
@@ -253,7 +254,9 @@ A2A = ("--exchange", "all_to_all")
                                         ("shard_uneven", PIPE), ("md_shard", PIPE),
                                         ("magma_shard", ()), ("magma_shard", PIPE), ("rate_shard", ()),
                                         ("shard_odd_cols", ()), ("shard_odd_cols", PIPE),
-                                        ("shard_tiny_rows", ()), ("shard_uneven", A2A), ("md_shard", A2A + PIPE)])
+                                        ("shard_tiny_rows", ()), ("shard_uneven", A2A), ("md_shard", A2A + PIPE),
+                                        ("tiny", PEER), ("md_shard", PEER), ("shard_uneven", PEER),
+                                        ("magma_shard", PEER), ("shard_odd_cols", PEER), ("shard_tiny_rows", PEER)])
 def test_sharded_step_matches_oracle(world, name, extra, tmp_path):
     """The Shard(0) path (rounds or waves of the exchange, Magma masking whole matrices)
     against the oracle's sharded semantics; the oracle replays the run's Magma seeds."""
@@ -497,3 +500,35 @@ def test_sharded_due_matrices_gloo():
         assert sum(col) <= 1  # updates at most once
         assert steps[j] == 1 + sum(col)
     assert any(any(sel) for sel in log)
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_peer_layout_disjoint_and_aligned(world):
+    """The peer exchange's arena layout (the same computation on every rank): for every owner,
+    the NS inputs of its chunks and the result slots of its shards of the other owners'
+    matrices are disjoint, 256-byte aligned, past the flag slots, and sized for the rows
+    that land there; the Llama-3-8B set and an uneven split with empty shards."""
+    from thorn_b200.sharded import PEER_FLAG_BYTES, peer_layout
+
+    for shapes in ([(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096), (14336, 4096),
+                    (4096, 14336)] * 2, [(66, 64), (5, 37), (2, 48), (130, 8)]):
+        rows = [r for r, _ in shapes]
+        cols = [c for _, c in shapes]
+        ld = [(c + 7) // 8 * 8 for c in cols]
+        parts = [shard_rows(r, world) for r in rows]
+        owners = assign_owners([ns_flops(r, c, 5) for r, c in shapes], world)
+        for r in range(world):
+            mine = [j for j in range(len(shapes)) if owners[j] == r]
+            chunks = [(rows[j], cols[j], "bf16", "f32", [j]) for j in mine]
+            x_off, u_off, f_off, total = peer_layout(r, owners, chunks, parts, cols, ld, 2, lambda j: rows[j] > cols[j])
+            spans = [(x_off[ci], rows[js[0]] * ld[js[0]] * 2) for ci, (_, _, _, _, js) in enumerate(chunks)]
+            for j, off in u_off.items():
+                assert owners[j] != r and parts[j][r][1] > 0
+                spans.append((off, parts[j][r][1] * cols[j] * 2))
+            for j, off in f_off.items():
+                spans.append((off, parts[j][r][1] * 4))
+            assert set(u_off) == {j for j in range(len(shapes)) if owners[j] != r and parts[j][r][1] > 0}
+            spans.sort()
+            assert all(o % 256 == 0 and o >= PEER_FLAG_BYTES for o, _ in spans)
+            assert all(a + n <= b for (a, n), (b, _) in zip(spans, spans[1:]))
+            assert spans[-1][0] + spans[-1][1] <= total

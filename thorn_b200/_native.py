@@ -105,6 +105,14 @@ _PROTOS = {
     "thorn_md_finalize_multi": (c_int, [POINTER(MdFinalTensor), c_int, c_int, c_void_p]),
     "thorn_sumsq_scratch_bytes": (c_int64, [c_int64, c_int64, c_int64]),
     "thorn_sumsq_multi": (c_int, [POINTER(SumsqTensor), c_int, c_int, c_void_p]),
+    "thorn_peer_alloc": (c_int, [c_int64, POINTER(c_void_p)]),
+    "thorn_peer_free": (c_int, [c_void_p]),
+    "thorn_ipc_handle": (c_int, [c_void_p, c_void_p]),
+    "thorn_ipc_open": (c_int, [c_void_p, POINTER(c_void_p)]),
+    "thorn_ipc_close": (c_int, [c_void_p]),
+    "thorn_copy_async": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
+    "thorn_peer_signal": (c_int, [POINTER(c_void_p), c_int, c_uint64, c_void_p]),
+    "thorn_peer_wait": (c_int, [c_void_p, c_int, c_uint64, c_uint64, c_void_p, c_void_p]),
 }
 
 _lock = threading.Lock()

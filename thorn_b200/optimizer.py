@@ -312,9 +312,11 @@ class THORN(Optimizer):
     # sharded path: exchange row slabs in waves of NS batches so that transfers overlap
     # the owners' Newton-Schulz work (False: every slab moves before any NS starts)
     pipeline_exchange: bool = False
-    # sharded path: "all_to_all" (one all_to_all_single collective per exchange) or
-    # "rounds" (world - 1 pairwise point-to-point rounds).  On 8 B200s the Llama-3-8B
-    # step takes 58.9 ms with all_to_all and 95.8 ms with rounds; on 2 they are even
+    # sharded path: "all_to_all" (one all_to_all_single collective per exchange),
+    # "rounds" (world - 1 pairwise point-to-point rounds) or "peer" (ranks of one node:
+    # the NS input pass stores rows into the owners' CUDA-IPC-mapped arenas, results come
+    # back by copy-engine peer copies, flags order both; see sharded.peer_exchange_and_ns).
+    # On 8 B200s the Llama-3-8B step takes 58.9 ms with all_to_all and 95.8 ms with rounds
     exchange: str = "all_to_all"
 
     def __init__(self, params, *, backend=torch.cuda, **conf):

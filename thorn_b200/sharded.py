@@ -310,6 +310,200 @@ def due_matrices(opt, mats, cfg, group):
     return [p for p, d in zip(mats, due) if d], [sc for sc, d in zip(scales, due) if d]
 
 
+PEER_FLAG_BYTES = 4096  # gather slots at 0, scatter slots at 512: 64 x 8 bytes each
+PEER_WAIT_LIMIT_NS = 10 * 1000 ** 3
+
+
+def _align(n: int, a: int = 256) -> int:
+    return (n + a - 1) // a * a
+
+
+def peer_layout(r, owners, chunks_r, parts, cols, ld, esz, pnn_rows):
+    """Byte offsets in owner r's arena (the same on every rank): the NS input of each of r's
+    chunks, then the result rows (and pnn row factors) of r's shard of every matrix another
+    rank owns.  ``cols[j]``, ``ld[j]``: columns and NS leading dimension of matrix j;
+    ``pnn_rows(j)``: whether matrix j's results carry per-row factors.  Returns
+    (x_off by chunk, u_off by matrix, f_off by matrix, total bytes)."""
+    off = PEER_FLAG_BYTES
+    x_off, u_off, f_off = {}, {}, {}
+    for ci, (R, C, _pdt, _sdt, js) in enumerate(chunks_r):
+        x_off[ci] = off
+        off += _align(len(js) * R * ld[js[0]] * esz)
+    for j in range(len(owners)):
+        n = parts[j][r][1]
+        if owners[j] != r and n > 0:
+            u_off[j] = off
+            off += _align(n * cols[j] * esz)
+            if pnn_rows(j):
+                f_off[j] = off
+                off += _align(n * 4)
+    return x_off, u_off, f_off, off
+
+
+class PeerArenas:
+    """This rank's exported device arena and its shard-group peers' arenas mapped by CUDA
+    IPC (``THORN.exchange = "peer"``).  Every rank computes the same size from the same
+    plan, so all ranks of the group re-export together when it grows."""
+
+    def __init__(self):
+        self.base = None
+        self.bytes = 0
+        self.ranks = None
+        self.ptrs = []  # arena of shard index s, as mapped into this process
+
+    def ensure(self, lib, need, ranks, me, group, dev):
+        need = _align(need, 1 << 20)
+        if self.base is not None and self.bytes >= need and self.ranks == ranks:
+            return
+        torch.cuda.synchronize(dev)  # nothing still reads or writes the old mappings
+        self.close(lib)
+        ptr = N.ctypes.c_void_p()
+        N.check(lib.thorn_peer_alloc(need, N.ctypes.byref(ptr)), "peer_alloc")
+        self.base, self.bytes, self.ranks = ptr.value, need, list(ranks)
+        h = (N.ctypes.c_char * 64)()
+        N.check(lib.thorn_ipc_handle(self.base, h), "ipc_handle")
+        handles = [None] * len(ranks)
+        dist.all_gather_object(handles, bytes(h), group=group)
+        self.ptrs = []
+        for s, hb in enumerate(handles):
+            if s == me:
+                self.ptrs.append(self.base)
+                continue
+            q = N.ctypes.c_void_p()
+            N.check(lib.thorn_ipc_open(hb, N.ctypes.byref(q)), "ipc_open")
+            self.ptrs.append(q.value)
+        dist.barrier(group=group)  # every rank has mapped every arena before any store
+
+    def close(self, lib):
+        for s, q in enumerate(self.ptrs):
+            if q is not None and q != self.base:
+                lib.thorn_ipc_close(q)
+        if self.base is not None:
+            lib.thorn_peer_free(self.base)
+        self.base, self.bytes, self.ptrs = None, 0, []
+
+
+def _signal_and_wait(lib, pa, world, me, slot0, value, err, stream, limit_ns):
+    """Release this rank's slot ``slot0 + me`` in every arena of the group (its own
+    included), then wait until all ``world`` slots of its own arena hold ``value``."""
+    slots = (N.ctypes.c_void_p * world)(*[pa.ptrs[s] + 8 * (slot0 + me) for s in range(world)])
+    N.check(lib.thorn_peer_signal(slots, world, value, stream), "peer_signal")
+    N.check(lib.thorn_peer_wait(pa.base + 8 * slot0, world, value, limit_ns, err.data_ptr(), stream), "peer_wait")
+
+
+def peer_exchange_and_ns(opt, lib, items, chunks, owner_chunks, owners, parts, rows_g, ld, world, me, ranks, group,
+                         dev, stream, arena, cfg, err, pnn_h, b1, write_grad, mark):
+    """Steps 2-5 of the sharded step over NVLink peer memory.
+
+    2+3. The NS input pass stores this rank's normalised rows straight into each owner's
+         arena (the gather is fused into that kernel); a flag release per owner and a
+         bounded wait on this rank's own slots order the stores before the owners' NS.
+    4.   Owners run batched NS (+ pnn factors) on their arena-resident inputs.
+    5.   Result rows and row factors go back to every shard by copy-engine peer copies
+         (cudaMemcpyAsync: no SMs taken from the GEMMs), ordered the same way.
+    Every rank passes every flag every step, so a rank with nothing to send still signals.
+    A flag that does not arrive within ``PEER_WAIT_LIMIT_NS`` sets the error flag
+    (``THORN.device_error()``) instead of hanging the GPU.
+    Returns (U, factors, slot, u_ptr, f_ptr) like the NCCL path."""
+    md = cfg.decouple_md
+    ns_dt = opt.ns_dtype
+    ns_code = N.dtype_code(ns_dt)
+    esz = torch.empty(0, dtype=ns_dt).element_size()
+    cols = [it.C for it in items]
+
+    def pnn_rows(j):
+        return cfg.needs_pnn(rows_g[j], cols[j])
+
+    chunks_of = [chunks if r == me else owner_chunks(r) for r in range(world)]
+    lay = [peer_layout(r, owners, chunks_of[r], parts, cols, ld, esz, pnn_rows) for r in range(world)]
+    arenas = opt.__dict__.setdefault("_peer_arenas", {})
+    pa = arenas.setdefault(dev, PeerArenas())
+    pa.ensure(lib, max(l[3] for l in lay), ranks, me, group, dev)
+    epoch = opt.__dict__.get("_peer_epoch", 0) + 1
+    opt._peer_epoch = epoch
+    limit = int(getattr(opt, "peer_wait_limit_ns", PEER_WAIT_LIMIT_NS))
+    where = {}  # j -> (chunk index, position) in its owner's chunk list
+    for r in range(world):
+        for ci, ch in enumerate(chunks_of[r]):
+            for k, j in enumerate(ch[4]):
+                where[j] = (ci, k)
+
+    # 2+3. normalised rows straight into the owners' NS inputs
+    casts: dict = {}
+    for j, it in enumerate(items):
+        r = owners[j]
+        ci, k = where[j]
+        r0, _n = parts[j][me]
+        dst = pa.ptrs[r] + lay[r][0][ci] + (k * rows_g[j] + r0) * ld[j] * esz
+        casts.setdefault((it.pdt, it.sdt), []).append(N.NsCastTensor(
+            it.g.data_ptr(), _local_of(it.state["moment"]).data_ptr(), arena.ptr(it.normsq), dst,
+            it.B, it.R, it.C, arena.ptr(it.rs) if md else None, arena.ptr(it.cs) if md else None,
+            1 if (md and not it.split) else 0, 1 if (md and not write_grad) else 0))
+    for (pdt, sdt), ts in casts.items():
+        udt = pdt if pdt == sdt else torch.float32
+        N.check(lib.thorn_ns_cast_multi(N.array(N.NsCastTensor, ts), len(ts), N.dtype_code(pdt), N.dtype_code(sdt),
+                                        N.dtype_code(udt), ns_code, b1, stream), "ns_cast_multi")
+    mark("gains_and_cast" if md else "cast")
+    _signal_and_wait(lib, pa, world, me, 0, 2 * epoch, err, stream, limit)
+    mark("exchange_out")
+
+    # 4. Newton-Schulz (+ pnn factors) on the owned, arena-resident inputs
+    coeffs = (N.ctypes.c_double * (3 * max(1, cfg.iters)))(*[x for abc in cfg.coeffs[:cfg.iters] for x in abc])
+    rs_ = list(cfg.restarts)
+    restarts = (N.ctypes.c_int32 * max(1, len(rs_)))(*rs_)
+    U, factors, slot = {}, {}, {}
+    for ci, (R, C, pdt, sdt, js) in enumerate(chunks):
+        nb = len(js)
+        for k, j in enumerate(js):
+            slot[j] = (ci, k)
+        U[ci] = torch.empty((nb, R, C), dtype=ns_dt, device=dev)
+        wsb = int(lib.thorn_ns_workspace_bytes(nb, R, C))
+        ws = torch.empty(max(256, wsb), dtype=torch.uint8, device=dev)
+        if opt.profile_ns is not None:
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev0.record()
+            f0 = N.gemm_flops()
+        N.check(lib.thorn_ns_batched(pa.base + lay[me][0][ci], U[ci].data_ptr(), ws.data_ptr(), wsb, nb, R, C,
+                                     ns_code, coeffs, cfg.iters, restarts, len(rs_), err.data_ptr(), stream),
+                "ns_batched")
+        if opt.profile_ns is not None:
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev1.record()
+            f1 = N.gemm_flops()
+            opt.profile_ns.append((ev0, ev1, f1[0] - f0[0], f1[1] - f0[1], (nb, R, C)))
+        del ws
+        if ci in pnn_h:
+            rsh, msh = pnn_h[ci]
+            (sp,) = opt._scratch(dev, [lib.thorn_pnn_scratch_bytes(nb, R)])
+            # the sharded reference runs pnn on fp32 u (thorn.py:1079-1081): no rounding, fp32 eps
+            pt = N.PnnTensor(U[ci].data_ptr(), arena.ptr(rsh), arena.ptr(msh), nb, R, C, sp, 1)
+            N.check(lib.thorn_pnn_stats_multi(N.array(N.PnnTensor, [pt]), 1, ns_code, N.F32, stream), "pnn_stats")
+            factors[ci] = arena.get(rsh).view(nb, R)
+    mark("newton_schulz")
+
+    # 5. result rows (+ row factors) to every other shard of each owned matrix
+    for ci, (R, C, pdt, sdt, js) in enumerate(chunks):
+        for k, j in enumerate(js):
+            for s in range(world):
+                r0, n = parts[j][s]
+                if s == me or n == 0:
+                    continue
+                src = U[ci].data_ptr() + (k * R + r0) * C * esz
+                N.check(lib.thorn_copy_async(pa.ptrs[s] + lay[s][1][j], src, n * C * esz, stream), "copy_async")
+                if ci in factors:
+                    fsrc = factors[ci].data_ptr() + (k * R + r0) * 4
+                    N.check(lib.thorn_copy_async(pa.ptrs[s] + lay[s][2][j], fsrc, n * 4, stream), "copy_async")
+    _signal_and_wait(lib, pa, world, me, 64, 2 * epoch + 1, err, stream, limit)
+    mark("exchange_back")
+    u_ptr = {j: pa.base + off for j, off in lay[me][1].items()}
+    f_ptr = {j: pa.base + off for j, off in lay[me][2].items()}
+    return U, factors, slot, u_ptr, f_ptr
+
+
+def _local_of(t):
+    return t.to_local() if isinstance(t, DTensor) else t
+
+
 def _stage_marks(opt):
     """A function that records a named CUDA event on the current stream into this step's
     stage list when ``opt.profile_stages`` is a list, else does nothing."""
@@ -413,117 +607,131 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
     if md:
         opt._md_gains(items, cfg, arena, stream)
 
-    # 2. normalised rows -> owner buffers / send slabs
-    X = {}
-    U = {}
-    slot = {}  # j -> (chunk index, position in chunk)
-    for ci, (R, C, pdt, sdt, js) in enumerate(chunks):
-        X[ci] = torch.empty((len(js), R, ld[js[0]]), dtype=ns_dt, device=dev)
-        U[ci] = torch.empty((len(js), R, C), dtype=ns_dt, device=dev)
-        for k, j in enumerate(js):
-            slot[j] = (ci, k)
-    # send slabs grouped by owner (matrix index ascending within an owner): each
-    # round's message to one owner is then one contiguous range of this buffer
-    send_rows = {}
-    n_send = sum(it.R * ld[j] for j, it in enumerate(items) if owners[j] != me)
-    send_buf = torch.empty(max(1, n_send), dtype=ns_dt, device=dev)
-    off = 0
-    for j in sorted((j for j in range(len(items)) if owners[j] != me), key=lambda j: (owners[j], j)):
-        it = items[j]
-        send_rows[j] = send_buf[off:off + it.R * ld[j]].view(it.R, ld[j])
-        off += it.R * ld[j]
-
-    def owner_rows(j, s):
-        ci, k = slot[j]
-        r0, n = parts[j][s]
-        return X[ci][k, r0:r0 + n]
-
-    casts: dict = {}
-    for j, it in enumerate(items):
-        dst = owner_rows(j, me) if owners[j] == me else send_rows[j]
-        casts.setdefault((it.pdt, it.sdt), []).append(N.NsCastTensor(
-            it.g.data_ptr(), _local(it.state["moment"]).data_ptr(), arena.ptr(it.normsq), dst.data_ptr(),
-            it.B, it.R, it.C, arena.ptr(it.rs) if md else None, arena.ptr(it.cs) if md else None,
-            1 if (md and not it.split) else 0, 1 if (md and not write_grad) else 0))
-    for (pdt, sdt), ts in casts.items():
-        udt = pdt if pdt == sdt else torch.float32
-        N.check(lib.thorn_ns_cast_multi(N.array(N.NsCastTensor, ts), len(ts), N.dtype_code(pdt), N.dtype_code(sdt),
-                                        N.dtype_code(udt), ns_code, b1, stream), "ns_cast_multi")
-    mark("gains_and_cast" if md else "cast")
-
-    xchg = exchange if getattr(opt, "exchange", "all_to_all") == "rounds" else exchange_all_to_all
-    # 3. slabs to owners: every wave's exchange is queued now (the NCCL stream runs them
-    # in order); each NS batch waits only for its own wave
-    gathers = []
-    for js in wave_js:
-        sends, recvs = plan_gather(owners, me, world, lambda j: send_rows[j], owner_rows, subset=js)
-        gathers.append(xchg(sends, recvs, ranks, group, wait=False))
-
-    # 5. (buffers) result rows (+ row factors) come back to every shard
-    u_loc, f_loc = {}, {}
-    for j, it in enumerate(items):
-        if owners[j] != me:
-            u_loc[j] = torch.empty((it.R, it.C), dtype=ns_dt, device=dev)
-            if cfg.needs_pnn(rows_g[j], it.C):
-                f_loc[j] = torch.empty(it.R, dtype=torch.float32, device=dev)
-    factors = {}
-
-    def owner_parts(j, s):
-        ci, k = slot[j]
-        r0, n = parts[j][s]
-        out = [U[ci][k, r0:r0 + n]]
-        if ci in factors:
-            out.append(factors[ci][k, r0:r0 + n])
-        return out
-
-    def my_parts(j):
-        return [u_loc[j]] + ([f_loc[j]] if j in f_loc else [])
-
-    # 4. Newton-Schulz (+ pnn factors) on owned matrices, wave by wave, and 5. each
-    # wave's results back to their shards
-    coeffs = (N.ctypes.c_double * (3 * max(1, cfg.iters)))(*[x for abc in cfg.coeffs[:cfg.iters] for x in abc])
-    rs_ = list(cfg.restarts)
-    restarts = (N.ctypes.c_int32 * max(1, len(rs_)))(*rs_)
-    scatters = []
-    for w, js_w in enumerate(wave_js):
-        gathers[w].wait()  # the current stream waits; the host does not
-        if n_waves == 1:
-            mark("exchange_out")
+    def _nccl_exchange_and_ns():
+        """Steps 2-5 with NCCL exchanges: (U, factors, slot, u_ptr, f_ptr) for the apply."""
+        # 2. normalised rows -> owner buffers / send slabs
+        X = {}
+        U = {}
+        slot = {}  # j -> (chunk index, position in chunk)
         for ci, (R, C, pdt, sdt, js) in enumerate(chunks):
-            if wave_of[js[0]] != w:
-                continue
-            nb = len(js)
-            wsb = int(lib.thorn_ns_workspace_bytes(nb, R, C))
-            ws = torch.empty(max(256, wsb), dtype=torch.uint8, device=dev)
-            if opt.profile_ns is not None:
-                ev0 = torch.cuda.Event(enable_timing=True)
-                ev0.record()
-                f0 = N.gemm_flops()
-            N.check(lib.thorn_ns_batched(X[ci].data_ptr(), U[ci].data_ptr(), ws.data_ptr(), wsb, nb, R, C, ns_code,
-                                         coeffs, cfg.iters, restarts, len(rs_), err.data_ptr(), stream), "ns_batched")
-            if opt.profile_ns is not None:
-                ev1 = torch.cuda.Event(enable_timing=True)
-                ev1.record()
-                f1 = N.gemm_flops()
-                opt.profile_ns.append((ev0, ev1, f1[0] - f0[0], f1[1] - f0[1], (nb, R, C)))
-            del ws
-            X[ci] = None
-            if ci in pnn_h:
-                rsh, msh = pnn_h[ci]
-                (sp,) = opt._scratch(dev, [lib.thorn_pnn_scratch_bytes(nb, R)])
-                # the sharded reference runs pnn on fp32 u (thorn.py:1079-1081): no rounding, fp32 eps
-                pt = N.PnnTensor(U[ci].data_ptr(), arena.ptr(rsh), arena.ptr(msh), nb, R, C, sp, 1)
-                N.check(lib.thorn_pnn_stats_multi(N.array(N.PnnTensor, [pt]), 1, ns_code, N.F32, stream),
-                        "pnn_stats")
-                factors[ci] = arena.get(rsh).view(nb, R)
-        if n_waves == 1:
-            mark("newton_schulz")
-        sends, recvs = plan_scatter(owners, me, world, owner_parts, my_parts, subset=js_w)
-        scatters.append(xchg(sends, recvs, ranks, group, wait=False))
-    for ex in scatters:
-        ex.wait()
-    mark("exchange_back" if n_waves == 1 else "exchange_and_newton_schulz")
-    del X, send_buf, send_rows
+            X[ci] = torch.empty((len(js), R, ld[js[0]]), dtype=ns_dt, device=dev)
+            U[ci] = torch.empty((len(js), R, C), dtype=ns_dt, device=dev)
+            for k, j in enumerate(js):
+                slot[j] = (ci, k)
+        # send slabs grouped by owner (matrix index ascending within an owner): each
+        # round's message to one owner is then one contiguous range of this buffer
+        send_rows = {}
+        n_send = sum(it.R * ld[j] for j, it in enumerate(items) if owners[j] != me)
+        send_buf = torch.empty(max(1, n_send), dtype=ns_dt, device=dev)
+        off = 0
+        for j in sorted((j for j in range(len(items)) if owners[j] != me), key=lambda j: (owners[j], j)):
+            it = items[j]
+            send_rows[j] = send_buf[off:off + it.R * ld[j]].view(it.R, ld[j])
+            off += it.R * ld[j]
+
+        def owner_rows(j, s):
+            ci, k = slot[j]
+            r0, n = parts[j][s]
+            return X[ci][k, r0:r0 + n]
+
+        casts: dict = {}
+        for j, it in enumerate(items):
+            dst = owner_rows(j, me) if owners[j] == me else send_rows[j]
+            casts.setdefault((it.pdt, it.sdt), []).append(N.NsCastTensor(
+                it.g.data_ptr(), _local(it.state["moment"]).data_ptr(), arena.ptr(it.normsq), dst.data_ptr(),
+                it.B, it.R, it.C, arena.ptr(it.rs) if md else None, arena.ptr(it.cs) if md else None,
+                1 if (md and not it.split) else 0, 1 if (md and not write_grad) else 0))
+        for (pdt, sdt), ts in casts.items():
+            udt = pdt if pdt == sdt else torch.float32
+            N.check(lib.thorn_ns_cast_multi(N.array(N.NsCastTensor, ts), len(ts), N.dtype_code(pdt), N.dtype_code(sdt),
+                                            N.dtype_code(udt), ns_code, b1, stream), "ns_cast_multi")
+        mark("gains_and_cast" if md else "cast")
+
+        xchg = exchange if getattr(opt, "exchange", "all_to_all") == "rounds" else exchange_all_to_all
+        # 3. slabs to owners: every wave's exchange is queued now (the NCCL stream runs them
+        # in order); each NS batch waits only for its own wave
+        gathers = []
+        for js in wave_js:
+            sends, recvs = plan_gather(owners, me, world, lambda j: send_rows[j], owner_rows, subset=js)
+            gathers.append(xchg(sends, recvs, ranks, group, wait=False))
+
+        # 5. (buffers) result rows (+ row factors) come back to every shard
+        u_loc, f_loc = {}, {}
+        for j, it in enumerate(items):
+            if owners[j] != me:
+                u_loc[j] = torch.empty((it.R, it.C), dtype=ns_dt, device=dev)
+                if cfg.needs_pnn(rows_g[j], it.C):
+                    f_loc[j] = torch.empty(it.R, dtype=torch.float32, device=dev)
+        factors = {}
+
+        def owner_parts(j, s):
+            ci, k = slot[j]
+            r0, n = parts[j][s]
+            out = [U[ci][k, r0:r0 + n]]
+            if ci in factors:
+                out.append(factors[ci][k, r0:r0 + n])
+            return out
+
+        def my_parts(j):
+            return [u_loc[j]] + ([f_loc[j]] if j in f_loc else [])
+
+        # 4. Newton-Schulz (+ pnn factors) on owned matrices, wave by wave, and 5. each
+        # wave's results back to their shards
+        coeffs = (N.ctypes.c_double * (3 * max(1, cfg.iters)))(*[x for abc in cfg.coeffs[:cfg.iters] for x in abc])
+        rs_ = list(cfg.restarts)
+        restarts = (N.ctypes.c_int32 * max(1, len(rs_)))(*rs_)
+        scatters = []
+        for w, js_w in enumerate(wave_js):
+            gathers[w].wait()  # the current stream waits; the host does not
+            if n_waves == 1:
+                mark("exchange_out")
+            for ci, (R, C, pdt, sdt, js) in enumerate(chunks):
+                if wave_of[js[0]] != w:
+                    continue
+                nb = len(js)
+                wsb = int(lib.thorn_ns_workspace_bytes(nb, R, C))
+                ws = torch.empty(max(256, wsb), dtype=torch.uint8, device=dev)
+                if opt.profile_ns is not None:
+                    ev0 = torch.cuda.Event(enable_timing=True)
+                    ev0.record()
+                    f0 = N.gemm_flops()
+                N.check(lib.thorn_ns_batched(X[ci].data_ptr(), U[ci].data_ptr(), ws.data_ptr(), wsb, nb, R, C, ns_code,
+                                             coeffs, cfg.iters, restarts, len(rs_), err.data_ptr(), stream), "ns_batched")
+                if opt.profile_ns is not None:
+                    ev1 = torch.cuda.Event(enable_timing=True)
+                    ev1.record()
+                    f1 = N.gemm_flops()
+                    opt.profile_ns.append((ev0, ev1, f1[0] - f0[0], f1[1] - f0[1], (nb, R, C)))
+                del ws
+                X[ci] = None
+                if ci in pnn_h:
+                    rsh, msh = pnn_h[ci]
+                    (sp,) = opt._scratch(dev, [lib.thorn_pnn_scratch_bytes(nb, R)])
+                    # the sharded reference runs pnn on fp32 u (thorn.py:1079-1081): no rounding, fp32 eps
+                    pt = N.PnnTensor(U[ci].data_ptr(), arena.ptr(rsh), arena.ptr(msh), nb, R, C, sp, 1)
+                    N.check(lib.thorn_pnn_stats_multi(N.array(N.PnnTensor, [pt]), 1, ns_code, N.F32, stream),
+                            "pnn_stats")
+                    factors[ci] = arena.get(rsh).view(nb, R)
+            if n_waves == 1:
+                mark("newton_schulz")
+            sends, recvs = plan_scatter(owners, me, world, owner_parts, my_parts, subset=js_w)
+            scatters.append(xchg(sends, recvs, ranks, group, wait=False))
+        for ex in scatters:
+            ex.wait()
+        mark("exchange_back" if n_waves == 1 else "exchange_and_newton_schulz")
+        del X, send_buf, send_rows
+        keep.extend([u_loc, f_loc])
+        return (U, factors, slot, {j: t.data_ptr() for j, t in u_loc.items()},
+                {j: t.data_ptr() for j, t in f_loc.items()})
+
+    keep = []  # the NCCL path's receive buffers live until the apply has been enqueued
+    if getattr(opt, "exchange", "all_to_all") == "peer" and world > 1:
+        # 2-5 over peer memory: rows stored into the owners' arenas, results copied back
+        U, factors, slot, u_ptr, f_ptr = peer_exchange_and_ns(
+            opt, lib, items, chunks, owner_chunks, owners, parts, rows_g, ld, world, me, ranks, group, dev, stream,
+            arena, cfg, err, pnn_h, b1, write_grad, mark)
+    else:
+        U, factors, slot, u_ptr, f_ptr = _nccl_exchange_and_ns()
 
     # 6. apply on local rows
     scr = opt._scratch(dev, [lib.thorn_sumsq_scratch_bytes(it.B, it.R, it.C) if md else 0 for it in items])
@@ -532,13 +740,13 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
         if owners[j] == me:
             ci, k = slot[j]
             r0, n = parts[j][me]
-            uj = U[ci][k, r0:r0 + n]
-            fj = factors[ci][k, r0:r0 + n] if ci in factors else None
+            uj = U[ci][k, r0:r0 + n].data_ptr()
+            fj = factors[ci][k, r0:r0 + n].data_ptr() if ci in factors else None
         else:
-            uj, fj = u_loc[j], f_loc.get(j)
+            uj, fj = u_ptr[j], f_ptr.get(j)
         lr_eff = float(cfg.lr) * cfg.lr_scale(rows_g[j], it.C) * scales[j]
         posts.setdefault(it.pdt, []).append(N.OrthoPostTensor(
-            uj.data_ptr(), it.p.data_ptr(), None if fj is None else fj.data_ptr(), None,
+            uj, it.p.data_ptr(), fj, None,
             arena.ptr(it.pnorm) if md else None, it.B, it.R, it.C, lr_eff, sp if md else None, 0))
     for pdt, ts in posts.items():
         N.check(lib.thorn_ortho_post_multi(N.array(N.OrthoPostTensor, ts), len(ts), ns_code, N.dtype_code(pdt),
@@ -549,5 +757,5 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
         opt._md_prep(items, arena, new=True, stream=stream)
         opt._md_finalize(items, arena, lambda it: True, stream)
         mark("md_renorm")
-    del U, u_loc, f_loc
+    del U, keep
     opt._finish(mats, cfg)
