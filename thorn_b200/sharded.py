@@ -743,7 +743,7 @@ def _step_matrices(opt, mats, cfg, ranks, group, world, me, dev, Arena, _local, 
             uj = U[ci][k, r0:r0 + n].data_ptr()
             fj = factors[ci][k, r0:r0 + n].data_ptr() if ci in factors else None
         else:
-            uj, fj = u_ptr[j], f_ptr.get(j)
+            uj, fj = u_ptr.get(j), f_ptr.get(j)  # none when this rank's shard of j is empty
         lr_eff = float(cfg.lr) * cfg.lr_scale(rows_g[j], it.C) * scales[j]
         posts.setdefault(it.pdt, []).append(N.OrthoPostTensor(
             uj, it.p.data_ptr(), fj, None,
