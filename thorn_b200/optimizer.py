@@ -396,6 +396,17 @@ class THORN(Optimizer):
         model._gradient_release_hooks = hooks
         self._update_rate = update_rate
 
+    def release_peer_memory(self) -> None:
+        """Free the device arenas of the peer-memory exchange (``exchange = "peer"``) and
+        unmap the peers' ones.  Collective: every rank of the shard group calls it at the
+        same point, between steps.  A later peer-exchange step allocates them again."""
+        arenas = self.__dict__.get("_peer_arenas", {})
+        if arenas:
+            lib = N.load()
+            for dev, pa in arenas.items():
+                pa.release(lib, dev)
+            arenas.clear()
+
     def device_error(self) -> bool:
         """True if a bounded device-side wait of a kernel gave up (reads a device flag; syncs)."""
         return any(int(t.item()) != 0 for t in self._err.values())

@@ -349,6 +349,7 @@ class PeerArenas:
         self.base = None
         self.bytes = 0
         self.ranks = None
+        self.group = None
         self.ptrs = []  # arena of shard index s, as mapped into this process
 
     def ensure(self, lib, need, ranks, me, group, dev):
@@ -359,7 +360,7 @@ class PeerArenas:
         self.close(lib)
         ptr = N.ctypes.c_void_p()
         N.check(lib.thorn_peer_alloc(need, N.ctypes.byref(ptr)), "peer_alloc")
-        self.base, self.bytes, self.ranks = ptr.value, need, list(ranks)
+        self.base, self.bytes, self.ranks, self.group = ptr.value, need, list(ranks), group
         h = (N.ctypes.c_char * 64)()
         N.check(lib.thorn_ipc_handle(self.base, h), "ipc_handle")
         handles = [None] * len(ranks)
@@ -373,6 +374,15 @@ class PeerArenas:
             N.check(lib.thorn_ipc_open(hb, N.ctypes.byref(q)), "ipc_open")
             self.ptrs.append(q.value)
         dist.barrier(group=group)  # every rank has mapped every arena before any store
+
+    def release(self, lib, dev):
+        """Unmap the peers' arenas and free this rank's, once no rank touches them any more:
+        every rank of the group must call this together (it synchronises and barriers)."""
+        if self.base is None:
+            return
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=self.group)
+        self.close(lib)
 
     def close(self, lib):
         for s, q in enumerate(self.ptrs):
