@@ -71,6 +71,7 @@ struct Params {
   float alpha, beta, diag2;
   int sym, trans_out, c_vec, d_vec, tma_epi, c_bcast, l2hint;
   int tiles_m, tiles_n, tiles_per_mat, total_tiles, num_kb;
+  int col_major;  // 2-CTA kernel, full tiles: tile index runs down the columns (tm fastest)
   int* err;
   uint64_t wait_limit_ns;  // limit of every mbarrier wait before the CTA gives up
   int test_stall;          // failure test: producers issue no loads, so the MMA warp's wait runs out
@@ -575,8 +576,13 @@ __device__ __forceinline__ void decode_tile2(const Params& p, int t, int& b, int
   b = t / p.tiles_per_mat;
   int l = t - b * p.tiles_per_mat;
   if (!p.sym) {
-    tm = l / p.tiles_n;
-    tn = l - tm * p.tiles_n;
+    if (p.col_major) {
+      tn = l / p.tiles_m;
+      tm = l - tn * p.tiles_m;
+    } else {
+      tm = l / p.tiles_n;
+      tn = l - tm * p.tiles_n;
+    }
     return;
   }
   tm = 0;
@@ -1204,6 +1210,11 @@ int run_gemm(const GemmOp& op, int dtype, int* err, cudaStream_t st) {
   prm.l2hint = pair && g_l2_hints.load() != 0;
   prm.tiles_m = (op.M + BMt - 1) / BMt;
   prm.tiles_n = (op.N + BN - 1) / BN;
+  // A wide output (the m x n products of Gram NS: 16 x 56 cluster tiles at 4096 x 14336)
+  // walked row by row has every wave of clusters read all of B's panels (the whole
+  // 117 MB n-side operand) while A's few panels sit idle in L2.  Down the columns a wave
+  // reads all of the small m-side operand (32 MB) and ~5 panels of B, which stay in L2.
+  prm.col_major = (pair && !op.sym && prm.tiles_n > prm.tiles_m) ? 1 : 0;
   if (op.sym) {
     int cnt = 0;
     for (int tm = 0; tm < prm.tiles_m; ++tm)
