@@ -880,6 +880,49 @@ def ortho_only(args):
                       "finite": bool(all(torch.isfinite(p).all() for p in ps))}), flush=True)
 
 
+def copy_rate(args):
+    """Host<->device copy rate of this box, the bound of the end-to-end figure (which moves
+    16 GB each way per Llama-3-8B step): 8 GiB of bf16 from pinned host memory to the
+    device, back, and both directions at once on two streams (CUDA events, best of 3)."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n = 4 * 1024 ** 3  # 4 Gi bf16 elements: 8 GiB per direction (the rate, not the size, is reported)
+    h_in = torch.empty(n, dtype=torch.bfloat16, pin_memory=True)
+    h_out = torch.empty(n, dtype=torch.bfloat16, pin_memory=True)
+    d_in = torch.empty(n, dtype=torch.bfloat16, device=dev)
+    d_out = torch.zeros(n, dtype=torch.bfloat16, device=dev)
+    s1, s2 = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    nbytes = n * 2
+
+    def timed(h2d, d2h):
+        best = None
+        for _ in range(3):
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            s1.wait_stream(torch.cuda.current_stream())
+            s2.wait_stream(torch.cuda.current_stream())
+            if h2d:
+                with torch.cuda.stream(s1):
+                    d_in.copy_(h_in, non_blocking=True)
+            if d2h:
+                with torch.cuda.stream(s2):
+                    h_out.copy_(d_out, non_blocking=True)
+            torch.cuda.current_stream().wait_stream(s1)
+            torch.cuda.current_stream().wait_stream(s2)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1)
+            best = ms if best is None else min(best, ms)
+        return round(nbytes / (best * 1e-3) / 1e9, 1)
+
+    print(json.dumps({"copy_rate_gbs": {"h2d": timed(True, False), "d2h": timed(False, True),
+                                        "both_each_direction": timed(True, True)},
+                      "bytes_per_direction": nbytes, "pinned": True}), flush=True)
+
+
 def small_config_groups(name):
     """(groups, param dtype, state dtype, grad std) of BASELINE configs[0]-[2]: lists of
     (orthogonalize, shapes, init std or None for ones, group options)."""
@@ -992,9 +1035,14 @@ def main():
     ap.add_argument("--model", default="llama8b", choices=["llama8b", "llama70b", "tiny", "vad", "qwen300m"],
                     help="parameter set: llama8b (BASELINE configs[3], the headline), llama70b (configs[4], 8 "
                          "GPUs), or tiny / vad / qwen300m (configs[0]-[2], one GPU, step timing only)")
+    ap.add_argument("--copy-rate", action="store_true",
+                    help="measure the host<->device copy rate (pinned, one direction and both at once)")
     ap.add_argument("--ortho-only", default=None,
                     help="BxRxC: time steps of one decouple_md group of B bf16 RxC matrices (profiling)")
     args = ap.parse_args()
+    if args.copy_rate:
+        copy_rate(args)
+        return
     if args.model in ("tiny", "vad", "qwen300m"):
         small_config(args)
         return
