@@ -516,6 +516,14 @@ def gpu_arm(args, rank, world, local_rank):
         if world > 1:
             dist.barrier(device_ids=[local_rank])
 
+    def host_buffers(ts):
+        """Pinned host copies of ``ts``' shapes: one block (one copy per direction and step)
+        when they share a dtype, else one allocation each."""
+        if len({t.dtype for t in ts}) == 1:
+            from thorn_b200.host_stepper import pinned_block
+            return pinned_block([tuple(t.shape) for t in ts], ts[0].dtype)
+        return [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in ts]
+
     def max_over_ranks(x):
         if world == 1:
             return x
@@ -603,10 +611,10 @@ def gpu_arm(args, rank, world, local_rank):
     # ---------------- end to end: grads in from pinned host memory, params back out
     e2e = None
     if not args.no_e2e:
-        h_grads = [torch.empty(local(g).shape, dtype=local(g).dtype, pin_memory=True) for g in grads]
+        h_grads = host_buffers([local(g) for g in grads])
         for h, g in zip(h_grads, grads):
             h.copy_(local(g))
-        h_params = [torch.empty(local(p).shape, dtype=local(p).dtype, pin_memory=True) for p in params]
+        h_params = host_buffers([local(p) for p in params])
         bi = sum(h.numel() * h.element_size() for h in h_grads)
         bo = sum(h.numel() * h.element_size() for h in h_params)
         # the device-resident grads of the timed loop are not needed any more

@@ -330,6 +330,50 @@ def test_gradient_release_matches_step():
         assert torch.equal(a, b)  # deterministic kernels: bitwise equal
 
 
+@pytest.mark.parametrize("block", [True, False])
+def test_pinned_stepper_matches_step(block):
+    """Steps fed from pinned host memory (PinnedStepper) give bitwise the parameters of the
+    same steps on device gradients, with the host buffers as one ``pinned_block`` (one copy
+    per direction) or as separate allocations (one copy per tensor)."""
+    from thorn_b200 import THORN, PinnedStepper, pinned_block
+
+    shapes = [(96, 64), (64, 37), (37,), (128, 128), (5,)]
+
+    def params():
+        torch.manual_seed(1)
+        return [torch.nn.Parameter(torch.randn(s, device="cuda").to(torch.bfloat16)) for s in shapes]
+
+    def opt(ps):
+        return THORN([{"params": [p for p in ps if p.ndim == 2], "orthogonalize": True, "decouple_md": True,
+                       "lr": 1e-2},
+                      {"params": [p for p in ps if p.ndim == 1], "orthogonalize": False, "lr": 1e-3}])
+
+    gen = torch.Generator().manual_seed(2)
+    grads = [[torch.randn(s, generator=gen).to(torch.bfloat16) for s in shapes] for _ in range(4)]
+    ref = params()
+    o_ref = opt(ref)
+    for gs in grads:
+        for p, g in zip(ref, gs):
+            p.grad = g.cuda()
+        o_ref.step()
+    ps = params()
+    if block:
+        hg, hp = pinned_block(shapes, torch.bfloat16), pinned_block(shapes, torch.bfloat16)
+    else:
+        hg = [torch.empty(s, dtype=torch.bfloat16, pin_memory=True) for s in shapes]
+        hp = [torch.empty(s, dtype=torch.bfloat16, pin_memory=True) for s in shapes]
+    st = PinnedStepper(opt(ps), ps, hg, hp)
+    assert (st.grads_flat is not None) == block
+    for gs in grads:
+        st.wait_host_grads()
+        for h, g in zip(hg, gs):
+            h.copy_(g)
+        st.step()
+    st.synchronize()
+    for a, h, p in zip(ref, hp, ps):
+        assert torch.equal(a.detach().cpu(), h) and torch.equal(a, p)
+
+
 def test_step_is_deterministic():
     """Reductions are done in a fixed order: two runs give bitwise-equal results."""
     _, a = run_gpu("md_small")

@@ -239,10 +239,13 @@ def test_custom_ops_registered_with_fake_impls():
                                   torch.zeros(32, 64, dtype=torch.float16), None, 1.0, 0.0)
 
 
-def test_pinned_stepper_data_flow_with_fake_streams(monkeypatch):
+@pytest.mark.parametrize("block", [False, True])
+def test_pinned_stepper_data_flow_with_fake_streams(monkeypatch, block):
     """Every line of PinnedStepper on CPU tensors, with CUDA streams and events replaced by
     recording fakes: each step sees that step's host gradients, and after synchronize the
-    host parameter buffers hold the parameters of the last step."""
+    host parameter buffers hold the parameters of the last step.  ``block``: the host
+    buffers are views of one allocation laid out like ``pinned_block``'s, so each direction
+    is one copy of the whole block."""
     import contextlib
 
     import thorn_b200.host_stepper as HS
@@ -286,9 +289,19 @@ def test_pinned_stepper_data_flow_with_fake_streams(monkeypatch):
                 p.grad = None
 
     opt = AddGrad()
-    hg = [torch.zeros(3, 2), torch.zeros(5)]
-    hp = [torch.zeros(3, 2), torch.zeros(5)]
+    if block:
+        offs, n = HS._block_layout([(3, 2), (5,)], torch.float32)
+        assert offs == [0, 64] and n == 128  # views start 256 bytes apart
+        fg, fp = torch.zeros(n), torch.zeros(n)
+        hg = [fg[0:6].view(3, 2), fg[64:69]]
+        hp = [fp[0:6].view(3, 2), fp[64:69]]
+    else:
+        hg = [torch.zeros(3, 2), torch.zeros(5)]
+        hp = [torch.zeros(3, 2), torch.zeros(5)]
     st = HS.PinnedStepper(opt, params, hg, hp)
+    assert (st.grads_flat is not None) == block and (st.snapshot_flat is not None) == block
+    if block:  # the device views mirror the host block's layout
+        assert st.h_grads_flat.numel() == 69 and st.grads[0][1].data_ptr() == st.grads_flat[0][64:].data_ptr()
     for k in range(4):
         st.wait_host_grads()  # the previous step's gradient copy has read the host buffers
         for h in hg:
@@ -504,3 +517,21 @@ def test_sharded_exchange_defaults_to_all_to_all():
 
     assert THORN.exchange == "all_to_all"
     assert THORN.pipeline_exchange is False
+
+
+def test_block_of_accepts_only_ordered_views_of_one_storage():
+    """The one-copy path of PinnedStepper needs the host tensors in parameter order inside one
+    allocation; anything else keeps the per-tensor copies."""
+    from thorn_b200.host_stepper import _block_of
+
+    f = torch.zeros(256)
+    flat, offs = _block_of([f[0:6].view(2, 3), f[64:69], f[128:128]])
+    assert offs == [0, 64, 128] and flat.numel() == 128 and flat.data_ptr() == f.data_ptr()
+    flat, offs = _block_of([f[8:16], f[16:20]])  # a block need not start at the storage's start
+    assert offs == [0, 8] and flat.numel() == 12 and flat.data_ptr() == f[8:].data_ptr()
+    assert _block_of([f[64:69], f[0:6]]) is None  # out of order
+    assert _block_of([f[0:8], f[4:12]]) is None  # overlapping
+    assert _block_of([f[0:8], torch.zeros(8)]) is None  # two allocations
+    assert _block_of([f[0:8], f[8:16].to(torch.float64)]) is None  # two dtypes
+    assert _block_of([f[0:16].view(4, 4).t()]) is None  # not contiguous
+    assert _block_of([]) is None
