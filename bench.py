@@ -652,22 +652,32 @@ def gpu_arm(args, rank, world, local_rank):
             t1 = torch.cuda.Event(enable_timing=True)
             t0.record()
             stepper.h2d.wait_stream(torch.cuda.current_stream())  # no copy starts before t0
+            marks = []  # end of each step's work on the compute stream
             for _ in range(args.steps):
                 # the documented loop: the host may rewrite its gradient buffers only after
                 # the previous step's copy has read them (the buffers stay as they are here)
                 stepper.wait_host_grads()
                 stepper.step()
+                marks.append(torch.cuda.Event(enable_timing=True))
+                marks[-1].record()
             stepper.wait_on()
             t1.record()
             torch.cuda.synchronize()
             barrier()
             e2e_ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
+            # once the pipeline is full: the first gradient copy (before step 1 can start)
+            # and the last parameter copy (after the last step) fall outside this period
+            steady_ms = max_over_ranks(marks[0].elapsed_time(marks[-1]) / (len(marks) - 1)) \
+                if len(marks) > 1 else None
             if world > 1:
                 t = torch.tensor([bi, bo], device=dev, dtype=torch.float64)
                 dist.all_reduce(t)
                 bi, bo = int(t[0]), int(t[1])
             e2e = {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
-                   "mode": "pipelined: both copies overlap the steps on two copy streams (thorn_b200.PinnedStepper)"}
+                   "mode": "pipelined: both copies overlap the steps on two copy streams (thorn_b200.PinnedStepper)",
+                   "steady_ms_per_step": None if steady_ms is None else round(steady_ms, 3),
+                   "steady_note": "period between consecutive steps with the copy pipeline full; value also "
+                                  "holds the first gradient copy and the last parameter copy, once per run"}
             progress(rank, "end-to-end steps done")
             del stepper, h_grads, h_params
         except Exception as exc:  # one GPU: keep the device-timed line and measure serially
