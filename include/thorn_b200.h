@@ -343,6 +343,32 @@ typedef struct {
 THORN_API int64_t thorn_sumsq_scratch_bytes(int64_t batch, int64_t rows, int64_t cols);
 THORN_API int thorn_sumsq_multi(const thorn_sumsq_tensor* tensors, int n, int dtype, void* stream);
 
+/* Magma momentum-aligned masking statistics (replaces the three sums of
+ * _momentum_aligned_mask, thorn.py:806-829, and the direction recovery
+ * g * gain of _recover_direction, thorn.py:896-905, that feeds it):
+ *   out[0] = sum g'*m,  out[1] = sum g'^2,  out[2] = sum m^2
+ * over every element of the tensor (viewed as batch x rows x cols), each an
+ * fp64 sum of fp32 products in a fixed order (bitwise reproducible), where
+ * g' = g, or under decouple_md with row_gain set
+ *   split gain:  g' = rn_G(g * rn_G(rn_G(softplus(row_gain[b*rows+r])) * rn_G(softplus(col_gain[b*cols+c]))))
+ *   scalar gain: g' = rn_G(g * rn_G(softplus(row_gain[0])))
+ * (rn_G: rounding to the gradient dtype; the gains have the gradient dtype).
+ * An empty tensor leaves its out[] untouched. */
+typedef struct {
+  const void* g;         /* gradient, g_dtype */
+  const void* m;         /* moment before this step's update, m_dtype, same shape */
+  const void* row_gain;  /* NULL: no direction recovery */
+  const void* col_gain;  /* split gain only */
+  int32_t scalar_gain;
+  int64_t batch, rows, cols;
+  double* out;           /* [3] */
+  void* scratch;         /* thorn_magma_scratch_bytes(batch, rows, cols) bytes, zero (kernels leave it zero) */
+} thorn_magma_tensor;
+
+THORN_API int64_t thorn_magma_scratch_bytes(int64_t batch, int64_t rows, int64_t cols);
+THORN_API int thorn_magma_stats_multi(const thorn_magma_tensor* tensors, int n, int g_dtype, int m_dtype,
+                                      void* stream);
+
 /* --------------------------------------------------------------------------
  * Peer-memory exchange of the FSDP2 Shard(0) path (THORN.exchange = "peer").
  * Replaces the reference's per-matrix dist.gather / dist.scatter of fp32 rows

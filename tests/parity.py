@@ -8,6 +8,32 @@ import numpy as np
 import cases as C
 
 
+def magma_stats_cpu(items, cfg, recovered):
+    """CPU stand-in for ``thorn_magma_stats_multi`` in host-logic tests (the kernel needs a
+    GPU): ``THORN._magma_stats``'s [n, 3] fp64 sums (g*m, g^2, m^2) of each item, the
+    gradient recovered as g * gain in its own dtype under decouple_md, as the kernel's
+    contract states."""
+    import torch
+    import torch.nn.functional as F
+
+    from thorn_b200.optimizer import _local
+
+    rows = []
+    for it in items:
+        g, st = it.g, it.state
+        m = getattr(it, "m_rows", None)
+        m = _local(st["moment"]) if m is None else m
+        if recovered and cfg.decouple_md:
+            if it.split:
+                gain = F.softplus(_local(st["row_gain"])) * F.softplus(_local(st["col_gain"]))
+            else:
+                gain = F.softplus(_local(st["gain"]))
+            g = g * gain
+        g, m = g.double().flatten(), m.double().flatten()
+        rows.append(torch.stack([(g * m).sum(), (g * g).sum(), (m * m).sum()]))
+    return torch.stack(rows)
+
+
 def load_golden(path: str) -> dict:
     with np.load(path) as z:
         return {k: z[k] for k in z.files}

@@ -56,6 +56,8 @@ STRUCTS = {
     "thorn_ortho_post_tensor": (N.OrthoPostTensor, ["U", "p", "row_scale", "mat_stats", "p_normsq", "batch",
                                                     "rows", "cols", "lr", "scratch", "round_u"]),
     "thorn_sumsq_tensor": (N.SumsqTensor, ["x", "out", "batch", "rows", "cols", "scratch"]),
+    "thorn_magma_tensor": (N.MagmaTensor, ["g", "m", "row_gain", "col_gain", "scalar_gain", "batch", "rows",
+                                           "cols", "out", "scratch"]),
     "thorn_md_prep_tensor": (N.MdPrepTensor, ["gain", "sp", "sig", "n"]),
     "thorn_md_grad_tensor": (N.MdGradTensor, ["gsum", "sig", "grad", "n"]),
     "thorn_md_final_tensor": (N.MdFinalTensor, ["p", "normsq", "target", "target_stride", "row_sp", "col_sp",
@@ -103,6 +105,10 @@ def test_host_only_entry_points(lib):
     assert lib.thorn_ortho_pre_scratch_bytes(2, 128, 512, 0) > 0
     assert lib.thorn_ortho_pre_scratch_bytes(2, 128, 512, 1) > lib.thorn_ortho_pre_scratch_bytes(2, 128, 512, 0)
     assert lib.thorn_pnn_scratch_bytes(3, 100) == (4 + 2 * 300) * 4
+    # Magma sums: one counter (16 bytes), then three fp64 partials per 64x256 tile
+    assert lib.thorn_magma_scratch_bytes(1, 64, 256) == 16 + 3 * 8
+    assert lib.thorn_magma_scratch_bytes(2, 130, 300) == 16 + 3 * 2 * 3 * 2 * 8
+    assert lib.thorn_magma_scratch_bytes(0, 8, 8) == 0
 
 
 def test_argument_validation_without_gpu(lib):
@@ -124,6 +130,13 @@ def test_argument_validation_without_gpu(lib):
     assert lib.thorn_ns_workspace_bytes(1, 1 << 62, 3) == -1
     assert lib.thorn_ns_batched(1024, 2048, 4096, 1 << 62, big, big, big, 2, co, 1, rs, 0, None, None) == 1
     assert lib.thorn_ns_batched_static(1024, 2048, big, big, big, 2, co, 1, rs, 0, None, None) == 5  # too large
+    mg = N.array(N.MagmaTensor, [N.MagmaTensor(None, None, None, None, 0, 1, 4, 4, None, None)])
+    assert lib.thorn_magma_stats_multi(mg, 1, 0, 0, None) == 1  # null operands
+    assert lib.thorn_magma_stats_multi(mg, 1, 9, 0, None) == 1  # bad dtype
+    split = N.array(N.MagmaTensor, [N.MagmaTensor(16, 16, 16, None, 0, 1, 4, 4, 16, 16)])
+    assert lib.thorn_magma_stats_multi(split, 1, 0, 0, None) == 1  # split gain without column gains
+    empty = N.array(N.MagmaTensor, [N.MagmaTensor(None, None, None, None, 0, 1, 0, 4, None, None)])
+    assert lib.thorn_magma_stats_multi(empty, 1, 0, 0, None) == 0  # empty tensor: nothing to do
     # symmetric GEMM needs 8-element leading dimensions
     assert lib.thorn_sym_addmm(16, 16, None, 16, 1, 12, 16, 0, 1.0, 0.0, 2, None, None) == 2
     pre = N.array(N.OrthoPreTensor, [N.OrthoPreTensor(None, None, None, None, 1, 4, 4, None, None, 0, None, None,

@@ -147,9 +147,10 @@ def test_magma_generator_matches_oracle():
 
 
 @pytest.mark.parametrize("decouple_md", [False, True])
-def test_magma_scores_and_masks_match_oracle(decouple_md):
-    """THORN._magma (torch glue around the kernels) on CPU tensors against the oracle's
-    masking: same masked steps, same smoothed score, over several steps."""
+def test_magma_scores_and_masks_match_oracle(decouple_md, monkeypatch):
+    """THORN._magma (the score, mask and state glue around the statistics kernel) on CPU
+    tensors against the oracle's masking: same masked steps, same smoothed score, over
+    several steps.  The three sums come from a CPU stand-in of the kernel."""
     from oracle import thorn_oracle as O
     from thorn_b200.optimizer import _Item
 
@@ -157,6 +158,7 @@ def test_magma_scores_and_masks_match_oracle(decouple_md):
     p = nn.Parameter(torch.randn(12, 8) * 0.1)
     opt = THORN([{"orthogonalize": True, "params": [p], "lr": 1e-3, "momentum_align": True,
                   "decouple_md": decouple_md}])
+    monkeypatch.setattr(opt, "_magma_stats", P.magma_stats_cpu)
     cfg = GroupConfig.from_kwargs(**opt.param_groups[0])
     p.grad = torch.randn_like(p)
     st = opt.state[p]

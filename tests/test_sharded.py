@@ -485,6 +485,7 @@ def _due_worker(rank, world, port, result):
         shapes = [(8, 4), (6, 4), (10, 4), (4, 4)]
         ps = [torch.nn.Parameter(distribute_tensor(torch.randn(s), mesh, [Shard(0)])) for s in shapes]
         opt = THORN([{"orthogonalize": True, "params": ps, "lr": 1e-3, "momentum_align": True}])
+        opt._magma_stats = P.magma_stats_cpu  # the statistics kernel needs a GPU
         opt._update_rate = 2
         cfg = GroupConfig.from_kwargs(**opt.param_groups[0])
         ranks, group = S.shard_group(ps[0], rank)

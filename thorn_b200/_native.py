@@ -55,6 +55,12 @@ class SumsqTensor(Structure):
                 ("scratch", c_void_p)]
 
 
+class MagmaTensor(Structure):
+    _fields_ = [("g", c_void_p), ("m", c_void_p), ("row_gain", c_void_p), ("col_gain", c_void_p),
+                ("scalar_gain", c_int32), ("batch", c_int64), ("rows", c_int64), ("cols", c_int64),
+                ("out", c_void_p), ("scratch", c_void_p)]
+
+
 class MdPrepTensor(Structure):
     _fields_ = [("gain", c_void_p), ("sp", c_void_p), ("sig", c_void_p), ("n", c_int64)]
 
@@ -105,6 +111,8 @@ _PROTOS = {
     "thorn_md_finalize_multi": (c_int, [POINTER(MdFinalTensor), c_int, c_int, c_void_p]),
     "thorn_sumsq_scratch_bytes": (c_int64, [c_int64, c_int64, c_int64]),
     "thorn_sumsq_multi": (c_int, [POINTER(SumsqTensor), c_int, c_int, c_void_p]),
+    "thorn_magma_scratch_bytes": (c_int64, [c_int64, c_int64, c_int64]),
+    "thorn_magma_stats_multi": (c_int, [POINTER(MagmaTensor), c_int, c_int, c_int, c_void_p]),
     "thorn_peer_alloc": (c_int, [c_int64, POINTER(c_void_p)]),
     "thorn_peer_free": (c_int, [c_void_p]),
     "thorn_ipc_handle": (c_int, [c_void_p, c_void_p]),

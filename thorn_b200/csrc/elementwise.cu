@@ -863,6 +863,105 @@ __global__ void __launch_bounds__(kThreads) sumsq_kernel(const __grid_constant__
   tile_sum_to(e.out, e.scratch, t, e.batch, e.rows, e.cols, sq, red);
 }
 
+// ===========================================================================
+// Magma statistics  (thorn.py:806-829, with the direction recovery of 896-905)
+// ===========================================================================
+// Scratch: one counter (padded to 16 bytes), then 3 fp64 partials per tile.
+__host__ __device__ inline int64_t magma_bytes(int64_t B, int64_t R, int64_t C) {
+  return 16 + 3 * B * tiles_per_mat(R, C) * 8;
+}
+
+struct MagmaArgs {
+  Pack<thorn_magma_tensor> pk;
+};
+
+// softplus(beta=1, threshold=20) rounded to the gain dtype, as F.softplus
+template <class G>
+__device__ __forceinline__ float softplus_g(const G* gain, int64_t i) {
+  const float x = to_f(gain[i]);
+  return rnd<G>(x > 20.f ? x : log1pf(expf(x)));
+}
+
+// Each tile block sums g'*m, g'^2 and m^2 of its 64 x 256 tile (fp32 sums of eight
+// products, accumulated in fp64) and stores three partials; the last block of the
+// tensor adds all partials in tile order and writes the three fp64 totals.
+template <class G, class M>
+__global__ void __launch_bounds__(kThreads) magma_stats_kernel(const __grid_constant__ MagmaArgs a) {
+  __shared__ double red[32];
+  const int ti = find_tensor(a.pk, blockIdx.x);
+  const thorn_magma_tensor& e = a.pk.t[ti];
+  const bool vec = a.pk.vec[ti];
+  const int64_t lt = int64_t(blockIdx.x) - a.pk.start[ti];
+  const Tile t = tile_of(lt, e.rows, e.cols);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t c = t.c0 + lane * 8;
+  const int nc = (int)max64(0, min64(8, e.cols - c));
+  const G* rg = (const G*)e.row_gain;
+  const G* cg = (const G*)e.col_gain;
+  float csp[8];  // softplus of this lane's column gains (split gain), or the scalar gain in csp[0]
+#pragma unroll
+  for (int k = 0; k < 8; ++k) csp[k] = 1.f;
+  if (rg != nullptr) {
+    if (e.scalar_gain) {
+      csp[0] = softplus_g(rg, 0);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (k < nc) csp[k] = softplus_g(cg, t.b * e.cols + c + k);
+    }
+  }
+  double dot = 0.0, gg = 0.0, mm = 0.0;
+  for (int rr = warp; rr < kTR; rr += 8) {
+    const int64_t r = t.r0 + rr;
+    if (r >= e.rows || nc == 0) break;
+    const int64_t off = (t.b * e.rows + r) * e.cols + c;
+    float g[8], m[8];
+    load_n((const G*)e.g + off, g, nc, vec);
+    load_n((const M*)e.m + off, m, nc, vec);
+    if (rg != nullptr) {
+      if (e.scalar_gain) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) g[k] = rnd<G>(__fmul_rn(g[k], csp[0]));
+      } else {
+        const float rsp = softplus_g(rg, t.b * e.rows + r);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) g[k] = rnd<G>(__fmul_rn(g[k], rnd<G>(__fmul_rn(rsp, csp[k]))));
+      }
+    }
+    float d8 = 0.f, g8 = 0.f, m8 = 0.f;  // zero past nc: load_n fills 0
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      d8 = __fmaf_rn(g[k], m[k], d8);
+      g8 = __fmaf_rn(g[k], g[k], g8);
+      m8 = __fmaf_rn(m[k], m[k], m8);
+    }
+    dot += (double)d8;
+    gg += (double)g8;
+    mm += (double)m8;
+  }
+  unsigned* cnt = (unsigned*)e.scratch;
+  double* part = reinterpret_cast<double*>((char*)e.scratch + 16);
+  const int64_t T = a.pk.start[ti + 1] - a.pk.start[ti];
+  const double sd = block_sum_d(dot, red);
+  const double sg = block_sum_d(gg, red);
+  const double sm = block_sum_d(mm, red);
+  if (threadIdx.x == 0) {
+    part[lt] = sd;
+    part[T + lt] = sg;
+    part[2 * T + lt] = sm;
+  }
+  if (last_block(cnt, (unsigned)T)) {
+    const double td = ordered_sum_d(part, T, red);
+    const double tg = ordered_sum_d(part + T, T, red);
+    const double tm = ordered_sum_d(part + 2 * T, T, red);
+    if (threadIdx.x == 0) {
+      e.out[0] = td;
+      e.out[1] = tg;
+      e.out[2] = tm;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // dispatch helpers
 // ---------------------------------------------------------------------------
@@ -1209,5 +1308,36 @@ extern "C" int thorn_sumsq_multi(const thorn_sumsq_tensor* ts, int n, int dtype,
     });
   });
   (void)dt_size;
+  return d ? d : rc;
+}
+
+extern "C" int64_t thorn_magma_scratch_bytes(int64_t batch, int64_t rows, int64_t cols) {
+  if (batch <= 0 || rows <= 0 || cols <= 0) return 0;
+  return magma_bytes(batch, rows, cols);
+}
+
+extern "C" int thorn_magma_stats_multi(const thorn_magma_tensor* ts, int n, int g_dtype, int m_dtype,
+                                       void* stream) {
+  if (n < 0 || (n > 0 && ts == nullptr) || !valid_dt(g_dtype) || !valid_dt(m_dtype)) return THORN_ERR_ARG;
+  for (int i = 0; i < n; ++i) {
+    const auto& e = ts[i];
+    if (e.batch < 0 || e.rows < 0 || e.cols < 0) return THORN_ERR_ARG;
+    if (e.batch * e.rows * e.cols == 0) continue;
+    if (!e.g || !e.m || !e.out || !e.scratch) return THORN_ERR_ARG;
+    if (e.row_gain && !e.scalar_gain && !e.col_gain) return THORN_ERR_ARG;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = THORN_OK;
+  auto blocks = [](const thorn_magma_tensor& e) { return tiles_of(e.batch, e.rows, e.cols); };
+  auto vec = [](const thorn_magma_tensor& e) { return (e.cols % 8) == 0 && aligned16(e.g) && aligned16(e.m); };
+  int d = dispatch2(g_dtype, m_dtype, [&](auto* pg, auto* pm) {
+    using G = std::remove_pointer_t<decltype(pg)>;
+    using M = std::remove_pointer_t<decltype(pm)>;
+    rc = launch_packed(ts, n, blocks, vec, [&](const Pack<thorn_magma_tensor>& pk, int64_t nb) {
+      MagmaArgs a;
+      a.pk = pk;
+      magma_stats_kernel<G, M><<<(unsigned)nb, kThreads, 0, st>>>(a);
+    });
+  });
   return d ? d : rc;
 }

@@ -461,8 +461,11 @@ class THORN(Optimizer):
         where the generator masks the step.  The score compares the gradient
         (direction-recovered under decouple_md when ``recovered``) with the moment
         before this step's update (``it.m_rows`` when set: the gathered moment
-        rows of a sparse update).  ``group``: shard process group: the three sums
-        of all items are all-reduced in one call and the cosine is formed in fp32
+        rows of a sparse update).  The three sums of every item come from one
+        ``thorn_magma_stats_multi`` launch per dtype pair (:meth:`_magma_stats`);
+        the cosine, the sigmoid and the smoothed score of all items are formed from
+        them with a few vectorised ops.  ``group``: shard process group: the sums
+        are all-reduced in one call and the cosine is formed in fp32
         (thorn.py:820-829).  The smoothed scores of all items are read back to the
         host once per call (the reference reads each with ``.item()``).
         """
@@ -470,39 +473,96 @@ class THORN(Optimizer):
             it.scale = 1.0
         if not cfg.momentum_align or not items:
             return
-        flats = []
-        for it in items:
-            st = it.state
-            g = it.g
-            if recovered and cfg.decouple_md:
-                if it.split:
-                    gain = F.softplus(_local(st["row_gain"])) * F.softplus(_local(st["col_gain"]))
-                else:
-                    gain = F.softplus(_local(st["gain"]))
-                g = g * gain
-            m = getattr(it, "m_rows", None)
-            if m is None:
-                m = _local(st["moment"])
-            flats.append((g.reshape(-1), m.reshape(-1)))
-        if group is not None:
-            stats = torch.stack([torch.stack([(g * m).sum(), g.square().sum(), m.square().sum()]).float()
-                                 for g, m in flats])
-            dist.all_reduce(stats, group=group)
-            cos = [stats[i, 0] / (stats[i, 1].sqrt() * stats[i, 2].sqrt()).clamp_min(1e-12) for i in range(len(flats))]
-        else:
-            cos = [F.cosine_similarity(g, m, dim=0) for g, m in flats]
-        scores = []
-        for it, c in zip(items, cos):
-            st = it.state
-            st["s"] = MAGMA_EMA * st["s"] + (1 - MAGMA_EMA) * torch.sigmoid(c / MAGMA_TAU)
-            scores.append(st["s"].float())
-        for it, v in zip(items, torch.stack(scores).tolist()):
+        stats = self._magma_stats(items, cfg, recovered)
+        scores = self._magma_scores(items, stats, group)
+        for it, v in zip(items, scores):
             st = it.state
             st["random_state"], out = _w1rand(int(st["random_state"]))
             if out % 2:
                 it.scale, it.apply = 0.0, False
             else:
                 it.scale = v
+
+    def _magma_stats(self, items, cfg, recovered: bool) -> torch.Tensor:
+        """``[len(items), 3]`` fp64 device tensor: sum g*m, sum g^2, sum m^2 of every item
+        (thorn.py:818-826), the gradient recovered as ``g * gain`` under decouple_md
+        (thorn.py:896-905) inside the kernel.  Items with no elements keep zeros."""
+        lib = N.load()
+        dev = items[0].g.device
+        stream = N.stream_of(dev)
+        stats = torch.zeros((len(items), 3), dtype=torch.float64, device=dev)
+        recs, keep = [], []
+        for it in items:
+            st = it.state
+            g = it.g if it.g.is_contiguous() else it.g.contiguous()
+            m = getattr(it, "m_rows", None)
+            if m is None:
+                m = _local(st["moment"])
+            if not m.is_contiguous():
+                m = m.contiguous()
+            if m.shape != g.shape:
+                raise ValueError(f"Magma: moment shape {tuple(m.shape)} differs from gradient {tuple(g.shape)}")
+            rg = cg = None
+            scalar = 0
+            if recovered and cfg.decouple_md:
+                if it.split:
+                    rg, cg = _local(st["row_gain"]), _local(st["col_gain"])
+                else:
+                    rg, scalar = _local(st["gain"]), 1
+            keep.append((g, m))
+            recs.append((g, m, rg, cg, scalar) + _mat_view(g.shape))
+        scr = self._scratch(dev, [lib.thorn_magma_scratch_bytes(B, R, C) for *_, B, R, C in recs])
+        by_dt: dict = {}
+        base = stats.data_ptr()
+        for i, ((g, m, rg, cg, scalar, B, R, C), sp) in enumerate(zip(recs, scr)):
+            if rg is not None and rg.dtype != g.dtype:
+                raise TypeError("Magma: the gains must have the gradient dtype")
+            by_dt.setdefault((N.dtype_code(g.dtype), N.dtype_code(m.dtype)), []).append(N.MagmaTensor(
+                g.data_ptr(), m.data_ptr(), None if rg is None else rg.data_ptr(),
+                None if cg is None else cg.data_ptr(), scalar, B, R, C, base + 24 * i, sp))
+        for (gc, mc), ts in by_dt.items():
+            N.check(lib.thorn_magma_stats_multi(N.array(N.MagmaTensor, ts), len(ts), gc, mc, stream),
+                    "magma_stats_multi")
+        del keep  # contiguous copies: freed in stream order after the launch
+        return stats
+
+    @staticmethod
+    def _magma_scores(items, stats: torch.Tensor, group=None) -> list:
+        """Smoothed scores ``s`` of the items from their three sums (thorn.py:818-833), stored
+        in ``it.state["s"]``; returns them as host floats.
+
+        Single device: the cosine of ``F.cosine_similarity`` (each norm clamped at 1e-8)
+        from the fp64 sums, in the promoted dtype of gradient and moment.  Sharded: the sums
+        rounded to fp32, all-reduced over ``group``, dot / (|g| |m|) clamped at 1e-12 in fp32.
+        Then ``s = 0.9 s + 0.1 sigmoid(cos / 2)`` with torch's dtype promotion, as the
+        reference's 0-d tensor ops, for all items of one dtype pair at once."""
+        n = len(items)
+        if group is not None:
+            st32 = stats.float()
+            dist.all_reduce(st32, group=group)
+            cos = st32[:, 0] / (st32[:, 1].sqrt() * st32[:, 2].sqrt()).clamp_min(1e-12)
+            cdts = [torch.float32] * n
+        else:
+            cos = (stats[:, 0] / (stats[:, 1].sqrt().clamp_min(1e-8) * stats[:, 2].sqrt().clamp_min(1e-8))).float()
+            cdts = [torch.promote_types(it.g.dtype, (it.m_rows if getattr(it, "m_rows", None) is not None
+                                                     else _local(it.state["moment"])).dtype) for it in items]
+        keys: dict = {}
+        for j, it in enumerate(items):
+            keys.setdefault((cdts[j], it.state["s"].dtype), []).append(j)
+        order, parts = [], []
+        for (cdt, _sdt), js in keys.items():
+            c = (cos if len(js) == n else torch.stack([cos[j] for j in js])).to(cdt)
+            s_old = torch.stack([items[j].state["s"] for j in js])
+            s_new = MAGMA_EMA * s_old + (1 - MAGMA_EMA) * torch.sigmoid(c / MAGMA_TAU)
+            for t, j in enumerate(js):
+                items[j].state["s"] = s_new[t]
+            order += js
+            parts.append(s_new.float())
+        vals = torch.cat(parts).tolist()
+        out = [0.0] * n
+        for j, v in zip(order, vals):
+            out[j] = v
+        return out
 
     def _step_params(self, params, cfg: GroupConfig, gdict):
         sharded, local = [], []
