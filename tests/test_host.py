@@ -146,6 +146,41 @@ def test_magma_generator_matches_oracle():
         assert _w1rand(s) == O.w1rand(s)
 
 
+def test_magma_scores_keep_the_reference_dtype_rules():
+    """THORN._magma_scores forms the smoothed scores of many parameters with a few vectorised
+    ops; each must equal the reference's own 0-d tensor ops for that parameter alone
+    (thorn.py:818-833): the cosine in the promoted dtype of gradient and moment, and
+    s = 0.9 s + 0.1 sigmoid(cos / 2) with torch's promotion (so a bf16 score next to an
+    fp32 cosine becomes fp32).  Mixed dtypes in one call, zero sums (an empty tensor)."""
+    from thorn_b200.optimizer import MAGMA_EMA, MAGMA_TAU, _Item
+
+    torch.manual_seed(5)
+    combos = [(torch.float32, torch.float32, torch.float32), (torch.bfloat16, torch.float32, torch.bfloat16),
+              (torch.bfloat16, torch.bfloat16, torch.bfloat16), (torch.float16, torch.float32, torch.float16),
+              (torch.float32, torch.float32, torch.float32), (torch.bfloat16, torch.float32, torch.float32)]
+    items, want = [], []
+    for gdt, mdt, sdt in combos:
+        it = _Item()
+        it.g = torch.zeros(3, 4, dtype=gdt)
+        it.state = {"moment": torch.zeros(3, 4, dtype=mdt), "s": torch.rand((), dtype=torch.float32).to(sdt)}
+        items.append(it)
+    stats = torch.rand(len(items), 3, dtype=torch.float64) * 1e-4
+    stats[:, 0] -= 0.5e-4  # negative and positive cross sums
+    stats[4] = 0.0  # no elements: the cosine is 0
+    for j, it in enumerate(items):
+        dot, gg, mm = stats[j]
+        cos = (dot / (gg.sqrt().clamp_min(1e-8) * mm.sqrt().clamp_min(1e-8))).float()
+        c = cos.to(torch.promote_types(it.g.dtype, it.state["moment"].dtype))
+        want.append(MAGMA_EMA * it.state["s"] + (1 - MAGMA_EMA) * torch.sigmoid(c / MAGMA_TAU))
+    got = THORN._magma_scores(items, stats)
+    for it, w, v in zip(items, want, got):
+        s_new = it.state["s"]
+        assert s_new.dtype == w.dtype and s_new.ndim == 0
+        assert float(s_new) == pytest.approx(float(w), rel=2 * torch.finfo(w.dtype).eps)
+        assert v == float(s_new)
+    assert items[1].state["s"].dtype == torch.float32 and items[2].state["s"].dtype == torch.bfloat16
+
+
 @pytest.mark.parametrize("decouple_md", [False, True])
 def test_magma_scores_and_masks_match_oracle(decouple_md, monkeypatch):
     """THORN._magma (the score, mask and state glue around the statistics kernel) on CPU
