@@ -6,6 +6,7 @@ row slab to its owner and every result slab back.  GPU: the full sharded step
 on the full tensors -- the reference's own MD + FSDP2 path does not run on
 torch 2.11, so the single-device algorithm on full tensors is the oracle.
 """
+import math
 import os
 import socket
 import subprocess
@@ -560,3 +561,80 @@ def test_peer_layout_disjoint_and_aligned(world):
             assert all(o % 256 == 0 and o >= PEER_FLAG_BYTES for o, _ in spans)
             assert all(a + n <= b for (a, n), (b, _) in zip(spans, spans[1:]))
             assert spans[-1][0] + spans[-1][1] <= total
+
+
+def _stepper_worker(rank, world, port, result):
+    import contextlib
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from torch.distributed.device_mesh import init_device_mesh
+        from torch.distributed.tensor import Shard, distribute_tensor
+
+        import thorn_b200.host_stepper as HS
+
+        class FakeEvent:
+            def record(self, stream=None):
+                pass
+
+            def synchronize(self):
+                pass
+
+        class FakeStream:
+            def wait_event(self, ev):
+                pass
+
+            def wait_stream(self, s):
+                pass
+
+            def synchronize(self):
+                pass
+
+        compute = FakeStream()
+        HS.torch.cuda.Stream = lambda dev=None: FakeStream()
+        HS.torch.cuda.Event = lambda *a, **k: FakeEvent()
+        HS.torch.cuda.current_stream = lambda dev=None: compute
+        HS.torch.cuda.stream = lambda s: contextlib.nullcontext()
+        torch.Tensor.is_pinned = lambda self: True
+
+        mesh = init_device_mesh("cpu", (world,))
+        shapes = [(5, 4), (8, 3), (1, 6)]  # uneven splits; rank 1 holds no row of the last
+        ps = [torch.nn.Parameter(distribute_tensor(torch.zeros(s), mesh, [Shard(0)])) for s in shapes]
+
+        class AddGrad:  # stands in for THORN: p -= grad on the local shards
+            def step(self):
+                for p in ps:
+                    p._local_tensor.sub_(p.grad.to_local())
+                    p.grad = None
+
+        local = [p.to_local().shape for p in ps]
+        offs, n = HS._block_layout(local, torch.float32)
+        fg, fp = torch.zeros(n), torch.zeros(n)
+        hg = [fg[o:o + math.prod(s)].view(s) for o, s in zip(offs, local)]
+        hp = [fp[o:o + math.prod(s)].view(s) for o, s in zip(offs, local)]
+        st = HS.PinnedStepper(AddGrad(), ps, hg, hp)
+        ok = st.grads_flat is None and st.snapshot_flat is not None  # DTensor grads stay per tensor
+        for k in range(3):
+            st.wait_host_grads()
+            for h in hg:
+                h.fill_(k + 1.0)
+            st.step()
+        st.synchronize()
+        ok &= all(torch.equal(h, torch.full(h.shape, -6.0)) for h in hp)
+        ok &= all(torch.equal(p.to_local(), torch.full(p.to_local().shape, -6.0)) for p in ps)
+        result[rank] = bool(ok)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_pinned_stepper_dtensor_shards_gloo():
+    """PinnedStepper on Shard(0) DTensor parameters (the bench's end-to-end run at N > 1):
+    gradients are copied per local shard into DTensor gradients, the parameter snapshot is
+    one block mirroring pinned_block's layout of the local shards (an empty shard included),
+    and after three steps the host buffers hold every rank's updated local rows."""
+    ctx = mp.get_context("spawn")
+    result = ctx.Manager().dict()
+    mp.start_processes(_stepper_worker, args=(2, _free_port(), result), nprocs=2, join=True, start_method="spawn")
+    assert dict(result) == {0: True, 1: True}
