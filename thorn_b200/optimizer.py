@@ -35,7 +35,6 @@ from typing import Any, Callable, Literal, Optional, Union
 import torch
 import torch.distributed as dist
 import torch.nn as nn
-import torch.nn.functional as F
 from torch.distributed.tensor import DTensor, Replicate
 from torch.optim import Optimizer
 
